@@ -1,0 +1,327 @@
+#!/usr/bin/env python
+"""Decode-step GEMV benchmark of rumik_fast_b200 on B200 (BASELINE config 1 + the config-2 int8 head).
+
+One step = the 36-layer decode-step projection set (per layer: QKV 5120x3072, o_proj 3072x3072,
+gate_up 16384x3072, down 3072x8192, int4 group-128) followed by the int8 audio head (16385x3072), launched
+as 145 separate kernels in stream order - each GEMV waits for the previous kernel before it reads its input,
+exactly as in a decode step - and replayed from one CUDA graph, the way rumik-fast's engine and its own
+full-step benchmark run it (engine/rumik_int4.py:225-245, kernels/bench_gemv.py:83-113). Inputs follow the
+reference benchmark: fixed activations (x_h for QKV/o/gate_up/head, x_i for down). The weights (1.98 GB)
+are larger than L2 (126 MB), so no L2 flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-prefetch]
+
+Prints one JSON line (rank 0). value = algorithmic HBM bytes of a step / device time of a step, summed over
+ranks (each rank runs an independent replica of the step: weak scaling).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS = 36
+METRIC = "decode-step GEMV HBM GB/s"
+UNIT = "GB/s"
+# DRAM bytes (read + write) per launch of gemv_int4_kernel, measured by ncu (profiles/); None until captured
+NCU_TRAFFIC_PER_LAUNCH = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-prefetch", action="store_true", help="do not stream weights before the PDL wait")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="length of the bounded CPU-baseline sample")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples every 200 ms while the timed region runs (read-only queries)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows, self.proc, self.thread = [], None, None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def mark(self):
+        return len(self.rows)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+            self.thread.join(timeout=2)
+
+    def summary(self, start=0, end=None):
+        rows = self.rows[start:end]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------------------------- workload
+def build_workload(dev, seed):
+    from rumik_fast_b200 import synthetic as syn
+    gen = syn.generator(seed, dev)
+    layers = [[syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES] for _ in range(LAYERS)]
+    head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
+    xh = syn.activations((3072,), gen, dev)
+    xi = syn.activations((8192,), gen, dev)
+    outs = [torch.empty(n, device=dev, dtype=torch.float16) for _, n, _ in syn.LAYER_SHAPES]
+    logits = torch.empty(syn.HEAD_SHAPE[0], device=dev, dtype=torch.float16)
+    int4_bytes = LAYERS * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES)
+    head_bytes = syn.int8_bytes(*syn.HEAD_SHAPE)
+    return dict(layers=layers, head=head, xh=xh, xi=xi, outs=outs, logits=logits, int4_bytes=int4_bytes,
+                head_bytes=head_bytes)
+
+
+def step_fn(w, with_head=True):
+    import rumik_fast_b200 as rb
+    layers, outs, xh, xi = w["layers"], w["outs"], w["xh"], w["xi"]
+
+    def step():
+        for L in layers:
+            rb.gemv_int4_cuda(xh, *L[0], out=outs[0])   # QKV
+            rb.gemv_int4_cuda(xh, *L[1], out=outs[1])   # o_proj
+            rb.gemv_int4_cuda(xh, *L[2], out=outs[2])   # gate_up
+            rb.gemv_int4_cuda(xi, *L[3], out=outs[3])   # down
+        if with_head:
+            rb.gemv_int8_cuda(xh, *w["head"], out=w["logits"])
+    return step
+
+
+def capture(fn):
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def timed(run, steps, warmup, world):
+    """Device time of `steps` calls of run() (CUDA events on the current stream), max over ranks, in ms."""
+    import torch.distributed as dist
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        run()
+    e.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = s.elapsed_time(e)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+# ---------------------------------------------------------------------------------------------- CPU side
+def cpu_oracle_sample(seconds, threads=None):
+    """The reference's CPU path (fp32 dequantise-then-matvec, restated in numpy by oracle/) on the config-1
+    layer shapes, timed on the host cores for about `seconds`. Returns (GB/s, threads, description, n)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import oracle as O
+    from rumik_fast_b200 import synthetic as syn
+    threads = threads or os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    mats = []
+    for _, n, k in syn.LAYER_SHAPES:
+        q = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+        s = rng.uniform(0.002, 0.02, size=(n, k // 128)).astype(np.float16)
+        m = (-7.5 * s.astype(np.float32) + rng.normal(0, 1e-3, size=s.shape)).astype(np.float16)
+        x = rng.normal(0, 1, size=k).astype(np.float16)
+        mats.append((q, s, m, x, syn.int4_bytes(n, k)))
+    pool = ThreadPoolExecutor(threads)
+
+    def gemv(q, s, m, x):
+        rows = q.shape[0]
+        chunk = max(64, (rows + threads - 1) // threads)
+        parts = pool.map(lambda r0: O.gemv_int4_ref(x, q[r0:r0 + chunk], s[r0:r0 + chunk], m[r0:r0 + chunk]),
+                         range(0, rows, chunk))
+        return np.concatenate(list(parts))
+
+    gemv(*mats[1][:4])                                   # warm the pool / BLAS
+    t0 = time.perf_counter()
+    nbytes, n = 0, 0
+    while True:
+        q, s, m, x, b = mats[n % len(mats)]
+        gemv(q, s, m, x)
+        nbytes += b
+        n += 1
+        if time.perf_counter() - t0 >= seconds and n % len(mats) == 0:
+            break
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    return nbytes / dt / 1e9, threads, f"{n} int4 GEMVs over the 4 config-1 layer shapes ({n // 4} layers), {dt:.1f} s", n
+
+
+# ---------------------------------------------------------------------------------------------- arms
+def run_reference(a):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    gbs, threads, desc, n = cpu_oracle_sample(a.cpu_seconds)
+    line = {"metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "n_gpus": a.gpus, "steps": n, "warmup": 1,
+            "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "config-1 decode-step projection set (36 x QKV/o/gate_up/down, int4 g128), "
+                                   "CPU dequantise-then-matvec sample", "batch": 1},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(a):
+    import rumik_fast_b200 as rb
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rb.set_weight_prefetch(not a.no_prefetch)
+    w = build_workload(dev, seed=1234 + rank)
+    step = step_fn(w)
+    g_step = capture(step)
+    g_int4 = capture(step_fn(w, with_head=False))
+    step_bytes = w["int4_bytes"] + w["head_bytes"]
+    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
+        if os.environ.get("CUDA_VISIBLE_DEVICES", "").replace(",", "").isdigit() else local
+
+    with ClockSampler(gpu_index) as clk:
+        m0 = clk.mark()
+        ms = timed(g_step.replay, a.steps, a.warmup, world)
+        m1 = clk.mark()
+    clocks = clk.summary(m0, m1)
+    ms_step = ms / a.steps
+
+    # dominant kernel: the int4 GEMV (97 % of the step's bytes), timed alone over the same steps
+    ms4 = timed(g_int4.replay, max(1, a.steps // 2), a.warmup, world) / max(1, a.steps // 2)
+    launches4 = LAYERS * 4
+    achieved = (w["int4_bytes"] / launches4) / (ms4 / launches4 * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+
+    # end to end through the public API: pinned host inputs -> device, step, logits -> pinned host
+    hx, hi = w["xh"].cpu().pin_memory(), w["xi"].cpu().pin_memory()
+    hl = torch.empty_like(w["logits"], device="cpu").pin_memory()
+
+    def e2e_step():
+        w["xh"].copy_(hx, non_blocking=True)
+        w["xi"].copy_(hi, non_blocking=True)
+        g_step.replay()
+        hl.copy_(w["logits"], non_blocking=True)
+    e2e_steps = max(1, a.steps // 2)
+    ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
+
+    line = None
+    if rank == 0:
+        gbs = world * step_bytes / (ms_step * 1e-3) / 1e9
+        cpu = None
+        if world == 1:
+            c_gbs, c_threads, c_desc, _ = cpu_oracle_sample(a.cpu_seconds)
+            cpu = {"value": round(c_gbs, 3), "unit": UNIT, "cores": c_threads, "kind": "port", "sample": c_desc}
+        line = {
+            "metric": METRIC, "value": round(gbs, 1), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "config-1 36-layer decode-step projection set (QKV 5120x3072, o 3072x3072, "
+                                   "gate_up 16384x3072, down 3072x8192; int4 g128) + config-2 int8 head "
+                                   "16385x3072, batch 1, 145 stream-ordered kernels in one CUDA graph",
+                       "batch": 1, "bytes_per_step": step_bytes, "parallelism": f"replica x{world}",
+                       "weight_prefetch": not a.no_prefetch,
+                       "l2": "no flush: 1.98 GB of weights per step > 126 MB L2"},
+            "tok_s": round(world * 1e3 / ms_step, 1),
+            "pct_of_peak": round(100 * gbs / world / peak, 1),
+            "e2e": {"value": round(world * step_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": UNIT,
+                    "h2d_bytes_per_step": (3072 + 8192) * 2, "d2h_bytes_per_step": w["logits"].numel() * 2,
+                    "ms_per_step": round(ms_e2e, 5)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "kernel": "gemv_int4_kernel", "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                         "algorithmic_bytes_per_launch": w["int4_bytes"] // launches4},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": a.steps * (launches4 + 1),
+        }
+        print(json.dumps(line), flush=True)
+    del g_step, g_int4
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_ours(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

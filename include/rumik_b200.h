@@ -1,0 +1,109 @@
+/*
+ * rumik_b200.h - C ABI of the B200 (sm_100a) weight-only quantised linear-layer kernels.
+ *
+ * These entry points are the native boundary that replaces rumik-fast's torch extension
+ * (kernels/cuda_gemv.py:214-218, load_inline(... functions=["gemv_int4", "gemv_int8"])) and its Triton
+ * prefill matmul (kernels/mm_int4.py:59-73). They take plain device pointers, sizes, dtype codes and a
+ * cudaStream_t passed as void*. They never allocate, never synchronise, and are safe to call while a CUDA
+ * graph is being captured on `stream`. Every function returns an rb_status code (0 = success); argument
+ * checks run before any CUDA call, so a bad argument is reported without touching the device.
+ *
+ * Weight format (kernels/int4_gemv.py:1-3, modal_export_int4.py:48-59):
+ *   q  uint8 [N, K/2]   two 4-bit codes per byte, low nibble = even column, high nibble = odd column
+ *   s  fp16  [N, K/128] per-group scale
+ *   m  fp16  [N, K/128] per-group min;            w[n,k] = code[n,k] * s[n,k/128] + m[n,k/128]
+ * int8 head (kernels/cuda_gemv.py:234-242): q uint8 [N, K] = int8 + 128 (or signed int8), one scale per row.
+ *
+ * Alignment: every base pointer must be 16-byte aligned, and the activation row strides (ldx) must be a
+ * multiple of 8 elements; the kernels move weights with 16-byte bulk copies.
+ */
+#ifndef RUMIK_B200_H
+#define RUMIK_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The reference raises RuntimeError through TORCH_CHECK (kernels/cuda_gemv.py:121,135,190);
+ * the Python layer of this library turns a non-zero status into the same exception type. */
+enum rb_status {
+  RB_OK = 0,
+  RB_ERR_NULL = 1,    /* a required pointer is NULL */
+  RB_ERR_SHAPE = 2,   /* unsupported N / K / M / batch (e.g. K % 128 != 0) */
+  RB_ERR_DTYPE = 3,   /* unsupported dtype code */
+  RB_ERR_ALIGN = 4,   /* a pointer is not 16-byte aligned or a stride is not a multiple of 8 elements */
+  RB_ERR_LAUNCH = 5,  /* the CUDA launch failed (error reported by cudaGetLastError) */
+  RB_ERR_DEVICE = 6,  /* no usable sm_100 device, or a device query failed */
+  RB_ERR_TIMEOUT = 7  /* a kernel gave up a bounded wait (reported by rb_get_device_error) */
+};
+
+/* Element type codes for activations, outputs and scales. */
+enum rb_dtype { RB_F16 = 0, RB_BF16 = 1, RB_F32 = 2 };
+
+/* Launch flags. */
+enum rb_flags {
+  /* Launch with programmatic dependent launch: the kernel may start while the previous kernel on the
+   * stream is still running; it waits for that kernel (griddepcontrol.wait) before touching x or y. */
+  RB_FLAG_PDL = 1,
+  /* With RB_FLAG_PDL: also stream the weights (q, s, m) into shared memory BEFORE that wait. Only valid
+   * when the weights are not written by the kernel immediately before this one on the stream, which holds
+   * for inference weights loaded once. This is what lets a chain of GEMVs keep HBM busy across kernel
+   * boundaries. */
+  RB_FLAG_PREFETCH_WEIGHTS = 2
+};
+
+/*
+ * int4 group-128 GEMV, batch 1..16:  y[b, n] = sum_k w[n, k] * x[b, k]   (fp32 accumulation).
+ * Replaces gemv_int4(x, q, s, m, y, warps, rows) (kernels/cuda_gemv.py:130-136) and its kernel
+ * gemv_int4_kernel (kernels/cuda_gemv.py:38-115); the Python wrapper gemv_int4_cuda (:226-231) calls this.
+ *   x       [batch, K] activations (x_dtype RB_F16 or RB_BF16), row stride ldx elements
+ *   y       [batch, N] output (y_dtype RB_F16 or RB_BF16), row stride ldy elements
+ *   N >= 1, K % 128 == 0, 128 <= K <= 16384, 1 <= batch <= 16 (batch 0 or N 0: no-op)
+ */
+int rb_gemv_int4(const void* x, int x_dtype, int64_t ldx,
+                 const uint8_t* q, const uint16_t* s, const uint16_t* m,
+                 void* y, int y_dtype, int64_t ldy,
+                 int64_t N, int64_t K, int64_t batch, int flags, void* stream);
+
+/*
+ * int8 per-row GEMV (tied audio head), batch 1..16:  y[b, n] = s[n] * sum_k v(q[n, k]) * x[b, k]
+ *   v(q) = q - 128 for q_signed == 0 (uint8 storage of int8 + 128, as quantize_int8_rows writes it),
+ *   v(q) = (int8)q  for q_signed != 0.
+ * Replaces gemv_int8(x, q, s, y) (kernels/cuda_gemv.py:188-195) and gemv_int8_kernel (:141-186); the
+ * Python wrapper gemv_int8_cuda (:245-249) calls this. s_dtype RB_F32 (engine) or RB_F16 (configs).
+ *   N >= 1 (no padding to 16 required), K % 64 == 0, 64 <= K <= 16384, 1 <= batch <= 16
+ */
+int rb_gemv_int8(const void* x, int x_dtype, int64_t ldx,
+                 const uint8_t* q, int q_signed, const void* s, int s_dtype,
+                 void* y, int y_dtype, int64_t ldy,
+                 int64_t N, int64_t K, int64_t batch, int flags, void* stream);
+
+/*
+ * int4-weight matrix product (prefill) on tcgen05 tensor cores:  Y[t, n] = sum_k X[t, k] * w[n, k].
+ * Replaces mm_int4(x, q, s, m) (kernels/mm_int4.py:59-73) and its Triton kernel _mm_int4 (:24-46).
+ *   X [M, K] fp16 or bf16, row stride ldx;  Y [M, N] fp16 or bf16, row stride ldy.
+ *   The weights are dequantised to fp16 in shared memory (never stored wider than int4 in HBM).
+ *   M >= 1, N >= 1, K % 128 == 0.
+ */
+int rb_mm_int4(const void* X, int x_dtype, int64_t ldx,
+               const uint8_t* q, const uint16_t* s, const uint16_t* m,
+               void* Y, int y_dtype, int64_t ldy,
+               int64_t M, int64_t N, int64_t K, int flags, void* stream);
+
+/* Human-readable text for a status code (static storage). */
+const char* rb_status_string(int status);
+
+/* Library ABI version (major * 100 + minor). */
+int rb_version(void);
+
+/* Read and clear the device-side error word of the current device (bit set by a kernel that gave up a
+ * bounded wait). Synchronises `stream`. *out receives the word; returns RB_OK or RB_ERR_DEVICE. */
+int rb_get_device_error(unsigned int* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RUMIK_B200_H */

@@ -1,0 +1,81 @@
+"""ctypes binding of the C ABI in include/rumik_b200.h (librumik_b200.so, built in-tree for sm_100a).
+
+There is no fallback: if the library is missing or the device is not an sm_100 GPU, calls raise.
+"""
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "librumik_b200.so")
+
+# status codes (enum rb_status)
+OK, ERR_NULL, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_LAUNCH, ERR_DEVICE, ERR_TIMEOUT = range(8)
+# dtype codes (enum rb_dtype)
+F16, BF16, F32 = 0, 1, 2
+# launch flags (enum rb_flags)
+FLAG_PDL, FLAG_PREFETCH_WEIGHTS = 1, 2
+
+_DTYPE_CODE = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
+
+_c = ctypes
+_vp, _i64, _int = _c.c_void_p, _c.c_int64, _c.c_int
+SIGNATURES = {
+    "rb_gemv_int4": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
+    "rb_gemv_int8": (_int, [_vp, _int, _i64, _vp, _int, _vp, _int, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
+    "rb_mm_int4": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
+    "rb_status_string": (_c.c_char_p, [_int]),
+    "rb_version": (_int, []),
+    "rb_get_device_error": (_int, [_c.POINTER(_c.c_uint), _vp]),
+}
+
+_lib = None
+
+
+class RumikKernelError(RuntimeError):
+    """A native entry point returned a non-zero rb_status (the reference raises RuntimeError too)."""
+
+    def __init__(self, fn, status):
+        self.status = status
+        super().__init__(f"{fn}: {lib().rb_status_string(status).decode()} (status {status})")
+
+
+def lib():
+    """Load librumik_b200.so (once). Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m rumik_fast_b200.build` "
+                              "(there is no non-CUDA fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+def dtype_code(dt):
+    try:
+        return _DTYPE_CODE[dt]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dt}") from None
+
+
+def stream_ptr(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def check(fn, status):
+    if status != OK:
+        raise RumikKernelError(fn, status)
+
+
+def device_error(device=None):
+    """Read and clear the device-side error word (non-zero: a kernel gave up a bounded wait)."""
+    out = ctypes.c_uint(0)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        check("rb_get_device_error", lib().rb_get_device_error(ctypes.byref(out), stream_ptr(dev)))
+    return out.value

@@ -1,0 +1,135 @@
+// capi.cu - the extern "C" boundary (include/rumik_b200.h). Validates arguments on the host (before any
+// CUDA call), picks the launch shape for the device's SM count and forwards to the kernel files.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+constexpr int kVersion = 100;
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool act_dtype_ok(int d) { return d == RB_F16 || d == RB_BF16; }
+
+int device_sms(int* sms) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return RB_ERR_DEVICE;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return RB_ERR_DEVICE;
+  if (major != 10) return RB_ERR_DEVICE;  // the cubins are sm_100a only
+  if (cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return RB_ERR_DEVICE;
+  return RB_OK;
+}
+
+// Shared checks of the activation / output side of a GEMV-shaped call.
+int check_act(const void* x, int x_dtype, int64_t ldx, const void* y, int y_dtype, int64_t ldy, int64_t K,
+              int64_t N, int64_t batch) {
+  if (!x || !y) return RB_ERR_NULL;
+  if (!act_dtype_ok(x_dtype) || !act_dtype_ok(y_dtype)) return RB_ERR_DTYPE;
+  if (batch > 1 && (ldx < K || ldy < N)) return RB_ERR_SHAPE;
+  if (!aligned16(x) || (batch > 1 && (ldx % 8) != 0)) return RB_ERR_ALIGN;
+  return RB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rb_version(void) { return kVersion; }
+
+const char* rb_status_string(int status) {
+  switch (status) {
+    case RB_OK: return "ok";
+    case RB_ERR_NULL: return "a required pointer is NULL";
+    case RB_ERR_SHAPE: return "unsupported shape";
+    case RB_ERR_DTYPE: return "unsupported dtype";
+    case RB_ERR_ALIGN: return "pointer not 16-byte aligned or row stride not a multiple of 8 elements";
+    case RB_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case RB_ERR_DEVICE: return "no usable sm_100 CUDA device";
+    case RB_ERR_TIMEOUT: return "a kernel gave up a bounded wait";
+    default: return "unknown status";
+  }
+}
+
+int rb_gemv_int4(const void* x, int x_dtype, int64_t ldx, const uint8_t* q, const uint16_t* s, const uint16_t* m,
+                 void* y, int y_dtype, int64_t ldy, int64_t N, int64_t K, int64_t batch, int flags, void* stream) {
+  if (N < 0 || K <= 0 || batch < 0) return RB_ERR_SHAPE;
+  if (K % 128 != 0 || K > 16384 || N > (int64_t(1) << 30)) return RB_ERR_SHAPE;
+  if (N == 0 || batch == 0) return RB_OK;
+  if (!q || !s || !m) return RB_ERR_NULL;
+  int st = check_act(x, x_dtype, ldx, y, y_dtype, ldy, K, N, batch);
+  if (st != RB_OK) return st;
+  if (!aligned16(q) || !aligned16(s) || !aligned16(m)) return RB_ERR_ALIGN;
+  int sms = 0;
+  if ((st = device_sms(&sms)) != RB_OK) return st;
+  rb::GemvArgs a = {};
+  a.x = x; a.x_dtype = x_dtype; a.ldx = batch > 1 ? ldx : K;
+  a.q = q; a.s = s; a.m = m;
+  a.y = y; a.y_dtype = y_dtype; a.ldy = batch > 1 ? ldy : N;
+  a.N = N; a.K = K; a.batch = batch; a.flags = flags;
+  st = rb::launch_gemv_int4(a, sms, static_cast<cudaStream_t>(stream));
+  if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+  return st;
+}
+
+int rb_gemv_int8(const void* x, int x_dtype, int64_t ldx, const uint8_t* q, int q_signed, const void* s,
+                 int s_dtype, void* y, int y_dtype, int64_t ldy, int64_t N, int64_t K, int64_t batch, int flags,
+                 void* stream) {
+  if (N < 0 || K <= 0 || batch < 0) return RB_ERR_SHAPE;
+  if (K % 64 != 0 || K > 16384 || N > (int64_t(1) << 30)) return RB_ERR_SHAPE;
+  if (N == 0 || batch == 0) return RB_OK;
+  if (!q || !s) return RB_ERR_NULL;
+  if (s_dtype != RB_F32 && s_dtype != RB_F16) return RB_ERR_DTYPE;
+  int st = check_act(x, x_dtype, ldx, y, y_dtype, ldy, K, N, batch);
+  if (st != RB_OK) return st;
+  if (!aligned16(q)) return RB_ERR_ALIGN;
+  int sms = 0;
+  if ((st = device_sms(&sms)) != RB_OK) return st;
+  rb::GemvArgs a = {};
+  a.x = x; a.x_dtype = x_dtype; a.ldx = batch > 1 ? ldx : K;
+  a.q = q; a.q_signed = q_signed; a.s_row = s; a.s_dtype = s_dtype;
+  a.y = y; a.y_dtype = y_dtype; a.ldy = batch > 1 ? ldy : N;
+  a.N = N; a.K = K; a.batch = batch; a.flags = flags;
+  st = rb::launch_gemv_int8(a, sms, static_cast<cudaStream_t>(stream));
+  if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+  return st;
+}
+
+int rb_mm_int4(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const uint16_t* s, const uint16_t* m,
+               void* Y, int y_dtype, int64_t ldy, int64_t M, int64_t N, int64_t K, int flags, void* stream) {
+  if (M < 0 || N < 0 || K <= 0) return RB_ERR_SHAPE;
+  if (K % 128 != 0 || N > (int64_t(1) << 30) || M > (int64_t(1) << 30)) return RB_ERR_SHAPE;
+  if (M == 0 || N == 0) return RB_OK;
+  if (!X || !Y || !q || !s || !m) return RB_ERR_NULL;
+  if (!act_dtype_ok(x_dtype) || !act_dtype_ok(y_dtype)) return RB_ERR_DTYPE;
+  if (ldx < K || ldy < N) return RB_ERR_SHAPE;
+  if (!aligned16(X) || !aligned16(Y) || (ldx % 8) != 0 || (ldy % 8) != 0) return RB_ERR_ALIGN;
+  if (!aligned16(q) || !aligned16(s) || !aligned16(m)) return RB_ERR_ALIGN;
+  int sms = 0, st = device_sms(&sms);
+  if (st != RB_OK) return st;
+  rb::MmArgs a = {};
+  a.X = X; a.x_dtype = x_dtype; a.ldx = ldx;
+  a.q = q; a.s = s; a.m = m;
+  a.Y = Y; a.y_dtype = y_dtype; a.ldy = ldy;
+  a.M = M; a.N = N; a.K = K; a.flags = flags;
+  st = rb::launch_mm_int4(a, sms, static_cast<cudaStream_t>(stream));
+  if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+  return st;
+}
+
+int rb_get_device_error(unsigned int* out, void* stream) {
+  if (!out) return RB_ERR_NULL;
+  unsigned int zero = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyFromSymbolAsync(out, rb::g_device_error, sizeof(unsigned int), 0, cudaMemcpyDeviceToHost, s) !=
+      cudaSuccess)
+    return RB_ERR_DEVICE;
+  if (cudaMemcpyToSymbolAsync(rb::g_device_error, &zero, sizeof(unsigned int), 0, cudaMemcpyHostToDevice, s) !=
+      cudaSuccess)
+    return RB_ERR_DEVICE;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return RB_ERR_DEVICE;
+  return RB_OK;
+}
+
+}  // extern "C"

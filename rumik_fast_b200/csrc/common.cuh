@@ -1,0 +1,201 @@
+// common.cuh - sm_100a device helpers shared by the GEMV and prefill kernels: mbarriers with bounded
+// waits, 1-D bulk async copies (TMA without a tensor map), programmatic-dependent-launch controls and the
+// warp-level f16 MMA used as an fp32-accumulating dot-product engine.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+namespace rb {
+
+// Device-side error word: a kernel that gives up a bounded wait ORs a bit in here and returns early.
+// The host reads and clears it with rb_get_device_error(). The library is one translation unit
+// (rumik_b200.cu), so this single definition is shared by every kernel.
+__device__ unsigned int g_device_error;
+
+enum : unsigned int {
+  ERR_GEMV4_FULL = 1u << 0,   // int4 GEMV consumer timed out waiting for a weight stage
+  ERR_GEMV4_EMPTY = 1u << 1,  // int4 GEMV producer timed out waiting for a free slot
+  ERR_GEMV8_FULL = 1u << 2,
+  ERR_GEMV8_EMPTY = 1u << 3,
+  ERR_MM4_WAIT = 1u << 4,     // prefill matmul timed out on an mbarrier
+};
+
+// Upper bound on the wall time of one mbarrier wait. Healthy waits here last microseconds (at most the
+// duration of the previous GEMV when a kernel starts early under PDL); four seconds means the wait is hung.
+constexpr unsigned long long kMaxWaitNs = 4000000000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and sets `err_bit` in g_device_error) if the phase did
+// not complete within kMaxWaitNs; the caller then skips its work and returns, so the context stays usable.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_bit) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kMaxWaitNs) {
+      atomicOr(&g_device_error, err_bit);
+      return false;
+    }
+  }
+  return true;
+}
+
+// 1-D bulk copy global -> shared (this CTA), completion counted on `bar` in bytes. dst, src and bytes
+// must be multiples of 16. No tensor map, no multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Programmatic dependent launch controls (no-ops when the kernel was launched without the attribute).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" :::);
+}
+
+// Named barrier among `nthreads` threads (multiple of 32) with id `id` (1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// D(16x8,f32) += A(16x16,f16) * B(16x8,f16); fragments in the standard m16n8k16 register layout:
+// a0:(g, 2t..2t+1) a1:(g+8, 2t..) a2:(g, 2t+8..) a3:(g+8, 2t+8..), b0:(k=2t.., n=g) b1:(k=2t+8.., n=g),
+// d0,d1:(g, 2t..2t+1) d2,d3:(g+8, 2t..2t+1), with g = lane/4, t = lane%4.
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                              uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smem_u32(p)));
+  return v;
+}
+
+// Activation load that bypasses L1 (the producer of x may be the kernel that just finished).
+__device__ __forceinline__ uint4 ldg_cg_128(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
+  return static_cast<uint32_t>(__half_as_ushort(lo)) |
+         (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+}
+
+// 8 activations (one 16-byte load) to fp16, from fp16 or bf16 storage.
+__device__ __forceinline__ void load8_as_half(const void* p, bool is_bf16, __half (&h)[8]) {
+  uint4 raw = ldg_cg_128(p);
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  if (is_bf16) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xffff0000u);
+      h[2 * i] = __float2half_rn(lo);
+      h[2 * i + 1] = __float2half_rn(hi);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      h[2 * i] = __ushort_as_half(static_cast<unsigned short>(w[i] & 0xffffu));
+      h[2 * i + 1] = __ushort_as_half(static_cast<unsigned short>(w[i] >> 16));
+    }
+  }
+}
+
+__device__ __forceinline__ void store_out(void* y, int64_t idx, float v, bool is_bf16) {
+  if (is_bf16)
+    reinterpret_cast<__nv_bfloat16*>(y)[idx] = __float2bfloat16_rn(v);
+  else
+    reinterpret_cast<__half*>(y)[idx] = __float2half_rn(v);
+}
+
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device), not on every call, so that a call
+// made while a CUDA graph is being captured issues nothing but the launch. Concurrent first calls may both
+// set the attribute, which is harmless.
+inline cudaError_t ensure_smem_limit(const void* kern, int bytes) {
+  static const void* keys[64] = {};
+  static unsigned long long done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  int slot = -1;
+  for (int i = 0; i < 64; ++i) {
+    if (keys[i] == kern || keys[i] == nullptr) {
+      keys[i] = kern;
+      slot = i;
+      break;
+    }
+  }
+  const bool cacheable = slot >= 0 && dev >= 0 && dev < 64;
+  if (cacheable && ((done[slot] >> dev) & 1ull)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && cacheable) done[slot] |= 1ull << dev;
+  return e;
+}
+
+}  // namespace rb

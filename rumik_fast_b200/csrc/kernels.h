@@ -1,0 +1,47 @@
+// kernels.h - internal launcher interface between the C ABI (capi.cu) and the kernel files.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/rumik_b200.h"
+
+namespace rb {
+
+// Arguments of one GEMV call after validation (sizes in elements; strides in elements of x/y).
+struct GemvArgs {
+  const void* x;
+  int x_dtype;
+  int64_t ldx;
+  const uint8_t* q;
+  const uint16_t* s;  // int4: per-group scale; int8: unused
+  const uint16_t* m;  // int4: per-group min;   int8: unused
+  const void* s_row;  // int8: per-row scale (fp32 or fp16)
+  int s_dtype;        // int8: RB_F32 or RB_F16
+  int q_signed;       // int8: codes are signed int8
+  void* y;
+  int y_dtype;
+  int64_t ldy;
+  int64_t N, K, batch;
+  int flags;
+};
+
+struct MmArgs {
+  const void* X;
+  int x_dtype;
+  int64_t ldx;
+  const uint8_t* q;
+  const uint16_t* s;
+  const uint16_t* m;
+  void* Y;
+  int y_dtype;
+  int64_t ldy;
+  int64_t M, N, K;
+  int flags;
+};
+
+int launch_gemv_int4(const GemvArgs& a, int num_sms, cudaStream_t stream);
+int launch_gemv_int8(const GemvArgs& a, int num_sms, cudaStream_t stream);
+int launch_mm_int4(const MmArgs& a, int num_sms, cudaStream_t stream);
+
+}  // namespace rb

@@ -1,0 +1,6 @@
+// rumik_b200.cu - single translation unit of librumik_b200.so, so that the kernels and the C ABI share
+// the device-side error word without relocatable device code.
+#include "capi.cu"
+#include "gemv_int4.cu"
+#include "gemv_int8.cu"
+#include "mm_int4.cu"

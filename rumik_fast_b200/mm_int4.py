@@ -1,0 +1,49 @@
+"""Drop-in for rumik-fast kernels/mm_int4.py on B200: the int4-weight prefill matmul on tcgen05 tensor cores.
+
+    mm_int4(x, q, s, m, BM=None, BN=64, num_warps=4, num_stages=3) -> y     (kernels/mm_int4.py:59)
+    warmup(shapes)                                                          (kernels/mm_int4.py:49)
+    G = 128
+Y[T, N] = X[T, K] @ W^T with W in the int4 group-128 layout. X may be fp16 or bf16 and strided in its
+first dimension; y has X's dtype and is newly allocated, as in the reference. The Triton tile knobs are
+accepted and ignored. The kernel is compiled ahead of time, so warmup() only performs one tiny call per
+shape (it makes the first call inside a CUDA-graph capture cheap).
+"""
+import torch
+
+from . import _lib, config
+from .cuda_gemv import _on_device, _require
+
+G = 128
+
+
+def mm_int4(x, q, s, m, BM=None, BN=64, num_warps=4, num_stages=3, out=None):
+    N, K = q.shape[0], q.shape[1] * 2
+    _require(x.is_cuda and x.dim() == 2 and x.shape[1] == K, f"x must be a CUDA [T, {K}] tensor")
+    _require(x.dtype in (torch.float16, torch.bfloat16), f"x must be fp16 or bf16, got {x.dtype}")
+    _require(q.dtype == torch.uint8 and q.is_contiguous(), "q must be a contiguous uint8 [N, K/2] tensor")
+    _require(K % G == 0, f"K={K} must be a multiple of {G}")
+    for t, nm in ((s, "s"), (m, "m")):
+        _require(t.dtype == torch.float16 and t.is_contiguous() and tuple(t.shape) == (N, K // G),
+                 f"{nm} must be a contiguous fp16 [{N}, {K // G}] tensor")
+    if x.stride(1) != 1 or x.stride(0) % 8 != 0 or x.data_ptr() % 16 != 0:
+        x = x.contiguous()
+    T = x.shape[0]
+    y = torch.empty(T, N, device=x.device, dtype=x.dtype) if out is None else out
+    _require(y.shape == (T, N) and y.stride(1) == 1, "out must be [T, N] with unit column stride")
+    L = _lib.lib()
+    with _on_device(x.device):
+        st = L.rb_mm_int4(x.data_ptr(), _lib.dtype_code(x.dtype), x.stride(0), q.data_ptr(), s.data_ptr(),
+                          m.data_ptr(), y.data_ptr(), _lib.dtype_code(y.dtype), y.stride(0), T, N, K,
+                          config.flags(), _lib.stream_ptr(x.device))
+    _lib.check("rb_mm_int4", st)
+    return y
+
+
+def warmup(shapes):
+    """One tiny call per (N, K) so nothing is initialised lazily later (kernels/mm_int4.py:49-56)."""
+    for n, k in shapes:
+        q = torch.zeros(n, k // 2, device="cuda", dtype=torch.uint8)
+        s = torch.zeros(n, k // G, device="cuda", dtype=torch.float16)
+        for T in (17, 33):
+            mm_int4(torch.zeros(T, k, device="cuda", dtype=torch.bfloat16), q, s, s)
+    torch.cuda.synchronize()

@@ -1,0 +1,107 @@
+"""Generate the golden fixtures of this directory from the reference's OWN functions.
+
+Run in a container where the rumik-fast reference is mounted (it is not needed anywhere else):
+
+    python tests/golden/make_golden.py [--ref /path/to/rumik-fast]
+
+It imports kernels/int4_gemv.py (quantize, dequantize) and kernels/cuda_gemv.py (quantize_int8_rows) from the
+reference on the CPU and records, for small seeded inputs, the reference's outputs:
+  * golden_int4.npz : bf16 weights -> reference quantize() -> (q, s, m); reference dequantize(); and
+                      y = dequantize(q, s, m) @ x.float() (kernels/bench_cuda.py:38) for fp16/bf16 x,
+                      batched x, and BASELINE-config-style codes/scales/mins.
+  * golden_int8.npz : bf16 head rows -> reference quantize_int8_rows(w, pad_to=16) -> (q, s); and
+                      y = ((q - 128) * s) @ x (kernels/cuda_gemv.py:245-246).
+  * golden_mm.npz   : Y = X.float() @ dequantize(q, s, m).t() (kernels/mm_int4.py:96).
+bf16 tensors are stored as uint16 bit patterns.
+"""
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def bits(t):
+    """bf16 tensor -> uint16 numpy bit pattern; fp16 -> numpy float16; others as is."""
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("RUMIK_REFERENCE", "/root/reference"))
+    a = ap.parse_args()
+    sys.path.insert(0, os.path.join(a.ref, "kernels"))
+    import int4_gemv as ref4  # noqa: E402  (reference module)
+    import cuda_gemv as refc  # noqa: E402  (reference module; load_inline is only called lazily)
+
+    out4 = {}
+    # (A) reference-style weights: randn * 0.02 in bf16 (kernels/bench_cuda.py:36), several shapes
+    for tag, (n, k, seed) in {"a": (64, 256, 0), "b": (24, 384, 1), "c": (8, 128, 2), "d": (40, 1024, 3)}.items():
+        g = torch.Generator().manual_seed(seed)
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+        q, s, m = ref4.quantize(w)
+        deq = ref4.dequantize(q, s, m)
+        x16 = torch.randn(k, generator=g).to(torch.float16)
+        xb = torch.randn(k, generator=g).to(torch.bfloat16)
+        xbat = torch.randn(3, k, generator=g).to(torch.float16)
+        out4.update({f"{tag}_w": bits(w), f"{tag}_q": bits(q), f"{tag}_s": bits(s), f"{tag}_m": bits(m),
+                     f"{tag}_deq": deq.numpy(),
+                     f"{tag}_x16": bits(x16), f"{tag}_y16": (deq @ x16.float()).numpy(),
+                     f"{tag}_xbf": bits(xb), f"{tag}_ybf": (deq @ xb.float()).numpy(),
+                     f"{tag}_xbat": bits(xbat), f"{tag}_ybat": (xbat.float() @ deq.t()).numpy()})
+    # (B) BASELINE config-0 style: codes uniform 0..15, scale ~U(0.002, 0.02), min = -7.5 scale + N(0, 1e-3)
+    g = torch.Generator().manual_seed(10)
+    n, k = 48, 512
+    codes = torch.randint(0, 16, (n, k), generator=g, dtype=torch.uint8)
+    q = (codes[:, 0::2] | (codes[:, 1::2] << 4)).contiguous()
+    s = (torch.rand(n, k // 128, generator=g) * 0.018 + 0.002).to(torch.float16)
+    m = (-7.5 * s.float() + torch.randn(n, k // 128, generator=g) * 1e-3).to(torch.float16)
+    x = torch.randn(k, generator=g).to(torch.float16)
+    deq = ref4.dequantize(q, s, m)
+    out4.update({"cfg_q": bits(q), "cfg_s": bits(s), "cfg_m": bits(m), "cfg_deq": deq.numpy(),
+                 "cfg_x16": bits(x), "cfg_y16": (deq @ x.float()).numpy()})
+    np.savez_compressed(os.path.join(HERE, "golden_int4.npz"), **out4)
+
+    out8 = {}
+    for tag, (n, k, seed) in {"a": (13, 256, 20), "b": (33, 192, 21)}.items():
+        g = torch.Generator().manual_seed(seed)
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+        q, s = refc.quantize_int8_rows(w)
+        x16 = torch.randn(k, generator=g).to(torch.float16)
+        xb = torch.randn(k, generator=g).to(torch.bfloat16)
+        wq = (q.int() - 128).float() * s[:, None]
+        out8.update({f"{tag}_w": bits(w), f"{tag}_q": bits(q), f"{tag}_s": bits(s),
+                     f"{tag}_x16": bits(x16), f"{tag}_y16": (wq @ x16.float()).numpy(),
+                     f"{tag}_xbf": bits(xb), f"{tag}_ybf": (wq @ xb.float()).numpy()})
+    # BASELINE config-2 style: W int8 uniform -127..127, fp16 row scale ~U(1e-4, 1e-3), unpadded N
+    g = torch.Generator().manual_seed(22)
+    n, k = 37, 320
+    wi8 = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int16).to(torch.int8)
+    s16 = (torch.rand(n, generator=g) * 9e-4 + 1e-4).to(torch.float16)
+    x = torch.randn(k, generator=g).to(torch.float16)
+    qu8 = (wi8.to(torch.int16) + 128).to(torch.uint8)          # the reference's storage of the same weights
+    y = (((qu8.int() - 128).float() * s16.float()[:, None]) @ x.float())
+    out8.update({"cfg_wi8": wi8.numpy(), "cfg_qu8": bits(qu8), "cfg_s16": bits(s16), "cfg_x16": bits(x),
+                 "cfg_y16": y.numpy()})
+    np.savez_compressed(os.path.join(HERE, "golden_int8.npz"), **out8)
+
+    outm = {}
+    for tag, (t, n, k, seed) in {"a": (5, 64, 256, 30), "b": (37, 80, 384, 31)}.items():
+        g = torch.Generator().manual_seed(seed)
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+        q, s, m = ref4.quantize(w)
+        X = torch.randn(t, k, generator=g).to(torch.float16)
+        outm.update({f"{tag}_q": bits(q), f"{tag}_s": bits(s), f"{tag}_m": bits(m), f"{tag}_X": bits(X),
+                     f"{tag}_Y": (X.float() @ ref4.dequantize(q, s, m).t()).numpy()})
+    np.savez_compressed(os.path.join(HERE, "golden_mm.npz"), **outm)
+    for f in ("golden_int4.npz", "golden_int8.npz", "golden_mm.npz"):
+        print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
+
+
+if __name__ == "__main__":
+    main()

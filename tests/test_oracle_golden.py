@@ -1,0 +1,101 @@
+"""Pin the CPU oracle to the reference: its functions must reproduce the outputs that the reference's own
+code produced for the committed fixtures (tests/golden/make_golden.py)."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def g4():
+    return np.load(os.path.join(GOLD, "golden_int4.npz"))
+
+
+@pytest.fixture(scope="module")
+def g8():
+    return np.load(os.path.join(GOLD, "golden_int8.npz"))
+
+
+@pytest.fixture(scope="module")
+def gm():
+    return np.load(os.path.join(GOLD, "golden_mm.npz"))
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c", "d"])
+def test_quantize_int4_bit_exact(g4, tag):
+    w = O.bf16_bits_to_f32(g4[f"{tag}_w"])
+    q, s, m = O.quantize_int4(w)
+    assert np.array_equal(q, g4[f"{tag}_q"])
+    assert np.array_equal(s.view(np.uint16), g4[f"{tag}_s"].view(np.uint16))
+    assert np.array_equal(m.view(np.uint16), g4[f"{tag}_m"].view(np.uint16))
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c", "d", "cfg"])
+def test_dequantize_int4_bit_exact(g4, tag):
+    deq = O.dequantize_int4(g4[f"{tag}_q"], g4[f"{tag}_s"], g4[f"{tag}_m"])
+    assert np.array_equal(deq.view(np.uint32), g4[f"{tag}_deq"].view(np.uint32))
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c", "d"])
+def test_gemv_int4_ref_matches_reference(g4, tag):
+    q, s, m = g4[f"{tag}_q"], g4[f"{tag}_s"], g4[f"{tag}_m"]
+    np.testing.assert_allclose(O.gemv_int4_ref(g4[f"{tag}_x16"], q, s, m), g4[f"{tag}_y16"], rtol=2e-5, atol=2e-6)
+    np.testing.assert_allclose(O.gemv_int4_ref(g4[f"{tag}_xbf"], q, s, m, x_dtype="bf16"), g4[f"{tag}_ybf"],
+                               rtol=2e-5, atol=2e-6)
+    np.testing.assert_allclose(O.gemv_int4_ref(g4[f"{tag}_xbat"], q, s, m), g4[f"{tag}_ybat"], rtol=2e-5, atol=2e-6)
+
+
+def test_gemv_int4_ref_config_style(g4):
+    y = O.gemv_int4_ref(g4["cfg_x16"], g4["cfg_q"], g4["cfg_s"], g4["cfg_m"])
+    np.testing.assert_allclose(y, g4["cfg_y16"], rtol=2e-5, atol=2e-5)
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_quantize_int8_rows_bit_exact(g8, tag):
+    q, s = O.quantize_int8_rows(O.bf16_bits_to_f32(g8[f"{tag}_w"]))
+    assert np.array_equal(q, g8[f"{tag}_q"])
+    assert np.array_equal(s.view(np.uint32), g8[f"{tag}_s"].view(np.uint32))
+    assert q.shape[0] % 16 == 0
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_gemv_int8_ref_matches_reference(g8, tag):
+    q, s = g8[f"{tag}_q"], g8[f"{tag}_s"]
+    np.testing.assert_allclose(O.gemv_int8_ref(g8[f"{tag}_x16"], q, s), g8[f"{tag}_y16"], rtol=2e-5, atol=2e-6)
+    np.testing.assert_allclose(O.gemv_int8_ref(g8[f"{tag}_xbf"], q, s, x_dtype="bf16"), g8[f"{tag}_ybf"],
+                               rtol=2e-5, atol=2e-6)
+
+
+def test_gemv_int8_signed_storage_equals_offset_storage(g8):
+    y_signed = O.gemv_int8_ref(g8["cfg_x16"], g8["cfg_wi8"], g8["cfg_s16"], signed=True)
+    y_u8 = O.gemv_int8_ref(g8["cfg_x16"], g8["cfg_qu8"], g8["cfg_s16"])
+    np.testing.assert_allclose(y_signed, g8["cfg_y16"], rtol=2e-5, atol=2e-6)
+    np.testing.assert_allclose(y_u8, g8["cfg_y16"], rtol=2e-5, atol=2e-6)
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_mm_int4_ref_matches_reference(gm, tag):
+    Y = O.mm_int4_ref(gm[f"{tag}_X"], gm[f"{tag}_q"], gm[f"{tag}_s"], gm[f"{tag}_m"])
+    np.testing.assert_allclose(Y, gm[f"{tag}_Y"], rtol=2e-5, atol=2e-6)
+
+
+def test_tolerance_check_detects_planted_error(g4):
+    """A mistake planted in the oracle's output must fail the acceptance criterion."""
+    ref = g4["a_y16"].astype(np.float64)
+    assert O.within_tolerance(ref, ref)
+    bad = ref.copy()
+    bad[3] += 0.01 * np.abs(ref).max()
+    assert not O.within_tolerance(bad, ref)
+    drift = ref * (1 + 3e-3)
+    assert not O.within_tolerance(drift, ref)
+
+
+def test_bf16_round_trip():
+    f = np.array([1.0, -2.5, 3.14159, 1e-3, 65504.0], np.float32)
+    b = O.f32_to_bf16_bits(f)
+    back = O.bf16_bits_to_f32(b)
+    assert np.all(np.abs(back - f) <= np.abs(f) * 2 ** -8)
