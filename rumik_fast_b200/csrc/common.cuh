@@ -115,23 +115,82 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 
 // D(16x8,f32) += A(16x16,f16) * B(16x8,f16); fragments in the standard m16n8k16 register layout:
 // a0:(g, 2t..2t+1) a1:(g+8, 2t..) a2:(g, 2t+8..) a3:(g+8, 2t+8..), b0:(k=2t.., n=g) b1:(k=2t+8.., n=g),
-// d0,d1:(g, 2t..2t+1) d2,d3:(g+8, 2t..2t+1), with g = lane/4, t = lane%4.
+// d0,d1:(g, 2t..2t+1) d2,d3:(g+8, 2t..2t+1), with g = lane/4, t = lane%4. A pure register operation (not
+// volatile), so the compiler may interleave independent MMAs with other work.
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                               uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint4 lds128(const void* p) {
+// D = A * B + C with C given as four separate (input-only) registers.
+__device__ __forceinline__ void mma_f16_16816_c(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1, const float4& c) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c.x), "f"(c.y), "f"(c.z), "f"(c.w));
+}
+
+// Same with a zero accumulator input: D = A * B.
+__device__ __forceinline__ void mma_f16_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
+// (a & b) | c in one LOP3. Callers pass b and c as runtime values (kernel parameters), not literals: with
+// two immediate operands the compiler emits two instructions for this expression.
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Shared-memory loads by 32-bit shared address. The "memory" clobber keeps them after the mbarrier wait that
+// guards the data; ptxas still schedules them freely against the arithmetic.
+__device__ __forceinline__ uint4 lds128_a(uint32_t a) {
   uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(smem_u32(p)));
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
   return v;
 }
+__device__ __forceinline__ float4 lds128f_a(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a) : "memory");
+  return v;
+}
+// Predicated forms: lanes with on == 0 issue no shared-memory access and get zeros.
+__device__ __forceinline__ uint4 lds128_pa(uint32_t a, uint32_t on) {
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %5, 0;\n\t@p ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n\t}"
+               : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w) : "r"(a), "r"(on) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 lds128f_pa(uint32_t a, uint32_t on) {
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %5, 0;\n\t@p ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n\t}"
+               : "+f"(v.x), "+f"(v.y), "+f"(v.z), "+f"(v.w) : "r"(a), "r"(on) : "memory");
+  return v;
+}
+__device__ __forceinline__ float2 lds64f_a(uint32_t a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ float lds_h2f_a(uint32_t a) {
+  unsigned short h;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a) : "memory");
+  return __half2float(__ushort_as_half(h));
+}
+
+// Shared-memory load as an ordinary C++ access, so the compiler orders it against the mbarrier waits
+// (which clobber memory) and can still schedule it freely otherwise.
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
 // Activation load that bypasses L1 (the producer of x may be the kernel that just finished).
 __device__ __forceinline__ uint4 ldg_cg_128(const void* p) {
@@ -147,9 +206,8 @@ __device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
          (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
 }
 
-// 8 activations (one 16-byte load) to fp16, from fp16 or bf16 storage.
-__device__ __forceinline__ void load8_as_half(const void* p, bool is_bf16, __half (&h)[8]) {
-  uint4 raw = ldg_cg_128(p);
+// 8 activations held in one 16-byte word (fp16 or bf16 storage) -> fp16.
+__device__ __forceinline__ void raw_to_half8(const uint4 raw, bool is_bf16, __half (&h)[8]) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
   if (is_bf16) {
 #pragma unroll
@@ -165,6 +223,11 @@ __device__ __forceinline__ void load8_as_half(const void* p, bool is_bf16, __hal
       h[2 * i + 1] = __ushort_as_half(static_cast<unsigned short>(w[i] >> 16));
     }
   }
+}
+
+// 8 activations (one 16-byte load, bypassing L1) to fp16.
+__device__ __forceinline__ void load8_as_half(const void* p, bool is_bf16, __half (&h)[8]) {
+  raw_to_half8(ldg_cg_128(p), is_bf16, h);
 }
 
 __device__ __forceinline__ void store_out(void* y, int64_t idx, float v, bool is_bf16) {

@@ -30,6 +30,8 @@ struct Gemv8Params {
   int N, K, C, batch;  // C = K / 64 chunks per row
   int x_bf16, y_bf16, s_f32, q_signed, prefetch;
   int ns, rs, stage_bytes, lp;
+  int nfull;  // full barriers = stages of the largest row band
+  int P, cps;  // K-slices per stage and 64-column chunks per slice
   uint32_t xs_off, xsum_off, part_off, red_off, bar_off;
 };
 
@@ -44,13 +46,13 @@ __device__ void gemv8_produce(const Gemv8Params& p, uint8_t* smem, uint64_t* ful
     const int r0 = row_begin + st * kStageRows;
     const int nr = min(kStageRows, row_end - r0);
     uint8_t* sb = smem + static_cast<size_t>(slot) * p.stage_bytes;
-    mbar_arrive_expect_tx(&full[slot], nr * row_bytes);
+    mbar_arrive_expect_tx(&full[st], nr * row_bytes);
     const uint8_t* qsrc = p.q + static_cast<int64_t>(r0) * row_bytes;
-    for (int rr = 0; rr < nr; ++rr) bulk_g2s(sb + rr * p.rs, qsrc + rr * row_bytes, row_bytes, &full[slot]);
+    bulk_g2s(sb, qsrc, nr * row_bytes, &full[st]);  // the stage's rows are one contiguous range
     issued = st + 1;
   }
   for (int st = max(0, issued - p.ns); st < issued; ++st)
-    mbar_wait(&full[st % p.ns], (st / p.ns) & 1, ERR_GEMV8_FULL);
+    mbar_wait(&full[st], 0, ERR_GEMV8_FULL);
 }
 
 // Activations -> fp16 B fragments: for chunk ch (64 columns) and lane quad qq, the S1 lane of batch b
@@ -106,16 +108,17 @@ template <int NP>
 __global__ void __launch_bounds__(kThreads, 1) gemv_int8_kernel(const __grid_constant__ Gemv8Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // one full barrier per stage (used for a single phase), one empty barrier per ring slot
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
-  uint64_t* empty = full + p.ns;
+  uint64_t* empty = full + p.nfull;
   const int row_begin = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
   const int row_end = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
   const int nst = (row_end - row_begin + kStageRows - 1) / kStageRows;
 
   if (tid == 0) {
+    for (int i = 0; i < nst; ++i) mbar_init(&full[i], 1);
     for (int i = 0; i < p.ns; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kConsumerWarps);
+      mbar_init(&empty[i], p.P);
     }
     fence_mbar_init();
   }
@@ -137,25 +140,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int8_kernel(const __grid_con
   const int r = lane >> 2, qd = lane & 3;
   const uint8_t* xs = smem + p.xs_off;
   const float* xsum = reinterpret_cast<const float*>(smem + p.xsum_off);
+  float* red = reinterpret_cast<float*>(smem + p.red_off);
   const uint32_t flip = p.q_signed ? 0x80808080u : 0u;
   bool dead = false;
-  for (int st = 0; st < nst; ++st) {
+  const int n_items = nst * p.P;
+  for (int it = warp; it < n_items; it += kConsumerWarps) {
+    const int st = it / p.P, sl = it - st * p.P;
     const int slot = st % p.ns;
-    const int r0 = row_begin + st * kStageRows;
-    const int nr = min(kStageRows, row_end - r0);
-    // row scale for the rows this thread may write, fetched early so its latency hides behind the stage
-    float srow = 0.f;
-    if (warp < NP && r < nr) {
-      srow = p.s_f32 ? __ldg(static_cast<const float*>(p.s) + r0 + r)
-                     : __half2float(__ldg(static_cast<const __half*>(p.s) + r0 + r));
-    }
-    if (!dead && !mbar_wait(&full[slot], (st / p.ns) & 1, ERR_GEMV8_FULL)) dead = true;
-    float d[NP][4];
+    if (!dead && !mbar_wait(&full[st], 0, ERR_GEMV8_FULL)) dead = true;
+    float d[NP][2][4];  // two independent MMA chains per pass
 #pragma unroll
-    for (int pp = 0; pp < NP; ++pp) d[pp][0] = d[pp][1] = d[pp][2] = d[pp][3] = 0.f;
+    for (int pp = 0; pp < NP; ++pp)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) d[pp][h][0] = d[pp][h][1] = d[pp][h][2] = d[pp][h][3] = 0.f;
     if (!dead) {
       const uint8_t* wrow = smem + static_cast<size_t>(slot) * p.stage_bytes + r * p.rs + qd * 16;
-      for (int ch = warp; ch < p.C; ch += kConsumerWarps) {
+      const int c0 = sl * p.cps, c1 = min(p.C, c0 + p.cps);
+      for (int ch = c0; ch < c1; ++ch) {
         const uint4 wq = lds128(wrow + ch * 64);
         const uint32_t wv[4] = {wq.x ^ flip, wq.y ^ flip, wq.z ^ flip, wq.w ^ flip};
         uint32_t a[2][4];
@@ -171,24 +172,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int8_kernel(const __grid_con
           const int lanes_p = 8 * min(4, p.batch - 4 * pp);
           uint4 bb = make_uint4(0, 0, 0, 0);
           if (lane < lanes_p) bb = lds128(xs + static_cast<size_t>((pp * p.C + ch) * p.lp + lane) * 16);
-          mma_f16_16816(d[pp], a[0][0], a[0][1], a[0][2], a[0][3], bb.x, bb.y);
-          mma_f16_16816(d[pp], a[1][0], a[1][1], a[1][2], a[1][3], bb.z, bb.w);
+          mma_f16_16816(d[pp][0], a[0][0], a[0][1], a[0][2], a[0][3], bb.x, bb.y);
+          mma_f16_16816(d[pp][1], a[1][0], a[1][1], a[1][2], a[1][3], bb.z, bb.w);
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    float* red = reinterpret_cast<float*>(smem + p.red_off) + (st & 1) * kConsumerWarps * NP * 32;
 #pragma unroll
-    for (int pp = 0; pp < NP; ++pp) red[(warp * NP + pp) * 32 + lane] = d[pp][0] + d[pp][3];
-    named_bar_sync(1, kConsumerWarps * 32);
-    if (!dead && warp < NP) {
-      float v = 0.f;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) v += red[(w * NP + warp) * 32 + lane];
-      const int b = warp * 4 + qd;
-      if (r < nr && b < p.batch) store_out(p.y, b * p.ldy + r0 + r, srow * (v - 1152.f * xsum[b]), p.y_bf16);
-    }
+    for (int pp = 0; pp < NP; ++pp)
+      red[((st * p.P + sl) * NP + pp) * 32 + lane] = (d[pp][0][0] + d[pp][0][3]) + (d[pp][1][0] + d[pp][1][3]);
+  }
+  named_bar_sync(1, kConsumerWarps * 32);
+  // fixed-order reduction over the K-slices of every stage, then scale and store
+  for (int o = tid; o < nst * NP * 32; o += kConsumerWarps * 32) {
+    const int st = o / (NP * 32), rem = o - st * NP * 32, pp = rem >> 5, l = rem & 31;
+    const int row = row_begin + st * kStageRows + (l >> 2), b = pp * 4 + (l & 3);
+    if (dead || row >= row_end || b >= p.batch) continue;
+    float v = 0.f;
+    for (int sl = 0; sl < p.P; ++sl) v += red[((st * p.P + sl) * NP + pp) * 32 + l];
+    const float srow = p.s_f32 ? __ldg(static_cast<const float*>(p.s) + row)
+                               : __half2float(__ldg(static_cast<const __half*>(p.s) + row));
+    store_out(p.y, b * p.ldy + row, srow * (v - 1152.f * xsum[b]), p.y_bf16);
   }
 }
 
@@ -200,8 +205,11 @@ int launch_gemv_int8(const GemvArgs& a, int num_sms, cudaStream_t stream) {
   const int ctas = static_cast<int>(std::min<int64_t>((a.N + kStageRows - 1) / kStageRows, num_sms));
   const int64_t rows_max = (a.N + ctas - 1) / ctas;
   const int nst_max = static_cast<int>((rows_max + kStageRows - 1) / kStageRows);
+  int P = 1;
+  while (P < 8 && nst_max * P < 2 * kConsumerWarps && C / (2 * P) >= 4) P *= 2;
+  const int cps = (C + P - 1) / P;
   const int K = static_cast<int>(a.K);
-  const int rs = K + ((K % 128) == 0 ? 64 : 0);
+  const int rs = K;  // rows packed as in HBM: one bulk copy per stage
   const int stage_bytes = (kStageRows * rs + 127) & ~127;
   constexpr int kSmemMax = 227 * 1024;
   constexpr int kCoResident = 110 * 1024;
@@ -217,9 +225,9 @@ int launch_gemv_int8(const GemvArgs& a, int num_sms, cudaStream_t stream) {
       if (np == 3) np = 4;
       lp = 8 * min(4, bc);
       const uint32_t xs_bytes = static_cast<uint32_t>(np) * C * lp * 16;
-      const uint32_t red_bytes = 2 * kConsumerWarps * np * 32 * 4;
+      const uint32_t red_bytes = static_cast<uint32_t>(nst_max) * P * np * 32 * 4;
       const uint32_t part_bytes = static_cast<uint32_t>(bc) * C * 4;
-      const uint32_t fixed = xs_bytes + 64 + part_bytes + red_bytes + 2 * 8 * 8 + 256;
+      const uint32_t fixed = xs_bytes + 64 + part_bytes + red_bytes + (nst_max + 8) * 8 + 256;
       int slots = static_cast<int>((static_cast<int64_t>(kCoResident) - fixed) / stage_bytes);
       slots = max(2, min(slots, 8));
       slots = min(slots, max(1, nst_max));
@@ -235,7 +243,7 @@ int launch_gemv_int8(const GemvArgs& a, int num_sms, cudaStream_t stream) {
       part_off = xsum_off + 64;
       red_off = part_off + ((part_bytes + 15) & ~15u);
       bar_off = red_off + red_bytes;
-      total = bar_off + 2 * ns * 8;
+      total = bar_off + (nst_max + ns) * 8;
       break;
     }
     Gemv8Params p;
@@ -255,9 +263,12 @@ int launch_gemv_int8(const GemvArgs& a, int num_sms, cudaStream_t stream) {
     p.q_signed = a.q_signed ? 1 : 0;
     p.prefetch = (a.flags & RB_FLAG_PDL) && (a.flags & RB_FLAG_PREFETCH_WEIGHTS) ? 1 : 0;
     p.ns = ns;
+    p.nfull = nst_max;
     p.rs = rs;
     p.stage_bytes = stage_bytes;
     p.lp = lp;
+    p.P = P;
+    p.cps = cps;
     p.xs_off = xs_off;
     p.xsum_off = xsum_off;
     p.part_off = part_off;

@@ -107,7 +107,7 @@ def test_strided_rows_and_out_dtype():
 def test_out_and_ignored_tuning_kwargs():
     N, K = 256, 512
     q, s, m = to_dev(*weights(N, K, seed=9))
-    x = syn.activations((K,), syn.generator(9, "cpu"), DEV)
+    x = syn.activations((K,), syn.generator(9, "cpu"), "cpu").to(DEV)
     out = torch.empty(N, device=DEV, dtype=torch.float16)
     y = rb.gemv_int4_cuda(x, q, s, m, out=out, warps=4, rows=1)
     assert y is out
@@ -116,7 +116,7 @@ def test_out_and_ignored_tuning_kwargs():
 
 def test_deterministic():
     q, s, m = to_dev(*weights(5120, 3072, seed=11))
-    x = syn.activations((3072,), syn.generator(12, "cpu"), DEV)
+    x = syn.activations((3072,), syn.generator(12, "cpu"), "cpu").to(DEV)
     y1 = rb.gemv_int4_cuda(x, q, s, m)
     y2 = rb.gemv_int4_cuda(x, q, s, m)
     assert torch.equal(y1, y2)
@@ -126,7 +126,7 @@ def test_misaligned_weights_raise():
     q, s, m = to_dev(*weights(64, 256, seed=1))
     qq = torch.empty(q.numel() + 8, dtype=torch.uint8, device=DEV)[8:].view(64, 128)
     with pytest.raises(RuntimeError, match="aligned"):
-        rb.gemv_int4_cuda(syn.activations((256,), syn.generator(1, "cpu"), DEV), qq, s, m)
+        rb.gemv_int4_cuda(syn.activations((256,), syn.generator(1, "cpu"), "cpu").to(DEV), qq, s, m)
 
 
 @pytest.mark.parametrize("prefetch", [False, True])
@@ -144,7 +144,7 @@ def test_dependent_chain(prefetch, graph):
         s = (s.float() * 0.35).half()                    # keep |y| ~ |x| along the chain
         m = (-7.5 * s.float()).half()
         mats.append(to_dev(q, s, m))
-    x0 = syn.activations((K,), g, DEV)
+    x0 = syn.activations((K,), g, "cpu").to(DEV)
     ys = [torch.empty(K, device=DEV, dtype=torch.float16) for _ in range(L)]
 
     def run():
@@ -168,3 +168,19 @@ def test_dependent_chain(prefetch, graph):
     for i, (q, s, m) in enumerate(mats):
         assert_close(ys[i], int4_ref(x, q, s, m), f"chain step {i}")
         x = ys[i]
+
+
+@pytest.mark.parametrize("N,K", [(65536, 3072), (24576, 8192), (40000, 1024), (32768, 16384)])
+def test_long_row_bands(N, K):
+    """Row bands of 20-56 eight-row stages with fewer ring slots than consumer warps (regression: a consumer
+    warp running a full ring lap ahead must still wait for its own stage's data). Checked on a row sample,
+    twice, to also catch races."""
+    q, s, m = weights(N, K, seed=N + K)
+    x = syn.activations((K,), syn.generator(K + 1, "cpu"), "cpu")
+    qd, sd, md, xd = to_dev(q, s, m, x)
+    y1 = rb.gemv_int4_cuda(xd, qd, sd, md)
+    y2 = rb.gemv_int4_cuda(xd, qd, sd, md)
+    assert torch.equal(y1, y2)
+    rows = torch.from_numpy(np.sort(np.random.default_rng(N).choice(N, 2048, replace=False)))
+    assert_close(y1.cpu()[rows], int4_ref(x, q[rows], s[rows], m[rows]), f"N={N} K={K}")
+    assert rb.device_error() == 0

@@ -85,3 +85,17 @@ def test_quantize_then_gemv_on_device():
     x = torch.randn(1024, generator=g).to(torch.bfloat16).to(DEV)
     y = rb.gemv_int8_cuda(x, q, s)
     assert_close(y, int8_ref(x, q, s), "engine head path")
+
+
+@pytest.mark.parametrize("N,K", [(65536, 3072), (20000, 8192)])
+def test_long_row_bands(N, K):
+    """Row bands with many more stages than ring slots (regression for early passes of a reused slot)."""
+    g = syn.generator(N, "cpu")
+    q, s = syn.int8_weights(N, K, g, "cpu")
+    x = syn.activations((K,), g, "cpu")
+    y1 = rb.gemv_int8_cuda(x.to(DEV), q.to(DEV), s.to(DEV))
+    y2 = rb.gemv_int8_cuda(x.to(DEV), q.to(DEV), s.to(DEV))
+    assert torch.equal(y1, y2)
+    rows = torch.from_numpy(np.sort(np.random.default_rng(N).choice(N, 2048, replace=False)))
+    assert_close(y1.cpu()[rows], int8_ref(x, q[rows], s[rows]), f"N={N} K={K}")
+    assert rb.device_error() == 0
