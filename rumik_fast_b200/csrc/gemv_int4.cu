@@ -282,7 +282,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_kernel(const __grid_con
   const int prow = (r & 1) * 4 + (r >> 1);  // the stage row this lane's MMA row carries
   const uint8_t* xs = smem + p.xs_off;
   const float4* cst = reinterpret_cast<const float4*>(smem + p.cst_off);
-  const uint8_t* zero = smem + p.zero_off;
   float* red = reinterpret_cast<float*>(smem + p.red_off);
   // per-lane constant parts of the addresses; lanes of unused batch columns point at the zero block
   uint32_t x0[NP], c0[NP], xhalf[NP];

@@ -4,9 +4,11 @@
     warmup(shapes)                                                          (kernels/mm_int4.py:49)
     G = 128
 Y[T, N] = X[T, K] @ W^T with W in the int4 group-128 layout. X may be fp16 or bf16 and strided in its
-first dimension; y has X's dtype and is newly allocated, as in the reference. The Triton tile knobs are
-accepted and ignored. The kernel is compiled ahead of time, so warmup() only performs one tiny call per
-shape (it makes the first call inside a CUDA-graph capture cheap).
+first dimension; y has X's dtype and is newly allocated, as in the reference. The tensor-core operands are
+fp16 (both operands of a kind::f16 MMA must share a type, and fp16 keeps the dequantised weight's rounding
+~8x smaller than bf16), so a bf16 X is first cast to fp16 on the device. The Triton tile knobs are accepted
+and ignored. The kernel is compiled ahead of time, so warmup() only performs one tiny call per shape (it
+makes the first call inside a CUDA-graph capture cheap).
 """
 import torch
 
@@ -25,10 +27,13 @@ def mm_int4(x, q, s, m, BM=None, BN=64, num_warps=4, num_stages=3, out=None):
     for t, nm in ((s, "s"), (m, "m")):
         _require(t.dtype == torch.float16 and t.is_contiguous() and tuple(t.shape) == (N, K // G),
                  f"{nm} must be a contiguous fp16 [{N}, {K // G}] tensor")
+    out_dtype = x.dtype
+    if x.dtype == torch.bfloat16:
+        x = x.to(torch.float16)
     if x.stride(1) != 1 or x.stride(0) % 8 != 0 or x.data_ptr() % 16 != 0:
         x = x.contiguous()
     T = x.shape[0]
-    y = torch.empty(T, N, device=x.device, dtype=x.dtype) if out is None else out
+    y = torch.empty(T, N, device=x.device, dtype=out_dtype) if out is None else out
     _require(y.shape == (T, N) and y.stride(1) == 1, "out must be [T, N] with unit column stride")
     L = _lib.lib()
     with _on_device(x.device):

@@ -1,0 +1,84 @@
+"""int4-weight prefill matmul (tcgen05) on the GPU against the CPU oracle and the reference's golden outputs.
+
+Tolerance (north star): rel-L2 <= 1e-3 and max-abs <= 2e-3 * max|ref| against X.float() @ dequantize(q,s,m).t()
+(kernels/mm_int4.py:96); bf16 outputs are held to the correctly rounded bf16 result (tests/helpers.py)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import rumik_fast_b200 as rb
+from oracle import oracle as O
+from rumik_fast_b200 import synthetic as syn
+from rumik_fast_b200.mm_int4 import mm_int4
+from tests.helpers import assert_close, np_act
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu(native_lib):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    yield
+    assert rb.device_error() == 0
+
+
+def mm_ref(X, q, s, m, cols=None):
+    """Oracle, optionally on a subset of output columns (weight rows) to keep big cases fast."""
+    xa, tag = np_act(X)
+    qn, sn, mn = q.cpu().numpy(), s.cpu().numpy(), m.cpu().numpy()
+    if cols is not None:
+        qn, sn, mn = qn[cols], sn[cols], mn[cols]
+    return O.mm_int4_ref(xa, qn, sn, mn, x_dtype=tag)
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_golden(tag):
+    g = np.load(os.path.join(GOLD, "golden_mm.npz"))
+    q, s, m = (torch.from_numpy(g[f"{tag}_{k}"]).to(DEV) for k in "qsm")
+    X = torch.from_numpy(g[f"{tag}_X"]).to(DEV)
+    Y = mm_int4(X, q, s, m)
+    assert Y.shape == (X.shape[0], q.shape[0]) and Y.dtype == torch.float16
+    assert_close(Y, g[f"{tag}_Y"], f"golden mm {tag}")
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 128, 128), (17, 200, 256), (34, 5120, 3072), (64, 3072, 8192), (300, 1000, 1024),
+                                   (256, 3072, 3072), (1024, 16384, 3072)])
+def test_shapes(M, N, K):
+    g = syn.generator(M * 31 + N + K, "cpu")
+    q, s, m = syn.int4_weights(N, K, g, "cpu")
+    X = syn.activations((M, K), g, "cpu")
+    Y = mm_int4(X.to(DEV), q.to(DEV), s.to(DEV), m.to(DEV)).cpu()
+    cols = np.sort(np.random.default_rng(N).choice(N, min(N, 512), replace=False))
+    assert_close(Y[:, cols], mm_ref(X, q, s, m, cols), f"M={M} N={N} K={K}")
+
+
+def test_bf16_strided_input():
+    g = syn.generator(7, "cpu")
+    q, s, m = syn.int4_weights(384, 1024, g, "cpu")
+    Xbig = syn.activations((40, 1024 + 64), g, "cpu", dtype=torch.bfloat16)
+    X = Xbig.to(DEV)[:, :1024]
+    Y = mm_int4(X, q.to(DEV), s.to(DEV), m.to(DEV))
+    assert Y.dtype == torch.bfloat16
+    assert_close(Y, mm_ref(Xbig[:, :1024], q, s, m), "bf16 strided")
+
+
+def test_matches_gemv_rows():
+    """Each row of the prefill product equals the decode GEMV of that token (same weights)."""
+    g = syn.generator(9, "cpu")
+    q, s, m = (t.to(DEV) for t in syn.int4_weights(3072, 3072, g, "cpu"))
+    X = syn.activations((8, 3072), g, "cpu").to(DEV)
+    Y = mm_int4(X, q, s, m).float()
+    Yg = rb.gemv_int4_cuda(X, q, s, m).float()
+    assert torch.allclose(Y, Yg, rtol=2e-3, atol=2e-3 * Yg.abs().max().item())
+
+
+def test_deterministic():
+    g = syn.generator(11, "cpu")
+    q, s, m = (t.to(DEV) for t in syn.int4_weights(1024, 2048, g, "cpu"))
+    X = syn.activations((100, 2048), g, "cpu").to(DEV)
+    assert torch.equal(mm_int4(X, q, s, m), mm_int4(X, q, s, m))
