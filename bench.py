@@ -43,7 +43,12 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefetch", action="store_true", help="do not stream weights before the PDL wait")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="length of the bounded CPU-baseline sample")
+    ap.add_argument("--mode", default="set", choices=["set", "chain"],
+                    help="set: the 144 projections as one persistent launch (Int4GemvSet); chain: one launch each")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="length of the bounded CPU-baseline sample (0: skip it)")
+    ap.add_argument("--layers", type=int, default=36,
+                    help="decoder layers in the step (36 = config 1; fewer only for small profiling cases)")
     return ap.parse_args()
 
 
@@ -112,31 +117,41 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------- workload
-def build_workload(dev, seed):
+def build_workload(dev, seed, nlayers=LAYERS):
     from rumik_fast_b200 import synthetic as syn
     gen = syn.generator(seed, dev)
-    layers = [[syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES] for _ in range(LAYERS)]
+    layers = [[syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES] for _ in range(nlayers)]
     head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
     xh = syn.activations((3072,), gen, dev)
     xi = syn.activations((8192,), gen, dev)
     outs = [torch.empty(n, device=dev, dtype=torch.float16) for _, n, _ in syn.LAYER_SHAPES]
     logits = torch.empty(syn.HEAD_SHAPE[0], device=dev, dtype=torch.float16)
-    int4_bytes = LAYERS * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES)
+    int4_bytes = nlayers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES)
     head_bytes = syn.int8_bytes(*syn.HEAD_SHAPE)
     return dict(layers=layers, head=head, xh=xh, xi=xi, outs=outs, logits=logits, int4_bytes=int4_bytes,
                 head_bytes=head_bytes)
 
 
-def step_fn(w, with_head=True):
+def step_fn(w, mode="set", with_head=True):
+    """One decode step's projections: 36 x (QKV, o_proj, gate_up with x_h; down with x_i) + the int8 head.
+    mode "set": the 144 int4 GEMVs as one persistent launch; "chain": one launch per GEMV (stream order)."""
     import rumik_fast_b200 as rb
     layers, outs, xh, xi = w["layers"], w["outs"], w["xh"], w["xi"]
+    if mode == "set":
+        entries = []
+        for L in layers:
+            entries += [(xh, *L[0], outs[0]), (xh, *L[1], outs[1]), (xh, *L[2], outs[2]), (xi, *L[3], outs[3])]
+        projections = rb.Int4GemvSet(entries)
+    else:
+        def projections():
+            for L in layers:
+                rb.gemv_int4_cuda(xh, *L[0], out=outs[0])   # QKV
+                rb.gemv_int4_cuda(xh, *L[1], out=outs[1])   # o_proj
+                rb.gemv_int4_cuda(xh, *L[2], out=outs[2])   # gate_up
+                rb.gemv_int4_cuda(xi, *L[3], out=outs[3])   # down
 
     def step():
-        for L in layers:
-            rb.gemv_int4_cuda(xh, *L[0], out=outs[0])   # QKV
-            rb.gemv_int4_cuda(xh, *L[1], out=outs[1])   # o_proj
-            rb.gemv_int4_cuda(xh, *L[2], out=outs[2])   # gate_up
-            rb.gemv_int4_cuda(xi, *L[3], out=outs[3])   # down
+        projections()
         if with_head:
             rb.gemv_int8_cuda(xh, *w["head"], out=w["logits"])
     return step
@@ -244,10 +259,10 @@ def run_ours(a):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     rb.set_weight_prefetch(not a.no_prefetch)
-    w = build_workload(dev, seed=1234 + rank)
-    step = step_fn(w)
+    w = build_workload(dev, seed=1234 + rank, nlayers=a.layers)
+    step = step_fn(w, a.mode)
     g_step = capture(step)
-    g_int4 = capture(step_fn(w, with_head=False))
+    g_int4 = capture(step_fn(w, a.mode, with_head=False))
     step_bytes = w["int4_bytes"] + w["head_bytes"]
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES", "").replace(",", "").isdigit() else local
@@ -259,9 +274,9 @@ def run_ours(a):
     clocks = clk.summary(m0, m1)
     ms_step = ms / a.steps
 
-    # dominant kernel: the int4 GEMV (97 % of the step's bytes), timed alone over the same steps
+    # dominant kernel: the int4 projections (97 % of the step's bytes), timed alone over the same steps
     ms4 = timed(g_int4.replay, max(1, a.steps // 2), a.warmup, world) / max(1, a.steps // 2)
-    launches4 = LAYERS * 4
+    launches4 = 1 if a.mode == "set" else a.layers * 4
     achieved = (w["int4_bytes"] / launches4) / (ms4 / launches4 * 1e-3) / 1e9
     peak, peak_kind = peaks()
 
@@ -281,7 +296,7 @@ def run_ours(a):
     if rank == 0:
         gbs = world * step_bytes / (ms_step * 1e-3) / 1e9
         cpu = None
-        if world == 1:
+        if world == 1 and a.cpu_seconds > 0:
             c_gbs, c_threads, c_desc, _ = cpu_oracle_sample(a.cpu_seconds)
             cpu = {"value": round(c_gbs, 3), "unit": UNIT, "cores": c_threads, "kind": "port", "sample": c_desc}
         line = {
@@ -290,7 +305,9 @@ def run_ours(a):
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
             "config": {"workload": "config-1 36-layer decode-step projection set (QKV 5120x3072, o 3072x3072, "
                                    "gate_up 16384x3072, down 3072x8192; int4 g128) + config-2 int8 head "
-                                   "16385x3072, batch 1, 145 stream-ordered kernels in one CUDA graph",
+                                   "16385x3072, batch 1, in one CUDA graph",
+                       "launches": "144 projections in one persistent launch + the head" if a.mode == "set"
+                       else "145 stream-ordered launches",
                        "batch": 1, "bytes_per_step": step_bytes, "parallelism": f"replica x{world}",
                        "weight_prefetch": not a.no_prefetch,
                        "l2": "no flush: 1.98 GB of weights per step > 126 MB L2"},
@@ -301,11 +318,13 @@ def run_ours(a):
                     "ms_per_step": round(ms_e2e, 5)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "kernel": "gemv_int4_kernel", "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                         "kernel": "gemv_int4_multi_kernel" if a.mode == "set" else "gemv_int4_kernel",
+                         "traffic": NCU_TRAFFIC_PER_LAUNCH,
                          "algorithmic_bytes_per_launch": w["int4_bytes"] // launches4},
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": a.steps * (launches4 + 1),
+            "mode": a.mode,
         }
         print(json.dumps(line), flush=True)
     del g_step, g_int4

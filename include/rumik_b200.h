@@ -92,6 +92,27 @@ int rb_mm_int4(const void* X, int x_dtype, int64_t ldx,
                void* Y, int y_dtype, int64_t ldy,
                int64_t M, int64_t N, int64_t K, int flags, void* stream);
 
+/* One int4 GEMV of a list (host-side description, read by rb_gemv_int4_multi during the call). */
+typedef struct rb_gemv_desc {
+  const void* x;        /* activations [K] (dtype x_dtype of the call), 16-byte aligned */
+  void* y;              /* output [N] (dtype y_dtype of the call) */
+  const uint8_t* q;     /* codes [N, K/2] */
+  const uint16_t* s;    /* fp16 scales [N, K/128] */
+  const uint16_t* m;    /* fp16 mins [N, K/128] */
+  int64_t N;            /* >= 1 */
+  int64_t K;            /* multiple of 128, <= 16384 */
+} rb_gemv_desc;
+
+/*
+ * A list of independent int4 GEMVs (batch 1) in one persistent launch: y_i = W_i x_i for every entry.
+ * No reference counterpart as a single call: it executes what rumik-fast's projection-set benchmark
+ * (kernels/bench_gemv.py:83-113) issues as one gemv_int4 launch per matrix, without the per-launch cost.
+ * Every x_i must be ready when the launch starts and no y_i may alias another entry's inputs. `descs` is a
+ * host array, copied into the launch (at most 256 entries and 8 distinct activation vectors per launch;
+ * longer lists are split into several launches).
+ */
+int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_dtype, int flags, void* stream);
+
 /* Human-readable text for a status code (static storage). */
 const char* rb_status_string(int status);
 

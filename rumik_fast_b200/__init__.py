@@ -11,8 +11,9 @@ from . import config  # noqa: F401
 from ._lib import RumikKernelError, device_error, lib  # noqa: F401
 from .config import set_weight_prefetch, weight_prefetch  # noqa: F401
 from .cuda_gemv import SHAPE, gemv_int4_cuda, gemv_int8_cuda, quantize_int8_rows  # noqa: F401
+from .gemv_set import Int4GemvSet  # noqa: F401
 from .int4_gemv import quantize  # noqa: F401
 from . import mm_int4  # noqa: F401  (module: mm_int4.mm_int4, mm_int4.warmup, as in the reference)
 
-__all__ = ["gemv_int4_cuda", "gemv_int8_cuda", "quantize_int8_rows", "quantize", "SHAPE",
+__all__ = ["Int4GemvSet", "gemv_int4_cuda", "gemv_int8_cuda", "quantize_int8_rows", "quantize", "SHAPE",
            "set_weight_prefetch", "weight_prefetch", "device_error", "RumikKernelError"]

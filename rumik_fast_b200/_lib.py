@@ -21,10 +21,17 @@ _DTYPE_CODE = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
 
 _c = ctypes
 _vp, _i64, _int = _c.c_void_p, _c.c_int64, _c.c_int
+
+
+class GemvDesc(ctypes.Structure):
+    """struct rb_gemv_desc (include/rumik_b200.h)."""
+    _fields_ = [("x", _vp), ("y", _vp), ("q", _vp), ("s", _vp), ("m", _vp), ("N", _i64), ("K", _i64)]
+
 SIGNATURES = {
     "rb_gemv_int4": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
     "rb_gemv_int8": (_int, [_vp, _int, _i64, _vp, _int, _vp, _int, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
     "rb_mm_int4": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
+    "rb_gemv_int4_multi": (_int, [_c.POINTER(GemvDesc), _int, _int, _int, _int, _vp]),
     "rb_status_string": (_c.c_char_p, [_int]),
     "rb_version": (_int, []),
     "rb_get_device_error": (_int, [_c.POINTER(_c.c_uint), _vp]),

@@ -96,6 +96,24 @@ int rb_gemv_int8(const void* x, int x_dtype, int64_t ldx, const uint8_t* q, int 
   return st;
 }
 
+int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_dtype, int flags, void* stream) {
+  if (count < 0) return RB_ERR_SHAPE;
+  if (count == 0) return RB_OK;
+  if (!descs) return RB_ERR_NULL;
+  if (!act_dtype_ok(x_dtype) || !act_dtype_ok(y_dtype)) return RB_ERR_DTYPE;
+  for (int i = 0; i < count; ++i) {
+    const rb_gemv_desc& d = descs[i];
+    if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.K > 16384 || d.N > (int64_t(1) << 30)) return RB_ERR_SHAPE;
+    if (!d.x || !d.y || !d.q || !d.s || !d.m) return RB_ERR_NULL;
+    if (!aligned16(d.x) || !aligned16(d.q) || !aligned16(d.s) || !aligned16(d.m)) return RB_ERR_ALIGN;
+  }
+  int sms = 0, st = device_sms(&sms);
+  if (st != RB_OK) return st;
+  st = rb::launch_gemv_int4_multi(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream));
+  if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+  return st;
+}
+
 int rb_mm_int4(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const uint16_t* s, const uint16_t* m,
                void* Y, int y_dtype, int64_t ldy, int64_t M, int64_t N, int64_t K, int flags, void* stream) {
   if (M < 0 || N < 0 || K <= 0) return RB_ERR_SHAPE;

@@ -23,6 +23,8 @@ enum : unsigned int {
   ERR_GEMV8_FULL = 1u << 2,
   ERR_GEMV8_EMPTY = 1u << 3,
   ERR_MM4_WAIT = 1u << 4,     // prefill matmul timed out on an mbarrier
+  ERR_MULTI_FULL = 1u << 5,   // multi-GEMV consumer timed out waiting for a tile
+  ERR_MULTI_EMPTY = 1u << 6,  // multi-GEMV producer timed out waiting for ring space
 };
 
 // Upper bound on the wall time of one mbarrier wait. Healthy waits here last microseconds (at most the

@@ -3,4 +3,5 @@
 #include "capi.cu"
 #include "gemv_int4.cu"
 #include "gemv_int8.cu"
+#include "gemv_int4_multi.cu"
 #include "mm_int4.cu"

@@ -1,0 +1,54 @@
+"""A fixed list of independent int4 GEMVs executed as ONE persistent kernel launch (rb_gemv_int4_multi).
+
+A decode step issued as one launch per projection pays a fixed cost per launch that on B200 is comparable
+to the whole step's weight-streaming time. When the GEMVs of a list are independent (all inputs ready at
+launch, as in rumik-fast's projection-set benchmark, kernels/bench_gemv.py:83-113), Int4GemvSet streams all
+of their weights through one persistent kernel instead:
+
+    step = Int4GemvSet([(x_h, *w_qkv, y_qkv), (x_h, *w_o, y_o), ...])   # built once
+    step()                                                             # every call: all GEMVs
+
+Entries are (x, q, s, m, y) with the layout of gemv_int4_cuda (x [K] fp16/bf16, q uint8 [N, K/2], s and m
+fp16 [N, K/128], y [N]); all x share one dtype and all y share one dtype. Calling is graph-capture safe.
+"""
+import ctypes
+
+import torch
+
+from . import _lib, config
+from .cuda_gemv import _on_device, _require
+
+G = 128
+
+
+class Int4GemvSet:
+    def __init__(self, entries):
+        _require(len(entries) > 0, "empty GEMV list")
+        self.entries = list(entries)
+        x0, y0 = self.entries[0][0], self.entries[0][4]
+        self.device = x0.device
+        self.x_dtype, self.y_dtype = x0.dtype, y0.dtype
+        descs = (_lib.GemvDesc * len(self.entries))()
+        for i, (x, q, s, m, y) in enumerate(self.entries):
+            N, K = q.shape[0], q.shape[1] * 2
+            _require(x.is_cuda and x.device == self.device, "all tensors must be on one CUDA device")
+            _require(x.dtype == self.x_dtype and y.dtype == self.y_dtype, "one x dtype and one y dtype per set")
+            _require(x.dtype in (torch.float16, torch.bfloat16), f"x must be fp16 or bf16, got {x.dtype}")
+            _require(y.dtype in (torch.float16, torch.bfloat16), f"y must be fp16 or bf16, got {y.dtype}")
+            _require(x.numel() == K and x.is_contiguous(), f"entry {i}: x must be a contiguous [{K}] vector")
+            _require(y.numel() == N and y.is_contiguous(), f"entry {i}: y must be a contiguous [{N}] vector")
+            _require(q.dtype == torch.uint8 and q.is_contiguous(), f"entry {i}: q must be contiguous uint8 [N, K/2]")
+            _require(K % G == 0, f"entry {i}: K={K} must be a multiple of {G}")
+            for t, nm in ((s, "s"), (m, "m")):
+                _require(t.dtype == torch.float16 and t.is_contiguous() and tuple(t.shape) == (N, K // G),
+                         f"entry {i}: {nm} must be a contiguous fp16 [{N}, {K // G}] tensor")
+            descs[i] = _lib.GemvDesc(x.data_ptr(), y.data_ptr(), q.data_ptr(), s.data_ptr(), m.data_ptr(), N, K)
+        self._descs = descs
+        self.bytes = sum(q.numel() + 4 * s.numel() + 2 * x.numel() + 2 * y.numel() for x, q, s, m, y in self.entries)
+
+    def __call__(self):
+        L = _lib.lib()
+        with _on_device(self.device):
+            st = L.rb_gemv_int4_multi(self._descs, len(self.entries), _lib.dtype_code(self.x_dtype),
+                                      _lib.dtype_code(self.y_dtype), config.flags(), _lib.stream_ptr(self.device))
+        _lib.check("rb_gemv_int4_multi", st)

@@ -1,0 +1,92 @@
+"""One-launch list of independent int4 GEMVs (Int4GemvSet / rb_gemv_int4_multi) against the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+import rumik_fast_b200 as rb
+from rumik_fast_b200 import synthetic as syn
+from tests.helpers import assert_close, int4_ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu(native_lib):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    yield
+    assert rb.device_error() == 0
+
+
+def build(shapes, nx=2, seed=0, dtype=torch.float16):
+    g = syn.generator(seed, "cpu")
+    xs = {}
+    host = []
+    for i, (n, k) in enumerate(shapes):
+        key = (i % nx, k)
+        if key not in xs:
+            xs[key] = syn.activations((k,), g, "cpu", dtype=dtype)
+        q, s, m = syn.int4_weights(n, k, g, "cpu")
+        host.append((xs[key], q, s, m))
+    dev_x = {key: v.to(DEV) for key, v in xs.items()}
+    out = []
+    for i, ((x, q, s, m), (n, k)) in enumerate(zip(host, shapes)):
+        key = (i % nx, k)
+        y = torch.full((n,), float("nan"), device=DEV, dtype=dtype)
+        out.append((dev_x[key], q.to(DEV), s.to(DEV), m.to(DEV), y))
+    return host, out
+
+
+def check(host, dev_entries, what):
+    for i, ((x, q, s, m), e) in enumerate(zip(host, dev_entries)):
+        assert_close(e[4], int4_ref(x, q, s, m), f"{what} entry {i}")
+
+
+def test_layer_set():
+    """Two layers of the config-1 projection set (QKV, o, gate_up with x_h; down with x_i)."""
+    shapes = [(n, k) for _ in range(2) for _, n, k in syn.LAYER_SHAPES]
+    host, ent = build(shapes, nx=1)
+    rb.Int4GemvSet(ent)()
+    check(host, ent, "layers")
+
+
+def test_ragged_and_mixed_k():
+    shapes = [(1, 128), (7, 256), (9, 3072), (100, 11008), (1000, 2048), (25088, 2048), (300, 16384), (5, 8192)]
+    host, ent = build(shapes, nx=3, seed=1)
+    rb.Int4GemvSet(ent)()
+    check(host, ent, "ragged")
+
+
+def test_many_entries_and_slots_split_launches():
+    """More than 256 entries and more than 8 distinct activation vectors: several launches."""
+    shapes = [(16 + (i % 5) * 8, 128 * (1 + i % 3)) for i in range(300)]
+    host, ent = build(shapes, nx=11, seed=2)
+    rb.Int4GemvSet(ent)()
+    check(host, ent, "split")
+
+
+def test_bf16_and_graph_replay():
+    shapes = [(3072, 3072), (640, 1024), (2000, 8192)]
+    host, ent = build(shapes, nx=2, seed=3, dtype=torch.bfloat16)
+    st = rb.Int4GemvSet(ent)
+    st()
+    torch.cuda.synchronize()
+    for e in ent:
+        e[4].fill_(float("nan"))
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        st()
+    gr.replay()
+    torch.cuda.synchronize()
+    check(host, ent, "bf16 graph")
+
+
+def test_matches_single_gemv_bitwise():
+    g = syn.generator(4, "cpu")
+    q, s, m = (t.to(DEV) for t in syn.int4_weights(5120, 3072, g, "cpu"))
+    x = syn.activations((3072,), g, "cpu").to(DEV)
+    y1 = rb.gemv_int4_cuda(x, q, s, m)
+    y2 = torch.empty_like(y1)
+    rb.Int4GemvSet([(x, q, s, m, y2)])()
+    assert torch.allclose(y1.float(), y2.float(), rtol=1e-3, atol=1e-3 * y1.float().abs().max().item())
