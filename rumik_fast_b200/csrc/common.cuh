@@ -184,6 +184,11 @@ __device__ __forceinline__ float2 lds64f_a(uint32_t a) {
   asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a) : "memory");
   return v;
 }
+__device__ __forceinline__ uint32_t lds32_a(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
 __device__ __forceinline__ float lds_h2f_a(uint32_t a) {
   unsigned short h;
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a) : "memory");
