@@ -1,13 +1,13 @@
 #!/usr/bin/env python
-"""Decode-step GEMV benchmark of rumik_fast_b200 on B200 (BASELINE config 1 + the config-2 int8 head).
+"""Decode-step GEMV benchmark of rumik_fast_b200 on B200 (the 36-layer decode-step projection set + the int8 audio head).
 
 One step = the 36-layer decode-step projection set (per layer: QKV 5120x3072, o_proj 3072x3072,
-gate_up 16384x3072, down 3072x8192, int4 group-128) followed by the int8 audio head (16385x3072), launched
-as 145 separate kernels in stream order - each GEMV waits for the previous kernel before it reads its input,
-exactly as in a decode step - and replayed from one CUDA graph, the way rumik-fast's engine and its own
-full-step benchmark run it (engine/rumik_int4.py:225-245, kernels/bench_gemv.py:83-113). Inputs follow the
-reference benchmark: fixed activations (x_h for QKV/o/gate_up/head, x_i for down). The weights (1.98 GB)
-are larger than L2 (126 MB), so no L2 flush is needed between steps.
+gate_up 16384x3072, down 3072x8192, int4 group-128) followed by the int8 audio head (16385x3072), replayed
+from one CUDA graph, the way rumik-fast's engine and its full-step benchmark run it (engine/rumik_int4.py:225-245,
+kernels/bench_gemv.py:83-113). Inputs follow the reference benchmark: fixed activations (x_h for
+QKV/o/gate_up/head, x_i for down). --mode set (default) runs the 144 projections as one persistent
+rb_gemv_int4_multi launch plus the head; --mode chain runs 145 stream-ordered launches, one per matrix. The
+weights (1.98 GB) are larger than L2 (126 MB), so no L2 flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-prefetch]
 
@@ -32,8 +32,9 @@ sys.path.insert(0, ROOT)
 LAYERS = 36
 METRIC = "decode-step GEMV HBM GB/s"
 UNIT = "GB/s"
-# DRAM bytes (read + write) per launch of gemv_int4_kernel, measured by ncu (profiles/); None until captured
-NCU_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) per launch of gemv_int4_multi_kernel on the 36-layer set: ncu capture of the 3-layer
+# case (160.49 MB read + 3.79 MB written) scaled x12 by tiles streamed
+NCU_TRAFFIC_PER_LAUNCH = 1971320832
 
 
 def parse():
@@ -319,7 +320,7 @@ def run_ours(a):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "kernel": "gemv_int4_multi_kernel" if a.mode == "set" else "gemv_int4_kernel",
-                         "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                         "traffic": NCU_TRAFFIC_PER_LAUNCH if a.mode == "set" and a.layers == LAYERS else None,
                          "algorithmic_bytes_per_launch": w["int4_bytes"] // launches4},
             "cpu_baseline": cpu,
             "clocks": clocks,

@@ -2,13 +2,13 @@
 
 Run in a container where the rumik-fast reference is mounted (it is not needed anywhere else):
 
-    python tests/golden/make_golden.py [--ref /path/to/rumik-fast]
+    python tests/golden/make_golden.py --ref /path/to/rumik-fast
 
 It imports kernels/int4_gemv.py (quantize, dequantize) and kernels/cuda_gemv.py (quantize_int8_rows) from the
 reference on the CPU and records, for small seeded inputs, the reference's outputs:
   * golden_int4.npz : bf16 weights -> reference quantize() -> (q, s, m); reference dequantize(); and
                       y = dequantize(q, s, m) @ x.float() (kernels/bench_cuda.py:38) for fp16/bf16 x,
-                      batched x, and BASELINE-config-style codes/scales/mins.
+                      batched x, and benchmark-config-style codes/scales/mins.
   * golden_int8.npz : bf16 head rows -> reference quantize_int8_rows(w, pad_to=16) -> (q, s); and
                       y = ((q - 128) * s) @ x (kernels/cuda_gemv.py:245-246).
   * golden_mm.npz   : Y = X.float() @ dequantize(q, s, m).t() (kernels/mm_int4.py:96).
@@ -33,7 +33,8 @@ def bits(t):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("RUMIK_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("RUMIK_REFERENCE"), required="RUMIK_REFERENCE" not in os.environ,
+                    help="root of the rumik-fast checkout (or set RUMIK_REFERENCE)")
     a = ap.parse_args()
     sys.path.insert(0, os.path.join(a.ref, "kernels"))
     import int4_gemv as ref4  # noqa: E402  (reference module)
@@ -54,7 +55,7 @@ def main():
                      f"{tag}_x16": bits(x16), f"{tag}_y16": (deq @ x16.float()).numpy(),
                      f"{tag}_xbf": bits(xb), f"{tag}_ybf": (deq @ xb.float()).numpy(),
                      f"{tag}_xbat": bits(xbat), f"{tag}_ybat": (xbat.float() @ deq.t()).numpy()})
-    # (B) BASELINE config-0 style: codes uniform 0..15, scale ~U(0.002, 0.02), min = -7.5 scale + N(0, 1e-3)
+    # (B) benchmark config-0 style: codes uniform 0..15, scale ~U(0.002, 0.02), min = -7.5 scale + N(0, 1e-3)
     g = torch.Generator().manual_seed(10)
     n, k = 48, 512
     codes = torch.randint(0, 16, (n, k), generator=g, dtype=torch.uint8)
@@ -78,7 +79,7 @@ def main():
         out8.update({f"{tag}_w": bits(w), f"{tag}_q": bits(q), f"{tag}_s": bits(s),
                      f"{tag}_x16": bits(x16), f"{tag}_y16": (wq @ x16.float()).numpy(),
                      f"{tag}_xbf": bits(xb), f"{tag}_ybf": (wq @ xb.float()).numpy()})
-    # BASELINE config-2 style: W int8 uniform -127..127, fp16 row scale ~U(1e-4, 1e-3), unpadded N
+    # benchmark config-2 style: W int8 uniform -127..127, fp16 row scale ~U(1e-4, 1e-3), unpadded N
     g = torch.Generator().manual_seed(22)
     n, k = 37, 320
     wi8 = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int16).to(torch.int8)
