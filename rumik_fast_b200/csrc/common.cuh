@@ -60,6 +60,15 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
       : "memory");
 }
 
+// Arrive `count` times at once (release semantics at CTA scope, like the single arrive).
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t count) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(count)
+      : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile(
       "{\n\t.reg .b64 st;\n\t"
@@ -165,6 +174,33 @@ __device__ __forceinline__ float4 lds128f_a(uint32_t a) {
   float4 v;
   asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a) : "memory");
   return v;
+}
+// Forms with a compile-time byte offset folded into the address (no separate address arithmetic).
+template <int OFF>
+__device__ __forceinline__ uint4 lds128_o(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4+%5];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a), "n"(OFF) : "memory");
+  return v;
+}
+template <int OFF>
+__device__ __forceinline__ float4 lds128f_o(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4+%5];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a), "n"(OFF) : "memory");
+  return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint32_t lds32_o(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF) : "memory");
+  return v;
+}
+template <int OFF>
+__device__ __forceinline__ float lds_h2f_o(uint32_t a) {
+  unsigned short h;
+  asm volatile("ld.shared.u16 %0, [%1+%2];" : "=h"(h) : "r"(a), "n"(OFF) : "memory");
+  return __half2float(__ushort_as_half(h));
 }
 // Predicated forms: lanes with on == 0 issue no shared-memory access and get zeros.
 __device__ __forceinline__ uint4 lds128_pa(uint32_t a, uint32_t on) {

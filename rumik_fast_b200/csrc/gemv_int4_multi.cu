@@ -22,15 +22,35 @@ namespace rb {
 
 namespace g4m {
 
-constexpr int kConsumerWarps = 16;  // work items need ~80 registers: 16 warps fit without spills
+// Build-time tuning (defaults measured best on B200): consumer warps, groups per work item, MMA chains per
+// group.
+#ifndef RB_MULTI_WARPS
+#define RB_MULTI_WARPS 15
+#endif
+#ifndef RB_MULTI_SLICE_GROUPS
+#define RB_MULTI_SLICE_GROUPS 12
+#endif
+#ifndef RB_MULTI_CHAINS
+#define RB_MULTI_CHAINS 1
+#endif
+constexpr int kConsumerWarps = RB_MULTI_WARPS;
+constexpr int kChains = RB_MULTI_CHAINS;
+// Registers per thread for one CTA per SM: each of the SM's four sub-partitions has 16,384 registers and
+// holds every fourth warp, allocated in multiples of 8 registers per thread.
+constexpr int kWarpsPerPartition = (RB_MULTI_WARPS + 1 + 3) / 4;
+constexpr int kMaxRegs = (16384 / (kWarpsPerPartition * 32)) / 8 * 8 > 255 ? 255
+                                                                            : (16384 / (kWarpsPerPartition * 32)) / 8 * 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxEntries = 256;
 constexpr int kMaxSlots = 8;
 constexpr int kWindow = 128;       // barrier window (tiles)
 constexpr int kRedSlots = 32;      // reduction slots (tiles), > kMaxOutstanding
 constexpr int kMaxP = 8;           // K-slices per step at most
-constexpr int kSliceGroups = 24;   // groups per work item at most (~12 KB of codes for 8 rows)
+constexpr int kSliceGroups = RB_MULTI_SLICE_GROUPS;  // groups per work item at most
 constexpr int kMaxOutstanding = 24;  // tiles in flight per CTA (window >= this + consumer warps)
+// A tile's ring space is released when its empty barrier has counted kRelease arrivals: each work item
+// arrives once with count 1, except the tile's last item, which arrives with kRelease - (ipt - 1).
+constexpr int kRelease = 2 * kMaxP;
 
 struct Entry {
   const uint8_t* q;
@@ -46,21 +66,33 @@ struct Slot {
   uint32_t tab_off, cst_off;
 };
 
-// Entry as kept in shared memory for the whole launch (per-tile lookups must not go to the parameter
-// block: it is indexed dynamically, and its misses in the constant cache stalled the producer).
-struct __align__(16) EntryS {
+// Per-entry data kept in shared memory for the whole launch (per-tile lookups must not go to the
+// parameter block: it is indexed dynamically, and its misses in the constant cache stalled the producer).
+// What the producer needs:
+struct __align__(16) EntryP {
   const uint8_t* q;
   const uint8_t* s;
   const uint8_t* m;
+  int N, G, tile_begin;
+  uint32_t tbytes, row_bytes, sblk;  // tile bytes in the ring, code bytes per row, bytes of one s (or m) block
+};
+// What the consumers need, plus this CTA's share of the entry: its tiles are the local tiles
+// [jlo, jlo + n) and their work items are the CTA-local items [ib, ib + n * ipt). An extra entry after the
+// last holds ib = the CTA's total item count.
+struct __align__(16) EntryC {
   void* y;
-  int N, K, G, tile_begin;
-  uint32_t tbytes, row_bytes, sblk, tab_off_x;  // tile bytes in the ring; x table offset of its slot
+  int N, tile_begin;
+  int G, rs;                     // groups per row, code bytes per row
+  uint32_t sblk, tab_off_x;      // s block bytes (the m block follows it); x table of its slot
   uint32_t cst_off_x;
-  int P, gps, ipt;  // K-slices per 8-row step, groups per slice, work items per tile (= steps * P)
+  int P, gps, ipt;               // K-slices per 8-row step, groups per slice, items per tile (steps * P)
+  int jlo, ib;
+  uint32_t mag_ipt, mag_p;       // ceil(2^32 / ipt), ceil(2^32 / P): division by multiply-high
 };
 
 struct MultiParams {
   int count, nslots, total_tiles, x_bf16, y_bf16, prefetch;
+  int maxp;  // largest K-slice count of the launch's entries (sizes the reduction area)
   uint32_t ring_bytes, ring_off, bar_off, start_off, zero_off, ent_off, red_off;
   uint32_t m_lo, m_hi, k1024, k64;
   Slot slots[kMaxSlots];
@@ -73,100 +105,118 @@ __host__ __device__ __forceinline__ uint32_t tile_bytes(int TR, int K, int G) {
   return ((static_cast<uint32_t>(TR) * (K / 2) + 64u + 2u * (2u * TR * G + 16u)) + 127u) & ~127u;
 }
 
-// Operands of one 128-column group for the TR/8 eight-row MMA steps of a tile. MMA row R of step t carries
-// tile row (R & 1) * TR/2 + t * 4 + R / 2, so the two rows a warp reads in one shared-memory phase come from
-// the two copies (64 bytes apart modulo 128) and hit disjoint banks.
-template <int ST>
-struct Ops16 {
-  uint4 w[ST];
-  float s[ST], m[ST];
-  uint4 b01, b23;
-  float4 c;
-};
-
-// Scales and mins of a pair of groups (g, g+1) for every step, loaded as half2: with 16-row tiles the
-// scale block of a tile starts 16-byte aligned, so for even G the pair is 4-byte aligned. Halves the
-// scale/min load instructions (and their bank conflicts: rows of one step share banks when G*2 is a
-// multiple of 128 bytes).
-template <int ST>
-struct SM2 {
-  uint32_t s[ST], m[ST];
-};
-
-template <int ST>
-__device__ __forceinline__ void load_sm2(uint32_t a_s, uint32_t s_step, uint32_t m_off, SM2<ST>& o) {
+// One 128-column group of an 8-row MMA step for this lane: w = its 32 codes (row prow, 16 bytes at qd*16
+// in the group), b01/b23 = the activation B fragments, c = {-offset, sum x, ., .} of the group. MMA row R
+// carries the row's columns 0-63 in rows 0-7 and 64-127 in rows 8-15; B column 0 carries x for the first
+// half and column 1 for the second, so D[r][0] + D[r+8][1] (d[0] + d[3] in lanes with qd = 0) is the row's
+// dot product. Lanes 8-31 load duplicates of lanes 0-7's activation fragments: their B columns 2-7 only
+// produce D columns that are never read. Returns acc + s * (dot - offset) + m * sum x.
+__device__ __forceinline__ float group_dot(const uint4& w4, const uint4& b01, const uint4& b23, const float4& c,
+                                           float s, float m, const g4::DequantK& k, const float4& zq,
+                                           float acc) {
+  const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+  uint32_t a[4][4];
 #pragma unroll
-  for (int t = 0; t < ST; ++t) {
-    o.s[t] = lds32_a(a_s + t * s_step);
-    o.m[t] = lds32_a(a_s + m_off + t * s_step);
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t w = wv[j], w8 = __umulhi(wv[j], 1u << 24);  // w >> 8 on the FMA pipe
+    a[j][0] = and_or(w, k.m_lo, k.k1024);
+    a[j][1] = and_or(w8, k.m_lo, k.k1024);
+    a[j][2] = and_or(w, k.m_hi, k.k64);
+    a[j][3] = and_or(w8, k.m_hi, k.k64);
   }
-}
-
-template <int ST>
-__device__ __forceinline__ void split_sm2(const SM2<ST>& v, Ops16<ST>& o0, Ops16<ST>& o1) {
-#pragma unroll
-  for (int t = 0; t < ST; ++t) {
-    const float2 s2 = __half22float2(*reinterpret_cast<const __half2*>(&v.s[t]));
-    const float2 m2 = __half22float2(*reinterpret_cast<const __half2*>(&v.m[t]));
-    o0.s[t] = s2.x;
-    o1.s[t] = s2.y;
-    o0.m[t] = m2.x;
-    o1.m[t] = m2.y;
-  }
-}
-
-struct Addr16 {
-  uint32_t w, s, x, c;   // step-0 code bytes, step-0 scale, activation fragments, constants
-  uint32_t xon, con;
-};
-
-template <int ST>
-__device__ __forceinline__ void load16(const Addr16& a, uint32_t w_step, uint32_t s_step, uint32_t m_off,
-                                       uint32_t xhalf, Ops16<ST>& o) {
-#pragma unroll
-  for (int t = 0; t < ST; ++t) {
-    o.w[t] = lds128_a(a.w + t * w_step);
-    o.s[t] = lds_h2f_a(a.s + t * s_step);
-    o.m[t] = lds_h2f_a(a.s + m_off + t * s_step);
-  }
-  o.b01 = lds128_pa(a.x, a.xon);
-  o.b23 = lds128_pa(a.x + xhalf, a.xon);
-  o.c = lds128f_pa(a.c, a.con);
-}
-
-// Codes, activation fragments and constants of one group (scales and mins come from load_sm2).
-template <int ST>
-__device__ __forceinline__ void load16w(const Addr16& a, uint32_t w_step, uint32_t xhalf, Ops16<ST>& o) {
-#pragma unroll
-  for (int t = 0; t < ST; ++t) o.w[t] = lds128_a(a.w + t * w_step);
-  o.b01 = lds128_pa(a.x, a.xon);
-  o.b23 = lds128_pa(a.x + xhalf, a.xon);
-  o.c = lds128f_pa(a.c, a.con);
-}
-
-template <int ST>
-__device__ __forceinline__ void math16(const Ops16<ST>& o, const float4& zq, const g4::DequantK& k,
-                                       float (&acc)[ST]) {
-#pragma unroll
-  for (int t = 0; t < ST; ++t) {
-    const uint32_t wv[4] = {o.w[t].x, o.w[t].y, o.w[t].z, o.w[t].w};
-    uint32_t a[4][4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t w = wv[j], w8 = __umulhi(wv[j], 1u << 24);  // w >> 8 on the FMA pipe
-      a[j][0] = and_or(w, k.m_lo, k.k1024);
-      a[j][1] = and_or(w8, k.m_lo, k.k1024);
-      a[j][2] = and_or(w, k.m_hi, k.k64);
-      a[j][3] = and_or(w8, k.m_hi, k.k64);
-    }
+  float dot;
+  if (kChains == 2) {
     float d0[4], d1[4];
-    mma_f16_16816_c(d0, a[0][0], a[0][1], a[0][2], a[0][3], o.b01.x, o.b01.y, o.c);
-    mma_f16_16816_c(d1, a[1][0], a[1][1], a[1][2], a[1][3], o.b01.z, o.b01.w, zq);
-    mma_f16_16816(d0, a[2][0], a[2][1], a[2][2], a[2][3], o.b23.x, o.b23.y);
-    mma_f16_16816(d1, a[3][0], a[3][1], a[3][2], a[3][3], o.b23.z, o.b23.w);
-    const float dot = (d0[0] + d0[3]) + (d1[0] + d1[3]);
-    acc[t] = fmaf(o.s[t], dot, fmaf(o.m[t], o.c.y, acc[t]));
+    mma_f16_16816_c(d0, a[0][0], a[0][1], a[0][2], a[0][3], b01.x, b01.y, c);
+    mma_f16_16816_c(d1, a[1][0], a[1][1], a[1][2], a[1][3], b01.z, b01.w, zq);
+    mma_f16_16816(d0, a[2][0], a[2][1], a[2][2], a[2][3], b23.x, b23.y);
+    mma_f16_16816(d1, a[3][0], a[3][1], a[3][2], a[3][3], b23.z, b23.w);
+    dot = (d0[0] + d0[3]) + (d1[0] + d1[3]);
+  } else {
+    float d0[4];
+    mma_f16_16816_c(d0, a[0][0], a[0][1], a[0][2], a[0][3], b01.x, b01.y, c);
+    mma_f16_16816(d0, a[1][0], a[1][1], a[1][2], a[1][3], b01.z, b01.w);
+    mma_f16_16816(d0, a[2][0], a[2][1], a[2][2], a[2][3], b23.x, b23.y);
+    mma_f16_16816(d0, a[3][0], a[3][1], a[3][2], a[3][3], b23.z, b23.w);
+    dot = d0[0] + d0[3];
   }
+  return fmaf(s, dot, fmaf(m, c.y, acc));
+}
+
+// Shared-memory addresses of one work item (8 rows x groups [g, g1)), advanced group by group.
+struct ItemAddr {
+  uint32_t w;  // this lane's 16 code bytes of group g
+  uint32_t x;  // activation fragments of group g (b01 at +0, b23 at +128; 256 bytes per group)
+  uint32_t c;  // constants of group g (16 bytes per group)
+  uint32_t s;  // scale of (row, g); the min is m_off bytes further
+};
+
+__device__ __forceinline__ float item_single(ItemAddr& A, uint32_t m_off, const g4::DequantK& k,
+                                             const float4& zq, float acc) {
+  const uint4 w = lds128_o<0>(A.w);
+  const uint4 b01 = lds128_o<0>(A.x), b23 = lds128_o<128>(A.x);
+  const float4 c = lds128f_o<0>(A.c);
+  const float s = lds_h2f_o<0>(A.s), m = lds_h2f_o<0>(A.s + m_off);
+  A.w += 64;
+  A.x += 256;
+  A.c += 16;
+  A.s += 2;
+  return group_dot(w, b01, b23, c, s, m, k, zq, acc);
+}
+
+// Operands of a pair of groups (g, g+1).
+struct PairOps {
+  uint32_t s2, m2;
+  uint4 w0, w1, x0, y0, x1, y1;
+  float4 c0, c1;
+};
+
+__device__ __forceinline__ void load_pair(const ItemAddr& A, uint32_t ma, PairOps& o) {
+  o.s2 = lds32_o<0>(A.s);
+  o.m2 = lds32_o<0>(ma);
+  o.w0 = lds128_o<0>(A.w);
+  o.w1 = lds128_o<64>(A.w);
+  o.x0 = lds128_o<0>(A.x);
+  o.y0 = lds128_o<128>(A.x);
+  o.x1 = lds128_o<256>(A.x);
+  o.y1 = lds128_o<384>(A.x);
+  o.c0 = lds128f_o<0>(A.c);
+  o.c1 = lds128f_o<16>(A.c);
+}
+
+__device__ __forceinline__ void pair_math(const PairOps& o, const g4::DequantK& k, const float4& zq, float& acc0,
+                                          float& acc1) {
+  const float2 sf = __half22float2(*reinterpret_cast<const __half2*>(&o.s2));
+  const float2 mf = __half22float2(*reinterpret_cast<const __half2*>(&o.m2));
+  acc0 = group_dot(o.w0, o.x0, o.y0, o.c0, sf.x, mf.x, k, zq, acc0);
+  acc1 = group_dot(o.w1, o.x1, o.y1, o.c1, sf.y, mf.y, k, zq, acc1);
+}
+
+// Dot products of this lane's row over groups [g0, g1) (scaled, offset-corrected, fp32).
+__device__ __forceinline__ float item_dot(ItemAddr A, uint32_t m_off, int G, int g0, int g1,
+                                          const g4::DequantK& k, const float4& zq) {
+  float acc0 = 0.f, acc1 = 0.f;
+  int g = g0;
+  if ((G & 1) == 0) {
+    // scale/min pairs (g, g+1) are 4-byte aligned for even g: one load each per pair
+    if (g & 1) {
+      acc1 = item_single(A, m_off, k, zq, acc1);
+      ++g;
+    }
+    uint32_t ma = A.s + m_off;
+    for (; g + 1 < g1; g += 2) {
+      PairOps o;
+      load_pair(A, ma, o);
+      A.w += 128;
+      A.x += 512;
+      A.c += 32;
+      A.s += 4;
+      ma += 4;
+      pair_math(o, k, zq, acc0, acc1);
+    }
+  }
+  for (; g < g1; ++g) acc0 = item_single(A, m_off, k, zq, acc0);
+  return acc0 + acc1;
 }
 
 // x of every slot -> fp16 B fragments [g][2][8 lanes][16 B] and constants {-offset, sum, 0, 0} per group
@@ -207,24 +257,25 @@ __device__ void stage_all_x(const MultiParams& p, uint8_t* smem, int tid) {
   }
 }
 
+// Producer (lane 0 of the producer warp): streams this CTA's tiles into the ring in order.
 template <int TR>
 __device__ void multi_produce(const MultiParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                               uint32_t* start) {
-  const EntryS* ent = reinterpret_cast<const EntryS*>(smem + p.ent_off);
+  const EntryP* ent = reinterpret_cast<const EntryP*>(smem + p.ent_off);
   const int C = gridDim.x, cta = blockIdx.x;
   const int ntiles = (p.total_tiles - cta + C - 1) / C;
   uint8_t* ring = smem + p.ring_off;
   uint32_t head = 0, tail = 0;  // FIFO ring: outstanding tiles occupy [tail, head) or, wrapped, [tail, end) + [0, head)
-  int old = 0;                  // oldest unreleased local tile
+  int old = 0;                  // oldest unreclaimed local tile
   int e = 0;
   bool ok = true;
   int j = 0;
   for (; j < ntiles && ok; ++j) {
     const int gt = cta + j * C;
     while (e + 1 < p.count && gt >= ent[e + 1].tile_begin) ++e;
-    const EntryS& E = ent[e];
+    const EntryP& E = ent[e];
     const uint32_t b = E.tbytes;
-    // allocate b bytes, releasing the oldest tiles (in order) until the space is free
+    // allocate b bytes, reclaiming the oldest tiles (in order) until the space is free
     uint32_t pos = 0;
     for (;;) {
       const int n_out = j - old;
@@ -283,49 +334,74 @@ __device__ void multi_produce(const MultiParams& p, uint8_t* smem, uint64_t* ful
     }
   }
   // no retirement with copies in flight
-  for (int t = old; t < j; ++t) mbar_wait(&full[t % kWindow], (t / kWindow) & 1, ERR_MULTI_FULL);
+  for (int t = old; t < j; ++t)
+    if (!mbar_wait(&full[t % kWindow], (t / kWindow) & 1, ERR_MULTI_FULL)) break;
+}
+
+// Number of this CTA's local tiles j (global tile cta + j * C) that lie below global tile T.
+__device__ __forceinline__ int local_tiles_below(int T, int cta, int C) { return T > cta ? (T - cta + C - 1) / C : 0; }
+
+// n / d for 0 <= n < 2^24 and 1 <= d <= 2^8 with mag = ceil(2^32 / d) (exact in that range); d == 1 apart.
+__device__ __forceinline__ int fdiv(int n, int d, uint32_t mag) {
+  return d == 1 ? n : static_cast<int>(__umulhi(static_cast<uint32_t>(n), mag));
+}
+__host__ __device__ __forceinline__ uint32_t div_magic(uint32_t d) {
+  return d <= 1 ? 0u : static_cast<uint32_t>((0xFFFFFFFFull + d) / d);
 }
 
 template <int TR>
-__global__ void __launch_bounds__(kThreads, 1) gemv_int4_multi_kernel(const __grid_constant__ MultiParams p) {
+__global__ void __maxnreg__(kMaxRegs) gemv_int4_multi_kernel(const __grid_constant__ MultiParams p) {
   constexpr int ST = TR / 8, H = TR / 2;
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int C = gridDim.x, cta = blockIdx.x;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   uint64_t* empty = full + kWindow;
   uint32_t* start = reinterpret_cast<uint32_t*>(smem + p.start_off);
   if (tid == 0) {
     for (int i = 0; i < kWindow; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], kRelease);
     }
     fence_mbar_init();
   }
   if (tid < 16) reinterpret_cast<uint32_t*>(smem + p.zero_off)[tid] = 0u;
-  int* cnt = reinterpret_cast<int*>(smem + p.red_off);  // [kRedSlots][ST + 1]: per-step and per-tile counters
-  for (int i = tid; i < kRedSlots * (ST + 1); i += kThreads) cnt[i] = 0;
-  EntryS* ent = reinterpret_cast<EntryS*>(smem + p.ent_off);
+  int* cnt = reinterpret_cast<int*>(smem + p.red_off);  // [kRedSlots][ST]: arrivals of the K-slices of a step
+  for (int i = tid; i < kRedSlots * ST; i += kThreads) cnt[i] = 0;
+  EntryP* entp = reinterpret_cast<EntryP*>(smem + p.ent_off);
+  EntryC* entc = reinterpret_cast<EntryC*>(smem + p.ent_off + p.count * sizeof(EntryP));
   for (int i = tid; i < p.count; i += kThreads) {
     const Entry& E = p.e[i];
     const Slot& S = p.slots[E.slot];
-    EntryS v;
-    v.q = E.q;
-    v.s = reinterpret_cast<const uint8_t*>(E.s);
-    v.m = reinterpret_cast<const uint8_t*>(E.m);
-    v.y = E.y;
-    v.N = E.N;
-    v.K = E.K;
-    v.G = E.G;
-    v.tile_begin = E.tile_begin;
-    v.tbytes = tile_bytes(TR, E.K, E.G);
-    v.row_bytes = static_cast<uint32_t>(E.K / 2);
-    v.sblk = 2u * TR * E.G + 16u;
-    v.tab_off_x = S.tab_off;
-    v.cst_off_x = S.cst_off;
-    v.P = min(kMaxP, (E.G + kSliceGroups - 1) / kSliceGroups);
-    v.gps = (E.G + v.P - 1) / v.P;
-    v.ipt = ST * v.P;
-    ent[i] = v;
+    EntryP a;
+    a.q = E.q;
+    a.s = reinterpret_cast<const uint8_t*>(E.s);
+    a.m = reinterpret_cast<const uint8_t*>(E.m);
+    a.N = E.N;
+    a.G = E.G;
+    a.tile_begin = E.tile_begin;
+    a.tbytes = tile_bytes(TR, E.K, E.G);
+    a.row_bytes = static_cast<uint32_t>(E.K / 2);
+    a.sblk = 2u * TR * E.G + 16u;
+    entp[i] = a;
+    EntryC c;
+    c.y = E.y;
+    c.N = E.N;
+    c.tile_begin = E.tile_begin;
+    c.G = E.G;
+    c.rs = E.K / 2;
+    c.sblk = a.sblk;
+    c.tab_off_x = S.tab_off;
+    c.cst_off_x = S.cst_off;
+    c.P = min(kMaxP, (E.G + kSliceGroups - 1) / kSliceGroups);
+    c.gps = (E.G + c.P - 1) / c.P;
+    c.ipt = ST * c.P;
+    const int tile_end = i + 1 < p.count ? p.e[i + 1].tile_begin : p.total_tiles;
+    c.jlo = local_tiles_below(E.tile_begin, cta, C);
+    c.ib = (local_tiles_below(tile_end, cta, C) - c.jlo) * c.ipt;  // this entry's items; prefix-summed below
+    c.mag_ipt = div_magic(c.ipt);
+    c.mag_p = div_magic(c.P);
+    entc[i] = c;
   }
   __syncthreads();
   griddep_launch_dependents();
@@ -338,121 +414,94 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_multi_kernel(const __gr
     return;
   }
 
+  if (warp == 0) {
+    // exclusive prefix sum of the item counts over the entries (and the total into the extra entry)
+    int carry = 0;
+    for (int base = 0; base <= p.count; base += 32) {
+      const int i = base + lane;
+      const int v = i < p.count ? entc[i].ib : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      if (i <= p.count) entc[i].ib = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
   griddep_wait();
   stage_all_x(p, smem, tid);
   named_bar_sync(1, kConsumerWarps * 32);
 
-  const int C = gridDim.x, cta = blockIdx.x;
-  const int ntiles = (p.total_tiles - cta + C - 1) / C;
   const int r = lane >> 2, qd = lane & 3;
   const int prow0 = (r & 1) * H + (r >> 1);  // tile row of this lane's MMA row in step 0 (step t: + 4t)
   const uint32_t zero_a = smem_u32(smem + p.zero_off);
   const float4 zq = lds128f_a(zero_a);
   const g4::DequantK dk = {p.m_lo, p.m_hi, p.k1024, p.k64};
-  const bool xl = lane < 8;   // batch 1: lanes 0-7 carry the activation columns
-  const bool cl = qd == 0;
-  const uint32_t xhalf = xl ? 8u * 16u : 0u;
-  const uint32_t xstep = xl ? 2u * 8u * 16u : 0u;
-  const uint32_t cstep = cl ? 16u : 0u;
   const uint8_t* ring = smem + p.ring_off;
-  float* red = reinterpret_cast<float*>(cnt + kRedSlots * (ST + 1));  // [kRedSlots][ST][kMaxP][8]
+  float* red = reinterpret_cast<float*>(cnt + kRedSlots * ST);  // [kRedSlots][ST][maxp][8] slice partials
+  const int total_items = entc[p.count].ib;
   bool dead = false;
-  // work items of this CTA, in order: tile j, item it = step * P + slice; warp w takes items w, w + 8, ...
-  int e = 0, j = 0, it = warp;
-  auto entry_of = [&](int jj) -> const EntryS& {
-    const int gt = cta + jj * C;
-    while (e + 1 < p.count && gt >= ent[e + 1].tile_begin) ++e;
-    return ent[e];
-  };
-  while (j < ntiles && it >= entry_of(j).ipt) { it -= entry_of(j).ipt; ++j; }
-  while (j < ntiles) {
-    const EntryS& E = entry_of(j);
+  // CTA-local work items in order (tile by tile, item it = step * P + slice within a tile); warp w takes
+  // items w, w + kConsumerWarps, ...; the entry of an item is found by scanning forward (items only grow)
+  int e = -1, next_ib = 0;
+  for (int I = warp; I < total_items; I += kConsumerWarps) {
+    while (I >= next_ib) {
+      ++e;
+      next_ib = entc[e + 1].ib;
+    }
+    const EntryC E = entc[e];  // re-read per item (four 16-byte loads): cheaper than holding it in registers
+    const int local = I - E.ib;
+    const int jj = fdiv(local, E.ipt, E.mag_ipt);
+    const int it = local - jj * E.ipt;
+    const int t = fdiv(it, E.P, E.mag_p);
+    const int sl = it - t * E.P;
+    const int j = E.jlo + jj;
     const int gt = cta + j * C;
-    const int P = E.P, t = it / P, sl = it - t * P;
     const int slot = j % kRedSlots;
     if (!dead && !mbar_wait(&full[j % kWindow], (j / kWindow) & 1, ERR_MULTI_FULL)) dead = true;
-    float acc0[1] = {0.f}, acc1[1] = {0.f};
+    if (dead) continue;
     const int row0 = (gt - E.tile_begin) * TR;
-    if (!dead) {
-      const uint8_t* sq = ring + start[j % kWindow];
-      const int rs = E.K / 2, G = E.G;
-      const int g0 = sl * E.gps, g1 = min(G, g0 + E.gps);
-      const int shift = static_cast<int>((static_cast<int64_t>(row0) * G * 2) & 15) >> 1;
-      Addr16 A;
-      A.w = smem_u32(sq + (r & 1) * (H * rs + 64) + ((r >> 1) + 4 * t) * rs + qd * 16) + g0 * 64;
-      A.s = smem_u32(sq + TR * rs + 64) + (shift + (prow0 + 4 * t) * G + g0) * 2;
-      A.x = (xl ? smem_u32(smem + E.tab_off_x) + lane * 16 : zero_a) + g0 * xstep;
-      A.c = (cl ? smem_u32(smem + E.cst_off_x) : zero_a) + g0 * cstep;
-      A.xon = xl;
-      A.con = cl;
-      const uint32_t m_off = E.sblk;
-      int g = g0;
-      if (((G | g0) & 1) == 0 && TR == 16) {  // scale/min pairs 4-byte aligned: one half2 load per pair
-        for (; g + 1 < g1; g += 2) {
-          Ops16<1> o0, o1;
-          SM2<1> sm2;
-          load_sm2<1>(A.s, 0u, m_off, sm2);
-          load16w<1>(A, 0u, xhalf, o0);
-          A.w += 64; A.x += xstep; A.c += cstep;
-          load16w<1>(A, 0u, xhalf, o1);
-          A.w += 64; A.s += 4; A.x += xstep; A.c += cstep;
-          split_sm2<1>(sm2, o0, o1);
-          math16<1>(o0, zq, dk, acc0);
-          math16<1>(o1, zq, dk, acc1);
-        }
-      }
-      for (; g + 1 < g1; g += 2) {
-        Ops16<1> o0, o1;
-        load16<1>(A, 0u, 0u, m_off, xhalf, o0);
-        A.w += 64; A.s += 2; A.x += xstep; A.c += cstep;
-        load16<1>(A, 0u, 0u, m_off, xhalf, o1);
-        A.w += 64; A.s += 2; A.x += xstep; A.c += cstep;
-        math16<1>(o0, zq, dk, acc0);
-        math16<1>(o1, zq, dk, acc1);
-      }
-      if (g < g1) {
-        Ops16<1> o0;
-        load16<1>(A, 0u, 0u, m_off, xhalf, o0);
-        math16<1>(o0, zq, dk, acc0);
-      }
-      const int row = row0 + prow0 + 4 * t;
-      const float v = acc0[0] + acc1[0];
-      if (P == 1) {
-        if (qd == 0 && row < E.N) store_out(E.y, row, v, p.y_bf16);
-      } else {
-        // K-sliced: the last slice of this step to finish adds the P partials in slice order
-        float* rp = red + ((slot * ST + t) * kMaxP) * 8;
-        if (qd == 0) rp[sl * 8 + r] = v;
-        __syncwarp();
-        int old = 0;
-        if (lane == 0) {
-          __threadfence_block();
-          old = atomicAdd(&cnt[slot * (ST + 1) + t], 1);
-        }
-        old = __shfl_sync(0xffffffffu, old, 0);
-        if (old == P - 1) {
-          __threadfence_block();
-          if (qd == 0) {
-            float sum = 0.f;
-            for (int k = 0; k < P; ++k) sum += rp[k * 8 + r];
-            if (row < E.N) store_out(E.y, row, sum, p.y_bf16);
-          }
-          if (lane == 0) cnt[slot * (ST + 1) + t] = 0;
-        }
-      }
-      // the last item of the tile releases its ring space (and its reduction slot)
+    const uint8_t* sq = ring + start[j % kWindow];
+    const int rs = E.rs, G = E.G;
+    const int g0 = sl * E.gps, g1 = min(G, g0 + E.gps);
+    ItemAddr A;
+    A.w = smem_u32(sq + (r & 1) * (H * rs + 64) + ((r >> 1) + 4 * t) * rs + qd * 16) + g0 * 64;
+    A.s = smem_u32(sq + TR * rs + 64) + ((prow0 + 4 * t) * G + g0) * 2;
+    A.x = smem_u32(smem + E.tab_off_x) + (lane & 7) * 16 + g0 * 256;
+    A.c = smem_u32(smem + E.cst_off_x) + g0 * 16;
+    const float v = item_dot(A, E.sblk, G, g0, g1, dk, zq);
+    const int row = row0 + prow0 + 4 * t;
+    float out = v;
+    bool store = E.P == 1;
+    if (E.P > 1) {
+      // K-sliced: the last slice of this step to finish adds the P partials in slice order (deterministic)
+      float* rp = red + ((slot * ST + t) * p.maxp) * 8;
+      if (qd == 0) rp[sl * 8 + r] = v;
       __syncwarp();
+      int prior = 0;
       if (lane == 0) {
         __threadfence_block();
-        const int done_items = atomicAdd(&cnt[slot * (ST + 1) + ST], 1);
-        if (done_items == E.ipt - 1) {
-          cnt[slot * (ST + 1) + ST] = 0;
-          mbar_arrive(&empty[j % kWindow]);
+        prior = atomicAdd(&cnt[slot * ST + t], 1);
+      }
+      prior = __shfl_sync(0xffffffffu, prior, 0);
+      if (prior == E.P - 1) {
+        __threadfence_block();
+        if (qd == 0) {
+          out = 0.f;
+          for (int k = 0; k < E.P; ++k) out += rp[k * 8 + r];
         }
+        if (lane == 0) cnt[slot * ST + t] = 0;
+        store = true;
       }
     }
-    it += kConsumerWarps;
-    while (j < ntiles && it >= entry_of(j).ipt) { it -= entry_of(j).ipt; ++j; }
+    __syncwarp();
+    // every item releases its share of the tile's ring space (the tile's reduction slot is reused only after
+    // the whole tile is reclaimed). The arrive has release semantics: it waits until this thread's earlier
+    // memory operations are performed, so the global store of y comes after it.
+    if (lane == 0) mbar_arrive_cnt(&empty[j % kWindow], it == E.ipt - 1 ? kRelease - (E.ipt - 1) : 1);
+    if (store && qd == 0 && row < E.N) store_out(E.y, row, out, p.y_bf16);
   }
 }
 
@@ -482,8 +531,9 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
     p.k64 = 0x54005400u;
     // distinct activation vectors -> slots; stop adding entries when the next one would not fit
     // (activation tables + two of the largest tiles must fit in shared memory)
-    constexpr uint32_t kFixed = 64 + 16 + kMaxEntries * sizeof(EntryS) + kWindow * 4 + 16 +
-                                kRedSlots * 3 * 4 + kRedSlots * 2 * kMaxP * 8 * 4 + 2 * kWindow * 8 + 128;
+    constexpr uint32_t kFixed = 64 + 16 + kMaxEntries * (sizeof(EntryP) + sizeof(EntryC)) + sizeof(EntryC) +
+                                kWindow * 4 + 16 + kRedSlots * 2 * 4 + kRedSlots * 2 * kMaxP * 8 * 4 +
+                                2 * kWindow * 8 + 128;
     int nslots = 0, tiles = 0;
     uint32_t x_bytes = 0, max_tile = 0;
     int take = 0;
@@ -521,6 +571,9 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
     p.count = take;
     p.nslots = nslots;
     p.total_tiles = tiles;
+    p.maxp = 1;
+    for (int i = 0; i < take; ++i)
+      p.maxp = std::max(p.maxp, std::min(kMaxP, (p.e[i].G + kSliceGroups - 1) / kSliceGroups));
     // layout: [x tables + constants][zero][start offsets][barriers][ring]
     uint32_t off = 0;
     for (int i = 0; i < nslots; ++i) {
@@ -533,12 +586,12 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
     off += 64;
     off = (off + 15) & ~15u;
     p.ent_off = off;
-    off += static_cast<uint32_t>(take) * sizeof(EntryS);
+    off += static_cast<uint32_t>(take) * sizeof(EntryP) + static_cast<uint32_t>(take + 1) * sizeof(EntryC);
     p.start_off = off;
     off += kWindow * 4;
     off = (off + 15) & ~15u;
     p.red_off = off;
-    off += kRedSlots * 3 * 4 + kRedSlots * 2 * kMaxP * 8 * 4;
+    off += kRedSlots * 2 * 4 + (p.maxp > 1 ? kRedSlots * 2 * p.maxp * 8 * 4 : 0);
     off = (off + 7) & ~7u;
     p.bar_off = off;
     off += 2 * kWindow * 8;
