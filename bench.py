@@ -50,6 +50,9 @@ def parse():
                     help="length of the bounded CPU-baseline sample (0: skip it)")
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers in the step (36 = config 1; fewer only for small profiling cases)")
+    ap.add_argument("--parallel", default="replica", choices=["replica", "tp"],
+                    help="replica: one independent decode stream per GPU (weak scaling); tp: one stream, every "
+                         "projection sharded over the GPUs with one NCCL all-reduce per layer (strong scaling)")
     return ap.parse_args()
 
 
@@ -250,6 +253,81 @@ def run_reference(a):
     return 0
 
 
+def run_tp(a, rank, world, dev):
+    """Tensor-parallel decode step (config 4): every rank holds 1/world of each projection (column-parallel
+    QKV/gate_up, row-parallel o/down, row-split int8 head); per layer one multi-GEMV launch of the rank's
+    shards and one NCCL all-reduce of the 6 KB hidden vector, then the head and an all-gather of the logits."""
+    import rumik_fast_b200 as rb
+    from rumik_fast_b200 import synthetic as syn
+    from rumik_fast_b200.tensor_parallel import TPDecodeStep
+    gen = syn.generator(1234, dev)                    # the same full model on every rank; each keeps its shards
+    layers = []
+    for _ in range(a.layers):
+        full = [syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES]
+        layers.append((full[0], full[1], full[2], full[3]))
+    head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
+    x_h = syn.activations((3072,), gen, dev)
+    x_attn = syn.activations((3072,), gen, dev)
+    x_act = syn.activations((8192,), gen, dev)
+    step = TPDecodeStep(layers, x_attn, x_act, head, rank, world)
+    del layers, head
+    torch.cuda.empty_cache()
+    step.h[0].copy_(x_h)
+    g = capture(step)
+    full_bytes = a.layers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES) + syn.int8_bytes(*syn.HEAD_SHAPE)
+    gpu_index = local_gpu_index(dev.index)
+    with ClockSampler(gpu_index) as clk:
+        m0 = clk.mark()
+        ms = timed(g.replay, a.steps, a.warmup, world)
+        m1 = clk.mark()
+    clocks = clk.summary(m0, m1)
+    ms_step = ms / a.steps
+    hx = x_h.cpu().pin_memory()
+    hl = torch.empty(step.logits_all.numel(), dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        step.h[0].copy_(hx, non_blocking=True)
+        g.replay()
+        hl.copy_(step.logits_all, non_blocking=True)
+    e2e_steps = max(1, a.steps // 2)
+    ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
+    peak, peak_kind = peaks()
+    rank_gbs = step.bytes / (ms_step * 1e-3) / 1e9
+    if rank == 0:
+        gbs = full_bytes / (ms_step * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(gbs, 1), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "config-4 tensor-parallel decode step: config-1 36-layer projection set + "
+                                   "int8 head sharded over the GPUs (column-parallel QKV/gate_up, row-parallel "
+                                   "o/down), one NCCL all-reduce of the hidden vector per layer, batch 1",
+                       "batch": 1, "bytes_per_step": full_bytes, "parallelism": f"tp{world}",
+                       "launches": "per layer: one multi-GEMV launch + add + all-reduce; head + all-gather",
+                       "l2": "no flush: 1.98 GB of weights per step over all ranks > 126 MB L2 per GPU"},
+            "tok_s": round(1e3 / ms_step, 1),
+            "e2e": {"value": round(full_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": UNIT,
+                    "h2d_bytes_per_step": 3072 * 2, "d2h_bytes_per_step": hl.numel() * 2,
+                    "ms_per_step": round(ms_e2e, 5)},
+            "roofline": {"bound": "hbm", "achieved": round(rank_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(rank_gbs / peak, 4), "peak_kind": peak_kind,
+                         "kernel": "whole tensor-parallel step per rank (GEMVs + all-reduces)", "traffic": None,
+                         "algorithmic_bytes_per_launch": None},
+            "cpu_baseline": None, "clocks": clocks,
+            "gpu_launches": a.steps * (a.layers + 1), "mode": "tp",
+        }
+        print(json.dumps(line), flush=True)
+    del g
+    return 0
+
+
+def local_gpu_index(local):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    if vis.replace(",", "").isdigit():
+        return int(vis.split(",")[local])
+    return local
+
+
 def run_ours(a):
     import rumik_fast_b200 as rb
     rank, world, local = dist_env()
@@ -260,13 +338,19 @@ def run_ours(a):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     rb.set_weight_prefetch(not a.no_prefetch)
+    if a.parallel == "tp":
+        rc = run_tp(a, rank, world, dev)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return rc
     w = build_workload(dev, seed=1234 + rank, nlayers=a.layers)
     step = step_fn(w, a.mode)
     g_step = capture(step)
     g_int4 = capture(step_fn(w, a.mode, with_head=False))
     step_bytes = w["int4_bytes"] + w["head_bytes"]
-    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
-        if os.environ.get("CUDA_VISIBLE_DEVICES", "").replace(",", "").isdigit() else local
+    gpu_index = local_gpu_index(local)
 
     with ClockSampler(gpu_index) as clk:
         m0 = clk.mark()
