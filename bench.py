@@ -32,9 +32,9 @@ sys.path.insert(0, ROOT)
 LAYERS = 36
 METRIC = "decode-step GEMV HBM GB/s"
 UNIT = "GB/s"
-# DRAM bytes (read + write) per launch of gemv_int4_multi_kernel on the 36-layer set: ncu capture of the 3-layer
-# case (160.49 MB read + 3.79 MB written) scaled x12 by tiles streamed
-NCU_TRAFFIC_PER_LAUNCH = 1971320832
+# DRAM bytes (read + write) per launch of gemv_int4_tc_kernel on the 36-layer set: ncu capture of the 3-layer
+# case (160.53 MB read + 4.80 MB written) scaled x12 by blocks streamed
+NCU_TRAFFIC_PER_LAUNCH = 1983999984
 
 
 def parse():
@@ -403,7 +403,7 @@ def run_ours(a):
                     "ms_per_step": round(ms_e2e, 5)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "kernel": "gemv_int4_multi_kernel" if a.mode == "set" else "gemv_int4_kernel",
+                         "kernel": "gemv_int4_tc_kernel" if a.mode == "set" else "gemv_int4_kernel",
                          "traffic": NCU_TRAFFIC_PER_LAUNCH if a.mode == "set" and a.layers == LAYERS else None,
                          "algorithmic_bytes_per_launch": w["int4_bytes"] // launches4},
             "cpu_baseline": cpu,

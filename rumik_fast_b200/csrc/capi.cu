@@ -109,7 +109,11 @@ int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_
   }
   int sms = 0, st = device_sms(&sms);
   if (st != RB_OK) return st;
+#ifdef RB_MULTI_LEGACY  // the warp-MMA multi-GEMV (gemv_int4_multi.cu), kept for comparison builds
   st = rb::launch_gemv_int4_multi(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream));
+#else
+  st = rb::launch_gemv_int4_tc(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream));
+#endif
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
 }

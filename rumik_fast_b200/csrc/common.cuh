@@ -25,6 +25,7 @@ enum : unsigned int {
   ERR_MM4_WAIT = 1u << 4,     // prefill matmul timed out on an mbarrier
   ERR_MULTI_FULL = 1u << 5,   // multi-GEMV consumer timed out waiting for a tile
   ERR_MULTI_EMPTY = 1u << 6,  // multi-GEMV producer timed out waiting for ring space
+  ERR_TC_WAIT = 1u << 7,      // tensor-core multi-GEMV timed out on an mbarrier
 };
 
 // Upper bound on the wall time of one mbarrier wait. Healthy waits here last microseconds (at most the

@@ -1,0 +1,530 @@
+// gemv_int4_tc.cu - a list of independent int4 group-128 GEMVs (batch 1) in one persistent launch on the
+// tcgen05 tensor cores of B200 (sm_100a), with the dequantised weights in tensor memory.
+//
+// y_i = W_i x_i for every entry, the operation of rumik-fast's gemv_int4_kernel (kernels/cuda_gemv.py:38-115)
+// applied to a decode step's projection set (kernels/bench_gemv.py:83-113).
+//
+// Work is cut into blocks of 128 weight rows (one UMMA M, one tensor-memory lane per row); the blocks of all
+// matrices are dealt round-robin to the CTAs, one CTA per SM. Per CTA:
+//  * warp 0 (producer) streams each block's int4 codes two groups (128 columns x 2) at a time with 2-D TMA
+//    (box 128 bytes x 128 rows, 128-byte swizzle, 16 KB) into a ring per converter set;
+//  * each converter set (four warps, one per tensor-memory lane quadrant, thread = weight row) unpacks one
+//    group of its row to unsigned 8-bit codes (three instructions per eight codes: no dequantisation at all,
+//    the codes 0..15 are the integer A operand) and writes the 32 columns to tensor memory (tcgen05.st);
+//  * one thread per set issues four tcgen05.mma.kind::i8 per group (K = 32 each): A = the codes in tensor
+//    memory (128 rows), B = the group's activations quantised to 16-bit integers and split into a signed
+//    high byte (B row 0) and a signed low byte (B row 1), read from shared memory by a K-major, no-swizzle
+//    descriptor; D = 128 x 8 int32 in tensor memory (columns 0 and 1 used), exact;
+//  * four groups later the converter reads its row's two accumulator columns (tcgen05.ld) and adds
+//    s * delta * (256 * D0 + D1) in fp32; m * sum(x) is added when the group is unpacked.
+// The activations are quantised per 128-column group with delta = max|x| / 32639 (relative error below
+// 2e-5 of the group's largest activation); the weights are used exactly. All mbarrier waits are bounded;
+// no multicast, no clusters.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rb {
+
+namespace g4t {
+
+#ifndef RB_TC_SETS
+#define RB_TC_SETS 3
+#endif
+constexpr int kSets = RB_TC_SETS;          // converter sets (four warps each); sets take alternate blocks
+constexpr int kRows = 128;                 // rows per block = UMMA M = tensor-memory lanes
+constexpr int kConvWarps = 4 * kSets;
+constexpr int kFirstConv = 1 + kSets;      // warp 0 producer, warps 1..kSets the MMA issuers of the sets
+constexpr int kThreads = (kFirstConv + kConvWarps) * 32;
+constexpr uint32_t kStageBytes = kRows * 128;  // two groups of codes for 128 rows
+constexpr int kMaxStages = 6;              // ring stages per set
+constexpr int kMaxEntries = 160;
+constexpr int kMaxSlots = 8;
+constexpr int kNB = 4;                      // tensor-memory A/D buffers per set (the epilogue's lag in groups)
+constexpr uint32_t kACols = 32, kDCols = 8, kSetCols = kNB * (kACols + kDCols);
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kXPad = 256;            // bytes the B descriptor's unused rows read past a table
+constexpr uint32_t kXGroupBytes = 256;     // per group: 8 chunks of (16 high bytes, 16 low bytes)
+
+struct Entry {
+  const uint16_t* s;
+  const uint16_t* m;
+  void* y;
+  int N, G, slot, block_begin;
+};
+
+struct Slot {
+  const void* x;
+  int K, G;
+  uint32_t tab_off, cst_off;
+};
+
+struct __align__(64) TcParams {
+  CUtensorMap maps[kMaxEntries];  // codes of each entry: [N rows, K/2 bytes], box 128 x 128, 128B swizzle
+  Entry e[kMaxEntries];
+  Slot slots[kMaxSlots];
+  int count, nslots, total_blocks, x_bf16, y_bf16, prefetch, nst;
+  uint32_t xs_off, bar_off, idesc;
+  uint32_t m_lo, m_hi, k1024, k64;
+};
+
+// B operand descriptor over an activation table: K-major, no swizzle, 16-byte rows at a 16-byte pitch (row 0
+// = 16 high bytes, row 1 = the 16 matching low bytes), the next 16 K-elements of a row 32 bytes further on
+// (leading byte offset 32), 8-row groups 128 bytes apart (unused with N = 8), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t x_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(32 >> 4) << 16) |
+         (static_cast<uint64_t>(128 >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::i8 (A unsigned, B signed, D int32), one CTA.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]) : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Accumulator columns 0 and 1 of this thread's lane; the registers are valid only after tmem_wait_ld, which
+// takes them as operands so that no use can be scheduled before it.
+__device__ __forceinline__ void tmem_ld2(uint32_t taddr, int& h, int& l) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(h), "=r"(l) : "r"(taddr) : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld(int& h, int& l) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(h), "+r"(l) : : "memory");
+}
+__device__ __forceinline__ float half_at(const uint4& v, int i) {  // i: compile-time 0..7
+  const uint32_t w = i < 2 ? v.x : i < 4 ? v.y : i < 6 ? v.z : v.w;
+  return __half2float(__ushort_as_half(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xFFFFu))));
+}
+
+// Activation tables: for every slot and 128-column group, x quantised to 16-bit integers
+// xi = rint(x / delta), delta = max|x| / 32639, split as xi = 256 * hi + lo with hi, lo signed bytes, in the
+// order in which a converter thread writes a group's codes to tensor memory (within each 8 columns: the four
+// even columns, then the four odd ones), stored per 16 positions as 16 high bytes then 16 low bytes; plus per
+// group {delta, sum(x)}.
+__device__ void stage_x_tables(const TcParams& p, uint8_t* xs, int ct, int nthreads) {
+  for (int sl = 0; sl < p.nslots; ++sl) {
+    const Slot& S = p.slots[sl];
+    uint8_t* tab = xs + S.tab_off;
+    float2* cst = reinterpret_cast<float2*>(xs + S.cst_off);
+    const int chunks = S.K / 8;  // 16 per group
+    for (int base = 0; base < chunks; base += nthreads) {
+      const int c = base + ct;
+      const bool valid = c < chunks;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (valid) {
+        __half h[8];
+        load8_as_half(static_cast<const uint8_t*>(S.x) + static_cast<int64_t>(c) * 16, p.x_bf16, h);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __half2float(h[i]);
+      }
+      float mx = 0.f, sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        mx = fmaxf(mx, fabsf(v[i]));
+        sum += v[i];
+      }
+      // a group is 16 chunks = 16 consecutive threads (nthreads is a multiple of 32)
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      }
+      const float delta = mx > 0.f ? mx / 32639.f : 1.f;
+      const float inv = 1.f / delta;
+      if (valid) {
+        uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
+#pragma unroll
+        for (int jp = 0; jp < 8; ++jp) {  // table position jp <- column (jp < 4 ? 2 jp : 2 (jp - 4) + 1)
+          const int col = jp < 4 ? 2 * jp : 2 * (jp - 4) + 1;
+          const int xi = __float2int_rn(fminf(fmaxf(v[col] * inv, -32639.f), 32639.f));
+          const int l = ((xi + 128) & 255) - 128;
+          const int h = (xi - l) >> 8;
+          hi[jp >> 2] |= (static_cast<uint32_t>(h) & 255u) << (8 * (jp & 3));
+          lo[jp >> 2] |= (static_cast<uint32_t>(l) & 255u) << (8 * (jp & 3));
+        }
+        // positions 8 * (c % 16) .. + 7 of the group: 16-position chunk (c % 16) / 2, half (c & 1)
+        uint8_t* dst = tab + (c >> 4) * kXGroupBytes + ((c & 15) >> 1) * 32 + (c & 1) * 8;
+        *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], hi[1]);
+        *reinterpret_cast<uint2*>(dst + 16) = make_uint2(lo[0], lo[1]);
+      }
+      if (valid && (c & 15) == 0) cst[c >> 4] = make_float2(delta, sum);
+    }
+    for (int i = ct; i < static_cast<int>(kXPad / 16); i += nthreads)
+      reinterpret_cast<uint4*>(tab + S.G * kXGroupBytes)[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+__device__ __forceinline__ const Entry& entry_of(const TcParams& p, int gb, int& e) {
+  while (e + 1 < p.count && gb >= p.e[e + 1].block_begin) ++e;
+  return p.e[e];
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_constant__ TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int C = gridDim.x, cta = blockIdx.x;
+  const int nst = p.nst;
+  const int nlocal = (p.total_blocks - cta + C - 1) / C;  // this CTA's blocks: cta + j * C
+  uint8_t* xs = smem + p.xs_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+  // per set: full[nst], empty[nst], afull[kNB], mdone[kNB]
+  const int per_set = 2 * nst + 2 * kNB;
+  auto full = [&](int s, int i) { return bars + s * per_set + i; };
+  auto empty = [&](int s, int i) { return bars + s * per_set + nst + i; };
+  auto afull = [&](int s, int b) { return bars + s * per_set + 2 * nst + b; };
+  auto mdone = [&](int s, int b) { return bars + s * per_set + 2 * nst + kNB + b; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kSets * per_set);
+
+  if (tid == 0) {
+    for (int s = 0; s < kSets; ++s) {
+      for (int i = 0; i < nst; ++i) {
+        mbar_init(full(s, i), 1);
+        mbar_init(empty(s, i), 4);
+      }
+      for (int b = 0; b < kNB; ++b) {
+        mbar_init(afull(s, b), 4);
+        mbar_init(mdone(s, b), 1);
+      }
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  mm4::tc_fence_before();
+  __syncthreads();
+  mm4::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      if (!p.prefetch) griddep_wait();
+      int j[kSets], k[kSets], nk[kSets], e[kSets], row0[kSets], issued[kSets];
+      bool live[kSets];
+      for (int s = 0; s < kSets; ++s) {
+        e[s] = 0;
+        j[s] = s;
+        k[s] = 0;
+        issued[s] = 0;
+        live[s] = j[s] < nlocal;
+        if (live[s]) {
+          const int gb = cta + j[s] * C;
+          const Entry& E = entry_of(p, gb, e[s]);
+          nk[s] = (E.G + 1) / 2;
+          row0[s] = (gb - E.block_begin) * kRows;
+        }
+      }
+      bool ok = true;
+      bool any = true;
+      while (any && ok) {
+        any = false;
+        for (int s = 0; s < kSets && ok; ++s) {
+          if (!live[s]) continue;
+          any = true;
+          const int slot = issued[s] % nst;
+          if (issued[s] >= nst && !mbar_wait(empty(s, slot), ((issued[s] / nst) - 1) & 1, ERR_TC_WAIT)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full(s, slot), kStageBytes);
+          mm4::tma_load_2d(smem + (static_cast<size_t>(s) * nst + slot) * kStageBytes, &p.maps[e[s]], k[s] * 128,
+                           row0[s], full(s, slot));
+          ++issued[s];
+          if (++k[s] == nk[s]) {
+            k[s] = 0;
+            j[s] += kSets;
+            live[s] = j[s] < nlocal;
+            if (live[s]) {
+              const int gb = cta + j[s] * C;
+              const Entry& E = entry_of(p, gb, e[s]);
+              nk[s] = (E.G + 1) / 2;
+              row0[s] = (gb - E.block_begin) * kRows;
+            }
+          }
+        }
+      }
+      // no retirement with copies in flight
+      for (int s = 0; s < kSets; ++s)
+        for (int t = max(0, issued[s] - nst); t < issued[s]; ++t)
+          if (!mbar_wait(full(s, t % nst), (t / nst) & 1, ERR_TC_WAIT)) break;
+    }
+  } else if (warp < kFirstConv) {
+    // ---------------- MMA issuer of set s ----------------
+    const int s = warp - 1;
+    named_bar_sync(1, (kSets + kConvWarps) * 32);  // activation tables staged
+    if (lane == 0) {
+      mm4::tc_fence_after();
+      int e = 0, q = 0;
+      bool ok = true;
+      for (int jj = s; jj < nlocal && ok; jj += kSets) {
+        const int gb = cta + jj * C;
+        const Entry& E = entry_of(p, gb, e);
+        const uint32_t xtab = smem_u32(xs + p.slots[E.slot].tab_off);
+        for (int g = 0; g < E.G; ++g, ++q) {
+          const int b = q % kNB;
+          if (!mbar_wait(afull(s, b), (q / kNB) & 1, ERR_TC_WAIT)) {
+            ok = false;
+            break;
+          }
+          mm4::tc_fence_after();
+          const uint32_t acol = s * kSetCols + b * kACols, dcol = s * kSetCols + kNB * kACols + b * kDCols;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            umma_ts(tmem + dcol, tmem + acol + 8 * i, x_desc(xtab + g * kXGroupBytes + 64 * i), p.idesc, i > 0);
+          mm4::umma_commit(mdone(s, b));
+        }
+      }
+    }
+  } else {
+    // ---------------- converters + epilogue of set s ----------------
+    const int cw = warp - kFirstConv;        // 0 .. kConvWarps-1
+    const int s = cw >> 2;
+    const int quad = warp & 3;               // tensor-memory lane quadrant this warp may access
+    const int rib = quad * 32 + lane;        // row in block = tensor-memory lane
+    griddep_wait();                          // x may come from the previous kernel; y is written below
+    stage_x_tables(p, xs, tid - kFirstConv * 32, kConvWarps * 32);
+    fence_proxy_async_smem();                // generic writes of the tables -> visible to the tensor core
+    named_bar_sync(1, (kSets + kConvWarps) * 32);
+    const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const g4::DequantK dk = {p.m_lo, p.m_hi, p.k1024, p.k64};
+    int e = 0, q = 0, st = 0;
+    bool ok = true;
+    for (int jj = s; jj < nlocal; jj += kSets) {
+      const int gb = cta + jj * C;
+      const Entry& E = entry_of(p, gb, e);
+      const int G = E.G;
+      const int row = (gb - E.block_begin) * kRows + rib;
+      const bool row_ok = row < E.N;
+      const uint16_t* srow = E.s + static_cast<int64_t>(row_ok ? row : 0) * G;
+      const uint16_t* mrow = E.m + static_cast<int64_t>(row_ok ? row : 0) * G;
+      const float2* cst = reinterpret_cast<const float2*>(xs + p.slots[E.slot].cst_off);
+      float acc = 0.f;
+      float pend[kNB] = {0.f, 0.f, 0.f, 0.f};  // s * delta of the groups whose results are pending, oldest first
+      const int q0 = q;
+      const uint32_t a_set = tq + s * kSetCols, d_set = tq + s * kSetCols + kNB * kACols;
+      // codes of the next group to convert (software-pipelined one group ahead)
+      uint4 wn[4];
+      uint8_t* stage = nullptr;
+      auto load_codes = [&](int g) {
+        if ((g & 1) == 0) {
+          const int slot = st % nst;
+          if (ok) ok = mbar_wait(full(s, slot), (st / nst) & 1, ERR_TC_WAIT);
+          stage = smem + (static_cast<size_t>(s) * nst + slot) * kStageBytes;
+        }
+        if (ok) {
+          const uint8_t* rowp = stage + rib * 128;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) wn[c] = lds128(rowp + ((((g & 1) * 4 + c) ^ (rib & 7)) << 4));
+        }
+      };
+      // one group: unpack its codes into tensor memory and retire the group kNB back
+      auto step = [&](int g, float sv, float mv) {
+        const uint4 w[4] = {wn[0], wn[1], wn[2], wn[3]};
+        if ((g & 1) == 1 || g == G - 1) {  // both groups of this stage are in registers: release it
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty(s, st % nst));
+          ++st;
+        }
+        uint32_t o[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t wv[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            o[c * 8 + t * 2 + 0] = wv[t] & 0x0F0F0F0Fu;         // even columns of these 8
+            o[c * 8 + t * 2 + 1] = (wv[t] >> 4) & 0x0F0F0F0Fu;  // odd columns
+          }
+        }
+        const float2 c2 = cst[g];
+        acc = fmaf(mv, c2.y, acc);
+        const int qq = q0 + g, b = qq % kNB;
+        const bool epi = g >= kNB;
+        int dh = 0, dl = 0;
+        ok = __all_sync(0xffffffffu, ok);  // tcgen05 loads / stores are warp-collective
+        if (epi && ok) {  // the group kNB back used this buffer: fetch its result once its MMAs are done
+          ok = __all_sync(0xffffffffu, mbar_wait(mdone(s, b), ((qq / kNB) - 1) & 1, ERR_TC_WAIT));
+          if (ok) {
+            mm4::tc_fence_after();
+            tmem_ld2(d_set + b * kDCols, dh, dl);
+          }
+        }
+        if (ok) tmem_st32(a_set + b * kACols, o);
+        if (g + 1 < G) load_codes(g + 1);  // overlaps the tensor-memory load and store above
+        ok = __all_sync(0xffffffffu, ok);
+        if (epi && ok) {
+          tmem_wait_ld(dh, dl);
+          acc = fmaf(pend[0], static_cast<float>(dh * 256 + dl), acc);
+        }
+        if (epi) {
+#pragma unroll
+          for (int i = 0; i + 1 < kNB; ++i) pend[i] = pend[i + 1];
+          pend[kNB - 1] = sv * c2.x;
+        } else {
+#pragma unroll
+          for (int i = 0; i < kNB; ++i)
+            if (i == g) pend[i] = sv * c2.x;
+        }
+        if (ok) {
+          tmem_wait_st();
+          mm4::tc_fence_before();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(afull(s, b));
+      };
+      load_codes(0);
+      if ((G & 7) == 0) {
+        // scales and mins of 8 groups per 16-byte load, fetched one 8-group chunk ahead
+        uint4 s8n = __ldg(reinterpret_cast<const uint4*>(srow)), m8n = __ldg(reinterpret_cast<const uint4*>(mrow));
+        for (int g8 = 0; g8 < G; g8 += 8) {
+          const uint4 s8 = s8n, m8 = m8n;
+          if (g8 + 8 < G) {
+            s8n = __ldg(reinterpret_cast<const uint4*>(srow + g8 + 8));
+            m8n = __ldg(reinterpret_cast<const uint4*>(mrow + g8 + 8));
+          }
+#pragma unroll
+          for (int h = 0; h < 8; ++h) step(g8 + h, half_at(s8, h), half_at(m8, h));
+        }
+      } else {
+        for (int g = 0; g < G; ++g)
+          step(g, __half2float(__ushort_as_half(__ldg(srow + g))), __half2float(__ushort_as_half(__ldg(mrow + g))));
+      }
+      q += G;
+      // drain this block's last (up to) kNB groups, oldest first
+      const int nd = min(G, kNB);
+#pragma unroll
+      for (int i = 0; i < kNB; ++i) {
+        if (i < nd) {
+          const int qq = q - nd + i;
+          const int b = qq % kNB;
+          if (ok) ok = mbar_wait(mdone(s, b), (qq / kNB) & 1, ERR_TC_WAIT);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) {
+            mm4::tc_fence_after();
+            int dh, dl;
+            tmem_ld2(d_set + b * kDCols, dh, dl);
+            tmem_wait_ld(dh, dl);
+            acc = fmaf(pend[i], static_cast<float>(dh * 256 + dl), acc);
+          }
+        }
+      }
+      if (ok && row_ok) store_out(E.y, row, acc, p.y_bf16);
+    }
+  }
+  mm4::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    mm4::tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+}  // namespace g4t
+
+int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,
+                        cudaStream_t stream) {
+  using namespace g4t;
+  constexpr uint32_t kSmemMax = 227 * 1024;
+  auto encode = mm4::encode_fn();
+  if (!encode) return RB_ERR_DEVICE;
+  TcParams p;  // ~27 KB, built on the host and passed by value in the launch
+  int done = 0;
+  while (done < count) {
+    const int n = std::min(count - done, kMaxEntries);
+    p.x_bf16 = x_dtype == RB_BF16;
+    p.y_bf16 = y_dtype == RB_BF16;
+    p.prefetch = (flags & RB_FLAG_PDL) && (flags & RB_FLAG_PREFETCH_WEIGHTS) ? 1 : 0;
+    p.m_lo = 0x000F000Fu;
+    p.m_hi = 0x00F000F0u;
+    p.k1024 = 0x64006400u;
+    p.k64 = 0x54005400u;
+    // instruction descriptor: D int32, A unsigned 8-bit, B signed 8-bit, both K-major, N = 8, M = 128
+    p.idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((8u >> 3) << 17) | ((static_cast<uint32_t>(kRows) >> 4) << 24);
+    const uint32_t kBars = kSets * (2 * kMaxStages + 2 * kNB) * 8 + 16;
+    int nslots = 0, blocks = 0, take = 0;
+    uint32_t x_bytes = 0;
+    for (; take < n; ++take) {
+      const rb_gemv_desc& D = d[done + take];
+      const uint32_t G = static_cast<uint32_t>(D.K / 128);
+      int slot = -1;
+      for (int i = 0; i < nslots; ++i)
+        if (p.slots[i].x == D.x && p.slots[i].K == static_cast<int>(D.K)) slot = i;
+      const uint32_t add_x = slot < 0 ? (G * kXGroupBytes + kXPad + ((G * 8 + 15) & ~15u)) : 0u;
+      if (slot < 0 && nslots == kMaxSlots) break;
+      if (1024 + kSets * 2 * kStageBytes + x_bytes + add_x + kBars > kSmemMax) break;
+      if (slot < 0) {
+        slot = nslots++;
+        p.slots[slot].x = D.x;
+        p.slots[slot].K = static_cast<int>(D.K);
+        p.slots[slot].G = static_cast<int>(G);
+        x_bytes += add_x;
+      }
+      Entry& E = p.e[take];
+      E.s = D.s;
+      E.m = D.m;
+      E.y = D.y;
+      E.N = static_cast<int>(D.N);
+      E.G = static_cast<int>(G);
+      E.slot = slot;
+      E.block_begin = blocks;
+      blocks += static_cast<int>((D.N + kRows - 1) / kRows);
+      const cuuint64_t dims[2] = {static_cast<cuuint64_t>(D.K / 2), static_cast<cuuint64_t>(D.N)};
+      const cuuint64_t strides[1] = {static_cast<cuuint64_t>(D.K / 2)};
+      const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(kRows)};
+      const cuuint32_t es[2] = {1, 1};
+      if (encode(&p.maps[take], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(D.q), dims, strides, box, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return RB_ERR_SHAPE;
+    }
+    if (take == 0) return RB_ERR_SHAPE;
+    p.count = take;
+    p.nslots = nslots;
+    p.total_blocks = blocks;
+    // layout (from a 1024-aligned base): [stages: kSets x nst x 16 KB][activation tables][barriers][tmem slot]
+    uint32_t off = 0;
+    for (int i = 0; i < nslots; ++i) {
+      p.slots[i].tab_off = off;
+      off += static_cast<uint32_t>(p.slots[i].G) * kXGroupBytes + kXPad;
+      p.slots[i].cst_off = off;
+      off += (static_cast<uint32_t>(p.slots[i].G) * 8 + 15) & ~15u;
+    }
+    const uint32_t xtot = off;
+    int nst = static_cast<int>((kSmemMax - 1024 - xtot - kBars) / (kSets * kStageBytes));
+    nst = std::min(nst, kMaxStages);
+    if (nst < 2) return RB_ERR_SHAPE;
+    p.nst = nst;
+    p.xs_off = static_cast<uint32_t>(kSets * nst) * kStageBytes;
+    p.bar_off = (p.xs_off + xtot + 15) & ~15u;
+    const uint32_t smem = 1024 + p.bar_off + kSets * (2 * nst + 2 * kNB) * 8 + 16;
+    cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gemv_int4_tc_kernel), static_cast<int>(kSmemMax));
+    if (e != cudaSuccess) return RB_ERR_LAUNCH;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::min(num_sms, std::max(1, blocks)));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = (flags & RB_FLAG_PDL) ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, gemv_int4_tc_kernel, p);
+    if (e != cudaSuccess) return RB_ERR_LAUNCH;
+    done += take;
+  }
+  return RB_OK;
+}
+
+}  // namespace rb
