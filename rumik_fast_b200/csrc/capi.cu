@@ -91,7 +91,13 @@ int rb_gemv_int8(const void* x, int x_dtype, int64_t ldx, const uint8_t* q, int 
   a.q = q; a.q_signed = q_signed; a.s_row = s; a.s_dtype = s_dtype;
   a.y = y; a.y_dtype = y_dtype; a.ldy = batch > 1 ? ldy : N;
   a.N = N; a.K = K; a.batch = batch; a.flags = flags;
+#ifdef RB_INT8_LEGACY  // the warp-MMA kernel for every call (comparison builds)
   st = rb::launch_gemv_int8(a, sms, static_cast<cudaStream_t>(stream));
+#else
+  // batch 1 with K % 128 == 0 runs on the tensor cores; other shapes on the warp-MMA kernel
+  st = rb::launch_gemv_int8_tc(a, sms, static_cast<cudaStream_t>(stream));
+  if (st == RB_ERR_SHAPE) st = rb::launch_gemv_int8(a, sms, static_cast<cudaStream_t>(stream));
+#endif
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
 }

@@ -64,7 +64,6 @@ struct __align__(64) TcParams {
   Slot slots[kMaxSlots];
   int count, nslots, total_blocks, x_bf16, y_bf16, prefetch, nst;
   uint32_t xs_off, bar_off, idesc;
-  uint32_t m_lo, m_hi, k1024, k64;
 };
 
 // B operand descriptor over an activation table: K-major, no swizzle, 16-byte rows at a 16-byte pitch (row 0
@@ -298,7 +297,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
     fence_proxy_async_smem();                // generic writes of the tables -> visible to the tensor core
     named_bar_sync(1, (kSets + kConvWarps) * 32);
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    const g4::DequantK dk = {p.m_lo, p.m_hi, p.k1024, p.k64};
     int e = 0, q = 0, st = 0;
     bool ok = true;
     for (int jj = s; jj < nlocal; jj += kSets) {
@@ -445,10 +443,6 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
     p.x_bf16 = x_dtype == RB_BF16;
     p.y_bf16 = y_dtype == RB_BF16;
     p.prefetch = (flags & RB_FLAG_PDL) && (flags & RB_FLAG_PREFETCH_WEIGHTS) ? 1 : 0;
-    p.m_lo = 0x000F000Fu;
-    p.m_hi = 0x00F000F0u;
-    p.k1024 = 0x64006400u;
-    p.k64 = 0x54005400u;
     // instruction descriptor: D int32, A unsigned 8-bit, B signed 8-bit, both K-major, N = 8, M = 128
     p.idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((8u >> 3) << 17) | ((static_cast<uint32_t>(kRows) >> 4) << 24);
     const uint32_t kBars = kSets * (2 * kMaxStages + 2 * kNB) * 8 + 16;

@@ -6,3 +6,4 @@
 #include "gemv_int4_multi.cu"
 #include "mm_int4.cu"
 #include "gemv_int4_tc.cu"
+#include "gemv_int8_tc.cu"
