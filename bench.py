@@ -50,6 +50,10 @@ def parse():
                     help="length of the bounded CPU-baseline sample (0: skip it)")
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers in the step (36 = config 1; fewer only for small profiling cases)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: config 1 + 2 (the headline); prefill: config 3, the int4-weight matmul over the "
+                         "36-layer projection set for --tokens prompt tokens")
+    ap.add_argument("--tokens", type=int, default=256, help="prefill prompt length M (config 3: 34, 256, 1024)")
     ap.add_argument("--parallel", default="replica", choices=["replica", "tp"],
                     help="replica: one independent decode stream per GPU (weak scaling); tp: one stream, every "
                          "projection sharded over the GPUs with one NCCL all-reduce per layer (strong scaling)")
@@ -420,10 +424,91 @@ def run_ours(a):
     return 0
 
 
+def run_prefill(a):
+    """Config 3: Y = X W^T for the 36-layer projection set (QKV, o_proj, gate_up, down) with X fp16 [M, K],
+    one mm_int4 call per matrix, replayed from one CUDA graph. value = 2 M sum(N K) / step time."""
+    import rumik_fast_b200 as rb
+    from rumik_fast_b200 import synthetic as syn
+    from rumik_fast_b200.mm_int4 import mm_int4
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    M = a.tokens
+    gen = syn.generator(4321 + rank, dev)
+    layers = [[syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES] for _ in range(a.layers)]
+    xs = {k: syn.activations((M, k), gen, dev) for k in (3072, 8192)}
+    ys = [torch.empty(M, n, device=dev, dtype=torch.float16) for _, n, _ in syn.LAYER_SHAPES]
+
+    def step():
+        for L in layers:
+            for i, ((_, n, k), w) in enumerate(zip(syn.LAYER_SHAPES, L)):
+                mm_int4(xs[k], *w, out=ys[i])
+    g = capture(step)
+    flops = 2 * M * a.layers * sum(n * k for _, n, k in syn.LAYER_SHAPES)
+    wbytes = a.layers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES)
+    with ClockSampler(local_gpu_index(local)) as clk:
+        m0 = clk.mark()
+        ms = timed(g.replay, a.steps, a.warmup, world)
+        m1 = clk.mark()
+    ms_step = ms / a.steps
+    hx = {k: v.cpu().pin_memory() for k, v in xs.items()}
+    hy = torch.empty(ys[0].shape, dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        for k, v in xs.items():
+            v.copy_(hx[k], non_blocking=True)
+        g.replay()
+        hy.copy_(ys[0], non_blocking=True)
+    e2e_steps = max(1, a.steps // 2)
+    ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
+    bound = "hbm" if M < 64 else "tensor"
+    j = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    if rank == 0:
+        tf = world * flops / (ms_step * 1e-3) / 1e12
+        if bound == "hbm":
+            peak, kind = peaks()
+            achieved, unit = wbytes / (ms_step * 1e-3) / 1e9, "GB/s"
+        else:
+            peak, kind = float(j.get("bf16_tflops", 1590.0)), "measured" if j else "fallback"
+            achieved, unit = flops / (ms_step * 1e-3) / 1e12, "TFLOP/s"
+        line = {
+            "metric": "prefill int4-weight matmul TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": f"config-3 prefill: X fp16 [{M}, K] against the 36-layer projection set "
+                                   "(QKV 5120x3072, o 3072x3072, gate_up 16384x3072, down 3072x8192; int4 g128), "
+                                   "one mm_int4 launch per matrix, in one CUDA graph",
+                       "tokens": M, "flops_per_step": flops, "weight_bytes_per_step": wbytes,
+                       "parallelism": f"replica x{world}", "l2": "no flush: 1.93 GB of weights per step > 126 MB L2"},
+            "e2e": {"value": round(world * flops / (ms_e2e * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": sum(v.numel() * 2 for v in xs.values()),
+                    "d2h_bytes_per_step": hy.numel() * 2, "ms_per_step": round(ms_e2e, 5)},
+            "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": peak, "unit": unit,
+                         "frac": round(achieved / peak, 4), "peak_kind": kind, "kernel": "whole prefill step",
+                         "traffic": None},
+            "cpu_baseline": None, "clocks": clk.summary(m0, m1),
+            "gpu_launches": a.steps * a.layers * 4, "mode": "prefill",
+        }
+        print(json.dumps(line), flush=True)
+    del g
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         return run_reference(a)
+    if a.workload == "prefill":
+        return run_prefill(a)
     return run_ours(a)
 
 

@@ -74,6 +74,8 @@ int rb_gemv_int4(const void* x, int x_dtype, int64_t ldx,
  * Replaces gemv_int8(x, q, s, y) (kernels/cuda_gemv.py:188-195) and gemv_int8_kernel (:141-186); the
  * Python wrapper gemv_int8_cuda (:245-249) calls this. s_dtype RB_F32 (engine) or RB_F16 (configs).
  *   N >= 1 (no padding to 16 required), K % 64 == 0, 64 <= K <= 16384, 1 <= batch <= 16
+ * Batch 1 with K % 128 == 0 runs on the tcgen05 tensor cores (the codes are the 8-bit A operand, x is
+ * quantised once to 16-bit integers, delta = max|x| / 32639); other shapes on the warp-level MMA kernel.
  */
 int rb_gemv_int8(const void* x, int x_dtype, int64_t ldx,
                  const uint8_t* q, int q_signed, const void* s, int s_dtype,
@@ -107,9 +109,11 @@ typedef struct rb_gemv_desc {
  * A list of independent int4 GEMVs (batch 1) in one persistent launch: y_i = W_i x_i for every entry.
  * No reference counterpart as a single call: it executes what rumik-fast's projection-set benchmark
  * (kernels/bench_gemv.py:83-113) issues as one gemv_int4 launch per matrix, without the per-launch cost.
- * Every x_i must be ready when the launch starts and no y_i may alias another entry's inputs. `descs` is a
- * host array, copied into the launch (at most 256 entries and 8 distinct activation vectors per launch;
- * longer lists are split into several launches).
+ * Runs on the tcgen05 tensor cores: the int4 codes are the unsigned 8-bit A operand in tensor memory and each
+ * x_i is quantised per 128-column group to 16-bit integers (delta = max|x| / 32639; error below 2e-5 of the
+ * group's largest |x|) split into two signed bytes. Every x_i must be ready when the launch starts and no y_i
+ * may alias another entry's inputs. `descs` is a host array, copied into the launch (at most 160 entries and 8
+ * distinct activation vectors per launch; longer lists are split into several launches).
  */
 int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_dtype, int flags, void* stream);
 

@@ -141,7 +141,11 @@ int rb_mm_int4(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const 
   a.q = q; a.s = s; a.m = m;
   a.Y = Y; a.y_dtype = y_dtype; a.ldy = ldy;
   a.M = M; a.N = N; a.K = K; a.flags = flags;
+#ifdef RB_MM_LEGACY  // dequantisation into shared memory, one CTA per tile (comparison builds)
   st = rb::launch_mm_int4(a, sms, static_cast<cudaStream_t>(stream));
+#else
+  st = rb::launch_mm_int4_tc(a, sms, static_cast<cudaStream_t>(stream));
+#endif
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
 }

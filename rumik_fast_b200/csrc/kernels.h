@@ -44,6 +44,7 @@ int launch_gemv_int4(const GemvArgs& a, int num_sms, cudaStream_t stream);
 int launch_gemv_int8(const GemvArgs& a, int num_sms, cudaStream_t stream);
 int launch_gemv_int8_tc(const GemvArgs& a, int num_sms, cudaStream_t stream);
 int launch_mm_int4(const MmArgs& a, int num_sms, cudaStream_t stream);
+int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream);
 int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,
                            cudaStream_t stream);
 int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,

@@ -1,0 +1,331 @@
+// mm_int4_tc.cu - the int4-weight prefill matmul Y[t, n] = sum_k X[t, k] w[n, k] on B200 tensor cores with
+// the dequantised weights in tensor memory (sm_100a).
+//
+// The operation of rumik-fast's Triton kernel _mm_int4 (kernels/mm_int4.py:24-46) and its wrapper mm_int4
+// (:59-73): w = code * s + m in the int4 group-128 layout, X fp16 [M, K], fp32 accumulation.
+//
+// Work items are (128-row weight block, token chunk of BT <= 128 tokens), block-major so that the CTAs working
+// at the same time on the chunks of one block share its codes through L2; items are dealt round-robin to one
+// CTA per SM and alternate between two converter sets. Per CTA:
+//  * warp 0 (producer) streams, per item and group, the block's codes (TMA box 64 bytes x 128 rows, 64-byte
+//    swizzle) and the chunk's two 64-column X atoms (TMA, 128-byte swizzle) into the set's ring;
+//  * each converter set (four warps, thread = weight row = tensor-memory lane) dequantises its row's group
+//    to fp16 (per code byte: PRMT, LOP3 to the fp16 magic numbers, HSUB2, HFMA2 with the row's scale and
+//    min, one rounding) and writes the 64 columns to tensor memory (tcgen05.st);
+//  * one thread per set issues eight tcgen05.mma.kind::f16 per group (M = 128, N = BT, K = 16): A from tensor
+//    memory, B = the X atoms in shared memory, D = 128 x BT fp32 in tensor memory accumulating over all of K;
+//  * the converter warps then read D (tcgen05.ld) and store Y.
+// All mbarrier waits are bounded; no multicast, no clusters.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rb {
+
+namespace mm4t {
+
+constexpr int kSets = 2;
+constexpr int kRows = 128;
+constexpr int kFirstConv = 1 + kSets;
+constexpr int kThreads = (kFirstConv + 4 * kSets) * 32;
+constexpr uint32_t kCodeBytes = kRows * 64;
+constexpr int kNB = 2;                       // tensor-memory A buffers per set
+constexpr uint32_t kACols = 64;
+constexpr uint32_t kSetCols = 256;           // per set: A buffers (128 columns) + D (<= 128 columns)
+constexpr uint32_t kTmemCols = 512;
+constexpr int kMaxStages = 6;
+
+struct __align__(64) MmtParams {
+  CUtensorMap qmap;  // [N rows, K/2 bytes], box 64 x 128, 64-byte swizzle
+  CUtensorMap xmap;  // [M rows, K fp16], box 64 x BT, 128-byte swizzle
+  const uint16_t* s;
+  const uint16_t* m;
+  void* y;
+  int64_t ldy;
+  int M, N, K, G, BT, nchunks, nitems, y_bf16, nst, prefetch;
+  uint32_t stage_bytes, bar_off, idesc;
+};
+
+__device__ __forceinline__ void umma_ts_f16(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];" : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]) : "r"(taddr) : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_constant__ MmtParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int C = gridDim.x, cta = blockIdx.x;
+  const int nst = p.nst, G = p.G, BT = p.BT;
+  const int nlocal = (p.nitems - cta + C - 1) / C;  // this CTA's items: cta + j * C
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+  const int per_set = 2 * nst + 2 * kNB + 2;
+  auto full = [&](int s, int i) { return bars + s * per_set + i; };
+  auto empty = [&](int s, int i) { return bars + s * per_set + nst + i; };
+  auto afull = [&](int s, int b) { return bars + s * per_set + 2 * nst + b; };
+  auto mdone = [&](int s, int b) { return bars + s * per_set + 2 * nst + kNB + b; };
+  auto dready = [&](int s) { return bars + s * per_set + 2 * nst + 2 * kNB; };
+  auto dfree = [&](int s) { return bars + s * per_set + 2 * nst + 2 * kNB + 1; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kSets * per_set);
+  auto stage_of = [&](int s, int slot) { return smem + (static_cast<size_t>(s) * nst + slot) * p.stage_bytes; };
+
+  if (tid == 0) {
+    for (int s = 0; s < kSets; ++s) {
+      for (int i = 0; i < nst; ++i) {
+        mbar_init(full(s, i), 1);
+        mbar_init(empty(s, i), 5);  // four converter warps (codes read) + one MMA commit (X read)
+      }
+      for (int b = 0; b < kNB; ++b) {
+        mbar_init(afull(s, b), 4);
+        mbar_init(mdone(s, b), 1);
+      }
+      mbar_init(dready(s), 1);
+      mbar_init(dfree(s), 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  mm4::tc_fence_before();
+  __syncthreads();
+  mm4::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_launch_dependents();
+  const uint32_t stage_tx = kCodeBytes + 2u * BT * 128u;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      griddep_wait();  // X may come from the previous kernel
+      int j[kSets], g[kSets], issued[kSets];
+      for (int s = 0; s < kSets; ++s) j[s] = s, g[s] = 0, issued[s] = 0;
+      bool ok = true, any = true;
+      while (any && ok) {
+        any = false;
+        for (int s = 0; s < kSets && ok; ++s) {
+          if (j[s] >= nlocal) continue;
+          any = true;
+          const int item = cta + j[s] * C;
+          const int row0 = (item / p.nchunks) * kRows, t0 = (item % p.nchunks) * BT;
+          const int slot = issued[s] % nst;
+          if (issued[s] >= nst && !mbar_wait(empty(s, slot), ((issued[s] / nst) - 1) & 1, ERR_MM4_WAIT)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = stage_of(s, slot);
+          mbar_arrive_expect_tx(full(s, slot), stage_tx);
+          mm4::tma_load_2d(st, &p.qmap, g[s] * 64, row0, full(s, slot));
+          mm4::tma_load_2d(st + kCodeBytes, &p.xmap, g[s] * 128, t0, full(s, slot));
+          mm4::tma_load_2d(st + kCodeBytes + BT * 128, &p.xmap, g[s] * 128 + 64, t0, full(s, slot));
+          ++issued[s];
+          if (++g[s] == G) g[s] = 0, j[s] += kSets;
+        }
+      }
+      for (int s = 0; s < kSets; ++s)  // no retirement with copies in flight
+        for (int t = max(0, issued[s] - nst); t < issued[s]; ++t)
+          if (!mbar_wait(full(s, t % nst), (t / nst) & 1, ERR_MM4_WAIT)) break;
+    }
+  } else if (warp < kFirstConv) {
+    // ---------------- MMA issuer of set s ----------------
+    const int s = warp - 1;
+    if (lane == 0) {
+      const uint32_t d_col = tmem + s * kSetCols + kNB * kACols;
+      int q = 0, used = 0, n = 0;
+      bool ok = true;
+      for (int jj = s; jj < nlocal && ok; jj += kSets, ++n) {
+        if (n >= 1 && !mbar_wait(dfree(s), (n - 1) & 1, ERR_MM4_WAIT)) break;  // D read by the last epilogue
+        for (int gg = 0; gg < G; ++gg, ++q, ++used) {
+          const int b = q % kNB, slot = used % nst;
+          if (!mbar_wait(afull(s, b), (q / kNB) & 1, ERR_MM4_WAIT) ||
+              !mbar_wait(full(s, slot), (used / nst) & 1, ERR_MM4_WAIT)) {
+            ok = false;
+            break;
+          }
+          mm4::tc_fence_after();
+          const uint32_t xb = smem_u32(stage_of(s, slot) + kCodeBytes);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            umma_ts_f16(d_col, tmem + s * kSetCols + b * kACols + 8 * i,
+                        mm4::sw128_desc(xb + (i >> 2) * BT * 128 + (i & 3) * 32), p.idesc, (gg | i) != 0);
+          mm4::umma_commit(mdone(s, b));     // A buffer b may be rewritten
+          mm4::umma_commit(empty(s, slot));  // the stage's X atoms may be refilled
+        }
+        if (ok) mm4::umma_commit(dready(s));
+      }
+    }
+  } else {
+    // ---------------- converters + epilogue of set s ----------------
+    const int cw = warp - kFirstConv;
+    const int s = cw >> 2;
+    const int quad = warp & 3;
+    const int rib = quad * 32 + lane;
+    const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t a_set = tq + s * kSetCols, d_set = tq + s * kSetCols + kNB * kACols;
+    const uint32_t magic = 0x54006400u, mask = 0x00F0000Fu;  // (1024 | low nibble, 64 | high nibble << 4)
+    griddep_wait();  // Y may still be read by the previous kernel
+    int q = 0, used = 0, n = 0;
+    bool ok = true;
+    for (int jj = s; jj < nlocal; jj += kSets, ++n) {
+      const int item = cta + jj * C;
+      const int row = (item / p.nchunks) * kRows + rib, t0 = (item % p.nchunks) * BT;
+      const bool row_ok = row < p.N;
+      const uint16_t* srow = p.s + static_cast<int64_t>(row_ok ? row : 0) * G;
+      const uint16_t* mrow = p.m + static_cast<int64_t>(row_ok ? row : 0) * G;
+      uint16_t s_next = __ldg(srow), m_next = __ldg(mrow);
+      for (int gg = 0; gg < G; ++gg, ++q, ++used) {
+        const uint16_t s16 = s_next, m16 = m_next;
+        if (gg + 1 < G) {  // the next group's scale and min
+          s_next = __ldg(srow + gg + 1);
+          m_next = __ldg(mrow + gg + 1);
+        }
+        const int slot = used % nst;
+        if (ok) ok = mbar_wait(full(s, slot), (used / nst) & 1, ERR_MM4_WAIT);
+        uint4 w4[4];
+        if (ok) {
+          const uint8_t* rowp = stage_of(s, slot) + rib * 64;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) w4[c] = lds128(rowp + ((c ^ ((rib >> 1) & 3)) << 4));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty(s, slot));  // codes are in registers
+        const uint32_t s2 = static_cast<uint32_t>(s16) * 0x10001u, m2 = static_cast<uint32_t>(m16) * 0x10001u;
+        uint32_t o[64];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t wv[4] = {w4[c].x, w4[c].y, w4[c].z, w4[c].w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+#pragma unroll
+            for (int bj = 0; bj < 4; ++bj) {  // byte bj of word: columns 2 bj, 2 bj + 1 of these 8
+              const uint32_t spread = __byte_perm(wv[t], 0u, 0x4040u | (0x0101u * bj));
+              const uint32_t tt = and_or(spread, mask, magic);  // (1024 + lo, 64 + hi), exact
+              o[c * 16 + t * 4 + bj] = mm4::hfma2_u(mm4::hsub2_u(tt, magic), s2, m2);  // (lo, hi) * s + m
+            }
+          }
+        }
+        const int b = q % kNB;
+        ok = __all_sync(0xffffffffu, ok);
+        if (q >= kNB && ok) ok = __all_sync(0xffffffffu, mbar_wait(mdone(s, b), ((q / kNB) - 1) & 1, ERR_MM4_WAIT));
+        if (ok) {
+          mm4::tc_fence_after();
+          g4t::tmem_st32(a_set + b * kACols, o);
+          g4t::tmem_st32(a_set + b * kACols + 32, o + 32);
+          g4t::tmem_wait_st();
+          mm4::tc_fence_before();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(afull(s, b));
+      }
+      // ---- epilogue of this item ----
+      if (ok) ok = mbar_wait(dready(s), n & 1, ERR_MM4_WAIT);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        mm4::tc_fence_after();
+        for (int c0 = 0; c0 < BT; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld32(d_set + c0, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = t0 + c0 + i;  // columns past BT belong to no token of this chunk
+            if (row_ok && c0 + i < BT && t < p.M) store_out(p.y, static_cast<int64_t>(t) * p.ldy + row, __uint_as_float(v[i]), p.y_bf16);
+          }
+        }
+        mm4::tc_fence_before();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dfree(s));
+    }
+  }
+  mm4::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    mm4::tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+}  // namespace mm4t
+
+int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
+  using namespace mm4t;
+  if (a.x_dtype != RB_F16) return RB_ERR_DTYPE;
+  auto encode = mm4::encode_fn();
+  if (!encode) return RB_ERR_DEVICE;
+  const int M = static_cast<int>(a.M), N = static_cast<int>(a.N), K = static_cast<int>(a.K);
+  // token chunks of at most 128 (multiples of 16)
+  const int nch = (M + 127) / 128;
+  int BT = (M + nch - 1) / nch;
+  BT = std::max(16, (BT + 15) / 16 * 16);
+  MmtParams p;
+  p.s = a.s;
+  p.m = a.m;
+  p.y = a.Y;
+  p.ldy = a.ldy;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.G = K / 128;
+  p.BT = BT;
+  p.nchunks = (M + BT - 1) / BT;
+  p.nitems = ((N + kRows - 1) / kRows) * p.nchunks;
+  p.y_bf16 = a.y_dtype == RB_BF16;
+  p.prefetch = 0;
+  p.stage_bytes = (kCodeBytes + 2u * BT * 128u + 1023u) & ~1023u;
+  constexpr uint32_t kSmemMax = 227 * 1024;
+  int nst = static_cast<int>((kSmemMax - 1024 - 512) / (kSets * p.stage_bytes));
+  nst = std::min(nst, kMaxStages);
+  if (nst < 2) return RB_ERR_SHAPE;
+  p.nst = nst;
+  p.bar_off = static_cast<uint32_t>(kSets * nst) * p.stage_bytes;
+  // instruction descriptor: D f32, A f16, B f16, both K-major, N = BT, M = 128
+  p.idesc = (1u << 4) | (static_cast<uint32_t>(BT >> 3) << 17) | (static_cast<uint32_t>(kRows >> 4) << 24);
+  const uint32_t smem = 1024 + p.bar_off + kSets * (2 * nst + 2 * kNB + 2) * 8 + 16;
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(N)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K / 2)};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kRows)};
+    const cuuint32_t es[2] = {1, 1};
+    if (encode(&p.qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.q), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return RB_ERR_SHAPE;
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.ldx) * 2};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(BT)};
+    const cuuint32_t es[2] = {1, 1};
+    if (encode(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.X), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return RB_ERR_SHAPE;
+  }
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(mm_int4_tc_kernel), kSmemMax);
+  if (e != cudaSuccess) return RB_ERR_LAUNCH;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(std::min(num_sms, p.nitems));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = (a.flags & RB_FLAG_PDL) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, mm_int4_tc_kernel, p);
+  return e == cudaSuccess ? RB_OK : RB_ERR_LAUNCH;
+}
+
+}  // namespace rb

@@ -7,3 +7,4 @@
 #include "mm_int4.cu"
 #include "gemv_int4_tc.cu"
 #include "gemv_int8_tc.cu"
+#include "mm_int4_tc.cu"
