@@ -54,6 +54,8 @@ def parse():
                     help="decode: config 1 + 2 (the headline); prefill: config 3, the int4-weight matmul over the "
                          "36-layer projection set for --tokens prompt tokens")
     ap.add_argument("--tokens", type=int, default=256, help="prefill prompt length M (config 3: 34, 256, 1024)")
+    ap.add_argument("--collective", default="nccl", choices=["peer", "nccl"],
+                    help="tp only: per-layer reduction by the peer-memory kernel or by add + NCCL all-reduce")
     ap.add_argument("--parallel", default="replica", choices=["replica", "tp"],
                     help="replica: one independent decode stream per GPU (weak scaling); tp: one stream, every "
                          "projection sharded over the GPUs with one NCCL all-reduce per layer (strong scaling)")
@@ -273,7 +275,7 @@ def run_tp(a, rank, world, dev):
     x_h = syn.activations((3072,), gen, dev)
     x_attn = syn.activations((3072,), gen, dev)
     x_act = syn.activations((8192,), gen, dev)
-    step = TPDecodeStep(layers, x_attn, x_act, head, rank, world)
+    step = TPDecodeStep(layers, x_attn, x_act, head, rank, world, collective=a.collective)
     del layers, head
     torch.cuda.empty_cache()
     step.h[0].copy_(x_h)
@@ -307,7 +309,9 @@ def run_tp(a, rank, world, dev):
                                    "int8 head sharded over the GPUs (column-parallel QKV/gate_up, row-parallel "
                                    "o/down), one NCCL all-reduce of the hidden vector per layer, batch 1",
                        "batch": 1, "bytes_per_step": full_bytes, "parallelism": f"tp{world}",
-                       "launches": "per layer: one multi-GEMV launch + add + all-reduce; head + all-gather",
+                       "launches": "per layer: one multi-GEMV launch + " + (
+                           "one peer-memory reduction kernel" if a.collective == "peer" else "add + NCCL all-reduce")
+                       + "; head + all-gather", "collective": a.collective,
                        "l2": "no flush: 1.98 GB of weights per step over all ranks > 126 MB L2 per GPU"},
             "tok_s": round(1e3 / ms_step, 1),
             "e2e": {"value": round(full_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": UNIT,
@@ -322,6 +326,11 @@ def run_tp(a, rank, world, dev):
         }
         print(json.dumps(line), flush=True)
     del g
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    step.close()
     return 0
 
 

@@ -117,6 +117,37 @@ typedef struct rb_gemv_desc {
  */
 int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_dtype, int flags, void* stream);
 
+/*
+ * Tensor-parallel per-layer reduction over NVLink peer memory:  out[i] = sum over ranks of (a[i] + b[i]).
+ * Replaces the add + all-reduce that follows a row-parallel layer pair (o_proj and down partials) in a
+ * tensor-parallel decode step; no reference counterpart (the reference engine runs on one GPU).
+ *   a, b, out  fp16 [n] on this rank's device (b may be NULL); 1 <= n <= 2^24
+ *   bufs       the `world` ranks' symmetric buffers (device pointers mapped into this process, bufs[rank] the
+ *              local one), each at least 8 * world * n bytes of data at offset 0, `world` uint32 flags at
+ *              flag_off and one uint32 counter at counter_off, all zero before the first call
+ * Every rank must make the same sequence of calls. A peer that does not arrive within 4 s sets a bit in the
+ * device error word (rb_get_device_error). 1 <= world <= 8.
+ */
+int rb_tp_allreduce_f16(const void* a, const void* b, void* out, int64_t n, void* const* bufs, int rank, int world,
+                        uint32_t flag_off, uint32_t counter_off, int flags, void* stream);
+
+/*
+ * Setup for rb_tp_allreduce_f16 (not part of the GEMV path, which never allocates): a zeroed device buffer of
+ * `bytes` on the current device from cudaMalloc, and its 64-byte cudaIpcMemHandle_t in handle_out for the
+ * other ranks. Release with rb_ipc_free.
+ */
+int rb_ipc_alloc(uint64_t bytes, void** ptr, void* handle_out);
+int rb_ipc_free(void* ptr);
+
+/*
+ * Map another process's device buffer (a 64-byte cudaIpcMemHandle_t of its allocation plus the buffer's byte
+ * offset in it) into this process for the CURRENT device, with peer access enabled between the current device
+ * and the buffer's device. *base receives the mapped allocation (pass it to rb_ipc_close), *ptr the buffer.
+ * Setup for rb_tp_allreduce_f16; no kernel is launched.
+ */
+int rb_ipc_open(const void* handle, uint64_t offset, void** base, void** ptr);
+int rb_ipc_close(void* base);
+
 /* Human-readable text for a status code (static storage). */
 const char* rb_status_string(int status);
 

@@ -35,6 +35,12 @@ SIGNATURES = {
     "rb_status_string": (_c.c_char_p, [_int]),
     "rb_version": (_int, []),
     "rb_get_device_error": (_int, [_c.POINTER(_c.c_uint), _vp]),
+    "rb_ipc_alloc": (_int, [_c.c_uint64, _c.POINTER(_vp), _vp]),
+    "rb_ipc_free": (_int, [_vp]),
+    "rb_ipc_open": (_int, [_vp, _c.c_uint64, _c.POINTER(_vp), _c.POINTER(_vp)]),
+    "rb_ipc_close": (_int, [_vp]),
+    "rb_tp_allreduce_f16": (_int, [_vp, _vp, _vp, _i64, _c.POINTER(_vp), _int, _int, _c.c_uint32, _c.c_uint32, _int,
+                                   _vp]),
 }
 
 _lib = None

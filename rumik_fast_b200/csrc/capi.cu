@@ -5,6 +5,8 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <cstring>
+
 namespace {
 
 constexpr int kVersion = 100;
@@ -148,6 +150,67 @@ int rb_mm_int4(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const 
 #endif
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
+}
+
+int rb_tp_allreduce_f16(const void* a, const void* b, void* out, int64_t n, void* const* bufs, int rank, int world,
+                        uint32_t flag_off, uint32_t counter_off, int flags, void* stream) {
+  if (!a || !out || !bufs) return RB_ERR_NULL;
+  if (n <= 0 || world < 1 || world > 8 || rank < 0 || rank >= world) return RB_ERR_SHAPE;
+  if ((flag_off % 4) != 0 || (counter_off % 4) != 0) return RB_ERR_ALIGN;
+  int sms = 0, st = device_sms(&sms);
+  if (st != RB_OK) return st;
+  st = rb::launch_tp_allreduce(static_cast<const __half*>(a), static_cast<const __half*>(b), static_cast<__half*>(out),
+                               n, bufs, rank, world, flag_off, counter_off, flags, static_cast<cudaStream_t>(stream));
+  if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+  return st;
+}
+
+int rb_ipc_alloc(uint64_t bytes, void** ptr, void* handle_out) {
+  if (!ptr || !handle_out) return RB_ERR_NULL;
+  if (bytes == 0) return RB_ERR_SHAPE;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return RB_ERR_DEVICE;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    cudaFree(p);
+    return RB_ERR_DEVICE;
+  }
+  std::memcpy(handle_out, &h, sizeof(h));
+  *ptr = p;
+  return RB_OK;
+}
+
+int rb_ipc_free(void* ptr) {
+  if (!ptr) return RB_ERR_NULL;
+  return cudaFree(ptr) == cudaSuccess ? RB_OK : RB_ERR_DEVICE;
+}
+
+int rb_ipc_open(const void* handle, uint64_t offset, void** base, void** ptr) {
+  if (!handle || !base || !ptr) return RB_ERR_NULL;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* b = nullptr;
+  if (cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return RB_ERR_DEVICE;
+  }
+  *base = b;
+  *ptr = static_cast<char*>(b) + offset;
+  return RB_OK;
+}
+
+int rb_ipc_close(void* base) {
+  if (!base) return RB_ERR_NULL;
+  if (cudaIpcCloseMemHandle(base) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return RB_ERR_DEVICE;
+  }
+  return RB_OK;
 }
 
 int rb_get_device_error(unsigned int* out, void* stream) {

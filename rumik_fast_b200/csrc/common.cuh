@@ -26,6 +26,7 @@ enum : unsigned int {
   ERR_MULTI_FULL = 1u << 5,   // multi-GEMV consumer timed out waiting for a tile
   ERR_MULTI_EMPTY = 1u << 6,  // multi-GEMV producer timed out waiting for ring space
   ERR_TC_WAIT = 1u << 7,      // tensor-core multi-GEMV timed out on an mbarrier
+  ERR_TP_WAIT = 1u << 8,      // tensor-parallel reduction timed out waiting for a peer's flag
 };
 
 // Upper bound on the wall time of one mbarrier wait. Healthy waits here last microseconds (at most the

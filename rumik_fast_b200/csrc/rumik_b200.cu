@@ -8,3 +8,4 @@
 #include "gemv_int4_tc.cu"
 #include "gemv_int8_tc.cu"
 #include "mm_int4_tc.cu"
+#include "allreduce.cu"

@@ -115,6 +115,66 @@ class TPLayerShards:
         return y_qkv, y_gu, part
 
 
+class PeerAllReduce:
+    """out = sum over the ranks of `group` of (a + b), for fp16 vectors of n elements: ONE kernel per call
+    (rb_tp_allreduce_f16) that stores each rank's partial into every rank's buffer over NVLink and sums the
+    slots in rank order, replacing the add kernel and the collective call of a row-parallel layer pair.
+    Each rank's buffer comes from cudaMalloc (rb_ipc_alloc) and is mapped into the other ranks with CUDA IPC,
+    opened for the mapping rank's own device with peer access enabled (rb_ipc_open): plain peer loads and
+    stores, no multicast object. Every rank must make the same sequence
+    of calls. Graph-capturable."""
+
+    def __init__(self, n, device, group=None):
+        import ctypes
+        import torch.distributed as dist
+        pg = group if group is not None else dist.group.WORLD
+        self.world, self.rank, self.n = dist.get_world_size(pg), dist.get_rank(pg), n
+        self.flag_off = (8 * self.world * n + 15) // 16 * 16
+        self.counter_off = self.flag_off + 4 * 8
+        from . import _lib
+        L = _lib.lib()
+        local, hbuf = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+        with torch.cuda.device(device):
+            _lib.check("rb_ipc_alloc", L.rb_ipc_alloc(self.counter_off + 16, ctypes.byref(local), hbuf))
+        self._local = local.value
+        metas = [None] * self.world
+        dist.all_gather_object(metas, (hbuf.raw, 0), group=pg)
+        self._bases = []  # mapped peer allocations, closed in close()
+        ptrs = []
+        with torch.cuda.device(device):
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(self._local)
+                    continue
+                handle, offset = metas[r]
+                base, ptr = ctypes.c_void_p(), ctypes.c_void_p()
+                _lib.check("rb_ipc_open", L.rb_ipc_open(handle, offset, ctypes.byref(base), ctypes.byref(ptr)))
+                self._bases.append(base.value)
+                ptrs.append(ptr.value)
+        self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
+        dist.barrier(group=pg)
+
+    def close(self):
+        """Unmap the peers' buffers and free the local one (after every call that uses them has completed on
+        every rank)."""
+        from . import _lib
+        for b in self._bases:
+            _lib.lib().rb_ipc_close(b)
+        self._bases = []
+        if self._local:
+            _lib.lib().rb_ipc_free(self._local)
+            self._local = None
+
+    def __call__(self, a, b, out):
+        from . import _lib, config
+        assert a.dtype == torch.float16 and out.dtype == torch.float16 and a.numel() == self.n == out.numel()
+        st = _lib.lib().rb_tp_allreduce_f16(a.data_ptr(), None if b is None else b.data_ptr(), out.data_ptr(),
+                                            self.n, self._bufs, self.rank, self.world, self.flag_off,
+                                            self.counter_off, config.flags(), _lib.stream_ptr(a.device))
+        _lib.check("rb_tp_allreduce_f16", st)
+        return out
+
+
 def allreduce_hidden(part, group=None):
     """Sum the ranks' partial hidden vectors (in place) with torch.distributed."""
     import torch.distributed as dist
@@ -126,16 +186,19 @@ class TPDecodeStep:
     """A tensor-parallel decode step's projections on one rank, CUDA-graph capturable.
 
     Per layer: ONE multi-GEMV launch of the rank's four shards (QKV and gate_up on the layer input, o_proj and
-    down on their slices of the attention and MLP activations), the partial sum o + down, and one all-reduce
-    (sum) of the fp16 hidden vector, which is the next layer's input. Then the int8 head, split by rows, and
+    down on their slices of the attention and MLP activations), then the sum over ranks of o + down, which is
+    the next layer's input: with collective="peer" one peer-memory reduction kernel (PeerAllReduce), with
+    "nccl" an add kernel and an NCCL all-reduce. Then the int8 head, split by rows, and
     an all-gather of the logits. The attention and MLP activations are fixed inputs: the step covers the
     weight-only linear layers, which are the part this library implements.
     """
 
-    def __init__(self, layers, x_attn, x_act, head, rank, world, group=None, q_rows=3072, kv_rows=1024):
+    def __init__(self, layers, x_attn, x_act, head, rank, world, group=None, q_rows=3072, kv_rows=1024,
+                 collective="nccl"):
         from .gemv_set import Int4GemvSet
         dev = x_attn.device
         self.rank, self.world, self.group = rank, world, group
+        self.ar = PeerAllReduce(x_attn.numel(), dev, group) if collective == "peer" and world > 1 else None
         H = x_attn.numel()
         self.h = [torch.zeros(H, device=dev, dtype=torch.float16) for _ in range(len(layers) + 1)]
         self.sets, self.outs = [], []
@@ -162,15 +225,23 @@ class TPDecodeStep:
         self.logits_all = torch.zeros(self.head_rows * world, device=dev, dtype=torch.float16)
         self.bytes = sum(s.bytes for s in self.sets) + hq[lo:hi].numel() + 2 * (hi - lo) + 2 * H + 2 * (hi - lo)
 
+    def close(self):
+        """Release the peer-memory reduction buffers (every rank, after its last step has completed)."""
+        if self.ar is not None:
+            self.ar.close()
+
     def __call__(self):
         import torch.distributed as dist
         from .cuda_gemv import gemv_int8_cuda
         for li, st in enumerate(self.sets):
             st()
             y_o, y_d = self.outs[li][2], self.outs[li][3]
-            torch.add(y_o, y_d, out=self.h[li + 1])
-            if self.world > 1:
-                dist.all_reduce(self.h[li + 1], op=dist.ReduceOp.SUM, group=self.group)
+            if self.ar is not None:
+                self.ar(y_o, y_d, self.h[li + 1])
+            else:
+                torch.add(y_o, y_d, out=self.h[li + 1])
+                if self.world > 1:
+                    dist.all_reduce(self.h[li + 1], op=dist.ReduceOp.SUM, group=self.group)
         nrows = self.head[0].shape[0]
         if nrows:
             gemv_int8_cuda(self.h[-1], *self.head, out=self.logits_part[:nrows])

@@ -139,3 +139,82 @@ def test_tensor_parallel_shards_through_cuda(native_lib, world):
     assert_close(qkv.float().cpu().numpy(), ref_qkv)
     assert_close(gu.float().cpu().numpy(), ref_gu)
     assert_close(hidden.cpu().numpy(), ref_h)
+
+
+def _peer_rank(rank, world, port, out):
+    import torch.distributed as dist
+    from rumik_fast_b200 import device_error
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+    try:
+        n = 3072
+        ar = tp.PeerAllReduce(n, dev)
+        ok = True
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        outs, refs = [], []
+        for it in range(5):  # several calls: both slot parities, epochs advancing
+            a = (torch.randn(n, generator=g, device=dev) * (it + 1)).half()
+            b = torch.randn(n, generator=g, device=dev).half()
+            o = torch.empty(n, device=dev, dtype=torch.float16)
+            ar(a, b, o)
+            part = a.float() + b.float()
+            parts = [torch.empty_like(part) for _ in range(world)]
+            dist.all_gather(parts, part)
+            ref = parts[0].clone()
+            for p_ in parts[1:]:
+                ref += p_
+            ok &= bool(torch.equal(o, ref.half()))
+        # graph replay of three calls
+        a = torch.randn(n, generator=g, device=dev).half()
+        b = torch.randn(n, generator=g, device=dev).half()
+        os_ = [torch.empty(n, device=dev, dtype=torch.float16) for _ in range(3)]
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for o in os_:
+                ar(a, b, o)
+        for _ in range(2):
+            gr.replay()
+        torch.cuda.synchronize()
+        part = a.float() + b.float()
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(parts, part)
+        ref = parts[0].clone()
+        for p_ in parts[1:]:
+            ref += p_
+        ok &= all(bool(torch.equal(o, ref.half())) for o in os_)
+        ok &= device_error(dev) == 0
+        out[rank] = ok
+        del gr
+        torch.cuda.synchronize()
+        dist.barrier()
+        ar.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_peer(world):
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        port = 29700 + (os.getpid() % 200) + world
+        procs = [ctx.Process(target=_peer_rank, args=(r, world, port, out)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(180)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        assert all(out.get(r) is True for r in range(world)), dict(out)
+
+
+@pytest.mark.gpu
+def test_peer_allreduce_world1(native_lib):
+    _run_peer(1)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_allreduce_world2(native_lib):
+    _run_peer(2)
