@@ -39,8 +39,9 @@ constexpr uint32_t kStageBytes = kRows * 128;  // two groups of codes for 128 ro
 constexpr int kMaxStages = 6;              // ring stages per set
 constexpr int kMaxEntries = 160;
 constexpr int kMaxSlots = 8;
-constexpr int kNB = 4;                      // tensor-memory A/D buffers per set (the epilogue's lag in groups)
-constexpr uint32_t kACols = 32, kDCols = 8, kSetCols = kNB * (kACols + kDCols);
+constexpr int kNP = 2;  // tensor-memory buffers per set, each for a PAIR of groups (one TMA stage): the epilogue
+                        // reads a pair's results two pairs after writing its codes
+constexpr uint32_t kACols = 64, kDCols = 16, kSetCols = kNP * (kACols + kDCols);  // group 0 | group 1 halves
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kXPad = 256;            // bytes the B descriptor's unused rows read past a table
 constexpr uint32_t kXGroupBytes = 256;     // per group: 8 chunks of (16 high bytes, 16 low bytes)
@@ -173,12 +174,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
   const int nlocal = (p.total_blocks - cta + C - 1) / C;  // this CTA's blocks: cta + j * C
   uint8_t* xs = smem + p.xs_off;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
-  // per set: full[nst], empty[nst], afull[kNB], mdone[kNB]
-  const int per_set = 2 * nst + 2 * kNB;
+  // per set: full[nst], empty[nst], afull[kNP], mdone[kNP]
+  const int per_set = 2 * nst + 2 * kNP;
   auto full = [&](int s, int i) { return bars + s * per_set + i; };
   auto empty = [&](int s, int i) { return bars + s * per_set + nst + i; };
   auto afull = [&](int s, int b) { return bars + s * per_set + 2 * nst + b; };
-  auto mdone = [&](int s, int b) { return bars + s * per_set + 2 * nst + kNB + b; };
+  auto mdone = [&](int s, int b) { return bars + s * per_set + 2 * nst + kNP + b; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kSets * per_set);
 
   if (tid == 0) {
@@ -187,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
         mbar_init(full(s, i), 1);
         mbar_init(empty(s, i), 4);
       }
-      for (int b = 0; b < kNB; ++b) {
+      for (int b = 0; b < kNP; ++b) {
         mbar_init(afull(s, b), 4);
         mbar_init(mdone(s, b), 1);
       }
@@ -271,17 +272,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
         const int gb = cta + jj * C;
         const Entry& E = entry_of(p, gb, e);
         const uint32_t xtab = smem_u32(xs + p.slots[E.slot].tab_off);
-        for (int g = 0; g < E.G; ++g, ++q) {
-          const int b = q % kNB;
-          if (!mbar_wait(afull(s, b), (q / kNB) & 1, ERR_TC_WAIT)) {
+        for (int g = 0; g < E.G; g += 2, ++q) {
+          const int b = q % kNP;
+          if (!mbar_wait(afull(s, b), (q / kNP) & 1, ERR_TC_WAIT)) {
             ok = false;
             break;
           }
           mm4::tc_fence_after();
-          const uint32_t acol = s * kSetCols + b * kACols, dcol = s * kSetCols + kNB * kACols + b * kDCols;
+          const uint32_t acol = s * kSetCols + b * kACols, dcol = s * kSetCols + kNP * kACols + b * kDCols;
+          const int ng = min(2, E.G - g);
+          for (int h = 0; h < ng; ++h)
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            umma_ts(tmem + dcol, tmem + acol + 8 * i, x_desc(xtab + g * kXGroupBytes + 64 * i), p.idesc, i > 0);
+            for (int i = 0; i < 4; ++i)
+              umma_ts(tmem + dcol + 8 * h, tmem + acol + 32 * h + 8 * i,
+                      x_desc(xtab + (g + h) * kXGroupBytes + 64 * i), p.idesc, i > 0);
           mm4::umma_commit(mdone(s, b));
         }
       }
@@ -309,33 +313,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
       const uint16_t* mrow = E.m + static_cast<int64_t>(row_ok ? row : 0) * G;
       const float2* cst = reinterpret_cast<const float2*>(xs + p.slots[E.slot].cst_off);
       float acc = 0.f;
-      float pend[kNB] = {0.f, 0.f, 0.f, 0.f};  // s * delta of the groups whose results are pending, oldest first
-      const int q0 = q;
-      const uint32_t a_set = tq + s * kSetCols, d_set = tq + s * kSetCols + kNB * kACols;
-      // codes of the next group to convert (software-pipelined one group ahead)
-      uint4 wn[4];
-      uint8_t* stage = nullptr;
-      auto load_codes = [&](int g) {
-        if ((g & 1) == 0) {
-          const int slot = st % nst;
-          if (ok) ok = mbar_wait(full(s, slot), (st / nst) & 1, ERR_TC_WAIT);
-          stage = smem + (static_cast<size_t>(s) * nst + slot) * kStageBytes;
-        }
+      // s * delta of the two groups of each pair whose results are pending, oldest pair first (0 for a missing
+      // second group: its accumulator columns hold stale finite integers, which the zero scale cancels)
+      float pa[kNP] = {0.f, 0.f}, pb[kNP] = {0.f, 0.f};
+      const int qp0 = q;  // pair counter of this set at the block's first pair
+      const uint32_t a_set = tq + s * kSetCols, d_set = tq + s * kSetCols + kNP * kACols;
+      const int npairs = (G + 1) / 2;
+      // codes of the next pair (both groups of one stage), software-pipelined one pair ahead
+      uint4 wn[8];
+      auto load_codes = [&](int k) {
+        const int slot = st % nst;
+        if (ok) ok = mbar_wait(full(s, slot), (st / nst) & 1, ERR_TC_WAIT);
         if (ok) {
-          const uint8_t* rowp = stage + rib * 128;
+          const uint8_t* rowp = smem + (static_cast<size_t>(s) * nst + slot) * kStageBytes + rib * 128;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) wn[c] = lds128(rowp + ((((g & 1) * 4 + c) ^ (rib & 7)) << 4));
+          for (int c = 0; c < 8; ++c) wn[c] = lds128(rowp + ((c ^ (rib & 7)) << 4));
         }
+        (void)k;
       };
-      // one group: unpack its codes into tensor memory and retire the group kNB back
-      auto step = [&](int g, float sv, float mv) {
-        const uint4 w[4] = {wn[0], wn[1], wn[2], wn[3]};
-        if ((g & 1) == 1 || g == G - 1) {  // both groups of this stage are in registers: release it
-          __syncwarp();
-          if (lane == 0) mbar_arrive(empty(s, st % nst));
-          ++st;
-        }
-        uint32_t o[32];
+      auto unpack = [&](const uint4* w, uint32_t* o) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const uint32_t wv[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
@@ -345,34 +341,57 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
             o[c * 8 + t * 2 + 1] = (wv[t] >> 4) & 0x0F0F0F0Fu;  // odd columns
           }
         }
-        const float2 c2 = cst[g];
-        acc = fmaf(mv, c2.y, acc);
-        const int qq = q0 + g, b = qq % kNB;
-        const bool epi = g >= kNB;
-        int dh = 0, dl = 0;
+      };
+      // one pair of groups (g, g + 1): codes into tensor memory, and the results of the pair kNP back
+      auto step = [&](int k, float s0, float m0, float s1, float m1) {
+        const int g = 2 * k;
+        const bool two = g + 1 < G;
+        const uint4 w[8] = {wn[0], wn[1], wn[2], wn[3], wn[4], wn[5], wn[6], wn[7]};
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty(s, st % nst));  // both groups of this stage are in registers
+        ++st;
+        const float2 ca = cst[g];
+        const float2 cb = two ? cst[g + 1] : make_float2(0.f, 0.f);
+        acc = fmaf(m0, ca.y, acc);
+        if (two) acc = fmaf(m1, cb.y, acc);
+        const int qq = qp0 + k, b = qq % kNP;
+        const bool epi = k >= kNP;
+        int h0 = 0, l0 = 0, h1 = 0, l1 = 0;
         ok = __all_sync(0xffffffffu, ok);  // tcgen05 loads / stores are warp-collective
-        if (epi && ok) {  // the group kNB back used this buffer: fetch its result once its MMAs are done
-          ok = __all_sync(0xffffffffu, mbar_wait(mdone(s, b), ((qq / kNB) - 1) & 1, ERR_TC_WAIT));
+        if (epi && ok) {  // the pair kNP back used this buffer: fetch its results once its MMAs are done
+          ok = __all_sync(0xffffffffu, mbar_wait(mdone(s, b), ((qq / kNP) - 1) & 1, ERR_TC_WAIT));
           if (ok) {
             mm4::tc_fence_after();
-            tmem_ld2(d_set + b * kDCols, dh, dl);
+            tmem_ld2(d_set + b * kDCols, h0, l0);
+            tmem_ld2(d_set + b * kDCols + 8, h1, l1);
           }
         }
-        if (ok) tmem_st32(a_set + b * kACols, o);
-        if (g + 1 < G) load_codes(g + 1);  // overlaps the tensor-memory load and store above
+        if (ok) {
+          uint32_t o[32];
+          unpack(w, o);
+          tmem_st32(a_set + b * kACols, o);
+          unpack(w + 4, o);
+          tmem_st32(a_set + b * kACols + 32, o);
+        }
+        if (k + 1 < npairs) load_codes(k + 1);  // overlaps the tensor-memory traffic above
         ok = __all_sync(0xffffffffu, ok);
         if (epi && ok) {
-          tmem_wait_ld(dh, dl);
-          acc = fmaf(pend[0], static_cast<float>(dh * 256 + dl), acc);
+          tmem_wait_ld(h0, l0);
+          tmem_wait_ld(h1, l1);
+          acc = fmaf(pa[0], static_cast<float>(h0 * 256 + l0), acc);
+          acc = fmaf(pb[0], static_cast<float>(h1 * 256 + l1), acc);
         }
         if (epi) {
-#pragma unroll
-          for (int i = 0; i + 1 < kNB; ++i) pend[i] = pend[i + 1];
-          pend[kNB - 1] = sv * c2.x;
+          pa[0] = pa[1];
+          pb[0] = pb[1];
+          pa[1] = s0 * ca.x;
+          pb[1] = two ? s1 * cb.x : 0.f;
+        } else if (k == 0) {
+          pa[0] = s0 * ca.x;
+          pb[0] = two ? s1 * cb.x : 0.f;
         } else {
-#pragma unroll
-          for (int i = 0; i < kNB; ++i)
-            if (i == g) pend[i] = sv * c2.x;
+          pa[1] = s0 * ca.x;
+          pb[1] = two ? s1 * cb.x : 0.f;
         }
         if (ok) {
           tmem_wait_st();
@@ -392,28 +411,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
             m8n = __ldg(reinterpret_cast<const uint4*>(mrow + g8 + 8));
           }
 #pragma unroll
-          for (int h = 0; h < 8; ++h) step(g8 + h, half_at(s8, h), half_at(m8, h));
+          for (int h = 0; h < 4; ++h)
+            step(g8 / 2 + h, half_at(s8, 2 * h), half_at(m8, 2 * h), half_at(s8, 2 * h + 1), half_at(m8, 2 * h + 1));
         }
       } else {
-        for (int g = 0; g < G; ++g)
-          step(g, __half2float(__ushort_as_half(__ldg(srow + g))), __half2float(__ushort_as_half(__ldg(mrow + g))));
+        for (int k = 0; k < npairs; ++k) {
+          const int g = 2 * k;
+          const bool two = g + 1 < G;
+          step(k, __half2float(__ushort_as_half(__ldg(srow + g))), __half2float(__ushort_as_half(__ldg(mrow + g))),
+               two ? __half2float(__ushort_as_half(__ldg(srow + g + 1))) : 0.f,
+               two ? __half2float(__ushort_as_half(__ldg(mrow + g + 1))) : 0.f);
+        }
       }
-      q += G;
-      // drain this block's last (up to) kNB groups, oldest first
-      const int nd = min(G, kNB);
+      q += npairs;
+      // drain this block's last (up to) kNP pairs, oldest first
+      const int nd = min(npairs, kNP);
 #pragma unroll
-      for (int i = 0; i < kNB; ++i) {
+      for (int i = 0; i < kNP; ++i) {
         if (i < nd) {
           const int qq = q - nd + i;
-          const int b = qq % kNB;
-          if (ok) ok = mbar_wait(mdone(s, b), (qq / kNB) & 1, ERR_TC_WAIT);
+          const int b = qq % kNP;
+          if (ok) ok = mbar_wait(mdone(s, b), (qq / kNP) & 1, ERR_TC_WAIT);
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
             mm4::tc_fence_after();
-            int dh, dl;
-            tmem_ld2(d_set + b * kDCols, dh, dl);
-            tmem_wait_ld(dh, dl);
-            acc = fmaf(pend[i], static_cast<float>(dh * 256 + dl), acc);
+            int h0, l0, h1, l1;
+            tmem_ld2(d_set + b * kDCols, h0, l0);
+            tmem_ld2(d_set + b * kDCols + 8, h1, l1);
+            tmem_wait_ld(h0, l0);
+            tmem_wait_ld(h1, l1);
+            acc = fmaf(pa[i], static_cast<float>(h0 * 256 + l0), acc);
+            acc = fmaf(pb[i], static_cast<float>(h1 * 256 + l1), acc);
           }
         }
       }
@@ -445,7 +473,7 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
     p.prefetch = (flags & RB_FLAG_PDL) && (flags & RB_FLAG_PREFETCH_WEIGHTS) ? 1 : 0;
     // instruction descriptor: D int32, A unsigned 8-bit, B signed 8-bit, both K-major, N = 8, M = 128
     p.idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((8u >> 3) << 17) | ((static_cast<uint32_t>(kRows) >> 4) << 24);
-    const uint32_t kBars = kSets * (2 * kMaxStages + 2 * kNB) * 8 + 16;
+    const uint32_t kBars = kSets * (2 * kMaxStages + 2 * kNP) * 8 + 16;
     int nslots = 0, blocks = 0, take = 0;
     uint32_t x_bytes = 0;
     for (; take < n; ++take) {
@@ -501,7 +529,7 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
     p.nst = nst;
     p.xs_off = static_cast<uint32_t>(kSets * nst) * kStageBytes;
     p.bar_off = (p.xs_off + xtot + 15) & ~15u;
-    const uint32_t smem = 1024 + p.bar_off + kSets * (2 * nst + 2 * kNB) * 8 + 16;
+    const uint32_t smem = 1024 + p.bar_off + kSets * (2 * nst + 2 * kNP) * 8 + 16;
     cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gemv_int4_tc_kernel), static_cast<int>(kSmemMax));
     if (e != cudaSuccess) return RB_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
