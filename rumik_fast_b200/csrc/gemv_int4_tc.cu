@@ -11,11 +11,12 @@
 //  * each converter set (four warps, one per tensor-memory lane quadrant, thread = weight row) unpacks one
 //    group of its row to unsigned 8-bit codes (three instructions per eight codes: no dequantisation at all,
 //    the codes 0..15 are the integer A operand) and writes the 32 columns to tensor memory (tcgen05.st);
-//  * one thread per set issues four tcgen05.mma.kind::i8 per group (K = 32 each): A = the codes in tensor
+//  * one thread per set issues four tcgen05.mma.kind::i8 per group (K = 32 each), eight per pair of groups
+//    (one TMA stage, the unit in which converters and MMA issuers synchronise): A = the codes in tensor
 //    memory (128 rows), B = the group's activations quantised to 16-bit integers and split into a signed
 //    high byte (B row 0) and a signed low byte (B row 1), read from shared memory by a K-major, no-swizzle
 //    descriptor; D = 128 x 8 int32 in tensor memory (columns 0 and 1 used), exact;
-//  * four groups later the converter reads its row's two accumulator columns (tcgen05.ld) and adds
+//  * two pairs later the converter reads its row's two accumulator columns per group (tcgen05.ld) and adds
 //    s * delta * (256 * D0 + D1) in fp32; m * sum(x) is added when the group is unpacked.
 // The activations are quantised per 128-column group with delta = max|x| / 32639 (relative error below
 // 2e-5 of the group's largest activation); the weights are used exactly. All mbarrier waits are bounded;
