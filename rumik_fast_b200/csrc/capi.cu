@@ -70,6 +70,16 @@ int rb_gemv_int4(const void* x, int x_dtype, int64_t ldx, const uint8_t* q, cons
   a.q = q; a.s = s; a.m = m;
   a.y = y; a.y_dtype = y_dtype; a.ldy = batch > 1 ? ldy : N;
   a.N = N; a.K = K; a.batch = batch; a.flags = flags;
+#ifndef RB_MULTI_LEGACY
+  // batch 1 with at least one 128-row block per SM: the tensor-core kernel (a one-entry list). Smaller
+  // matrices keep the warp-MMA kernel, which spreads 8-row stages over every SM.
+  if (batch == 1 && N >= static_cast<int64_t>(sms) * 128) {
+    rb_gemv_desc d = {x, y, q, s, m, N, K};
+    st = rb::launch_gemv_int4_tc(&d, 1, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream));
+    if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+    return st;
+  }
+#endif
   st = rb::launch_gemv_int4(a, sms, static_cast<cudaStream_t>(stream));
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;

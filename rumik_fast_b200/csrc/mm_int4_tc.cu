@@ -6,7 +6,8 @@
 //
 // Work items are (128-row weight block, token chunk of BT <= 128 tokens), block-major so that the CTAs working
 // at the same time on the chunks of one block share its codes through L2; items are dealt round-robin to one
-// CTA per SM and alternate between two converter sets. Per CTA:
+// CTA per SM. Both converter sets work on every item, set s on its groups g = s, s + 2, ..., each into its own
+// accumulator; the epilogue adds the two in a fixed order. Per CTA:
 //  * warp 0 (producer) streams, per item and group, the block's codes (TMA box 64 bytes x 128 rows, 64-byte
 //    swizzle) and the chunk's two 64-column X atoms (TMA, 128-byte swizzle) into the set's ring;
 //  * each converter set (four warps, thread = weight row = tensor-memory lane) dequantises its row's group
@@ -14,7 +15,7 @@
 //    min, one rounding) and writes the 64 columns to tensor memory (tcgen05.st);
 //  * one thread per set issues eight tcgen05.mma.kind::f16 per group (M = 128, N = BT, K = 16): A from tensor
 //    memory, B = the X atoms in shared memory, D = 128 x BT fp32 in tensor memory accumulating over all of K;
-//  * the converter warps then read D (tcgen05.ld) and store Y.
+//  * the converter warps then read D0 + D1 (tcgen05.ld; set s takes every other 32-column chunk) and store Y.
 // All mbarrier waits are bounded; no multicast, no clusters.
 #include "common.cuh"
 #include "kernels.h"
@@ -67,14 +68,14 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
   const int nst = p.nst, G = p.G, BT = p.BT;
   const int nlocal = (p.nitems - cta + C - 1) / C;  // this CTA's items: cta + j * C
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
-  const int per_set = 2 * nst + 2 * kNB + 2;
+  const int per_set = 2 * nst + 2 * kNB + 1;
   auto full = [&](int s, int i) { return bars + s * per_set + i; };
   auto empty = [&](int s, int i) { return bars + s * per_set + nst + i; };
   auto afull = [&](int s, int b) { return bars + s * per_set + 2 * nst + b; };
   auto mdone = [&](int s, int b) { return bars + s * per_set + 2 * nst + kNB + b; };
   auto dready = [&](int s) { return bars + s * per_set + 2 * nst + 2 * kNB; };
-  auto dfree = [&](int s) { return bars + s * per_set + 2 * nst + 2 * kNB + 1; };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kSets * per_set);
+  uint64_t* dfree = bars + kSets * per_set;  // both sets' epilogues have read both accumulators
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfree + 1);
   auto stage_of = [&](int s, int slot) { return smem + (static_cast<size_t>(s) * nst + slot) * p.stage_bytes; };
 
   if (tid == 0) {
@@ -88,8 +89,8 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
         mbar_init(mdone(s, b), 1);
       }
       mbar_init(dready(s), 1);
-      mbar_init(dfree(s), 4);
     }
+    mbar_init(dfree, 4 * kSets);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -109,16 +110,13 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
     // ---------------- producer ----------------
     if (lane == 0) {
       griddep_wait();  // X may come from the previous kernel
-      int j[kSets], g[kSets], issued[kSets];
-      for (int s = 0; s < kSets; ++s) j[s] = s, g[s] = 0, issued[s] = 0;
-      bool ok = true, any = true;
-      while (any && ok) {
-        any = false;
-        for (int s = 0; s < kSets && ok; ++s) {
-          if (j[s] >= nlocal) continue;
-          any = true;
-          const int item = cta + j[s] * C;
-          const int row0 = (item / p.nchunks) * kRows, t0 = (item % p.nchunks) * BT;
+      int issued[kSets] = {};
+      bool ok = true;
+      for (int j = 0; j < nlocal && ok; ++j) {
+        const int item = cta + j * C;
+        const int row0 = (item / p.nchunks) * kRows, t0 = (item % p.nchunks) * BT;
+        for (int g = 0; g < G && ok; ++g) {
+          const int s = g % kSets;
           const int slot = issued[s] % nst;
           if (issued[s] >= nst && !mbar_wait(empty(s, slot), ((issued[s] / nst) - 1) & 1, ERR_MM4_WAIT)) {
             ok = false;
@@ -126,11 +124,10 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
           }
           uint8_t* st = stage_of(s, slot);
           mbar_arrive_expect_tx(full(s, slot), stage_tx);
-          mm4::tma_load_2d(st, &p.qmap, g[s] * 64, row0, full(s, slot));
-          mm4::tma_load_2d(st + kCodeBytes, &p.xmap, g[s] * 128, t0, full(s, slot));
-          mm4::tma_load_2d(st + kCodeBytes + BT * 128, &p.xmap, g[s] * 128 + 64, t0, full(s, slot));
+          mm4::tma_load_2d(st, &p.qmap, g * 64, row0, full(s, slot));
+          mm4::tma_load_2d(st + kCodeBytes, &p.xmap, g * 128, t0, full(s, slot));
+          mm4::tma_load_2d(st + kCodeBytes + BT * 128, &p.xmap, g * 128 + 64, t0, full(s, slot));
           ++issued[s];
-          if (++g[s] == G) g[s] = 0, j[s] += kSets;
         }
       }
       for (int s = 0; s < kSets; ++s)  // no retirement with copies in flight
@@ -142,11 +139,11 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
     const int s = warp - 1;
     if (lane == 0) {
       const uint32_t d_col = tmem + s * kSetCols + kNB * kACols;
-      int q = 0, used = 0, n = 0;
+      int q = 0, used = 0;
       bool ok = true;
-      for (int jj = s; jj < nlocal && ok; jj += kSets, ++n) {
-        if (n >= 1 && !mbar_wait(dfree(s), (n - 1) & 1, ERR_MM4_WAIT)) break;  // D read by the last epilogue
-        for (int gg = 0; gg < G; ++gg, ++q, ++used) {
+      for (int jj = 0; jj < nlocal && ok; ++jj) {
+        if (jj >= 1 && !mbar_wait(dfree, (jj - 1) & 1, ERR_MM4_WAIT)) break;  // D read by the last epilogue
+        for (int gg = s; gg < G; gg += kSets, ++q, ++used) {
           const int b = q % kNB, slot = used % nst;
           if (!mbar_wait(afull(s, b), (q / kNB) & 1, ERR_MM4_WAIT) ||
               !mbar_wait(full(s, slot), (used / nst) & 1, ERR_MM4_WAIT)) {
@@ -158,11 +155,11 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
 #pragma unroll
           for (int i = 0; i < 8; ++i)
             umma_ts_f16(d_col, tmem + s * kSetCols + b * kACols + 8 * i,
-                        mm4::sw128_desc(xb + (i >> 2) * BT * 128 + (i & 3) * 32), p.idesc, (gg | i) != 0);
+                        mm4::sw128_desc(xb + (i >> 2) * BT * 128 + (i & 3) * 32), p.idesc, (gg >= kSets) || i != 0);
           mm4::umma_commit(mdone(s, b));     // A buffer b may be rewritten
           mm4::umma_commit(empty(s, slot));  // the stage's X atoms may be refilled
         }
-        if (ok) mm4::umma_commit(dready(s));
+        if (ok) mm4::umma_commit(dready(s));  // (with no group of this set in the item, arrives at once)
       }
     }
   } else {
@@ -172,23 +169,27 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
     const int quad = warp & 3;
     const int rib = quad * 32 + lane;
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    const uint32_t a_set = tq + s * kSetCols, d_set = tq + s * kSetCols + kNB * kACols;
+    const uint32_t a_set = tq + s * kSetCols;
     const uint32_t magic = 0x54006400u, mask = 0x00F0000Fu;  // (1024 | low nibble, 64 | high nibble << 4)
     griddep_wait();  // Y may still be read by the previous kernel
-    int q = 0, used = 0, n = 0;
+    int q = 0, used = 0;
     bool ok = true;
-    for (int jj = s; jj < nlocal; jj += kSets, ++n) {
+    for (int jj = 0; jj < nlocal; ++jj) {
       const int item = cta + jj * C;
       const int row = (item / p.nchunks) * kRows + rib, t0 = (item % p.nchunks) * BT;
       const bool row_ok = row < p.N;
       const uint16_t* srow = p.s + static_cast<int64_t>(row_ok ? row : 0) * G;
       const uint16_t* mrow = p.m + static_cast<int64_t>(row_ok ? row : 0) * G;
-      uint16_t s_next = __ldg(srow), m_next = __ldg(mrow);
-      for (int gg = 0; gg < G; ++gg, ++q, ++used) {
+      uint16_t s_next = 0, m_next = 0;
+      if (s < G) {
+        s_next = __ldg(srow + s);
+        m_next = __ldg(mrow + s);
+      }
+      for (int gg = s; gg < G; gg += kSets, ++q, ++used) {
         const uint16_t s16 = s_next, m16 = m_next;
-        if (gg + 1 < G) {  // the next group's scale and min
-          s_next = __ldg(srow + gg + 1);
-          m_next = __ldg(mrow + gg + 1);
+        if (gg + kSets < G) {  // the set's next group's scale and min
+          s_next = __ldg(srow + gg + kSets);
+          m_next = __ldg(mrow + gg + kSets);
         }
         const int slot = used % nst;
         if (ok) ok = mbar_wait(full(s, slot), (used / nst) & 1, ERR_MM4_WAIT);
@@ -228,24 +229,33 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
         __syncwarp();
         if (lane == 0) mbar_arrive(afull(s, b));
       }
-      // ---- epilogue of this item ----
-      if (ok) ok = mbar_wait(dready(s), n & 1, ERR_MM4_WAIT);
+      // ---- epilogue of this item: D0 + D1 in that order; set s stores every other 32-column chunk ----
+      for (int t = 0; t < kSets; ++t)
+        if (ok) ok = mbar_wait(dready(t), jj & 1, ERR_MM4_WAIT);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         mm4::tc_fence_after();
-        for (int c0 = 0; c0 < BT; c0 += 32) {
-          uint32_t v[32];
-          tmem_ld32(d_set + c0, v);
+        for (int c0 = 32 * s; c0 < BT; c0 += 32 * kSets) {
+          float acc[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+          for (int t = 0; t < kSets; ++t) {
+            if (t >= G) break;  // that set had no group in this item
+            uint32_t v[32];
+            tmem_ld32(tq + t * kSetCols + kNB * kACols + c0, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(v[i]);
+          }
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int t = t0 + c0 + i;  // columns past BT belong to no token of this chunk
-            if (row_ok && c0 + i < BT && t < p.M) store_out(p.y, static_cast<int64_t>(t) * p.ldy + row, __uint_as_float(v[i]), p.y_bf16);
+            const int tok = t0 + c0 + i;  // columns past BT belong to no token of this chunk
+            if (row_ok && c0 + i < BT && tok < p.M) store_out(p.y, static_cast<int64_t>(tok) * p.ldy + row, acc[i], p.y_bf16);
           }
         }
         mm4::tc_fence_before();
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(dfree(s));
+      if (lane == 0) mbar_arrive(dfree);
     }
   }
   mm4::tc_fence_before();
@@ -291,7 +301,7 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   p.bar_off = static_cast<uint32_t>(kSets * nst) * p.stage_bytes;
   // instruction descriptor: D f32, A f16, B f16, both K-major, N = BT, M = 128
   p.idesc = (1u << 4) | (static_cast<uint32_t>(BT >> 3) << 17) | (static_cast<uint32_t>(kRows >> 4) << 24);
-  const uint32_t smem = 1024 + p.bar_off + kSets * (2 * nst + 2 * kNB + 2) * 8 + 16;
+  const uint32_t smem = 1024 + p.bar_off + (kSets * (2 * nst + 2 * kNB + 1) + 1) * 8 + 16;
   {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(N)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K / 2)};
