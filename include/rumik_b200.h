@@ -94,6 +94,19 @@ int rb_mm_int4(const void* X, int x_dtype, int64_t ldx,
                void* Y, int y_dtype, int64_t ldy,
                int64_t M, int64_t N, int64_t K, int flags, void* stream);
 
+/*
+ * The same product with a caller-provided fp32 workspace, which lets a call whose 128-row x token-chunk tiles
+ * would leave SMs idle (small N or few tokens) split K into slices: every slice writes its fp32 partial to the
+ * workspace and a second kernel adds the slices in slice order into Y (deterministic). rb_mm_int4_workspace
+ * returns the bytes this needs for (M, N, K) on the current device (0: no split, ws may be NULL); a smaller
+ * workspace runs the call without a split.
+ */
+int64_t rb_mm_int4_workspace(int64_t M, int64_t N, int64_t K);
+int rb_mm_int4_ws(const void* X, int x_dtype, int64_t ldx,
+                  const uint8_t* q, const uint16_t* s, const uint16_t* m,
+                  void* Y, int y_dtype, int64_t ldy,
+                  int64_t M, int64_t N, int64_t K, void* ws, int64_t ws_bytes, int flags, void* stream);
+
 /* One int4 GEMV of a list (host-side description, read by rb_gemv_int4_multi during the call). */
 typedef struct rb_gemv_desc {
   const void* x;        /* activations [K] (dtype x_dtype of the call), 16-byte aligned */

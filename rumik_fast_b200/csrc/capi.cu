@@ -136,8 +136,9 @@ int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_
   return st;
 }
 
-int rb_mm_int4(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const uint16_t* s, const uint16_t* m,
-               void* Y, int y_dtype, int64_t ldy, int64_t M, int64_t N, int64_t K, int flags, void* stream) {
+static int mm_int4_impl(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const uint16_t* s,
+                        const uint16_t* m, void* Y, int y_dtype, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                        void* ws, int64_t ws_bytes, int flags, void* stream) {
   if (M < 0 || N < 0 || K <= 0) return RB_ERR_SHAPE;
   if (K % 128 != 0 || N > (int64_t(1) << 30) || M > (int64_t(1) << 30)) return RB_ERR_SHAPE;
   if (M == 0 || N == 0) return RB_OK;
@@ -146,6 +147,7 @@ int rb_mm_int4(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const 
   if (ldx < K || ldy < N) return RB_ERR_SHAPE;
   if (!aligned16(X) || !aligned16(Y) || (ldx % 8) != 0 || (ldy % 8) != 0) return RB_ERR_ALIGN;
   if (!aligned16(q) || !aligned16(s) || !aligned16(m)) return RB_ERR_ALIGN;
+  if (ws && !aligned16(ws)) return RB_ERR_ALIGN;
   int sms = 0, st = device_sms(&sms);
   if (st != RB_OK) return st;
   rb::MmArgs a = {};
@@ -153,6 +155,7 @@ int rb_mm_int4(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const 
   a.q = q; a.s = s; a.m = m;
   a.Y = Y; a.y_dtype = y_dtype; a.ldy = ldy;
   a.M = M; a.N = N; a.K = K; a.flags = flags;
+  a.ws = static_cast<float*>(ws); a.ws_bytes = ws ? ws_bytes : 0;
 #ifdef RB_MM_LEGACY  // dequantisation into shared memory, one CTA per tile (comparison builds)
   st = rb::launch_mm_int4(a, sms, static_cast<cudaStream_t>(stream));
 #else
@@ -160,6 +163,23 @@ int rb_mm_int4(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const 
 #endif
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
+}
+
+int rb_mm_int4(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const uint16_t* s, const uint16_t* m,
+               void* Y, int y_dtype, int64_t ldy, int64_t M, int64_t N, int64_t K, int flags, void* stream) {
+  return mm_int4_impl(X, x_dtype, ldx, q, s, m, Y, y_dtype, ldy, M, N, K, nullptr, 0, flags, stream);
+}
+
+int64_t rb_mm_int4_workspace(int64_t M, int64_t N, int64_t K) {
+  int sms = 0;
+  if (M <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || device_sms(&sms) != RB_OK) return 0;
+  return rb::mm_int4_tc_workspace(M, N, K, sms);
+}
+
+int rb_mm_int4_ws(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const uint16_t* s, const uint16_t* m,
+                  void* Y, int y_dtype, int64_t ldy, int64_t M, int64_t N, int64_t K, void* ws, int64_t ws_bytes,
+                  int flags, void* stream) {
+  return mm_int4_impl(X, x_dtype, ldx, q, s, m, Y, y_dtype, ldy, M, N, K, ws, ws_bytes, flags, stream);
 }
 
 int rb_tp_allreduce_f16(const void* a, const void* b, void* out, int64_t n, void* const* bufs, int rank, int world,

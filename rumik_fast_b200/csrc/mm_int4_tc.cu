@@ -4,7 +4,7 @@
 // The operation of rumik-fast's Triton kernel _mm_int4 (kernels/mm_int4.py:24-46) and its wrapper mm_int4
 // (:59-73): w = code * s + m in the int4 group-128 layout, X fp16 [M, K], fp32 accumulation.
 //
-// Work items are (128-row weight block, token chunk of BT <= 128 tokens), block-major so that the CTAs working
+// Work items are (128-row weight block, token chunk of BT <= 128 tokens, K slice), block-major so that the CTAs working
 // at the same time on the chunks of one block share its codes through L2; items are dealt round-robin to one
 // CTA per SM. Both converter sets work on every item, set s on its groups g = s, s + 2, ..., each into its own
 // accumulator; the epilogue adds the two in a fixed order. Per CTA:
@@ -15,7 +15,9 @@
 //    min, one rounding) and writes the 64 columns to tensor memory (tcgen05.st);
 //  * one thread per set issues eight tcgen05.mma.kind::f16 per group (M = 128, N = BT, K = 16): A from tensor
 //    memory, B = the X atoms in shared memory, D = 128 x BT fp32 in tensor memory accumulating over all of K;
-//  * the converter warps then read D0 + D1 (tcgen05.ld; set s takes every other 32-column chunk) and store Y.
+//  * the converter warps then read D0 + D1 (tcgen05.ld; set s takes every other 32-column chunk) and store Y,
+//    or, when K is split into slices (a call with fewer row-block x chunk items than SMs), the slice's fp32
+//    partial into a caller-provided workspace; mm_int4_reduce then adds the slices in slice order.
 // All mbarrier waits are bounded; no multicast, no clusters.
 #include "common.cuh"
 #include "kernels.h"
@@ -42,7 +44,8 @@ struct __align__(64) MmtParams {
   const uint16_t* m;
   void* y;
   int64_t ldy;
-  int M, N, K, G, BT, nchunks, nitems, y_bf16, nst, prefetch;
+  float* ws;  // [kslices][M][N] fp32 partials when kslices > 1
+  int M, N, K, G, BT, nchunks, kslices, gps, nitems, y_bf16, nst, prefetch;
   uint32_t stage_bytes, bar_off, idesc;
 };
 
@@ -109,22 +112,45 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
+      // The codes do not depend on the previous kernel: the first stages' code loads go out before
+      // griddepcontrol.wait (overlapping the previous kernel's tail); X loads only after it.
+      int pre[kSets] = {};
+      for (int j = 0; j < nlocal; ++j) {
+        const int item = cta + j * C;
+        const int rem = item % (p.nchunks * p.kslices);
+        const int row0 = (item / (p.nchunks * p.kslices)) * kRows;
+        const int g0 = (rem % p.kslices) * p.gps, g1 = min(G, g0 + p.gps);
+        bool room = false;
+        for (int g = g0; g < g1; ++g) {
+          const int s = (g - g0) % kSets;
+          if (pre[s] >= nst) continue;
+          room = true;
+          const int slot = pre[s]++;
+          mbar_arrive_expect_tx(full(s, slot), stage_tx);
+          mm4::tma_load_2d(stage_of(s, slot), &p.qmap, g * 64, row0, full(s, slot));
+        }
+        if (!room) break;
+      }
       griddep_wait();  // X may come from the previous kernel
       int issued[kSets] = {};
       bool ok = true;
       for (int j = 0; j < nlocal && ok; ++j) {
         const int item = cta + j * C;
-        const int row0 = (item / p.nchunks) * kRows, t0 = (item % p.nchunks) * BT;
-        for (int g = 0; g < G && ok; ++g) {
-          const int s = g % kSets;
+        const int rem = item % (p.nchunks * p.kslices);
+        const int row0 = (item / (p.nchunks * p.kslices)) * kRows, t0 = (rem / p.kslices) * BT;
+        const int g0 = (rem % p.kslices) * p.gps, g1 = min(G, g0 + p.gps);
+        for (int g = g0; g < g1 && ok; ++g) {
+          const int s = (g - g0) % kSets;
           const int slot = issued[s] % nst;
-          if (issued[s] >= nst && !mbar_wait(empty(s, slot), ((issued[s] / nst) - 1) & 1, ERR_MM4_WAIT)) {
-            ok = false;
-            break;
-          }
           uint8_t* st = stage_of(s, slot);
-          mbar_arrive_expect_tx(full(s, slot), stage_tx);
-          mm4::tma_load_2d(st, &p.qmap, g * 64, row0, full(s, slot));
+          if (issued[s] >= pre[s]) {
+            if (issued[s] >= nst && !mbar_wait(empty(s, slot), ((issued[s] / nst) - 1) & 1, ERR_MM4_WAIT)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(full(s, slot), stage_tx);
+            mm4::tma_load_2d(st, &p.qmap, g * 64, row0, full(s, slot));
+          }
           mm4::tma_load_2d(st + kCodeBytes, &p.xmap, g * 128, t0, full(s, slot));
           mm4::tma_load_2d(st + kCodeBytes + BT * 128, &p.xmap, g * 128 + 64, t0, full(s, slot));
           ++issued[s];
@@ -143,7 +169,9 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
       bool ok = true;
       for (int jj = 0; jj < nlocal && ok; ++jj) {
         if (jj >= 1 && !mbar_wait(dfree, (jj - 1) & 1, ERR_MM4_WAIT)) break;  // D read by the last epilogue
-        for (int gg = s; gg < G; gg += kSets, ++q, ++used) {
+        const int item = cta + jj * C;
+        const int g0 = (item % (p.nchunks * p.kslices) % p.kslices) * p.gps, g1 = min(G, g0 + p.gps);
+        for (int gg = g0 + s; gg < g1; gg += kSets, ++q, ++used) {
           const int b = q % kNB, slot = used % nst;
           if (!mbar_wait(afull(s, b), (q / kNB) & 1, ERR_MM4_WAIT) ||
               !mbar_wait(full(s, slot), (used / nst) & 1, ERR_MM4_WAIT)) {
@@ -155,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
 #pragma unroll
           for (int i = 0; i < 8; ++i)
             umma_ts_f16(d_col, tmem + s * kSetCols + b * kACols + 8 * i,
-                        mm4::sw128_desc(xb + (i >> 2) * BT * 128 + (i & 3) * 32), p.idesc, (gg >= kSets) || i != 0);
+                        mm4::sw128_desc(xb + (i >> 2) * BT * 128 + (i & 3) * 32), p.idesc, (gg - g0 >= kSets) || i != 0);
           mm4::umma_commit(mdone(s, b));     // A buffer b may be rewritten
           mm4::umma_commit(empty(s, slot));  // the stage's X atoms may be refilled
         }
@@ -171,23 +199,25 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t a_set = tq + s * kSetCols;
     const uint32_t magic = 0x54006400u, mask = 0x00F0000Fu;  // (1024 | low nibble, 64 | high nibble << 4)
-    griddep_wait();  // Y may still be read by the previous kernel
+    bool waited = false;  // griddepcontrol.wait before the first write of Y or of the workspace
     int q = 0, used = 0;
     bool ok = true;
     for (int jj = 0; jj < nlocal; ++jj) {
       const int item = cta + jj * C;
-      const int row = (item / p.nchunks) * kRows + rib, t0 = (item % p.nchunks) * BT;
+      const int rem = item % (p.nchunks * p.kslices);
+      const int row = (item / (p.nchunks * p.kslices)) * kRows + rib, t0 = (rem / p.kslices) * BT;
+      const int ks = rem % p.kslices, g0 = ks * p.gps, g1 = min(G, g0 + p.gps);
       const bool row_ok = row < p.N;
       const uint16_t* srow = p.s + static_cast<int64_t>(row_ok ? row : 0) * G;
       const uint16_t* mrow = p.m + static_cast<int64_t>(row_ok ? row : 0) * G;
       uint16_t s_next = 0, m_next = 0;
-      if (s < G) {
-        s_next = __ldg(srow + s);
-        m_next = __ldg(mrow + s);
+      if (g0 + s < g1) {
+        s_next = __ldg(srow + g0 + s);
+        m_next = __ldg(mrow + g0 + s);
       }
-      for (int gg = s; gg < G; gg += kSets, ++q, ++used) {
+      for (int gg = g0 + s; gg < g1; gg += kSets, ++q, ++used) {
         const uint16_t s16 = s_next, m16 = m_next;
-        if (gg + kSets < G) {  // the set's next group's scale and min
+        if (gg + kSets < g1) {  // the set's next group's scale and min
           s_next = __ldg(srow + gg + kSets);
           m_next = __ldg(mrow + gg + kSets);
         }
@@ -230,6 +260,10 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
         if (lane == 0) mbar_arrive(afull(s, b));
       }
       // ---- epilogue of this item: D0 + D1 in that order; set s stores every other 32-column chunk ----
+      if (!waited) {
+        griddep_wait();  // Y (and a reused workspace) may still be read by the previous kernel
+        waited = true;
+      }
       for (int t = 0; t < kSets; ++t)
         if (ok) ok = mbar_wait(dready(t), jj & 1, ERR_MM4_WAIT);
       ok = __all_sync(0xffffffffu, ok);
@@ -240,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
 #pragma unroll
           for (int i = 0; i < 32; ++i) acc[i] = 0.f;
           for (int t = 0; t < kSets; ++t) {
-            if (t >= G) break;  // that set had no group in this item
+            if (t >= g1 - g0) break;  // that set had no group in this item
             uint32_t v[32];
             tmem_ld32(tq + t * kSetCols + kNB * kACols + c0, v);
 #pragma unroll
@@ -249,7 +283,12 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int tok = t0 + c0 + i;  // columns past BT belong to no token of this chunk
-            if (row_ok && c0 + i < BT && tok < p.M) store_out(p.y, static_cast<int64_t>(tok) * p.ldy + row, acc[i], p.y_bf16);
+            if (row_ok && c0 + i < BT && tok < p.M) {
+              if (p.kslices == 1)
+                store_out(p.y, static_cast<int64_t>(tok) * p.ldy + row, acc[i], p.y_bf16);
+              else
+                p.ws[(static_cast<int64_t>(ks) * p.M + tok) * p.N + row] = acc[i];
+            }
           }
         }
         mm4::tc_fence_before();
@@ -266,7 +305,46 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
   }
 }
 
+// Y[t, n] = sum over slices (in slice order) of ws[slice][t][n].
+__global__ void __launch_bounds__(256) mm_int4_reduce_kernel(const float* ws, void* y, int64_t ldy, int M, int N,
+                                                             int kslices, int y_bf16) {
+  griddep_wait();
+  const int64_t total = static_cast<int64_t>(M) * N;
+  for (int64_t i = blockIdx.x * 256 + threadIdx.x; i < total; i += static_cast<int64_t>(gridDim.x) * 256) {
+    float acc = 0.f;
+    for (int k = 0; k < kslices; ++k) acc += ws[k * total + i];
+    const int64_t t = i / N, n = i - t * N;
+    store_out(y, t * ldy + n, acc, y_bf16);
+  }
+}
+
+// Token chunking and K slicing of a call: chunks of <= 128 tokens; K is split into slices (>= 2 groups each)
+// when the row-block x chunk items would leave SMs idle.
+struct MmPlan {
+  int BT, nchunks, kslices, gps;
+};
+inline MmPlan mm_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
+  MmPlan pl;
+  const int nch = static_cast<int>((M + 127) / 128);
+  int BT = static_cast<int>((M + nch - 1) / nch);
+  pl.BT = std::max(16, (BT + 15) / 16 * 16);
+  pl.nchunks = static_cast<int>((M + pl.BT - 1) / pl.BT);
+  const int G = static_cast<int>(K / 128);
+  const int items = static_cast<int>((N + kRows - 1) / kRows) * pl.nchunks;
+  int ks = 1;
+  if (2 * items <= num_sms) ks = std::min(num_sms / items, G / 2);  // at most one wave of items
+  ks = std::max(ks, 1);
+  pl.gps = (G + ks - 1) / ks;
+  pl.kslices = (G + pl.gps - 1) / pl.gps;
+  return pl;
+}
+
 }  // namespace mm4t
+
+int64_t mm_int4_tc_workspace(int64_t M, int64_t N, int64_t K, int num_sms) {
+  const mm4t::MmPlan pl = mm4t::mm_plan(M, N, K, num_sms);
+  return pl.kslices > 1 ? static_cast<int64_t>(pl.kslices) * M * N * 4 : 0;
+}
 
 int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   using namespace mm4t;
@@ -274,11 +352,16 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   auto encode = mm4::encode_fn();
   if (!encode) return RB_ERR_DEVICE;
   const int M = static_cast<int>(a.M), N = static_cast<int>(a.N), K = static_cast<int>(a.K);
-  // token chunks of at most 128 (multiples of 16)
-  const int nch = (M + 127) / 128;
-  int BT = (M + nch - 1) / nch;
-  BT = std::max(16, (BT + 15) / 16 * 16);
+  MmPlan pl = mm_plan(M, N, K, num_sms);
+  if (pl.kslices > 1 && (!a.ws || a.ws_bytes < static_cast<int64_t>(pl.kslices) * M * N * 4)) {
+    pl.kslices = 1;  // no (or too small a) workspace: no split
+    pl.gps = K / 128;
+  }
+  const int BT = pl.BT;
   MmtParams p;
+  p.ws = a.ws;
+  p.kslices = pl.kslices;
+  p.gps = pl.gps;
   p.s = a.s;
   p.m = a.m;
   p.y = a.Y;
@@ -288,8 +371,8 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   p.K = K;
   p.G = K / 128;
   p.BT = BT;
-  p.nchunks = (M + BT - 1) / BT;
-  p.nitems = ((N + kRows - 1) / kRows) * p.nchunks;
+  p.nchunks = pl.nchunks;
+  p.nitems = ((N + kRows - 1) / kRows) * p.nchunks * p.kslices;
   p.y_bf16 = a.y_dtype == RB_BF16;
   p.prefetch = 0;
   p.stage_bytes = (kCodeBytes + 2u * BT * 128u + 1023u) & ~1023u;
@@ -335,7 +418,20 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, mm_int4_tc_kernel, p);
-  return e == cudaSuccess ? RB_OK : RB_ERR_LAUNCH;
+  if (e != cudaSuccess) return RB_ERR_LAUNCH;
+  if (p.kslices > 1) {
+    cudaLaunchConfig_t rc = {};
+    const int64_t total = static_cast<int64_t>(M) * N;
+    rc.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 4 * num_sms)));
+    rc.blockDim = dim3(256);
+    rc.stream = stream;
+    rc.attrs = attr;
+    rc.numAttrs = 1;
+    e = cudaLaunchKernelEx(&rc, mm_int4_reduce_kernel, static_cast<const float*>(p.ws), a.Y, a.ldy, M, N,
+                           p.kslices, p.y_bf16);
+    if (e != cudaSuccess) return RB_ERR_LAUNCH;
+  }
+  return RB_OK;
 }
 
 }  // namespace rb

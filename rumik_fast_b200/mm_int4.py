@@ -37,9 +37,13 @@ def mm_int4(x, q, s, m, BM=None, BN=64, num_warps=4, num_stages=3, out=None):
     _require(y.shape == (T, N) and y.stride(1) == 1, "out must be [T, N] with unit column stride")
     L = _lib.lib()
     with _on_device(x.device):
-        st = L.rb_mm_int4(x.data_ptr(), _lib.dtype_code(x.dtype), x.stride(0), q.data_ptr(), s.data_ptr(),
-                          m.data_ptr(), y.data_ptr(), _lib.dtype_code(y.dtype), y.stride(0), T, N, K,
-                          config.flags(), _lib.stream_ptr(x.device))
+        # a call with few 128-row x token-chunk tiles splits K over the idle SMs through an fp32 workspace
+        ws_bytes = L.rb_mm_int4_workspace(T, N, K)
+        ws = torch.empty(ws_bytes // 4, device=x.device, dtype=torch.float32) if ws_bytes > 0 else None
+        st = L.rb_mm_int4_ws(x.data_ptr(), _lib.dtype_code(x.dtype), x.stride(0), q.data_ptr(), s.data_ptr(),
+                             m.data_ptr(), y.data_ptr(), _lib.dtype_code(y.dtype), y.stride(0), T, N, K,
+                             None if ws is None else ws.data_ptr(), ws_bytes, config.flags(),
+                             _lib.stream_ptr(x.device))
     _lib.check("rb_mm_int4", st)
     return y
 
