@@ -102,6 +102,19 @@ int rb_mm_int4(const void* X, int x_dtype, int64_t ldx,
  * workspace runs the call without a split.
  */
 int64_t rb_mm_int4_workspace(int64_t M, int64_t N, int64_t K);
+
+/*
+ * rb_mm_int4_ws for callers that cannot allocate device memory: the split-K partials go to a file-scope
+ * `static __device__` scratch array of 8 MiB (8,388,608 bytes) inside this library, so the call allocates
+ * nothing. Returns RB_ERR_SHAPE when the split it would use needs more than 8 MiB
+ * (rb_mm_int4_workspace(M, N, K) > 8 MiB); nothing in the scratch needs to start at zero. The scratch is one
+ * per device and shared by every call: calls that overlap in time (on two streams, or otherwise not ordered
+ * one after the other) race on it. Consecutive calls on one stream are safe.
+ */
+int rb_mm_int4_static(const void* X, int x_dtype, int64_t ldx,
+                      const uint8_t* q, const uint16_t* s, const uint16_t* m,
+                      void* Y, int y_dtype, int64_t ldy,
+                      int64_t M, int64_t N, int64_t K, int flags, void* stream);
 int rb_mm_int4_ws(const void* X, int x_dtype, int64_t ldx,
                   const uint8_t* q, const uint16_t* s, const uint16_t* m,
                   void* Y, int y_dtype, int64_t ldy,

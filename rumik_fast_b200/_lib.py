@@ -32,6 +32,7 @@ SIGNATURES = {
     "rb_gemv_int8": (_int, [_vp, _int, _i64, _vp, _int, _vp, _int, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
     "rb_mm_int4": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
     "rb_mm_int4_workspace": (_i64, [_i64, _i64, _i64]),
+    "rb_mm_int4_static": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
     "rb_mm_int4_ws": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _vp, _i64, _int, _vp]),
     "rb_gemv_int4_multi": (_int, [_c.POINTER(GemvDesc), _int, _int, _int, _int, _vp]),
     "rb_status_string": (_c.c_char_p, [_int]),

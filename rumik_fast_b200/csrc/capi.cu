@@ -138,7 +138,7 @@ int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_
 
 static int mm_int4_impl(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const uint16_t* s,
                         const uint16_t* m, void* Y, int y_dtype, int64_t ldy, int64_t M, int64_t N, int64_t K,
-                        void* ws, int64_t ws_bytes, int flags, void* stream) {
+                        void* ws, int64_t ws_bytes, int flags, void* stream, bool static_scratch = false) {
   if (M < 0 || N < 0 || K <= 0) return RB_ERR_SHAPE;
   if (K % 128 != 0 || N > (int64_t(1) << 30) || M > (int64_t(1) << 30)) return RB_ERR_SHAPE;
   if (M == 0 || N == 0) return RB_OK;
@@ -156,6 +156,11 @@ static int mm_int4_impl(const void* X, int x_dtype, int64_t ldx, const uint8_t* 
   a.Y = Y; a.y_dtype = y_dtype; a.ldy = ldy;
   a.M = M; a.N = N; a.K = K; a.flags = flags;
   a.ws = static_cast<float*>(ws); a.ws_bytes = ws ? ws_bytes : 0;
+  if (static_scratch) {
+    st = rb::launch_mm_int4_tc_static(a, sms, static_cast<cudaStream_t>(stream));
+    if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+    return st;
+  }
 #ifdef RB_MM_LEGACY  // dequantisation into shared memory, one CTA per tile (comparison builds)
   st = rb::launch_mm_int4(a, sms, static_cast<cudaStream_t>(stream));
 #else
@@ -180,6 +185,12 @@ int rb_mm_int4_ws(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, con
                   void* Y, int y_dtype, int64_t ldy, int64_t M, int64_t N, int64_t K, void* ws, int64_t ws_bytes,
                   int flags, void* stream) {
   return mm_int4_impl(X, x_dtype, ldx, q, s, m, Y, y_dtype, ldy, M, N, K, ws, ws_bytes, flags, stream);
+}
+
+int rb_mm_int4_static(const void* X, int x_dtype, int64_t ldx, const uint8_t* q, const uint16_t* s, const uint16_t* m,
+                      void* Y, int y_dtype, int64_t ldy, int64_t M, int64_t N, int64_t K, int flags, void* stream) {
+  if (x_dtype != RB_F16 && x_dtype != RB_BF16) return RB_ERR_DTYPE;
+  return mm_int4_impl(X, x_dtype, ldx, q, s, m, Y, y_dtype, ldy, M, N, K, nullptr, 0, flags, stream, true);
 }
 
 int rb_tp_allreduce_f16(const void* a, const void* b, void* out, int64_t n, void* const* bufs, int rank, int world,

@@ -49,6 +49,7 @@ int launch_gemv_int8_tc(const GemvArgs& a, int num_sms, cudaStream_t stream);
 int launch_mm_int4(const MmArgs& a, int num_sms, cudaStream_t stream);
 int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream);
 int64_t mm_int4_tc_workspace(int64_t M, int64_t N, int64_t K, int num_sms);
+int launch_mm_int4_tc_static(MmArgs a, int num_sms, cudaStream_t stream);
 int launch_tp_allreduce(const __half* a, const __half* b, __half* out, int64_t n, void* const* bufs, int rank,
                         int world, uint32_t flag_off, uint32_t counter_off, int flags, cudaStream_t stream);
 int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,

@@ -341,6 +341,14 @@ inline MmPlan mm_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
 
 }  // namespace mm4t
 
+// Scratch of the no-allocation entry point (rb_mm_int4_static): the split-K partials live in this file-scope
+// array instead of a caller-provided workspace. 8 MiB bounds calls to kslices * M * N * 4 <= 8 MiB (e.g. the
+// M = 34 prefill of every config-1 matrix needs at most 2.5 MiB). Every element a reduce reads is written by
+// the same call first, so nothing needs to start at zero. The array is shared: calls that overlap in time
+// (two streams, or two calls in flight without stream order) race on it.
+constexpr int64_t kStaticScratchBytes = int64_t(8) << 20;
+static __device__ __align__(256) float g_mm_scratch[kStaticScratchBytes / 4];
+
 int64_t mm_int4_tc_workspace(int64_t M, int64_t N, int64_t K, int num_sms) {
   const mm4t::MmPlan pl = mm4t::mm_plan(M, N, K, num_sms);
   return pl.kslices > 1 ? static_cast<int64_t>(pl.kslices) * M * N * 4 : 0;
@@ -432,6 +440,32 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
     if (e != cudaSuccess) return RB_ERR_LAUNCH;
   }
   return RB_OK;
+}
+
+// rb_mm_int4_static: the split-K scratch from g_mm_scratch; allocates nothing. RB_ERR_SHAPE when the call's
+// split would need more than kStaticScratchBytes.
+int launch_mm_int4_tc_static(MmArgs a, int num_sms, cudaStream_t stream) {
+  const int64_t need = mm_int4_tc_workspace(a.M, a.N, a.K, num_sms);
+  if (need > kStaticScratchBytes) return RB_ERR_SHAPE;
+  a.ws = nullptr;
+  a.ws_bytes = 0;
+  if (need > 0) {
+    // the symbol's device address, looked up once per device (return code checked)
+    static void* addr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return RB_ERR_DEVICE;
+    if (!addr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_mm_scratch) != cudaSuccess || !p) {
+        (void)cudaGetLastError();
+        return RB_ERR_DEVICE;
+      }
+      addr[dev] = p;
+    }
+    a.ws = static_cast<float*>(addr[dev]);
+    a.ws_bytes = kStaticScratchBytes;
+  }
+  return launch_mm_int4_tc(a, num_sms, stream);
 }
 
 }  // namespace rb
