@@ -50,7 +50,8 @@ def parse():
                     help="length of the bounded CPU-baseline sample (0: skip it)")
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers in the step (36 = config 1; fewer only for small profiling cases)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+    ap.add_argument("--pos", type=int, default=511, help="step workload: position of the token (cache slots read)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "step"],
                     help="decode: config 1 + 2 (the headline); prefill: config 3, the int4-weight matmul over the "
                          "36-layer projection set for --tokens prompt tokens")
     ap.add_argument("--tokens", type=int, default=256, help="prefill prompt length M (config 3: 34, 256, 1024)")
@@ -512,12 +513,142 @@ def run_prefill(a):
     return 0
 
 
+# ---------------------------------------------------------------------------------------------- full decode step
+STEP_SHAPE = dict(H=3072, nq=24, nkv=8, hd=128, inter=8192, S=2048, eps=1e-5)
+
+
+def build_step(dev, seed, nlayers, pos):
+    """A whole decode step at the config-1 shapes (3072 hidden, 24 query / 8 key-value heads of 128, MLP 8192,
+    36 layers, int8 head), laid out as rumik-fast's fused engine runs it (engine/rumik_fused.py:83-118), with the
+    glue fused: per layer [add_ln + QKV + gate_up + rope/KV/silu*up] (one launch), attention (one launch),
+    [o_proj + down_proj] (one launch); then the final add + LayerNorm and the int8 head. Random weights, a cache
+    filled with random keys/values, and the token at position `pos` (slots 0..pos are read)."""
+    import rumik_fast_b200 as rb
+    from rumik_fast_b200 import fused
+    from rumik_fast_b200 import synthetic as syn
+    from rumik_fast_b200.attention import DecodeAttention
+    c = STEP_SHAPE
+    H, nq, nkv, hd, inter, S = c["H"], c["nq"], c["nkv"], c["hd"], c["inter"], c["S"]
+    assert 0 <= pos < S
+    gen = syn.generator(seed, dev)
+    f16 = torch.float16
+    x_emb = syn.activations((H,), gen, dev)
+    lnw = [(1 + 0.1 * syn.activations((H,), gen, dev).float()).to(f16) for _ in range(nlayers + 1)]
+    inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=dev).float() / hd))
+    ang = torch.outer(torch.arange(S, device=dev).float(), inv).repeat_interleave(2, -1)
+    cos, sin = ang.cos().to(f16), ang.sin().to(f16)
+    kc = torch.randn(nlayers, nkv, S, hd, generator=gen, device=dev).to(f16)
+    vc = torch.randn(nlayers, nkv, S, hd, generator=gen, device=dev).to(f16)
+    xr = [torch.empty(H, device=dev, dtype=f16) for _ in range(2)]
+    q_out, ob = (torch.empty(nq * hd, device=dev, dtype=f16) for _ in range(2))
+    act = torch.empty(inter, device=dev, dtype=f16)
+    buf_o, buf_d, hn = (torch.empty(H, device=dev, dtype=f16) for _ in range(3))
+    logits = torch.empty(syn.HEAD_SHAPE[0], device=dev, dtype=f16)
+    pos_t = torch.tensor([pos], device=dev, dtype=torch.int64)
+    layer_in, attn, layer_out = [], [], []
+    xin = x_emb
+    for L in range(nlayers):
+        xout = xr[L % 2]
+        ln = fused.AddLn(xin, buf_o if L else None, buf_d if L else None, lnw[L], xout, eps=c["eps"])
+        qkv = syn.int4_weights((nq + 2 * nkv) * hd, H, gen, dev)
+        gu = fused.interleave_gate_up(*syn.int4_weights(2 * inter, H, gen, dev))
+        layer_in.append(fused.AddLnGemvPost(qkv, gu, add_ln=ln, pos=pos_t, cos=cos, sin=sin, k_cache=kc[L],
+                                            v_cache=vc[L], q_out=q_out, act=act, n_q_heads=nq, n_kv_heads=nkv,
+                                            rope=L % 4 != 3))
+        attn.append(DecodeAttention(q_out, kc[L], vc[L], pos_t, ob, nq, nkv))
+        wo = syn.int4_weights(H, nq * hd, gen, dev)
+        wd = syn.int4_weights(H, inter, gen, dev)
+        layer_out.append(rb.Int4GemvSet([(ob, *wo, buf_o), (act, *wd, buf_d)]))
+        xin = xout
+    final = fused.AddLn(xin, buf_o, buf_d, lnw[nlayers], None, eps=c["eps"], h_out=hn)
+    head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
+
+    def step():
+        for L in range(nlayers):
+            layer_in[L]()
+            attn[L]()
+            layer_out[L]()
+        fused.add_layernorm(final)
+        rb.gemv_int8_cuda(hn, *head, out=logits)
+
+    shapes = [((nq + 2 * nkv) * hd, H), (2 * inter, H), (H, nq * hd), (H, inter)]
+    wbytes = nlayers * sum(syn.int4_bytes(n, k) for n, k in shapes) + syn.int8_bytes(*syn.HEAD_SHAPE)
+    kvbytes = nlayers * attn[0].bytes_read(pos)
+    return dict(step=step, x_emb=x_emb, logits=logits, wbytes=wbytes, kvbytes=kvbytes,
+                launches=3 * nlayers + 2, keep=(layer_in, attn, layer_out, final, head, kc, vc))
+
+
+def run_step(a):
+    """The whole decode step (fused glue + attention + head) replayed from one CUDA graph. value = tokens/s
+    (one token per step per GPU, replicas); the roofline is HBM over the step's algorithmic bytes (int4 weights,
+    int8 head, K/V slots read)."""
+    import rumik_fast_b200 as rb
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rb.set_weight_prefetch(not a.no_prefetch)
+    w = build_step(dev, 777 + rank, a.layers, a.pos)
+    g = capture(w["step"])
+    with ClockSampler(local_gpu_index(local)) as clk:
+        m0 = clk.mark()
+        ms = timed(g.replay, a.steps, a.warmup, world)
+        m1 = clk.mark()
+    ms_step = ms / a.steps
+    hx = w["x_emb"].cpu().pin_memory()
+    hy = torch.empty(w["logits"].shape, dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        w["x_emb"].copy_(hx, non_blocking=True)
+        g.replay()
+        hy.copy_(w["logits"], non_blocking=True)
+    e2e_steps = max(1, a.steps // 2)
+    ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
+    if rank == 0:
+        peak, kind = peaks()
+        total = w["wbytes"] + w["kvbytes"]
+        gbs = total / (ms_step * 1e-3) / 1e9
+        line = {
+            "metric": "full decode step tok/s", "value": round(world * 1e3 / ms_step, 1), "unit": "tok/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": f"{a.layers}-layer decode step at position {a.pos}: per layer add_ln + QKV "
+                                   "5120x3072 + gate_up 16384x3072 + rope/KV write/silu*up (one launch), attention "
+                                   "24/8 heads x 128 (one launch), o_proj 3072x3072 + down 3072x8192 (one launch); "
+                                   "final add_ln + int8 head 16385x3072; one CUDA graph",
+                       "pos": a.pos, "bytes_per_step": total, "weight_bytes": w["wbytes"], "kv_bytes": w["kvbytes"],
+                       "parallelism": f"replica x{world}", "weight_prefetch": not a.no_prefetch,
+                       "l2": "no flush: 2.0 GB of weights per step > 126 MB L2"},
+            "hbm_gbs": round(gbs, 1),
+            "e2e": {"value": round(world * 1e3 / ms_e2e, 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2,
+                    "ms_per_step": round(ms_e2e, 5)},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_kind": kind, "kernel": "whole decode step",
+                         "traffic": None},
+            "cpu_baseline": None, "clocks": clk.summary(m0, m1),
+            "gpu_launches": a.steps * w["launches"], "mode": "step",
+        }
+        print(json.dumps(line), flush=True)
+    del g
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         return run_reference(a)
     if a.workload == "prefill":
         return run_prefill(a)
+    if a.workload == "step":
+        return run_step(a)
     return run_ours(a)
 
 

@@ -144,6 +144,110 @@ typedef struct rb_gemv_desc {
 int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_dtype, int flags, void* stream);
 
 /*
+ * The same list with a caller-provided workspace that lets a launch with few 128-row blocks (fewer than
+ * 3 x the SM count: a decode layer's projections, 18-35 MB, rather than a whole step's) split K. Each block's
+ * pairs of groups are cut into slices run by different converter sets; every slice writes its fp32 partial sums
+ * to the workspace, and the block's last slice to finish (a per-block counter in the workspace) adds them in slice
+ * order - the result does not depend on which finishes last - and stores the rows.
+ * rb_gemv_int4_workspace returns the bytes a list needs on the current device (0: no split; negative: -status).
+ * The workspace must be 16-byte aligned and zero before its first use; every launch leaves it zero again
+ * (except after a device error, when it must be cleared). A smaller workspace runs the list unsplit. Calls
+ * sharing a workspace must not overlap in time (one stream).
+ */
+int64_t rb_gemv_int4_workspace(const rb_gemv_desc* descs, int count);
+int rb_gemv_int4_multi_ws(const rb_gemv_desc* descs, int count, void* ws, int64_t ws_bytes, int x_dtype, int y_dtype,
+                          int flags, void* stream);
+
+/*
+ * Decode-layer glue fused into the GEMV launch (rumik-fast engine/fused.py): an add + LayerNorm prologue that
+ * produces the activations of the GEMVs, and per-entry epilogues that route each GEMV's rows to where the
+ * engine's next kernels read them. One call replaces, per layer, the engine's
+ *     add_ln (engine/fused.py:29-40)  ->  gemv(w_in) (engine/rumik_fused.py:84)  ->  post (engine/fused.py:43-84)
+ * launch sequence (engine/rumik_fused.py:84-87,115-116).
+ *
+ * Prologue (rb_add_ln), engine/fused.py:29-40:  s = x + a + b in fp32, rounded to the activation dtype
+ * (the new residual, written to x_out), then h = (s - mean(s)) * rsqrt(var(s) + eps) * w, rounded to the
+ * activation dtype (Cohere LayerNorm: centred, no bias). Entries whose `x` is NULL multiply h. H % 128 == 0,
+ * H <= 12288. x_out (and h_out, optional) must not overlap x, a, b or w: every CTA reads x while one writes
+ * x_out, so the residual stream alternates between two buffers.
+ *
+ * Epilogues (rb_gemv_epi), engine/fused.py:43-84, on the GEMV result rounded to the output dtype as the
+ * engine's y buffer would hold it:
+ *   RB_EPI_STORE    y[n] (as rb_gemv_int4_multi).
+ *   RB_EPI_ROPE_KV  rows are n_q_heads query heads, n_kv_heads key heads, n_kv_heads value heads of head_dim
+ *                   rows each (N = (n_q_heads + 2 n_kv_heads) head_dim, head_dim even). With `rope`, query and
+ *                   key heads are rotated by the interleaved rotary embedding at position *pos (pairs (2j, 2j+1),
+ *                   cos/sin [cache_len, head_dim] at [pos, 2j]); queries go to q_out [n_q_heads, head_dim],
+ *                   keys and values to slot *pos of k_cache / v_cache [n_kv_heads, cache_len, head_dim].
+ *   RB_EPI_SWIGLU   rows hold gate and up channels interleaved in tiles of 64 (rows 128 t .. 128 t + 63 = gate
+ *                   channels 64 t .., rows 128 t + 64 .. = the matching up channels; rb-side helper
+ *                   interleave_gate_up); act_out[c] = silu(gate[c]) * up[c], N / 2 channels, N % 128 == 0.
+ * cos, sin, q_out, the caches and act_out are in the output dtype. `y` may be NULL for ROPE_KV and SWIGLU
+ * (when given, the plain result is stored as well). *pos is read on the device (int64); a position outside
+ * [0, cache_len) stores no query, key or value and sets the RB_DEVERR_ARG bit of the device error word.
+ * At most 160 entries and 8 activation vectors (the whole call is one launch), at most 4 ROPE_KV / SWIGLU
+ * entries.
+ */
+typedef struct rb_add_ln {
+  const void* x;        /* residual stream [H] (activation dtype) */
+  const void* a;        /* added term [H] or NULL (e.g. the o_proj output) */
+  const void* b;        /* added term [H] or NULL (e.g. the down_proj output) */
+  const void* w;        /* LayerNorm weight [H] (activation dtype) */
+  void* x_out;          /* new residual x + a + b [H], or NULL */
+  void* h_out;          /* the normalised vector [H], or NULL */
+  int64_t H;
+  float eps;
+} rb_add_ln;
+
+enum rb_epi_kind { RB_EPI_STORE = 0, RB_EPI_ROPE_KV = 1, RB_EPI_SWIGLU = 2 };
+
+typedef struct rb_gemv_epi {
+  int kind;                  /* rb_epi_kind */
+  int rope;                  /* RB_EPI_ROPE_KV: rotate the query and key heads (0 = copy only) */
+  int n_q_heads, n_kv_heads, head_dim;
+  int64_t cache_len;         /* slots per head in k_cache / v_cache */
+  const int64_t* pos;        /* device pointer to the position */
+  const void* cos;           /* [cache_len, head_dim] */
+  const void* sin;
+  void* q_out;               /* [n_q_heads, head_dim] */
+  void* k_cache;             /* [n_kv_heads, cache_len, head_dim] */
+  void* v_cache;
+  void* act_out;             /* RB_EPI_SWIGLU: [N / 2] */
+} rb_gemv_epi;
+
+/* Device error bit set by rb_gemv_int4_fused when *pos is outside [0, cache_len). */
+#define RB_DEVERR_ARG (1u << 9)
+
+/* descs[i], epis[i] (epis may be NULL: all RB_EPI_STORE); ln may be NULL (no entry may then have x == NULL).
+ * ws / ws_bytes: the split-K workspace of rb_gemv_int4_multi_ws (rb_gemv_int4_workspace(descs, count) bytes),
+ * or NULL / 0. A split entry runs its epilogue in the last slice of each block. */
+int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int count, const rb_add_ln* ln,
+                       void* ws, int64_t ws_bytes, int x_dtype, int y_dtype, int flags, void* stream);
+
+/* The add + LayerNorm alone (engine/fused.py:29-40 as launched at engine/rumik_fused.py:115-116 for the final
+ * norm in front of the head): one CTA; results bit-identical to rb_gemv_int4_fused's prologue. dtype is the
+ * activation dtype of every vector. */
+int rb_add_layernorm(const rb_add_ln* ln, int dtype, int flags, void* stream);
+
+/*
+ * Decode attention of one token over the KV cache, grouped-query heads, ONE launch. Replaces rumik-fast's
+ * flash-decoding pair attn_split + attn_combine (engine/fused.py:120-200, launched at
+ * engine/rumik_fused.py:88-94) and its single-kernel form attn (engine/fused.py:92-118):
+ *   out[h] = sum_{t <= *pos} softmax_t(q[h] . k_cache[h / rep, t] * scale) v_cache[h / rep, t]
+ *   q [n_q_heads, head_dim], k_cache / v_cache [n_kv_heads, cache_len, head_dim], out [n_q_heads, head_dim], all
+ *   in `dtype` (RB_F16 / RB_BF16); *pos on the device (int64), 0 <= *pos < cache_len, else nothing is written
+ *   and the RB_DEVERR_ARG bit of the device error word is set. head_dim == 128, rep = n_q_heads / n_kv_heads
+ *   in 1..8, n_kv_heads <= 64. Scores, softmax and the weighted sum are fp32.
+ *   ws: rb_attn_decode_workspace(...) bytes of device memory, 16-byte aligned; its first 256 bytes (per-head
+ *   completion counters) must be zero before the first call and are zero again after each call. Calls that
+ *   share a workspace must not overlap in time (one stream).
+ */
+int64_t rb_attn_decode_workspace(int n_q_heads, int n_kv_heads, int head_dim);
+int rb_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
+                   int n_q_heads, int n_kv_heads, int head_dim, int64_t cache_len, float scale, void* ws,
+                   int64_t ws_bytes, int dtype, int flags, void* stream);
+
+/*
  * Tensor-parallel per-layer reduction over NVLink peer memory:  out[i] = sum over ranks of (a[i] + b[i]).
  * Replaces the add + all-reduce that follows a row-parallel layer pair (o_proj and down partials) in a
  * tensor-parallel decode step; no reference counterpart (the reference engine runs on one GPU).

@@ -27,6 +27,22 @@ class GemvDesc(ctypes.Structure):
     """struct rb_gemv_desc (include/rumik_b200.h)."""
     _fields_ = [("x", _vp), ("y", _vp), ("q", _vp), ("s", _vp), ("m", _vp), ("N", _i64), ("K", _i64)]
 
+class AddLn(ctypes.Structure):
+    """struct rb_add_ln (include/rumik_b200.h)."""
+    _fields_ = [("x", _vp), ("a", _vp), ("b", _vp), ("w", _vp), ("x_out", _vp), ("h_out", _vp), ("H", _i64),
+                ("eps", _c.c_float)]
+
+
+class GemvEpi(ctypes.Structure):
+    """struct rb_gemv_epi (include/rumik_b200.h)."""
+    _fields_ = [("kind", _int), ("rope", _int), ("n_q_heads", _int), ("n_kv_heads", _int), ("head_dim", _int),
+                ("cache_len", _i64), ("pos", _vp), ("cos", _vp), ("sin", _vp), ("q_out", _vp), ("k_cache", _vp),
+                ("v_cache", _vp), ("act_out", _vp)]
+
+
+EPI_STORE, EPI_ROPE_KV, EPI_SWIGLU = 0, 1, 2
+DEVERR_ARG = 1 << 9
+
 SIGNATURES = {
     "rb_gemv_int4": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
     "rb_gemv_int8": (_int, [_vp, _int, _i64, _vp, _int, _vp, _int, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
@@ -35,6 +51,14 @@ SIGNATURES = {
     "rb_mm_int4_static": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
     "rb_mm_int4_ws": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _vp, _i64, _int, _vp]),
     "rb_gemv_int4_multi": (_int, [_c.POINTER(GemvDesc), _int, _int, _int, _int, _vp]),
+    "rb_gemv_int4_fused": (_int, [_c.POINTER(GemvDesc), _c.POINTER(GemvEpi), _int, _c.POINTER(AddLn), _vp, _i64,
+                                  _int, _int, _int, _vp]),
+    "rb_gemv_int4_workspace": (_i64, [_c.POINTER(GemvDesc), _int]),
+    "rb_gemv_int4_multi_ws": (_int, [_c.POINTER(GemvDesc), _int, _vp, _i64, _int, _int, _int, _vp]),
+    "rb_add_layernorm": (_int, [_c.POINTER(AddLn), _int, _int, _vp]),
+    "rb_attn_decode_workspace": (_i64, [_int, _int, _int]),
+    "rb_attn_decode": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _int, _i64, _c.c_float, _vp, _i64, _int, _int,
+                              _vp]),
     "rb_status_string": (_c.c_char_p, [_int]),
     "rb_version": (_int, []),
     "rb_get_device_error": (_int, [_c.POINTER(_c.c_uint), _vp]),

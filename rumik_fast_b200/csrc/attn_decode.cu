@@ -1,0 +1,284 @@
+// attn_decode.cu - decode attention of one token over the KV cache (grouped-query heads), one launch on B200.
+//
+// o_h = sum_{t <= pos} softmax_t(q_h . k_t * scale) v_t for every query head h, k/v from key-value head
+// h / rep: rumik-fast's decode attention (engine/fused.py:92-118, split as :120-200, launched at
+// engine/rumik_fused.py:88-97; eager form engine/rumik_int4.py:163-171,217).
+//
+// Grid = n_kv_heads x nsplit CTAs (nsplit ~ SMs / n_kv_heads); the filled slots 0..pos are cut into nsplit
+// chunks whose length is computed from *pos on the device (one CUDA graph serves every position). A CTA reads
+// its chunk of K and V once for all `rep` query heads of its key-value head. Each warp takes 8 slots per step:
+// every lane holds 4 of the 128 dimensions of each row (8-byte loads, one 256-byte row per warp-load), the 8
+// x rep partial dot products are reduced across the warp with a butterfly that sums 8 values in 9 shuffles,
+// and an online softmax (running max, running sum, rescaled accumulator) folds them in. The CTA merges its
+// warps and writes an fp32 partial (acc, max, sum); the last CTA of each key-value head to finish (an atomic
+// ticket) merges the nsplit partials in split order and writes the heads' outputs, so no second launch.
+// HBM-bound at long contexts: 2 x (pos + 1) x 256 bytes per key-value head.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rb {
+
+namespace attn {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kHd = 128;       // head_dim: 4 dimensions per lane
+constexpr int kStep = 8;       // slots per warp step
+constexpr int kMaxRep = 8;
+constexpr int kMaxSplit = 64;
+constexpr int kMaxKv = 64;
+constexpr int64_t kTicketBytes = kMaxKv * 4;
+
+struct AttnParams {
+  const void* q;
+  const void* kc;
+  const void* vc;
+  const int64_t* pos;
+  void* out;
+  unsigned int* ticket;  // [n_kv_heads], zero between calls
+  float* po;             // [n_q_heads, nsplit, 128] partial accumulators
+  float* pm;             // [n_q_heads, nsplit] partial maxima
+  float* pl;             // [n_q_heads, nsplit] partial sums
+  int64_t S;
+  float scale;
+  int nsplit, bf16;
+};
+
+__device__ __forceinline__ void unpack4(uint2 u, bool bf, float (&f)[4]) {
+  if (bf) {
+    f[0] = __uint_as_float(u.x << 16);
+    f[1] = __uint_as_float(u.x & 0xffff0000u);
+    f[2] = __uint_as_float(u.y << 16);
+    f[3] = __uint_as_float(u.y & 0xffff0000u);
+  } else {
+    f[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(u.x & 0xffffu)));
+    f[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(u.x >> 16)));
+    f[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(u.y & 0xffffu)));
+    f[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(u.y >> 16)));
+  }
+}
+
+// Sum of s[j] over the 32 lanes for 8 values at once: afterwards lane l holds the sum for slot j = l >> 2.
+__device__ __forceinline__ float reduce8(const float (&s)[8], int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+  float k1[4], k2[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = b4 ? s[i] : s[i + 4];
+    k1[i] = (b4 ? s[i + 4] : s[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = b3 ? k1[i] : k1[i + 2];
+    k2[i] = (b3 ? k1[i + 2] : k1[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  const float send = b2 ? k2[0] : k2[1];
+  float v = (b2 ? k2[1] : k2[0]) + __shfl_xor_sync(0xffffffffu, send, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v;
+}
+
+template <int REP>
+__global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
+  __shared__ float sm_m[kWarps][REP], sm_l[kWarps][REP];
+  __shared__ __align__(16) float sm_o[kWarps][REP][kHd];
+  __shared__ int is_last;
+  const int g = blockIdx.x / p.nsplit, sp = blockIdx.x - g * p.nsplit;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool bf = p.bf16 != 0;
+  griddep_launch_dependents();
+  griddep_wait();  // q and the cache slot of this token come from the previous kernel
+  uint2 qraw[REP];  // issued together with the position load: one round trip for both
+#pragma unroll
+  for (int r = 0; r < REP; ++r)
+    qraw[r] = __ldcg(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(p.q) +
+                                                    (static_cast<int64_t>(g * REP + r) * kHd + 4 * lane) * 2));
+  const int64_t pos = __ldcg(p.pos);
+  if (pos < 0 || pos >= p.S) {  // the same decision in every CTA: none takes a ticket
+    if (tid == 0 && blockIdx.x == 0) atomicOr(&g_device_error, ERR_ARG);
+    return;
+  }
+  const int64_t n = pos + 1;
+  const int64_t ch = ((n + p.nsplit - 1) / p.nsplit + kWarps * kStep - 1) / (kWarps * kStep) * (kWarps * kStep);
+  const int active = static_cast<int>((n + ch - 1) / ch);  // splits with slots; the others leave at once
+  if (sp >= active) return;
+  const int64_t start = static_cast<int64_t>(sp) * ch, end = start + ch < n ? start + ch : n;
+
+  float qv[REP][4], m[REP], l[REP], o[REP][4];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    unpack4(qraw[r], bf, qv[r]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      qv[r][i] *= p.scale;
+      o[r][i] = 0.f;
+    }
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+  }
+  const uint8_t* kb = static_cast<const uint8_t*>(p.kc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
+  const uint8_t* vb = static_cast<const uint8_t*>(p.vc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
+  const int jl = lane >> 2;  // the slot of the step whose score this lane ends up holding
+  for (int64_t t0 = start + warp * kStep; t0 < end; t0 += kWarps * kStep) {
+    uint2 kr[kStep], vr[kStep];
+#pragma unroll
+    for (int j = 0; j < kStep; ++j) {
+      const bool in = t0 + j < end;
+      kr[j] = in ? __ldg(reinterpret_cast<const uint2*>(kb + (t0 + j) * kHd * 2)) : make_uint2(0u, 0u);
+      vr[j] = in ? __ldg(reinterpret_cast<const uint2*>(vb + (t0 + j) * kHd * 2)) : make_uint2(0u, 0u);
+    }
+    float kf[kStep][4];
+#pragma unroll
+    for (int j = 0; j < kStep; ++j) unpack4(kr[j], bf, kf[j]);
+    const bool mine_in = t0 + jl < end;
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      float s[kStep];
+#pragma unroll
+      for (int j = 0; j < kStep; ++j)
+        s[j] = qv[r][0] * kf[j][0] + qv[r][1] * kf[j][1] + qv[r][2] * kf[j][2] + qv[r][3] * kf[j][3];
+      float sc = reduce8(s, lane);
+      if (!mine_in) sc = -INFINITY;
+      float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float m_new = fmaxf(m[r], mx);         // finite: slot t0 is always in range
+      const float alpha = __expf(m[r] - m_new);    // 0 on the first step (m = -inf)
+      const float pj = __expf(sc - m_new);         // 0 for slots past the end
+      l[r] = l[r] * alpha + pj;                    // per lane; the 4 lanes of a slot hold the same value
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[r][i] *= alpha;
+#pragma unroll
+      for (int j = 0; j < kStep; ++j) {
+        const float pb = __shfl_sync(0xffffffffu, pj, 4 * j);
+        float vf[4];
+        unpack4(vr[j], bf, vf);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[r][i] = fmaf(pb, vf[i], o[r][i]);
+      }
+      m[r] = m_new;
+    }
+  }
+  // merge the warps of this CTA
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    float lt = l[r] + __shfl_xor_sync(0xffffffffu, l[r], 4);  // one lane per slot group of the step
+    lt += __shfl_xor_sync(0xffffffffu, lt, 8);
+    lt += __shfl_xor_sync(0xffffffffu, lt, 16);
+    if (lane == 0) {
+      sm_m[warp][r] = m[r];
+      sm_l[warp][r] = lt;
+    }
+    *reinterpret_cast<float4*>(&sm_o[warp][r][4 * lane]) = make_float4(o[r][0], o[r][1], o[r][2], o[r][3]);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w][r]);
+    float O = 0.f, L = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float e = __expf(sm_m[w][r] - M);
+        O = fmaf(e, sm_o[w][r][tid], O);
+        L = fmaf(e, sm_l[w][r], L);
+      }
+    }
+    if (active == 1) {  // one split holds every slot: no partials, no merge
+      store_out(p.out, static_cast<int64_t>(g * REP + r) * kHd + tid, O / L, bf);
+      continue;
+    }
+    const int64_t hs = static_cast<int64_t>(g * REP + r) * p.nsplit + sp;
+    p.po[hs * kHd + tid] = O;
+    if (tid == 0) {
+      p.pm[hs] = M;
+      p.pl[hs] = L;
+    }
+  }
+  if (active == 1) return;
+  __threadfence();  // this CTA's partial is visible device-wide before its ticket
+  __syncthreads();
+  if (tid == 0) is_last = atomicAdd(&p.ticket[g], 1u) == static_cast<unsigned int>(active - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // The last CTA of key-value head g merges the active partials of its query heads in split order, each
+  // thread for its dimension, with an online rescale (running max) so that every load of the merge - maxima,
+  // sums and accumulators of all splits - is independent of the others and issued at once.
+  const int64_t hg = static_cast<int64_t>(g * REP) * p.nsplit;
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    const float* pm = p.pm + hg + r * p.nsplit;
+    const float* pl = p.pl + hg + r * p.nsplit;
+    const float* po = p.po + (hg + r * p.nsplit) * kHd + tid;
+    float M = -INFINITY, O = 0.f, L = 0.f;
+#pragma unroll 6
+    for (int s = 0; s < active; ++s) {
+      const float ms = __ldcg(pm + s), ls = __ldcg(pl + s), os = __ldcg(po + s * kHd);
+      const float Mn = fmaxf(M, ms);
+      const float a = __expf(M - Mn), w = __expf(ms - Mn);  // a = 0 for the first split (M = -inf)
+      O = fmaf(O, a, w * os);
+      L = fmaf(L, a, w * ls);
+      M = Mn;
+    }
+    store_out(p.out, static_cast<int64_t>(g * REP + r) * kHd + tid, O / L, bf);
+  }
+  if (tid == 0) p.ticket[g] = 0u;  // ready for the next call
+}
+
+int64_t nsplit_for(int nkv, int sms) { return std::max(1, std::min(kMaxSplit, sms / nkv)); }
+
+}  // namespace attn
+
+int64_t attn_decode_workspace(int nq, int nkv, int hd) {
+  using namespace attn;
+  if (hd != kHd || nkv < 1 || nkv > kMaxKv || nq < nkv || nq % nkv != 0 || nq / nkv > kMaxRep) return -1;
+  return kTicketBytes + static_cast<int64_t>(nq) * kMaxSplit * (kHd + 2) * 4;
+}
+
+int launch_attn_decode(const void* q, const void* kc, const void* vc, const int64_t* pos, void* out, int nq, int nkv,
+                       int64_t S, float scale, void* ws, int dtype, int flags, int num_sms, cudaStream_t stream) {
+  using namespace attn;
+  AttnParams p;
+  p.q = q;
+  p.kc = kc;
+  p.vc = vc;
+  p.pos = pos;
+  p.out = out;
+  p.S = S;
+  p.scale = scale;
+  p.bf16 = dtype == RB_BF16;
+  p.nsplit = static_cast<int>(nsplit_for(nkv, num_sms));
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  p.ticket = reinterpret_cast<unsigned int*>(w);
+  p.po = reinterpret_cast<float*>(w + kTicketBytes);
+  p.pm = p.po + static_cast<int64_t>(nq) * p.nsplit * kHd;
+  p.pl = p.pm + static_cast<int64_t>(nq) * p.nsplit;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nkv * p.nsplit);
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = (flags & RB_FLAG_PDL) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
+  switch (nq / nkv) {
+    case 1: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<1>, p); break;
+    case 2: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<2>, p); break;
+    case 3: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<3>, p); break;
+    case 4: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<4>, p); break;
+    case 5: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<5>, p); break;
+    case 6: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<6>, p); break;
+    case 7: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<7>, p); break;
+    case 8: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<8>, p); break;
+    default: return RB_ERR_SHAPE;
+  }
+  return e == cudaSuccess ? RB_OK : RB_ERR_LAUNCH;
+}
+
+}  // namespace rb

@@ -114,9 +114,7 @@ int rb_gemv_int8(const void* x, int x_dtype, int64_t ldx, const uint8_t* q, int 
   return st;
 }
 
-int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_dtype, int flags, void* stream) {
-  if (count < 0) return RB_ERR_SHAPE;
-  if (count == 0) return RB_OK;
+static int check_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_dtype) {
   if (!descs) return RB_ERR_NULL;
   if (!act_dtype_ok(x_dtype) || !act_dtype_ok(y_dtype)) return RB_ERR_DTYPE;
   for (int i = 0; i < count; ++i) {
@@ -125,13 +123,169 @@ int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_
     if (!d.x || !d.y || !d.q || !d.s || !d.m) return RB_ERR_NULL;
     if (!aligned16(d.x) || !aligned16(d.q) || !aligned16(d.s) || !aligned16(d.m)) return RB_ERR_ALIGN;
   }
-  int sms = 0, st = device_sms(&sms);
+  return RB_OK;
+}
+
+static int multi_impl(const rb_gemv_desc* descs, int count, void* ws, int64_t ws_bytes, int x_dtype, int y_dtype,
+                      int flags, void* stream) {
+  if (count < 0) return RB_ERR_SHAPE;
+  if (count == 0) return RB_OK;
+  int st = check_multi(descs, count, x_dtype, y_dtype);
+  if (st != RB_OK) return st;
+  if (ws && !aligned16(ws)) return RB_ERR_ALIGN;
+  int sms = 0;
+  st = device_sms(&sms);
   if (st != RB_OK) return st;
 #ifdef RB_MULTI_LEGACY  // the warp-MMA multi-GEMV (gemv_int4_multi.cu), kept for comparison builds
+  (void)ws;
+  (void)ws_bytes;
   st = rb::launch_gemv_int4_multi(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream));
 #else
-  st = rb::launch_gemv_int4_tc(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream));
+  st = rb::launch_gemv_int4_tc(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream), nullptr,
+                               nullptr, ws, ws_bytes);
 #endif
+  if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+  return st;
+}
+
+int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_dtype, int flags, void* stream) {
+  return multi_impl(descs, count, nullptr, 0, x_dtype, y_dtype, flags, stream);
+}
+
+int rb_gemv_int4_multi_ws(const rb_gemv_desc* descs, int count, void* ws, int64_t ws_bytes, int x_dtype,
+                          int y_dtype, int flags, void* stream) {
+  return multi_impl(descs, count, ws, ws_bytes, x_dtype, y_dtype, flags, stream);
+}
+
+int64_t rb_gemv_int4_workspace(const rb_gemv_desc* descs, int count) {
+  if (count < 0) return -RB_ERR_SHAPE;
+  if (count == 0) return 0;
+  if (!descs) return -RB_ERR_NULL;
+  for (int i = 0; i < count; ++i) {
+    const rb_gemv_desc& d = descs[i];
+    if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.K > 16384 || d.N > (int64_t(1) << 30)) return -RB_ERR_SHAPE;
+    if (!d.q) return -RB_ERR_NULL;
+  }
+  int sms = 0, st = device_sms(&sms);
+  if (st != RB_OK) return -st;
+  // entries with x == NULL read a prologue's vector: only the slot bookkeeping looks at it here
+  static const uint8_t dummy[16] = {};
+  rb_add_ln ln = {};
+  ln.x = dummy;
+  ln.w = dummy;
+  bool from_ln = false;
+  for (int i = 0; i < count; ++i) from_ln |= descs[i].x == nullptr;
+  int64_t need = 0;
+  st = rb::launch_gemv_int4_tc(descs, count, RB_F16, RB_F16, 0, sms, nullptr, nullptr, from_ln ? &ln : nullptr,
+                               nullptr, 0, &need);
+  return st == RB_OK ? need : -st;
+}
+
+static bool ranges_overlap(const void* a, int64_t abytes, const void* b, int64_t bbytes) {
+  if (!a || !b) return false;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + static_cast<uintptr_t>(bbytes) && b0 < a0 + static_cast<uintptr_t>(abytes);
+}
+
+static int check_add_ln(const rb_add_ln* ln) {
+  if (!ln->x || !ln->w) return RB_ERR_NULL;
+  if (ln->H < 128 || ln->H % 128 != 0 || ln->H > 12288) return RB_ERR_SHAPE;
+  if (!(ln->eps >= 0.f)) return RB_ERR_SHAPE;
+  const void* in[4] = {ln->x, ln->a, ln->b, ln->w};
+  const void* out[2] = {ln->x_out, ln->h_out};
+  for (const void* v : in)
+    if (v && !aligned16(v)) return RB_ERR_ALIGN;
+  for (const void* v : out)
+    if (v && !aligned16(v)) return RB_ERR_ALIGN;
+  const int64_t bytes = ln->H * 2;
+  for (const void* o : out)
+    for (const void* v : in)
+      if (ranges_overlap(o, bytes, v, bytes)) return RB_ERR_SHAPE;
+  if (ranges_overlap(ln->x_out, bytes, ln->h_out, bytes)) return RB_ERR_SHAPE;
+  return RB_OK;
+}
+
+int rb_add_layernorm(const rb_add_ln* ln, int dtype, int flags, void* stream) {
+  if (!ln) return RB_ERR_NULL;
+  if (!act_dtype_ok(dtype)) return RB_ERR_DTYPE;
+  int st = check_add_ln(ln);
+  if (st != RB_OK) return st;
+  int sms = 0;
+  st = device_sms(&sms);
+  if (st != RB_OK) return st;
+  st = rb::launch_add_ln(ln, dtype, flags, static_cast<cudaStream_t>(stream));
+  if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+  return st;
+}
+
+int64_t rb_attn_decode_workspace(int n_q_heads, int n_kv_heads, int head_dim) {
+  return rb::attn_decode_workspace(n_q_heads, n_kv_heads, head_dim);
+}
+
+int rb_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
+                   int n_q_heads, int n_kv_heads, int head_dim, int64_t cache_len, float scale, void* ws,
+                   int64_t ws_bytes, int dtype, int flags, void* stream) {
+  const int64_t need = rb::attn_decode_workspace(n_q_heads, n_kv_heads, head_dim);
+  if (need < 0 || cache_len < 1 || cache_len > (int64_t(1) << 31)) return RB_ERR_SHAPE;
+  if (!q || !k_cache || !v_cache || !pos || !out || !ws) return RB_ERR_NULL;
+  if (!act_dtype_ok(dtype)) return RB_ERR_DTYPE;
+  if (!(scale == scale)) return RB_ERR_SHAPE;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out) || !aligned16(ws))
+    return RB_ERR_ALIGN;
+  if (ws_bytes < need) return RB_ERR_SHAPE;
+  int sms = 0, st = device_sms(&sms);
+  if (st != RB_OK) return st;
+  st = rb::launch_attn_decode(q, k_cache, v_cache, pos, out, n_q_heads, n_kv_heads, cache_len, scale, ws, dtype, flags,
+                              sms, static_cast<cudaStream_t>(stream));
+  if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+  return st;
+}
+
+int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int count, const rb_add_ln* ln,
+                       void* ws, int64_t ws_bytes, int x_dtype, int y_dtype, int flags, void* stream) {
+  if (count < 0 || count > 160) return RB_ERR_SHAPE;
+  if (count == 0) return RB_OK;
+  if (!descs) return RB_ERR_NULL;
+  if (!act_dtype_ok(x_dtype) || !act_dtype_ok(y_dtype)) return RB_ERR_DTYPE;
+  if (ln) {
+    const int st = check_add_ln(ln);
+    if (st != RB_OK) return st;
+  }
+  int routed = 0;
+  for (int i = 0; i < count; ++i) {
+    const rb_gemv_desc& d = descs[i];
+    const int kind = epis ? epis[i].kind : RB_EPI_STORE;
+    if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.K > 16384 || d.N > (int64_t(1) << 30)) return RB_ERR_SHAPE;
+    if (!d.q || !d.s || !d.m) return RB_ERR_NULL;
+    if (!d.x && !ln) return RB_ERR_NULL;
+    if (!d.x && d.K != ln->H) return RB_ERR_SHAPE;
+    if ((d.x && !aligned16(d.x)) || !aligned16(d.q) || !aligned16(d.s) || !aligned16(d.m)) return RB_ERR_ALIGN;
+    if (kind == RB_EPI_STORE) {
+      if (!d.y) return RB_ERR_NULL;
+      continue;
+    }
+    ++routed;
+    const rb_gemv_epi& e = epis[i];
+    if (kind == RB_EPI_ROPE_KV) {
+      if (e.head_dim < 2 || e.head_dim % 2 != 0 || e.n_q_heads < 0 || e.n_kv_heads < 0 || e.cache_len < 1)
+        return RB_ERR_SHAPE;
+      if (d.N != static_cast<int64_t>(e.n_q_heads + 2 * e.n_kv_heads) * e.head_dim) return RB_ERR_SHAPE;
+      if (!e.pos || (e.n_q_heads > 0 && !e.q_out) || (e.n_kv_heads > 0 && (!e.k_cache || !e.v_cache)))
+        return RB_ERR_NULL;
+      if (e.rope && (!e.cos || !e.sin)) return RB_ERR_NULL;
+    } else if (kind == RB_EPI_SWIGLU) {
+      if (d.N % 128 != 0) return RB_ERR_SHAPE;
+      if (!e.act_out) return RB_ERR_NULL;
+    } else {
+      return RB_ERR_SHAPE;
+    }
+  }
+  if (routed > 4) return RB_ERR_SHAPE;
+  if (ws && !aligned16(ws)) return RB_ERR_ALIGN;
+  int sms = 0, st = device_sms(&sms);
+  if (st != RB_OK) return st;
+  st = rb::launch_gemv_int4_tc(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream), epis,
+                               ln, ws, ws_bytes);
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
 }

@@ -27,6 +27,7 @@ enum : unsigned int {
   ERR_MULTI_EMPTY = 1u << 6,  // multi-GEMV producer timed out waiting for ring space
   ERR_TC_WAIT = 1u << 7,      // tensor-core multi-GEMV timed out on an mbarrier
   ERR_TP_WAIT = 1u << 8,      // tensor-parallel reduction timed out waiting for a peer's flag
+  ERR_ARG = 1u << 9,          // a device-side argument (a decode position) was out of range; nothing stored
 };
 
 // Upper bound on the wall time of one mbarrier wait. Healthy waits here last microseconds (at most the
@@ -273,6 +274,37 @@ __device__ __forceinline__ void raw_to_half8(const uint4 raw, bool is_bf16, __ha
 // 8 activations (one 16-byte load, bypassing L1) to fp16.
 __device__ __forceinline__ void load8_as_half(const void* p, bool is_bf16, __half (&h)[8]) {
   raw_to_half8(ldg_cg_128(p), is_bf16, h);
+}
+
+// 8 activations held in one 16-byte word (fp16 or bf16 storage) -> fp32, exactly.
+__device__ __forceinline__ void raw_to_f32(const uint4 raw, bool is_bf16, float (&v)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (is_bf16) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    } else {
+      v[2 * i] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[i] & 0xffffu)));
+      v[2 * i + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[i] >> 16)));
+    }
+  }
+}
+
+// 8 activations (one 16-byte load, bypassing L1) to fp32, exactly.
+__device__ __forceinline__ void load8_f32(const void* p, bool is_bf16, float (&v)[8]) {
+  raw_to_f32(ldg_cg_128(p), is_bf16, v);
+}
+
+// v rounded to the 16-bit activation type (nearest even), back in fp32: the value a bf16/fp16 buffer holds.
+__device__ __forceinline__ float round_act(float v, bool is_bf16) {
+  return is_bf16 ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
+}
+
+// One element of a bf16 or fp16 array, to fp32.
+__device__ __forceinline__ float load_act(const void* p, int64_t idx, bool is_bf16) {
+  const unsigned short u = reinterpret_cast<const unsigned short*>(p)[idx];
+  return is_bf16 ? __uint_as_float(static_cast<uint32_t>(u) << 16) : __half2float(__ushort_as_half(u));
 }
 
 __device__ __forceinline__ void store_out(void* y, int64_t idx, float v, bool is_bf16) {

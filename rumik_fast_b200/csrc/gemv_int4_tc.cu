@@ -47,15 +47,44 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kXPad = 256;            // bytes the B descriptor's unused rows read past a table
 constexpr uint32_t kXGroupBytes = 256;     // per group: 8 chunks of (16 high bytes, 16 low bytes)
 
+constexpr int kMaxEpis = 4;                // routed (non-store) epilogues per launch
+constexpr int kLnIter = 4;                 // prologue: 8-element chunks per converter thread (H <= 4 x 384 x 8)
+constexpr int kBarLn = 2 + kSets;          // named barriers: 1 = tables staged, 2 + s = set s, kBarLn = prologue
+enum : int { kEpiStore = RB_EPI_STORE, kEpiRopeKv = RB_EPI_ROPE_KV, kEpiSwiglu = RB_EPI_SWIGLU };
+
 struct Entry {
   const uint16_t* s;
   const uint16_t* m;
   void* y;
   int N, G, slot, block_begin;
+  int epi, ep;  // epilogue kind, index into TcParams::epis
+  // K split: each 128-row block is cut into `ks` slices of `ppk` pairs of groups (the last may be shorter);
+  // work item i of this entry (i from item_begin) is block i / ks, slice i % ks
+  int ks, ppk, item_begin;
+};
+
+// Where the rows of a routed entry go (rb_gemv_epi).
+struct EpiP {
+  const int64_t* pos;
+  const void* cos;
+  const void* sin;
+  void* q_out;
+  void* k_cache;
+  void* v_cache;
+  void* act;
+  int64_t S;
+  int rope, nq, nkv, hd;
 };
 
 struct Slot {
-  const void* x;
+  const void* x;  // activations; for the prologue slot the residual stream
+  const void* a;  // prologue (ln != 0): x + a + b -> LayerNorm with weight w
+  const void* b;
+  const void* w;
+  void* x_out;
+  void* h_out;
+  float eps;
+  int ln;
   int K, G;
   uint32_t tab_off, cst_off;
 };
@@ -64,9 +93,20 @@ struct __align__(64) TcParams {
   CUtensorMap maps[kMaxEntries];  // codes of each entry: [N rows, K/2 bytes], box 128 x 128, 128B swizzle
   Entry e[kMaxEntries];
   Slot slots[kMaxSlots];
-  int count, nslots, total_blocks, x_bf16, y_bf16, prefetch, nst;
-  uint32_t xs_off, bar_off, idesc;
+  EpiP epis[kMaxEpis];
+  int count, nslots, total_blocks, total_items, x_bf16, y_bf16, prefetch, nst;
+  uint32_t xs_off, bar_off, aux_off, idesc;
+  float* ws_part;           // split K: fp32 partial results, 128 per work item
+  unsigned int* ws_ticket;  // split K: slices finished per block (global block index), zero between launches
 };
+static_assert(sizeof(TcParams) <= 32000, "kernel parameter block too large");
+
+// Auxiliary shared memory: the prologue's two reduction arrays, per set two 64-float exchange buffers of the
+// SwiGLU epilogue (up values handed to the gate rows), then per set the split-K "last slice" flag.
+constexpr uint32_t kAuxBytes = 2 * kConvWarps * 4 + kSets * 2 * 64 * 4 + 16;
+
+// Split-K workspace: one completion counter per 128-row block (rounded up to 256 bytes), then the partials.
+inline int64_t split_ticket_bytes(int blocks) { return (static_cast<int64_t>(blocks) * 4 + 255) / 256 * 256; }
 
 // B operand descriptor over an activation table: K-major, no swizzle, 16-byte rows at a 16-byte pitch (row 0
 // = 16 high bytes, row 1 = the 16 matching low bytes), the next 16 K-elements of a row 32 bytes further on
@@ -108,61 +148,209 @@ __device__ __forceinline__ float half_at(const uint4& v, int i) {  // i: compile
 // order in which a converter thread writes a group's codes to tensor memory (within each 8 columns: the four
 // even columns, then the four odd ones), stored per 16 positions as 16 high bytes then 16 low bytes; plus per
 // group {delta, sum(x)}.
-__device__ void stage_x_tables(const TcParams& p, uint8_t* xs, int ct, int nthreads) {
+//
+// One chunk: positions 8c .. 8c + 7 of a slot. All 32 lanes call this together (a group is 16 chunks = 16
+// consecutive threads, reduced with shuffles); lanes with valid == false contribute zeros and write nothing.
+__device__ __forceinline__ void quant_chunk(const float (&v)[8], bool valid, int c, uint8_t* tab, float2* cst) {
+  float mx = 0.f, sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    mx = fmaxf(mx, fabsf(v[i]));
+    sum += v[i];
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  const float delta = mx > 0.f ? mx / 32639.f : 1.f;
+  const float inv = 1.f / delta;
+  if (valid) {
+    uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
+#pragma unroll
+    for (int jp = 0; jp < 8; ++jp) {  // table position jp <- column (jp < 4 ? 2 jp : 2 (jp - 4) + 1)
+      const int col = jp < 4 ? 2 * jp : 2 * (jp - 4) + 1;
+      const int xi = __float2int_rn(fminf(fmaxf(v[col] * inv, -32639.f), 32639.f));
+      const int l = ((xi + 128) & 255) - 128;
+      const int h = (xi - l) >> 8;
+      hi[jp >> 2] |= (static_cast<uint32_t>(h) & 255u) << (8 * (jp & 3));
+      lo[jp >> 2] |= (static_cast<uint32_t>(l) & 255u) << (8 * (jp & 3));
+    }
+    // positions 8 * (c % 16) .. + 7 of the group: 16-position chunk (c % 16) / 2, half (c & 1)
+    uint8_t* dst = tab + (c >> 4) * kXGroupBytes + ((c & 15) >> 1) * 32 + (c & 1) * 8;
+    *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], hi[1]);
+    *reinterpret_cast<uint2*>(dst + 16) = make_uint2(lo[0], lo[1]);
+    if ((c & 15) == 0) cst[c >> 4] = make_float2(delta, sum);
+  }
+}
+
+// Sum of one value per converter thread, the same fp32 result in every thread (fixed order).
+__device__ __forceinline__ float conv_sum(float v, float* red, int ct, int nthreads) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((ct & 31) == 0) red[ct >> 5] = v;
+  named_bar_sync(kBarLn, nthreads);
+  float t = 0.f;
+  for (int i = 0; i < nthreads / 32; ++i) t += red[i];
+  return t;
+}
+
+__device__ __forceinline__ void store8_act(void* p, const float (&v)[8], bool is_bf16) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (is_bf16) {
+      w[i] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i]))) |
+             (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1]))) << 16);
+    } else {
+      w[i] = pack_half2(__float2half_rn(v[2 * i]), __float2half_rn(v[2 * i + 1]));
+    }
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// The add + LayerNorm prologue of rumik-fast's add_ln (engine/fused.py:29-40), computed by every CTA from
+// global memory: s = (x + a) + b in fp32 rounded to the activation type, h = (s - mean) * rsqrt(var + eps) * w
+// rounded likewise (mean and var over the H elements, two passes as the reference), then tabulated like any
+// other activation vector. CTA 0 also writes s (the new residual) and h.
+template <bool kTab>
+__device__ void stage_ln_slot(const Slot& S, bool bf, uint8_t* tab, float2* cst, float* red, int ct, int nthreads) {
+  const int chunks = S.K / 8;
+  const bool writer = blockIdx.x == 0;
+  float v[kLnIter][8];
+  uint4 wraw[kLnIter];  // the LayerNorm weight, loaded with x, a and b
+  float part = 0.f;
+#pragma unroll
+  for (int it = 0; it < kLnIter; ++it) {
+    const int c = it * nthreads + ct;
+    wraw[it] = c < chunks ? ldg_cg_128(static_cast<const uint8_t*>(S.w) + static_cast<int64_t>(c) * 16)
+                          : make_uint4(0u, 0u, 0u, 0u);
+    if (c < chunks) {
+      load8_f32(static_cast<const uint8_t*>(S.x) + static_cast<int64_t>(c) * 16, bf, v[it]);
+      float t[8];
+      if (S.a) {
+        load8_f32(static_cast<const uint8_t*>(S.a) + static_cast<int64_t>(c) * 16, bf, t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[it][i] += t[i];
+      }
+      if (S.b) {
+        load8_f32(static_cast<const uint8_t*>(S.b) + static_cast<int64_t>(c) * 16, bf, t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[it][i] += t[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[it][i] = round_act(v[it][i], bf);
+        part += v[it][i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[it][i] = 0.f;
+    }
+  }
+  const float inv_h = 1.f / static_cast<float>(S.K);
+  const float mean = conv_sum(part, red, ct, nthreads) * inv_h;
+  float sq = 0.f;
+#pragma unroll
+  for (int it = 0; it < kLnIter; ++it)
+    if (it * nthreads + ct < chunks) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[it][i] - mean;
+        sq += d * d;
+      }
+    }
+  const float rstd = rsqrtf(conv_sum(sq, red + nthreads / 32, ct, nthreads) * inv_h + S.eps);
+#pragma unroll
+  for (int it = 0; it < kLnIter; ++it) {
+    if (it * nthreads >= chunks) break;  // uniform over the converter threads
+    const int c = it * nthreads + ct;
+    const bool valid = c < chunks;
+    float h[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (valid) {
+      float w[8];
+      raw_to_f32(wraw[it], bf, w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = round_act((v[it][i] - mean) * rstd * w[i], bf);
+      if (writer && S.x_out) store8_act(static_cast<uint8_t*>(S.x_out) + static_cast<int64_t>(c) * 16, v[it], bf);
+      if (writer && S.h_out) store8_act(static_cast<uint8_t*>(S.h_out) + static_cast<int64_t>(c) * 16, h, bf);
+    }
+    if (kTab) quant_chunk(h, valid, c, tab, cst);
+  }
+}
+
+// The same add + LayerNorm on its own (the final norm in front of the head): one CTA of the converter
+// threads' shape, so that its results are bit-identical to the fused prologue's.
+__global__ void __launch_bounds__(kConvWarps * 32, 1) add_ln_kernel(const __grid_constant__ Slot S, int bf) {
+  __shared__ float red[2 * kConvWarps];
+  griddep_wait();
+  stage_ln_slot<false>(S, bf != 0, nullptr, nullptr, red, threadIdx.x, kConvWarps * 32);
+  griddep_launch_dependents();
+}
+
+constexpr int kPreChunks = 8;  // chunks of 8 activations a converter thread loads before it quantises any
+
+__device__ void stage_x_tables(const TcParams& p, uint8_t* xs, float* red, int ct, int nthreads) {
+  // The plain slots' activations were written by the previous kernel: issue every load first (up to
+  // kPreChunks per thread, one round trip to memory), then quantise. Lists with more activations per thread
+  // load the rest chunk by chunk.
+  uint4 pre[kPreChunks];
+#pragma unroll
+  for (int i = 0; i < kPreChunks; ++i) {  // the i-th chunk this thread will quantise (constant index: registers)
+    int rem = i, c = -1;
+    const void* src = nullptr;
+    for (int sl = 0; sl < p.nslots; ++sl) {
+      const Slot& S = p.slots[sl];
+      if (S.ln) continue;
+      const int iters = (S.K / 8 + nthreads - 1) / nthreads;
+      if (rem < iters) {
+        c = rem * nthreads + ct;
+        src = c < S.K / 8 ? S.x : nullptr;
+        break;
+      }
+      rem -= iters;
+    }
+    pre[i] = src ? ldg_cg_128(static_cast<const uint8_t*>(src) + static_cast<int64_t>(c) * 16)
+                 : make_uint4(0u, 0u, 0u, 0u);
+  }
+  int n = 0;
   for (int sl = 0; sl < p.nslots; ++sl) {
     const Slot& S = p.slots[sl];
     uint8_t* tab = xs + S.tab_off;
     float2* cst = reinterpret_cast<float2*>(xs + S.cst_off);
-    const int chunks = S.K / 8;  // 16 per group
-    for (int base = 0; base < chunks; base += nthreads) {
-      const int c = base + ct;
-      const bool valid = c < chunks;
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (valid) {
-        __half h[8];
-        load8_as_half(static_cast<const uint8_t*>(S.x) + static_cast<int64_t>(c) * 16, p.x_bf16, h);
+    if (S.ln) {
+      stage_ln_slot<true>(S, p.x_bf16 != 0, tab, cst, red, ct, nthreads);
+    } else {
+      const int chunks = S.K / 8;  // 16 per group
+      for (int base = 0; base < chunks; base += nthreads, ++n) {
+        const int c = base + ct;
+        const bool valid = c < chunks;
+        uint4 raw = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __half2float(h[i]);
+        for (int i = 0; i < kPreChunks; ++i)
+          if (i == n) raw = pre[i];
+        if (n >= kPreChunks && valid) raw = ldg_cg_128(static_cast<const uint8_t*>(S.x) + static_cast<int64_t>(c) * 16);
+        float v[8];
+        raw_to_f32(raw, p.x_bf16, v);
+        quant_chunk(v, valid, c, tab, cst);
       }
-      float mx = 0.f, sum = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        mx = fmaxf(mx, fabsf(v[i]));
-        sum += v[i];
-      }
-      // a group is 16 chunks = 16 consecutive threads (nthreads is a multiple of 32)
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) {
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      }
-      const float delta = mx > 0.f ? mx / 32639.f : 1.f;
-      const float inv = 1.f / delta;
-      if (valid) {
-        uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
-#pragma unroll
-        for (int jp = 0; jp < 8; ++jp) {  // table position jp <- column (jp < 4 ? 2 jp : 2 (jp - 4) + 1)
-          const int col = jp < 4 ? 2 * jp : 2 * (jp - 4) + 1;
-          const int xi = __float2int_rn(fminf(fmaxf(v[col] * inv, -32639.f), 32639.f));
-          const int l = ((xi + 128) & 255) - 128;
-          const int h = (xi - l) >> 8;
-          hi[jp >> 2] |= (static_cast<uint32_t>(h) & 255u) << (8 * (jp & 3));
-          lo[jp >> 2] |= (static_cast<uint32_t>(l) & 255u) << (8 * (jp & 3));
-        }
-        // positions 8 * (c % 16) .. + 7 of the group: 16-position chunk (c % 16) / 2, half (c & 1)
-        uint8_t* dst = tab + (c >> 4) * kXGroupBytes + ((c & 15) >> 1) * 32 + (c & 1) * 8;
-        *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], hi[1]);
-        *reinterpret_cast<uint2*>(dst + 16) = make_uint2(lo[0], lo[1]);
-      }
-      if (valid && (c & 15) == 0) cst[c >> 4] = make_float2(delta, sum);
     }
     for (int i = ct; i < static_cast<int>(kXPad / 16); i += nthreads)
       reinterpret_cast<uint4*>(tab + S.G * kXGroupBytes)[i] = make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
-__device__ __forceinline__ const Entry& entry_of(const TcParams& p, int gb, int& e) {
-  while (e + 1 < p.count && gb >= p.e[e + 1].block_begin) ++e;
+// Block (within its entry) and pair range [p0, p1) of global work item gi of entry E.
+__device__ __forceinline__ void item_range(const Entry& E, int gi, int& blk, int& p0, int& p1) {
+  const int li = gi - E.item_begin;
+  blk = li / E.ks;
+  p0 = (li - blk * E.ks) * E.ppk;
+  p1 = min(p0 + E.ppk, (E.G + 1) / 2);
+}
+
+// The entry of global work item gi (entries hold consecutive item ranges; e only moves forward).
+__device__ __forceinline__ const Entry& entry_of(const TcParams& p, int gi, int& e) {
+  while (e + 1 < p.count && gi >= p.e[e + 1].item_begin) ++e;
   return p.e[e];
 }
 
@@ -172,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int C = gridDim.x, cta = blockIdx.x;
   const int nst = p.nst;
-  const int nlocal = (p.total_blocks - cta + C - 1) / C;  // this CTA's blocks: cta + j * C
+  const int nlocal = (p.total_items - cta + C - 1) / C;  // this CTA's work items: cta + j * C
   uint8_t* xs = smem + p.xs_off;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   // per set: full[nst], empty[nst], afull[kNP], mdone[kNP]
@@ -182,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
   auto afull = [&](int s, int b) { return bars + s * per_set + 2 * nst + b; };
   auto mdone = [&](int s, int b) { return bars + s * per_set + 2 * nst + kNP + b; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kSets * per_set);
+  float* aux = reinterpret_cast<float*>(smem + p.aux_off);  // [2 x kConvWarps] reduction, then SwiGLU exchange
 
   if (tid == 0) {
     for (int s = 0; s < kSets; ++s) {
@@ -221,10 +410,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
         issued[s] = 0;
         live[s] = j[s] < nlocal;
         if (live[s]) {
-          const int gb = cta + j[s] * C;
-          const Entry& E = entry_of(p, gb, e[s]);
-          nk[s] = (E.G + 1) / 2;
-          row0[s] = (gb - E.block_begin) * kRows;
+          const int gi = cta + j[s] * C;
+          const Entry& E = entry_of(p, gi, e[s]);
+          int blk;
+          item_range(E, gi, blk, k[s], nk[s]);
+          row0[s] = blk * kRows;
         }
       }
       bool ok = true;
@@ -244,14 +434,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
                            row0[s], full(s, slot));
           ++issued[s];
           if (++k[s] == nk[s]) {
-            k[s] = 0;
             j[s] += kSets;
             live[s] = j[s] < nlocal;
             if (live[s]) {
-              const int gb = cta + j[s] * C;
-              const Entry& E = entry_of(p, gb, e[s]);
-              nk[s] = (E.G + 1) / 2;
-              row0[s] = (gb - E.block_begin) * kRows;
+              const int gi = cta + j[s] * C;
+              const Entry& E = entry_of(p, gi, e[s]);
+              int blk;
+              item_range(E, gi, blk, k[s], nk[s]);
+              row0[s] = blk * kRows;
             }
           }
         }
@@ -270,10 +460,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
       int e = 0, q = 0;
       bool ok = true;
       for (int jj = s; jj < nlocal && ok; jj += kSets) {
-        const int gb = cta + jj * C;
-        const Entry& E = entry_of(p, gb, e);
+        const int gi = cta + jj * C;
+        const Entry& E = entry_of(p, gi, e);
+        int blk, p0, p1;
+        item_range(E, gi, blk, p0, p1);
         const uint32_t xtab = smem_u32(xs + p.slots[E.slot].tab_off);
-        for (int g = 0; g < E.G; g += 2, ++q) {
+        for (int g = 2 * p0; g < 2 * p1; g += 2, ++q) {
           const int b = q % kNP;
           if (!mbar_wait(afull(s, b), (q / kNP) & 1, ERR_TC_WAIT)) {
             ok = false;
@@ -298,17 +490,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
     const int quad = warp & 3;               // tensor-memory lane quadrant this warp may access
     const int rib = quad * 32 + lane;        // row in block = tensor-memory lane
     griddep_wait();                          // x may come from the previous kernel; y is written below
-    stage_x_tables(p, xs, tid - kFirstConv * 32, kConvWarps * 32);
+    stage_x_tables(p, xs, aux, tid - kFirstConv * 32, kConvWarps * 32);
     fence_proxy_async_smem();                // generic writes of the tables -> visible to the tensor core
     named_bar_sync(1, (kSets + kConvWarps) * 32);
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     int e = 0, q = 0, st = 0;
     bool ok = true;
     for (int jj = s; jj < nlocal; jj += kSets) {
-      const int gb = cta + jj * C;
-      const Entry& E = entry_of(p, gb, e);
+      const int gi = cta + jj * C;
+      const Entry& E = entry_of(p, gi, e);
       const int G = E.G;
-      const int row = (gb - E.block_begin) * kRows + rib;
+      int blk, p0, p1;
+      item_range(E, gi, blk, p0, p1);
+      const int row = blk * kRows + rib;
       const bool row_ok = row < E.N;
       const uint16_t* srow = E.s + static_cast<int64_t>(row_ok ? row : 0) * G;
       const uint16_t* mrow = E.m + static_cast<int64_t>(row_ok ? row : 0) * G;
@@ -317,9 +511,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
       // s * delta of the two groups of each pair whose results are pending, oldest pair first (0 for a missing
       // second group: its accumulator columns hold stale finite integers, which the zero scale cancels)
       float pa[kNP] = {0.f, 0.f}, pb[kNP] = {0.f, 0.f};
-      const int qp0 = q;  // pair counter of this set at the block's first pair
+      const int qp0 = q;  // pair counter of this set at the item's first pair
       const uint32_t a_set = tq + s * kSetCols, d_set = tq + s * kSetCols + kNP * kACols;
-      const int npairs = (G + 1) / 2;
+      const int npairs = p1 - p0;  // pairs of this item: p0 .. p1 - 1 of the block
       // codes of the next pair (both groups of one stage), software-pipelined one pair ahead
       uint4 wn[8];
       auto load_codes = [&](int k) {
@@ -343,9 +537,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
           }
         }
       };
-      // one pair of groups (g, g + 1): codes into tensor memory, and the results of the pair kNP back
+      // the item's pair k (groups g, g + 1 of the block): codes into tensor memory, results of the pair kNP back
       auto step = [&](int k, float s0, float m0, float s1, float m1) {
-        const int g = 2 * k;
+        const int g = 2 * (p0 + k);
         const bool two = g + 1 < G;
         const uint4 w[8] = {wn[0], wn[1], wn[2], wn[3], wn[4], wn[5], wn[6], wn[7]};
         __syncwarp();
@@ -402,22 +596,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
         if (lane == 0) mbar_arrive(afull(s, b));
       };
       load_codes(0);
+      const int g0 = 2 * p0, g1 = min(2 * p1, G);  // this item's groups
       if ((G & 7) == 0) {
-        // scales and mins of 8 groups per 16-byte load, fetched one 8-group chunk ahead
-        uint4 s8n = __ldg(reinterpret_cast<const uint4*>(srow)), m8n = __ldg(reinterpret_cast<const uint4*>(mrow));
-        for (int g8 = 0; g8 < G; g8 += 8) {
+        // scales and mins of 8 groups (4 pairs) per 16-byte load, fetched one chunk ahead. With G % 8 == 0 every
+        // item starts on a multiple of 8 groups and holds a multiple of 8 groups (slices are a multiple of 4
+        // pairs), so all four pairs of a chunk exist.
+        uint4 s8n = __ldg(reinterpret_cast<const uint4*>(srow + g0)), m8n = __ldg(reinterpret_cast<const uint4*>(mrow + g0));
+        for (int g8 = g0; g8 < g1; g8 += 8) {
           const uint4 s8 = s8n, m8 = m8n;
-          if (g8 + 8 < G) {
+          if (g8 + 8 < g1) {
             s8n = __ldg(reinterpret_cast<const uint4*>(srow + g8 + 8));
             m8n = __ldg(reinterpret_cast<const uint4*>(mrow + g8 + 8));
           }
+          const int k0 = (g8 - g0) >> 1;
 #pragma unroll
           for (int h = 0; h < 4; ++h)
-            step(g8 / 2 + h, half_at(s8, 2 * h), half_at(m8, 2 * h), half_at(s8, 2 * h + 1), half_at(m8, 2 * h + 1));
+            step(k0 + h, half_at(s8, 2 * h), half_at(m8, 2 * h), half_at(s8, 2 * h + 1), half_at(m8, 2 * h + 1));
         }
       } else {
         for (int k = 0; k < npairs; ++k) {
-          const int g = 2 * k;
+          const int g = 2 * (p0 + k);
           const bool two = g + 1 < G;
           step(k, __half2float(__ushort_as_half(__ldg(srow + g))), __half2float(__ushort_as_half(__ldg(mrow + g))),
                two ? __half2float(__ushort_as_half(__ldg(srow + g + 1))) : 0.f,
@@ -446,7 +644,62 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
           }
         }
       }
-      if (ok && row_ok) store_out(E.y, row, acc, p.y_bf16);
+      // ---- split K: every slice leaves its partial sums; the block's last slice to finish (an atomic ticket)
+      // adds them in slice order (the same result whichever slice finishes last) and runs the epilogue
+      if (E.ks > 1) {
+        p.ws_part[static_cast<int64_t>(gi) * kRows + rib] = acc;
+        __threadfence();
+        named_bar_sync(2 + s, 128);
+        volatile int* last = reinterpret_cast<volatile int*>(aux + 2 * kConvWarps + kSets * 2 * 64) + s;
+        if (rib == 0)
+          *last = atomicAdd(p.ws_ticket + E.block_begin + blk, 1u) == static_cast<unsigned int>(E.ks - 1) ? 1 : 0;
+        named_bar_sync(2 + s, 128);
+        if (!*last) continue;
+        __threadfence();
+        const float* parts = p.ws_part + static_cast<int64_t>(E.item_begin + blk * E.ks) * kRows + rib;
+        acc = 0.f;
+#pragma unroll 4
+        for (int k = 0; k < E.ks; ++k) acc += __ldcg(parts + k * kRows);
+        if (rib == 0) p.ws_ticket[E.block_begin + blk] = 0u;  // ready for the next launch
+      }
+      // ---- the block's results: stored, or routed as the engine's post kernel would (engine/fused.py:43-84)
+      if (E.epi == kEpiStore) {
+        if (ok && row_ok) store_out(E.y, row, acc, p.y_bf16);
+      } else {
+        const EpiP& P = p.epis[E.ep];
+        if (E.y && ok && row_ok) store_out(E.y, row, acc, p.y_bf16);
+        const float r = round_act(acc, p.y_bf16);  // what the engine's y buffer would hold
+        if (E.epi == kEpiRopeKv) {
+          const float pr = __shfl_xor_sync(0xffffffffu, r, 1);  // the other element of the rotary pair
+          const int64_t pos = *P.pos;
+          const bool pos_ok = pos >= 0 && pos < P.S;
+          if (!pos_ok && rib == 0) atomicOr(&g_device_error, ERR_ARG);
+          if (ok && row_ok && pos_ok) {
+            const int head = row / P.hd, dd = row - head * P.hd;
+            float o = r;
+            if (P.rope && head < P.nq + P.nkv) {  // pairs (2j, 2j + 1) rotated by pos * theta_j
+              const int64_t ci = pos * P.hd + (dd & ~1);
+              const float c = load_act(P.cos, ci, p.y_bf16), sn = load_act(P.sin, ci, p.y_bf16);
+              o = (dd & 1) ? r * c + pr * sn : r * c - pr * sn;
+            }
+            if (head < P.nq)
+              store_out(P.q_out, static_cast<int64_t>(head) * P.hd + dd, o, p.y_bf16);
+            else if (head < P.nq + P.nkv)
+              store_out(P.k_cache, (static_cast<int64_t>(head - P.nq) * P.S + pos) * P.hd + dd, o, p.y_bf16);
+            else
+              store_out(P.v_cache, (static_cast<int64_t>(head - P.nq - P.nkv) * P.S + pos) * P.hd + dd, o,
+                        p.y_bf16);
+          }
+        } else {  // kEpiSwiglu: rows 0..63 of the block are gate channels, rows 64..127 the matching up channels
+          float* xch = aux + 2 * kConvWarps + (s * 2 + (((jj - s) / kSets) & 1)) * 64;  // double-buffered per set
+          if (rib >= 64) xch[rib - 64] = r;
+          named_bar_sync(2 + s, 128);
+          if (rib < 64 && ok && row_ok) {
+            const float a = r / (1.f + __expf(-r)) * xch[rib];
+            store_out(P.act, static_cast<int64_t>(blk) * 64 + rib, a, p.y_bf16);
+          }
+        }
+      }
     }
   }
   mm4::tc_fence_before();
@@ -459,9 +712,81 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
 
 }  // namespace g4t
 
-int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,
-                        cudaStream_t stream) {
+int launch_add_ln(const rb_add_ln* ln, int dtype, int flags, cudaStream_t stream) {
   using namespace g4t;
+  Slot S = {};
+  S.x = ln->x;
+  S.a = ln->a;
+  S.b = ln->b;
+  S.w = ln->w;
+  S.x_out = ln->x_out;
+  S.h_out = ln->h_out;
+  S.eps = ln->eps;
+  S.ln = 1;
+  S.K = static_cast<int>(ln->H);
+  S.G = static_cast<int>(ln->H / 128);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kConvWarps * 32);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = (flags & RB_FLAG_PDL) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, add_ln_kernel, S, dtype == RB_BF16 ? 1 : 0) == cudaSuccess ? RB_OK : RB_ERR_LAUNCH;
+}
+
+namespace g4t {
+
+// Split-K plan of one launch. A converter set finishes about one pair of groups per microsecond, so a launch
+// with fewer 128-row blocks than num_sms x kSets sets (a decode layer's projections, 18-35 MB) would leave most
+// sets idle; its blocks are cut into slices of about ppk pairs so that about one item per set runs (a multiple
+// of 4 pairs where K % 1024 == 0, so that the 8-group scale loads stay aligned). Sets every entry's ks / ppk /
+// item_begin and p.total_items, and returns the workspace bytes the plan needs (0 without a split). Without
+// that much workspace the launch is not split.
+int64_t plan_split(TcParams& p, int num_sms, int64_t ws_bytes) {
+  int64_t pairs = 0;
+  int maxnp = 1;
+  for (int i = 0; i < p.count; ++i) {
+    const int np = (p.e[i].G + 1) / 2, nb = (p.e[i].N + kRows - 1) / kRows;
+    pairs += static_cast<int64_t>(np) * nb;
+    maxnp = std::max(maxnp, np);
+  }
+  auto assign = [&](int ppk) -> int64_t {
+    int items = 0;
+    bool split = false;
+    for (int i = 0; i < p.count; ++i) {
+      Entry& E = p.e[i];
+      const int np = (E.G + 1) / 2, nb = (E.N + kRows - 1) / kRows;
+      const int pk = (E.G & 7) == 0 ? (ppk + 3) & ~3 : ppk;
+      E.ks = pk >= np ? 1 : (np + pk - 1) / pk;
+      E.ppk = E.ks == 1 ? np : pk;
+      E.item_begin = items;
+      items += nb * E.ks;
+      split |= E.ks > 1;
+    }
+    p.total_items = items;
+    return split ? split_ticket_bytes(p.total_blocks) + static_cast<int64_t>(items) * kRows * 4 : 0;
+  };
+  const int64_t sets = static_cast<int64_t>(num_sms) * kSets;
+  if (ws_bytes > 0 && p.total_blocks < sets) {
+    const int64_t t = std::max<int64_t>(2, (pairs + sets - 1) / sets);
+    if (t < maxnp) {
+      const int64_t need = assign(static_cast<int>(t));
+      if (need <= ws_bytes) return need;
+    }
+  }
+  return assign(maxnp);
+}
+
+}  // namespace g4t
+
+int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,
+                        cudaStream_t stream, const rb_gemv_epi* epi, const rb_add_ln* ln, void* ws,
+                        int64_t ws_bytes, int64_t* query) {
+  using namespace g4t;
+  if (query) *query = 0;
   constexpr uint32_t kSmemMax = 227 * 1024;
   auto encode = mm4::encode_fn();
   if (!encode) return RB_ERR_DEVICE;
@@ -474,23 +799,40 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
     p.prefetch = (flags & RB_FLAG_PDL) && (flags & RB_FLAG_PREFETCH_WEIGHTS) ? 1 : 0;
     // instruction descriptor: D int32, A unsigned 8-bit, B signed 8-bit, both K-major, N = 8, M = 128
     p.idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((8u >> 3) << 17) | ((static_cast<uint32_t>(kRows) >> 4) << 24);
-    const uint32_t kBars = kSets * (2 * kMaxStages + 2 * kNP) * 8 + 16;
-    int nslots = 0, blocks = 0, take = 0;
+    const uint32_t kBars = kSets * (2 * kMaxStages + 2 * kNP) * 8 + 16 + 16 + kAuxBytes;
+    int nslots = 0, blocks = 0, take = 0, nepis = 0;
     uint32_t x_bytes = 0;
     for (; take < n; ++take) {
       const rb_gemv_desc& D = d[done + take];
       const uint32_t G = static_cast<uint32_t>(D.K / 128);
+      const bool from_ln = D.x == nullptr;  // multiplies the prologue's normalised vector
+      const int kind = epi ? epi[done + take].kind : kEpiStore;
+      if (from_ln && !ln) return RB_ERR_NULL;
       int slot = -1;
       for (int i = 0; i < nslots; ++i)
-        if (p.slots[i].x == D.x && p.slots[i].K == static_cast<int>(D.K)) slot = i;
+        if (p.slots[i].ln == (from_ln ? 1 : 0) && (from_ln || p.slots[i].x == D.x) &&
+            p.slots[i].K == static_cast<int>(D.K))
+          slot = i;
       const uint32_t add_x = slot < 0 ? (G * kXGroupBytes + kXPad + ((G * 8 + 15) & ~15u)) : 0u;
       if (slot < 0 && nslots == kMaxSlots) break;
       if (1024 + kSets * 2 * kStageBytes + x_bytes + add_x + kBars > kSmemMax) break;
+      if (kind != kEpiStore && nepis == kMaxEpis) break;
       if (slot < 0) {
         slot = nslots++;
-        p.slots[slot].x = D.x;
-        p.slots[slot].K = static_cast<int>(D.K);
-        p.slots[slot].G = static_cast<int>(G);
+        Slot& S = p.slots[slot];
+        S = Slot{};
+        S.x = from_ln ? ln->x : D.x;
+        if (from_ln) {
+          S.ln = 1;
+          S.a = ln->a;
+          S.b = ln->b;
+          S.w = ln->w;
+          S.x_out = ln->x_out;
+          S.h_out = ln->h_out;
+          S.eps = ln->eps;
+        }
+        S.K = static_cast<int>(D.K);
+        S.G = static_cast<int>(G);
         x_bytes += add_x;
       }
       Entry& E = p.e[take];
@@ -501,6 +843,25 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
       E.G = static_cast<int>(G);
       E.slot = slot;
       E.block_begin = blocks;
+      E.epi = kind;
+      E.ep = 0;
+      if (kind != kEpiStore) {
+        const rb_gemv_epi& X = epi[done + take];
+        EpiP& P = p.epis[nepis];
+        P.pos = X.pos;
+        P.cos = X.cos;
+        P.sin = X.sin;
+        P.q_out = X.q_out;
+        P.k_cache = X.k_cache;
+        P.v_cache = X.v_cache;
+        P.act = X.act_out;
+        P.S = X.cache_len;
+        P.rope = X.rope;
+        P.nq = X.n_q_heads;
+        P.nkv = X.n_kv_heads;
+        P.hd = X.head_dim;
+        E.ep = nepis++;
+      }
       blocks += static_cast<int>((D.N + kRows - 1) / kRows);
       const cuuint64_t dims[2] = {static_cast<cuuint64_t>(D.K / 2), static_cast<cuuint64_t>(D.N)};
       const cuuint64_t strides[1] = {static_cast<cuuint64_t>(D.K / 2)};
@@ -512,9 +873,18 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
         return RB_ERR_SHAPE;
     }
     if (take == 0) return RB_ERR_SHAPE;
+    if ((epi || ln) && take < count) return RB_ERR_SHAPE;  // the fused glue needs the whole list in one launch
     p.count = take;
     p.nslots = nslots;
     p.total_blocks = blocks;
+    const int64_t need = plan_split(p, num_sms, query ? INT64_MAX : (ws ? ws_bytes : 0));
+    if (query) {
+      *query = std::max(*query, need);
+      done += take;
+      continue;
+    }
+    p.ws_ticket = static_cast<unsigned int*>(ws);
+    p.ws_part = need ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + split_ticket_bytes(blocks)) : nullptr;
     // layout (from a 1024-aligned base): [stages: kSets x nst x 16 KB][activation tables][barriers][tmem slot]
     uint32_t off = 0;
     for (int i = 0; i < nslots; ++i) {
@@ -530,11 +900,12 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
     p.nst = nst;
     p.xs_off = static_cast<uint32_t>(kSets * nst) * kStageBytes;
     p.bar_off = (p.xs_off + xtot + 15) & ~15u;
-    const uint32_t smem = 1024 + p.bar_off + kSets * (2 * nst + 2 * kNP) * 8 + 16;
+    p.aux_off = (p.bar_off + kSets * (2 * nst + 2 * kNP) * 8 + 16 + 15) & ~15u;
+    const uint32_t smem = 1024 + p.aux_off + kAuxBytes;
     cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gemv_int4_tc_kernel), static_cast<int>(kSmemMax));
     if (e != cudaSuccess) return RB_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(std::min(num_sms, std::max(1, blocks)));
+    cfg.gridDim = dim3(std::min(num_sms, std::max(1, p.total_items)));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;

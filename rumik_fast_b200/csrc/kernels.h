@@ -54,7 +54,18 @@ int launch_tp_allreduce(const __half* a, const __half* b, __half* out, int64_t n
                         int world, uint32_t flag_off, uint32_t counter_off, int flags, cudaStream_t stream);
 int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,
                            cudaStream_t stream);
+// Decode attention (attn_decode.cu): workspace bytes (-1: unsupported shape) and the launch.
+int64_t attn_decode_workspace(int nq, int nkv, int hd);
+int launch_attn_decode(const void* q, const void* kc, const void* vc, const int64_t* pos, void* out, int nq, int nkv,
+                       int64_t S, float scale, void* ws, int dtype, int flags, int num_sms, cudaStream_t stream);
+// The add + LayerNorm of rb_add_layernorm (one CTA), bit-identical to the prologue of rb_gemv_int4_fused.
+int launch_add_ln(const rb_add_ln* ln, int dtype, int flags, cudaStream_t stream);
+// epi (per entry, may be null) and ln (may be null): the fused decode-layer glue of rb_gemv_int4_fused; a call
+// with either must fit one launch (RB_ERR_SHAPE otherwise).
+// ws / ws_bytes: split-K workspace (may be null: no split). With `query` non-null nothing is launched and
+// *query receives the workspace bytes the launches of this list would use.
 int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,
-                        cudaStream_t stream);
+                        cudaStream_t stream, const rb_gemv_epi* epi = nullptr, const rb_add_ln* ln = nullptr,
+                        void* ws = nullptr, int64_t ws_bytes = 0, int64_t* query = nullptr);
 
 }  // namespace rb

@@ -9,3 +9,4 @@
 #include "gemv_int8_tc.cu"
 #include "mm_int4_tc.cu"
 #include "allreduce.cu"
+#include "attn_decode.cu"

@@ -1,0 +1,160 @@
+"""Decode-layer glue fused into the int4 GEMV launch (rb_gemv_int4_fused, rb_add_layernorm).
+
+rumik-fast's decode step runs, per layer (engine/rumik_fused.py:84-116),
+
+    gemv(h, w_in) -> post -> attention -> gemv(w_o), gemv(w_down) -> add_ln
+
+where add_ln (engine/fused.py:29-40) forms the next residual x + o + down and its LayerNorm h, and post
+(engine/fused.py:43-84) applies the rotary embedding, writes the new key/value to the cache and forms
+silu(gate) * up. Here the add_ln runs inside the NEXT layer's input GEMV launch (every CTA normalises the
+3072-element vector while it stages its activation tables) and post runs in that launch's epilogue (each
+output row is routed to the query buffer, the caches or the MLP activation as it is produced), so the input
+side of a layer is one kernel:
+
+    layer = AddLnGemvPost(qkv, gate_up_interleaved, add_ln=AddLn(x, o_out, down_out, ln_w, x_next, eps), ...)
+    layer()                       # add_ln + QKV GEMV + gate_up GEMV + rope + KV write + silu(gate) * up
+
+Weights: the engine's fused w_in rows [q | k | v | gate | up] (engine/rumik_int4.py:95-100) are split with
+split_w_in into the q|k|v rows (unchanged) and the gate|up rows re-ordered by interleave_gate_up (tiles of 64
+gate rows followed by the 64 matching up rows), so that a gate channel and its up channel land in one
+128-row block of the kernel. Both are one-time permutations at load; the codes themselves are unchanged.
+
+The residual stream alternates between two buffers (every CTA reads x while one CTA writes x + o + down).
+"""
+import ctypes
+
+import torch
+
+from . import _lib, config
+from .cuda_gemv import _on_device, _require
+from .gemv_set import _ws_len, _ws_ptr, workspace
+
+G = 128
+TILE = 64  # gate (or up) channels per 128-row block of the SwiGLU epilogue
+
+
+# ---------------------------------------------------------------------------------------------- weight layout
+def gate_up_order(inter, device=None):
+    """Row permutation of interleave_gate_up: new row r reads old row order[r] of [gate (inter) | up (inter)]."""
+    _require(inter % TILE == 0, f"MLP width {inter} must be a multiple of {TILE}")
+    c = torch.arange(inter, device=device).view(-1, TILE)
+    return torch.stack([c, c + inter], 1).reshape(-1)
+
+
+def interleave_gate_up(q, s, m):
+    """[gate; up] int4 rows (q [2I, K/2], s/m [2I, K/128]) -> the SwiGLU epilogue's order: per 128-row block,
+    64 gate channels then the same 64 up channels."""
+    _require(q.shape[0] % (2 * TILE) == 0, f"gate_up rows {q.shape[0]} must be a multiple of {2 * TILE}")
+    order = gate_up_order(q.shape[0] // 2, q.device)
+    return q[order].contiguous(), s[order].contiguous(), m[order].contiguous()
+
+
+def split_w_in(q, s, m, n_q_heads, n_kv_heads, head_dim):
+    """The engine's fused w_in rows [q | k | v | gate | up] -> ((q, s, m) of q|k|v, (q, s, m) of gate|up in the
+    SwiGLU order)."""
+    nqkv = (n_q_heads + 2 * n_kv_heads) * head_dim
+    _require(q.shape[0] > nqkv, "w_in has no MLP rows after q|k|v")
+    qkv = tuple(t[:nqkv].contiguous() for t in (q, s, m))
+    gu = interleave_gate_up(*(t[nqkv:] for t in (q, s, m)))
+    return qkv, gu
+
+
+# ---------------------------------------------------------------------------------------------- descriptors
+class AddLn:
+    """The add + LayerNorm prologue: x_out = x + a + b (fp32 sum, rounded once), h = LayerNorm(x_out) * w
+    (engine/fused.py:29-40). a and b may be None; h_out (optional) receives h."""
+
+    def __init__(self, x, a, b, w, x_out, eps=1e-5, h_out=None):
+        H = x.numel()
+        for t, nm in ((x, "x"), (a, "a"), (b, "b"), (w, "w"), (x_out, "x_out"), (h_out, "h_out")):
+            if t is None:
+                continue
+            _require(t.is_cuda and t.device == x.device, f"{nm} must be on x's CUDA device")
+            _require(t.dtype == x.dtype and t.numel() == H and t.is_contiguous(),
+                     f"{nm} must be a contiguous [{H}] {x.dtype} vector")
+        _require(H % G == 0 and H <= 12288, f"H={H} must be a multiple of {G} and <= 12288")
+        self.tensors = (x, a, b, w, x_out, h_out)
+        self.H, self.eps, self.dtype, self.device = H, float(eps), x.dtype, x.device
+        ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+        self.c = _lib.AddLn(ptr(x), ptr(a), ptr(b), ptr(w), ptr(x_out), ptr(h_out), H, self.eps)
+
+
+def add_layernorm(ln: AddLn):
+    """Run the add + LayerNorm on its own (the final norm in front of the head)."""
+    with _on_device(ln.device):
+        st = _lib.lib().rb_add_layernorm(ctypes.byref(ln.c), _lib.dtype_code(ln.dtype), config.flags(),
+                                         _lib.stream_ptr(ln.device))
+    _lib.check("rb_add_layernorm", st)
+
+
+def _int4(w, K=None):
+    q, s, m = w
+    N, Kq = q.shape[0], q.shape[1] * 2
+    _require(q.dtype == torch.uint8 and q.is_contiguous() and q.is_cuda, "q must be contiguous CUDA uint8 [N, K/2]")
+    _require(K is None or Kq == K, f"weights have K={Kq}, activations {K}")
+    for t, nm in ((s, "s"), (m, "m")):
+        _require(t.dtype == torch.float16 and t.is_contiguous() and tuple(t.shape) == (N, Kq // G),
+                 f"{nm} must be a contiguous fp16 [{N}, {Kq // G}] tensor")
+    return q, s, m, N, Kq
+
+
+class AddLnGemvPost:
+    """One decode layer's input side as ONE launch: [add_ln ->] gemv(w_qkv), gemv(w_gate_up) -> post.
+
+    qkv      (q, s, m) of the q|k|v rows, N = (n_q_heads + 2 n_kv_heads) head_dim
+    gate_up  (q, s, m) of the gate|up rows in interleave_gate_up order
+    add_ln   an AddLn (its h is the GEMV input), or None with h = the input vector
+    pos      int64 [1] device tensor: the position (cache slot) of this token
+    cos, sin [cache_len, head_dim] rotary tables (engine/rumik_int4.py:107-109)
+    k_cache, v_cache  [n_kv_heads, cache_len, head_dim];  q_out [n_q_heads * head_dim];  act [inter]
+    rope     False for the layers without position embedding
+    y_qkv, y_gate_up  optional buffers that also receive the plain GEMV results
+    Built once (graph-capture safe to call); every tensor must stay alive.
+    """
+
+    def __init__(self, qkv, gate_up, *, pos, cos, sin, k_cache, v_cache, q_out, act, n_q_heads, n_kv_heads,
+                 add_ln=None, h=None, rope=True, y_qkv=None, y_gate_up=None):
+        _require((add_ln is None) != (h is None), "give exactly one of add_ln and h")
+        src = add_ln.tensors[0] if add_ln is not None else h
+        self.device, self.x_dtype = src.device, src.dtype
+        H = src.numel()
+        dt = act.dtype
+        _require(dt in (torch.float16, torch.bfloat16), "act must be fp16 or bf16")
+        for t, nm in ((cos, "cos"), (sin, "sin"), (k_cache, "k_cache"), (v_cache, "v_cache"), (q_out, "q_out")):
+            _require(t.dtype == dt and t.is_contiguous() and t.device == self.device,
+                     f"{nm} must be a contiguous {dt} tensor on {self.device}")
+        _require(pos.dtype == torch.int64 and pos.device == self.device, "pos must be an int64 tensor on the device")
+        nkv, S, hd = k_cache.shape
+        _require(nkv == n_kv_heads and tuple(v_cache.shape) == (nkv, S, hd), "caches must be [n_kv_heads, S, hd]")
+        _require(tuple(cos.shape) == (S, hd) and tuple(sin.shape) == (S, hd), f"cos/sin must be [{S}, {hd}]")
+        _require(q_out.numel() == n_q_heads * hd, "q_out must hold n_q_heads * head_dim elements")
+        qq, qs, qm, Nqkv, K1 = _int4(qkv, H)
+        gq, gs, gm, Ngu, K2 = _int4(gate_up, H)
+        _require(Nqkv == (n_q_heads + 2 * n_kv_heads) * hd, "qkv rows must be (n_q_heads + 2 n_kv_heads) head_dim")
+        _require(Ngu % (2 * TILE) == 0 and act.numel() == Ngu // 2, "act must hold the N/2 MLP channels")
+        for y, N in ((y_qkv, Nqkv), (y_gate_up, Ngu)):
+            _require(y is None or (y.dtype == dt and y.numel() == N and y.is_contiguous()), "bad y buffer")
+        xp = None if add_ln is not None else h.data_ptr()
+        yp = lambda y: y.data_ptr() if y is not None else None  # noqa: E731
+        descs = (_lib.GemvDesc * 2)()
+        descs[0] = _lib.GemvDesc(xp, yp(y_qkv), qq.data_ptr(), qs.data_ptr(), qm.data_ptr(), Nqkv, H)
+        descs[1] = _lib.GemvDesc(xp, yp(y_gate_up), gq.data_ptr(), gs.data_ptr(), gm.data_ptr(), Ngu, H)
+        epis = (_lib.GemvEpi * 2)()
+        epis[0] = _lib.GemvEpi(_lib.EPI_ROPE_KV, int(bool(rope)), n_q_heads, n_kv_heads, hd, S, pos.data_ptr(),
+                               cos.data_ptr(), sin.data_ptr(), q_out.data_ptr(), k_cache.data_ptr(),
+                               v_cache.data_ptr(), None)
+        epis[1] = _lib.GemvEpi(_lib.EPI_SWIGLU, 0, 0, 0, 0, 0, None, None, None, None, None, None, act.data_ptr())
+        self._descs, self._epis, self._ln = descs, epis, add_ln
+        self.ws = workspace(descs, 2, self.device)
+        self._keep = (qkv, gate_up, pos, cos, sin, k_cache, v_cache, q_out, act, h, y_qkv, y_gate_up)
+        self.y_dtype = dt
+        self.bytes = sum(t.numel() for t in (qq, gq)) + 4 * (qs.numel() + gs.numel())
+
+    def __call__(self):
+        L = _lib.lib()
+        lnp = ctypes.byref(self._ln.c) if self._ln is not None else None
+        with _on_device(self.device):
+            st = L.rb_gemv_int4_fused(self._descs, self._epis, 2, lnp, _ws_ptr(self.ws), _ws_len(self.ws),
+                                      _lib.dtype_code(self.x_dtype), _lib.dtype_code(self.y_dtype), config.flags(),
+                                      _lib.stream_ptr(self.device))
+        _lib.check("rb_gemv_int4_fused", st)

@@ -45,10 +45,30 @@ class Int4GemvSet:
             descs[i] = _lib.GemvDesc(x.data_ptr(), y.data_ptr(), q.data_ptr(), s.data_ptr(), m.data_ptr(), N, K)
         self._descs = descs
         self.bytes = sum(q.numel() + 4 * s.numel() + 2 * x.numel() + 2 * y.numel() for x, q, s, m, y in self.entries)
+        self.ws = workspace(descs, len(self.entries), self.device)
 
     def __call__(self):
         L = _lib.lib()
         with _on_device(self.device):
-            st = L.rb_gemv_int4_multi(self._descs, len(self.entries), _lib.dtype_code(self.x_dtype),
-                                      _lib.dtype_code(self.y_dtype), config.flags(), _lib.stream_ptr(self.device))
-        _lib.check("rb_gemv_int4_multi", st)
+            st = L.rb_gemv_int4_multi_ws(self._descs, len(self.entries), _ws_ptr(self.ws), _ws_len(self.ws),
+                                         _lib.dtype_code(self.x_dtype), _lib.dtype_code(self.y_dtype), config.flags(),
+                                         _lib.stream_ptr(self.device))
+        _lib.check("rb_gemv_int4_multi_ws", st)
+
+
+def workspace(descs, count, device):
+    """The zeroed split-K workspace of a GEMV list (None when its launches do not split K): a list with fewer
+    128-row blocks than 3 x the SM count spreads each block over several converter sets."""
+    with _on_device(device):
+        need = _lib.lib().rb_gemv_int4_workspace(descs, count)
+    if need < 0:
+        _lib.check("rb_gemv_int4_workspace", -need)
+    return torch.zeros(need, dtype=torch.uint8, device=device) if need > 0 else None
+
+
+def _ws_ptr(ws):
+    return ws.data_ptr() if ws is not None else None
+
+
+def _ws_len(ws):
+    return ws.numel() if ws is not None else 0

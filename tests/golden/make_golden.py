@@ -12,7 +12,13 @@ reference on the CPU and records, for small seeded inputs, the reference's outpu
   * golden_int8.npz : bf16 head rows -> reference quantize_int8_rows(w, pad_to=16) -> (q, s); and
                       y = ((q - 128) * s) @ x (kernels/cuda_gemv.py:245-246).
   * golden_mm.npz   : Y = X.float() @ dequantize(q, s, m).t() (kernels/mm_int4.py:96).
-bf16 tensors are stored as uint16 bit patterns.
+  * golden_glue.npz : the decode-layer glue around the GEMVs, with engine/rumik_int4.py's own cohere_ln
+                      (:38-43) and rope (:46-52): add_ln's residual sum (engine/fused.py:35-36, restated: an fp32
+                      sum rounded once) then cohere_ln; rope of query/key heads at one position with the rotary
+                      tables built as engine/rumik_int4.py:107-109; silu(gate) * up in fp32 (engine/fused.py:83,
+                      with torch's silu), for bf16 (the engine's type) and fp16; decode attention with the
+                      reference's _attend (engine/rumik_int4.py:163-171) and its decode mask (:204), bf16.
+bf16 tensors are stored as uint16 bit patterns.  `--which glue` (or int4, int8, mm) regenerates one file.
 """
 import argparse
 import os
@@ -35,8 +41,13 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RUMIK_REFERENCE"), required="RUMIK_REFERENCE" not in os.environ,
                     help="root of the rumik-fast checkout (or set RUMIK_REFERENCE)")
+    ap.add_argument("--which", default="all", choices=["all", "int4", "int8", "mm", "glue"])
     a = ap.parse_args()
     sys.path.insert(0, os.path.join(a.ref, "kernels"))
+    if a.which in ("all", "glue"):
+        make_glue(a.ref)
+    if a.which == "glue":
+        return
     import int4_gemv as ref4  # noqa: E402  (reference module)
     import cuda_gemv as refc  # noqa: E402  (reference module; load_inline is only called lazily)
 
@@ -102,6 +113,56 @@ def main():
     np.savez_compressed(os.path.join(HERE, "golden_mm.npz"), **outm)
     for f in ("golden_int4.npz", "golden_int8.npz", "golden_mm.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
+
+
+def make_glue(ref_root):
+    sys.path.insert(0, os.path.join(ref_root, "engine"))
+    import rumik_int4 as refe  # noqa: E402  (reference module: cohere_ln, rope)
+    import torch.nn.functional as F
+
+    out = {}
+    for dname, dt in (("bf16", torch.bfloat16), ("f16", torch.float16)):
+        g = torch.Generator().manual_seed(40 if dt == torch.bfloat16 else 41)
+        H, eps = 384, 1e-5
+        x = (torch.randn(H, generator=g) * 4).to(dt)
+        a_ = torch.randn(H, generator=g).to(dt)
+        b_ = (torch.randn(H, generator=g) * 0.5).to(dt)
+        w = (1 + 0.1 * torch.randn(H, generator=g)).to(dt)
+        s = (x.float() + a_.float() + b_.float()).to(dt)          # engine/fused.py:35-36
+        h = refe.cohere_ln(s, w, eps)
+        hn = refe.cohere_ln(x, w, eps)                            # no added terms
+        out.update({f"{dname}_ln_x": bits(x), f"{dname}_ln_a": bits(a_), f"{dname}_ln_b": bits(b_),
+                    f"{dname}_ln_w": bits(w), f"{dname}_ln_s": bits(s), f"{dname}_ln_h": bits(h),
+                    f"{dname}_ln_hn": bits(hn)})
+        nq, nkv, hd, S, pos, theta = 3, 2, 64, 40, 17, 10000.0
+        inv = 1.0 / (theta ** (torch.arange(0, hd, 2).float() / hd))   # engine/rumik_int4.py:107-109
+        ang = torch.outer(torch.arange(S).float(), inv).repeat_interleave(2, -1)
+        cos, sin = ang.cos().to(dt), ang.sin().to(dt)
+        y = torch.randn((nq + 2 * nkv) * hd, generator=g).to(dt)
+        qh = y[:nq * hd].view(nq, 1, hd)
+        kh = y[nq * hd:(nq + nkv) * hd].view(nkv, 1, hd)
+        out.update({f"{dname}_rope_y": bits(y), f"{dname}_rope_cos": bits(cos), f"{dname}_rope_sin": bits(sin),
+                    f"{dname}_rope_q": bits(refe.rope(qh, cos[pos:pos + 1], sin[pos:pos + 1]).reshape(-1)),
+                    f"{dname}_rope_k": bits(refe.rope(kh, cos[pos:pos + 1], sin[pos:pos + 1]).reshape(nkv, hd)),
+                    f"{dname}_rope_meta": np.array([nq, nkv, hd, S, pos, theta])})
+        inter = 256
+        gt = (torch.randn(inter, generator=g) * 2).to(dt)
+        up = torch.randn(inter, generator=g).to(dt)
+        out.update({f"{dname}_sw_g": bits(gt), f"{dname}_sw_u": bits(up),
+                    f"{dname}_sw_act": bits((F.silu(gt.float()) * up.float()).to(dt))})
+    # decode attention: 6 query heads on 2 key-value heads, 50 cache slots, position 33
+    import types
+    g = torch.Generator().manual_seed(42)
+    nq, nkv, hd, S, pos = 6, 2, 128, 50, 33
+    q = torch.randn(nq * hd, generator=g).to(torch.bfloat16)
+    kc = torch.randn(nkv, S, hd, generator=g).to(torch.bfloat16)
+    vc = torch.randn(nkv, S, hd, generator=g).to(torch.bfloat16)
+    bias = torch.where(torch.arange(S) <= pos, 0.0, float("-inf"))
+    o = refe.RumikInt4._attend(types.SimpleNamespace(hd=hd), q.view(nq, 1, hd), kc, vc, bias)[0]
+    out.update({"attn_q": bits(q), "attn_k": bits(kc), "attn_v": bits(vc), "attn_o": bits(o),
+                "attn_meta": np.array([nq, nkv, hd, S, pos])})
+    np.savez_compressed(os.path.join(HERE, "golden_glue.npz"), **out)
+    print("golden_glue.npz", os.path.getsize(os.path.join(HERE, "golden_glue.npz")), "bytes")
 
 
 if __name__ == "__main__":

@@ -90,3 +90,42 @@ def test_matches_single_gemv_bitwise():
     y2 = torch.empty_like(y1)
     rb.Int4GemvSet([(x, q, s, m, y2)])()
     assert torch.allclose(y1.float(), y2.float(), rtol=1e-3, atol=1e-3 * y1.float().abs().max().item())
+
+
+def _plain(ent):
+    """The same list through rb_gemv_int4_multi (no workspace: never split)."""
+    import ctypes  # noqa: F401
+    from rumik_fast_b200 import _lib
+    set_ = rb.Int4GemvSet(ent)
+    L = _lib.lib()
+    st = L.rb_gemv_int4_multi(set_._descs, len(ent), _lib.dtype_code(set_.x_dtype), _lib.dtype_code(set_.y_dtype),
+                              rb.config.flags(), _lib.stream_ptr(torch.device(DEV)))
+    _lib.check("rb_gemv_int4_multi", st)
+
+
+@pytest.mark.parametrize("shapes", [
+    [(3072, 3072), (3072, 8192)],                    # a decode layer's o_proj + down_proj: 48 blocks
+    [(5120, 3072), (16384, 3072)],                   # QKV + gate_up: 168 blocks
+    [(1000, 384), (130, 640), (7, 1152), (256, 16384)],  # odd group counts (G = 3, 5, 9), ragged N, long K
+])
+def test_split_k_lists(shapes):
+    """Lists with fewer blocks than 3 x the SM count run with K split over converter sets: the result matches
+    the oracle, is the same on every call, and the per-block counters are zero again afterwards."""
+    host, ent = build(shapes, nx=2, seed=7)
+    st = rb.Int4GemvSet(ent)
+    assert st.ws is not None                         # these lists do split
+    st()
+    torch.cuda.synchronize()
+    check(host, ent, "split-K")
+    first = [e[4].clone() for e in ent]
+    for _ in range(3):
+        st()
+    torch.cuda.synchronize()
+    assert all(torch.equal(a, e[4]) for a, e in zip(first, ent))
+    n_blocks = sum((n + 127) // 128 for n, _ in shapes)
+    assert torch.count_nonzero(st.ws[:4 * n_blocks]) == 0
+    for e in ent:                                    # unsplit launch of the same list: the same GEMVs
+        e[4].fill_(float("nan"))
+    _plain(ent)
+    torch.cuda.synchronize()
+    check(host, ent, "unsplit")

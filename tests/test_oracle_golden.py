@@ -99,3 +99,59 @@ def test_bf16_round_trip():
     b = O.f32_to_bf16_bits(f)
     back = O.bf16_bits_to_f32(b)
     assert np.all(np.abs(back - f) <= np.abs(f) * 2 ** -8)
+
+
+# ---- decode-layer glue (engine/fused.py add_ln / post), pinned to the reference's cohere_ln and rope ----
+@pytest.fixture(scope="module")
+def gg():
+    return np.load(os.path.join(GOLD, "golden_glue.npz"))
+
+
+def _stored(a, dt):
+    """Fixture storage (bf16 bit patterns or float16) -> float32 values."""
+    return O.act_to_f32(a, dt)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_add_ln_matches_reference(gg, dt):
+    s, h = O.add_ln_ref(gg[f"{dt}_ln_x"], gg[f"{dt}_ln_a"], gg[f"{dt}_ln_b"], gg[f"{dt}_ln_w"], 1e-5, dt)
+    assert np.array_equal(s, _stored(gg[f"{dt}_ln_s"], dt))           # one fp32 sum, one rounding: exact
+    # the mean and variance are fp32 sums in another order than torch's: at most one unit in the last place
+    assert O.ulp_diff(h, _stored(gg[f"{dt}_ln_h"], dt), dt).max() <= 1
+    _, hn = O.add_ln_ref(gg[f"{dt}_ln_x"], None, None, gg[f"{dt}_ln_w"], 1e-5, dt)
+    assert O.ulp_diff(hn, _stored(gg[f"{dt}_ln_hn"], dt), dt).max() <= 1
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_rope_kv_matches_reference(gg, dt):
+    nq, nkv, hd, S, pos, theta = (int(v) if i < 5 else float(v) for i, v in enumerate(gg[f"{dt}_rope_meta"]))
+    cos, sin = O.rope_tables(S, hd, theta, dt)
+    # the oracle's tables against the reference's: fp32 cos/sin of the same angles, rounded to 16 bits
+    assert O.ulp_diff(_stored(cos, dt), _stored(gg[f"{dt}_rope_cos"], dt), dt).max() <= 1
+    assert O.ulp_diff(_stored(sin, dt), _stored(gg[f"{dt}_rope_sin"], dt), dt).max() <= 1
+    y = _stored(gg[f"{dt}_rope_y"], dt)
+    q, k, v = O.rope_kv_ref(y, pos, gg[f"{dt}_rope_cos"], gg[f"{dt}_rope_sin"], nq, nkv, hd, True, dt)
+    assert np.array_equal(q, _stored(gg[f"{dt}_rope_q"], dt))
+    assert np.array_equal(k, _stored(gg[f"{dt}_rope_k"], dt).reshape(nkv, hd))
+    assert np.array_equal(v, y[(nq + nkv) * hd:].reshape(nkv, hd))
+    q0, k0, _ = O.rope_kv_ref(y, pos, None, None, nq, nkv, hd, False, dt)   # no position embedding: a copy
+    assert np.array_equal(q0, y[:nq * hd]) and np.array_equal(k0.reshape(-1), y[nq * hd:(nq + nkv) * hd])
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_swiglu_matches_reference(gg, dt):
+    act = O.swiglu_ref(_stored(gg[f"{dt}_sw_g"], dt), _stored(gg[f"{dt}_sw_u"], dt), dt)
+    assert O.ulp_diff(act, _stored(gg[f"{dt}_sw_act"], dt), dt).max() <= 1
+
+
+def test_gate_up_order_is_a_tiled_interleave():
+    order = O.gate_up_order(256)
+    assert sorted(order.tolist()) == list(range(512))
+    assert order[:64].tolist() == list(range(64)) and order[64:128].tolist() == list(range(256, 320))
+    assert order[128:192].tolist() == list(range(64, 128))
+
+
+def test_attention_matches_reference(gg):
+    nq, nkv, hd, S, pos = (int(v) for v in gg["attn_meta"])
+    o = O.attention_ref(gg["attn_q"], gg["attn_k"], gg["attn_v"], pos, nq, nkv, hd, hd ** -0.5, "bf16")
+    assert O.ulp_diff(o, _stored(gg["attn_o"], "bf16"), "bf16").max() <= 1
