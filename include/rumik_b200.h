@@ -51,7 +51,12 @@ enum rb_flags {
    * when the weights are not written by the kernel immediately before this one on the stream, which holds
    * for inference weights loaded once. This is what lets a chain of GEMVs keep HBM busy across kernel
    * boundaries. */
-  RB_FLAG_PREFETCH_WEIGHTS = 2
+  RB_FLAG_PREFETCH_WEIGHTS = 2,
+  /* GEMV lists (rb_gemv_int4_multi / _multi_ws / _fused): run on the tcgen05 kernel, or on the warp-MMA kernel,
+   * whatever the list's size. Without either, lists whose codes total less than 128 MiB (a decode layer's
+   * projections, latency-bound) run on the warp-MMA kernel and longer lists on the tcgen05 kernel. */
+  RB_FLAG_KERNEL_TC = 4,
+  RB_FLAG_KERNEL_MMA = 8
 };
 
 /*
@@ -149,12 +154,13 @@ int rb_gemv_int4_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_
  * pairs of groups are cut into slices run by different converter sets; every slice writes its fp32 partial sums
  * to the workspace, and the block's last slice to finish (a per-block counter in the workspace) adds them in slice
  * order - the result does not depend on which finishes last - and stores the rows.
- * rb_gemv_int4_workspace returns the bytes a list needs on the current device (0: no split; negative: -status).
+ * rb_gemv_int4_workspace returns the bytes a list needs on the current device with those launch flags (0: no
+ * split, e.g. a list that runs on the warp-MMA kernel, which splits K inside each CTA; negative: -status).
  * The workspace must be 16-byte aligned and zero before its first use; every launch leaves it zero again
  * (except after a device error, when it must be cleared). A smaller workspace runs the list unsplit. Calls
  * sharing a workspace must not overlap in time (one stream).
  */
-int64_t rb_gemv_int4_workspace(const rb_gemv_desc* descs, int count);
+int64_t rb_gemv_int4_workspace(const rb_gemv_desc* descs, int count, int flags);
 int rb_gemv_int4_multi_ws(const rb_gemv_desc* descs, int count, void* ws, int64_t ws_bytes, int x_dtype, int y_dtype,
                           int flags, void* stream);
 
@@ -179,9 +185,9 @@ int rb_gemv_int4_multi_ws(const rb_gemv_desc* descs, int count, void* ws, int64_
  *                   key heads are rotated by the interleaved rotary embedding at position *pos (pairs (2j, 2j+1),
  *                   cos/sin [cache_len, head_dim] at [pos, 2j]); queries go to q_out [n_q_heads, head_dim],
  *                   keys and values to slot *pos of k_cache / v_cache [n_kv_heads, cache_len, head_dim].
- *   RB_EPI_SWIGLU   rows hold gate and up channels interleaved in tiles of 64 (rows 128 t .. 128 t + 63 = gate
- *                   channels 64 t .., rows 128 t + 64 .. = the matching up channels; rb-side helper
- *                   interleave_gate_up); act_out[c] = silu(gate[c]) * up[c], N / 2 channels, N % 128 == 0.
+ *   RB_EPI_SWIGLU   rows hold gate and up channels in pairs: row 2c = gate channel c, row 2c + 1 = up channel c
+ *                   (Python helper interleave_gate_up); act_out[c] = silu(gate[c]) * up[c], N / 2 channels,
+ *                   N even.
  * cos, sin, q_out, the caches and act_out are in the output dtype. `y` may be NULL for ROPE_KV and SWIGLU
  * (when given, the plain result is stored as well). *pos is read on the device (int64); a position outside
  * [0, cache_len) stores no query, key or value and sets the RB_DEVERR_ARG bit of the device error word.

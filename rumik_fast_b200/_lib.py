@@ -15,7 +15,8 @@ OK, ERR_NULL, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_LAUNCH, ERR_DEVICE, ERR_TIMEO
 # dtype codes (enum rb_dtype)
 F16, BF16, F32 = 0, 1, 2
 # launch flags (enum rb_flags)
-FLAG_PDL, FLAG_PREFETCH_WEIGHTS = 1, 2
+FLAG_PDL, FLAG_PREFETCH_WEIGHTS, FLAG_KERNEL_TC, FLAG_KERNEL_MMA = 1, 2, 4, 8
+KERNEL_FLAGS = {None: 0, "tc": FLAG_KERNEL_TC, "mma": FLAG_KERNEL_MMA}
 
 _DTYPE_CODE = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
 
@@ -53,7 +54,7 @@ SIGNATURES = {
     "rb_gemv_int4_multi": (_int, [_c.POINTER(GemvDesc), _int, _int, _int, _int, _vp]),
     "rb_gemv_int4_fused": (_int, [_c.POINTER(GemvDesc), _c.POINTER(GemvEpi), _int, _c.POINTER(AddLn), _vp, _i64,
                                   _int, _int, _int, _vp]),
-    "rb_gemv_int4_workspace": (_i64, [_c.POINTER(GemvDesc), _int]),
+    "rb_gemv_int4_workspace": (_i64, [_c.POINTER(GemvDesc), _int, _int]),
     "rb_gemv_int4_multi_ws": (_int, [_c.POINTER(GemvDesc), _int, _vp, _i64, _int, _int, _int, _vp]),
     "rb_add_layernorm": (_int, [_c.POINTER(AddLn), _int, _int, _vp]),
     "rb_attn_decode_workspace": (_i64, [_int, _int, _int]),

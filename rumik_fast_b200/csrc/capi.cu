@@ -126,6 +126,27 @@ static int check_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_
   return RB_OK;
 }
 
+// Lists whose int4 codes total less than this run on the warp-MMA multi-GEMV (gemv_int4_multi.cu): a decode
+// layer's projections (18-35 MB) are latency-bound, and its per-launch cost is about half the tensor-core
+// kernel's. Longer lists (a whole step's projections, 1.9 GB) are HBM-bound and run on the tcgen05 kernel.
+#ifndef RB_SMALL_LIST_BYTES
+#define RB_SMALL_LIST_BYTES (int64_t(128) << 20)
+#endif
+static bool small_list(const rb_gemv_desc* d, int count, int flags) {
+#ifdef RB_MULTI_LEGACY  // comparison builds: every list on the warp-MMA kernel
+  (void)d;
+  (void)count;
+  (void)flags;
+  return true;
+#else
+  if (flags & RB_FLAG_KERNEL_TC) return false;
+  if (flags & RB_FLAG_KERNEL_MMA) return true;
+  int64_t bytes = 0;
+  for (int i = 0; i < count; ++i) bytes += d[i].N * (d[i].K / 2);
+  return bytes < RB_SMALL_LIST_BYTES;
+#endif
+}
+
 static int multi_impl(const rb_gemv_desc* descs, int count, void* ws, int64_t ws_bytes, int x_dtype, int y_dtype,
                       int flags, void* stream) {
   if (count < 0) return RB_ERR_SHAPE;
@@ -136,14 +157,11 @@ static int multi_impl(const rb_gemv_desc* descs, int count, void* ws, int64_t ws
   int sms = 0;
   st = device_sms(&sms);
   if (st != RB_OK) return st;
-#ifdef RB_MULTI_LEGACY  // the warp-MMA multi-GEMV (gemv_int4_multi.cu), kept for comparison builds
-  (void)ws;
-  (void)ws_bytes;
-  st = rb::launch_gemv_int4_multi(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream));
-#else
-  st = rb::launch_gemv_int4_tc(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream), nullptr,
-                               nullptr, ws, ws_bytes);
-#endif
+  if (small_list(descs, count, flags))
+    st = rb::launch_gemv_int4_multi(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream));
+  else
+    st = rb::launch_gemv_int4_tc(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream),
+                                 nullptr, nullptr, ws, ws_bytes);
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
 }
@@ -157,7 +175,7 @@ int rb_gemv_int4_multi_ws(const rb_gemv_desc* descs, int count, void* ws, int64_
   return multi_impl(descs, count, ws, ws_bytes, x_dtype, y_dtype, flags, stream);
 }
 
-int64_t rb_gemv_int4_workspace(const rb_gemv_desc* descs, int count) {
+int64_t rb_gemv_int4_workspace(const rb_gemv_desc* descs, int count, int flags) {
   if (count < 0) return -RB_ERR_SHAPE;
   if (count == 0) return 0;
   if (!descs) return -RB_ERR_NULL;
@@ -166,6 +184,7 @@ int64_t rb_gemv_int4_workspace(const rb_gemv_desc* descs, int count) {
     if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.K > 16384 || d.N > (int64_t(1) << 30)) return -RB_ERR_SHAPE;
     if (!d.q) return -RB_ERR_NULL;
   }
+  if (small_list(descs, count, flags)) return 0;  // the warp-MMA kernel splits K inside each CTA
   int sms = 0, st = device_sms(&sms);
   if (st != RB_OK) return -st;
   // entries with x == NULL read a prologue's vector: only the slot bookkeeping looks at it here
@@ -274,7 +293,7 @@ int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int c
         return RB_ERR_NULL;
       if (e.rope && (!e.cos || !e.sin)) return RB_ERR_NULL;
     } else if (kind == RB_EPI_SWIGLU) {
-      if (d.N % 128 != 0) return RB_ERR_SHAPE;
+      if (d.N % 2 != 0) return RB_ERR_SHAPE;
       if (!e.act_out) return RB_ERR_NULL;
     } else {
       return RB_ERR_SHAPE;
@@ -284,8 +303,12 @@ int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int c
   if (ws && !aligned16(ws)) return RB_ERR_ALIGN;
   int sms = 0, st = device_sms(&sms);
   if (st != RB_OK) return st;
-  st = rb::launch_gemv_int4_tc(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream), epis,
-                               ln, ws, ws_bytes);
+  if (small_list(descs, count, flags))
+    st = rb::launch_gemv_int4_multi(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream), epis,
+                                    ln);
+  else
+    st = rb::launch_gemv_int4_tc(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream), epis,
+                                 ln, ws, ws_bytes);
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
 }

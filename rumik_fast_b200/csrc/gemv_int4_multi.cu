@@ -16,6 +16,7 @@
 //  * full/empty mbarriers are per tile, reused modulo a window that is provably larger than any consumer's
 //    lead over the oldest unreleased tile, so a waiting warp can never see a stale phase.
 #include "common.cuh"
+#include "glue.cuh"
 #include "kernels.h"
 
 namespace rb {
@@ -58,10 +59,18 @@ struct Entry {
   const uint16_t* m;
   void* y;
   int N, K, G, slot, tile_begin, pad;
+  int epi, ep;  // epilogue kind (rb_epi_kind), index into MultiParams::epis
 };
 
 struct Slot {
-  const void* x;
+  const void* x;  // activations; for the prologue slot (ln != 0) the residual stream of rb_add_ln
+  const void* a;
+  const void* b;
+  const void* w;
+  void* x_out;
+  void* h_out;
+  float eps;
+  int ln;
   int K, G;
   uint32_t tab_off, cst_off;
 };
@@ -88,15 +97,17 @@ struct __align__(16) EntryC {
   int P, gps, ipt;               // K-slices per 8-row step, groups per slice, items per tile (steps * P)
   int jlo, ib;
   uint32_t mag_ipt, mag_p;       // ceil(2^32 / ipt), ceil(2^32 / P): division by multiply-high
+  int epi, ep;                   // epilogue kind and its index into MultiParams::epis
 };
 
 struct MultiParams {
   int count, nslots, total_tiles, x_bf16, y_bf16, prefetch;
   int maxp;  // largest K-slice count of the launch's entries (sizes the reduction area)
   uint32_t ring_bytes, ring_off, bar_off, start_off, zero_off, ent_off, red_off;
-  uint32_t m_lo, m_hi, k1024, k64;
+  uint32_t m_lo, m_hi, k1024, k64, ln_off;
   Slot slots[kMaxSlots];
   Entry e[kMaxEntries];
+  EpiP epis[4];
 };
 
 // A tile of TR rows (16, or 8 when the largest K needs smaller tiles) arrives as two contiguous copies of
@@ -220,39 +231,63 @@ __device__ __forceinline__ float item_dot(ItemAddr A, uint32_t m_off, int G, int
 }
 
 // x of every slot -> fp16 B fragments [g][2][8 lanes][16 B] and constants {-offset, sum, 0, 0} per group
+// One 8-activation chunk (it = 16 g + 4 qq + j: elements 32 qq + 8 j .. + 7 of group g) of a slot's table:
+// fp16 B fragments and, summed over the group's 16 chunks (16 consecutive lanes), the group's constants.
+__device__ __forceinline__ void table_chunk(const __half (&h)[8], bool valid, int it, uint8_t* xs, float4* cst) {
+  float off = 0.f, sum = 0.f;
+  if (valid) {
+    const int g = it >> 4, qq = (it >> 2) & 3, j = it & 3;
+    uint8_t* tab = xs + static_cast<size_t>((g * 2 + (j >> 1)) * 8) * 16;
+    uint32_t* l1 = reinterpret_cast<uint32_t*>(tab + qq * 16) + (j & 1) * 2;
+    uint32_t* l2 = reinterpret_cast<uint32_t*>(tab + (4 + qq) * 16) + (j & 1) * 2;
+    l1[0] = pack_half2(h[0], h[4]);
+    l1[1] = pack_half2(h[1], h[5]);
+    l2[0] = pack_half2(h[2], h[6]);
+    l2[1] = pack_half2(h[3], h[7]);
+    const float ev = __half2float(h[0]) + __half2float(h[2]) + __half2float(h[4]) + __half2float(h[6]);
+    const float od = __half2float(h[1]) + __half2float(h[3]) + __half2float(h[5]) + __half2float(h[7]);
+    off = 1024.f * ev + 64.f * od;
+    sum = ev + od;
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) {
+    off += __shfl_xor_sync(0xffffffffu, off, o);
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  if (valid && (it & 15) == 0) cst[it >> 4] = make_float4(-off, sum, 0.f, 0.f);
+}
+
 __device__ void stage_all_x(const MultiParams& p, uint8_t* smem, int tid) {
   for (int sl = 0; sl < p.nslots; ++sl) {
     const Slot& S = p.slots[sl];
     const int items = S.G * 16;
     uint8_t* xs = smem + S.tab_off;
     float4* cst = reinterpret_cast<float4*>(smem + S.cst_off);
+    if (S.ln) {  // the add + LayerNorm prologue (engine/fused.py:29-40) produces this slot's vector
+      LnSrc L;
+      L.x = S.x;
+      L.a = S.a;
+      L.b = S.b;
+      L.w = S.w;
+      L.x_out = S.x_out;
+      L.h_out = S.h_out;
+      L.eps = S.eps;
+      L.K = S.K;
+      stage_ln<4>(L, p.x_bf16 != 0, reinterpret_cast<float*>(smem + p.ln_off), 2, tid, kConsumerWarps * 32,
+                  blockIdx.x == 0, [&](const float (&v)[8], bool valid, int it) {
+                    __half h[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) h[i] = __float2half_rn(v[i]);
+                    table_chunk(h, valid, it, xs, cst);
+                  });
+      continue;
+    }
     for (int base = 0; base < items; base += kConsumerWarps * 32) {
       const int it = base + tid;
       const bool valid = it < items;
-      float off = 0.f, sum = 0.f;
-      if (valid) {
-        const int g = it >> 4, qq = (it >> 2) & 3, j = it & 3;
-        __half h[8];
-        load8_as_half(static_cast<const uint8_t*>(S.x) + (static_cast<int64_t>(g) * 128 + 32 * qq + 8 * j) * 2,
-                      p.x_bf16, h);
-        uint8_t* tab = xs + static_cast<size_t>((g * 2 + (j >> 1)) * 8) * 16;
-        uint32_t* l1 = reinterpret_cast<uint32_t*>(tab + qq * 16) + (j & 1) * 2;
-        uint32_t* l2 = reinterpret_cast<uint32_t*>(tab + (4 + qq) * 16) + (j & 1) * 2;
-        l1[0] = pack_half2(h[0], h[4]);
-        l1[1] = pack_half2(h[1], h[5]);
-        l2[0] = pack_half2(h[2], h[6]);
-        l2[1] = pack_half2(h[3], h[7]);
-        const float ev = __half2float(h[0]) + __half2float(h[2]) + __half2float(h[4]) + __half2float(h[6]);
-        const float od = __half2float(h[1]) + __half2float(h[3]) + __half2float(h[5]) + __half2float(h[7]);
-        off = 1024.f * ev + 64.f * od;
-        sum = ev + od;
-      }
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) {
-        off += __shfl_xor_sync(0xffffffffu, off, o);
-        sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      }
-      if (valid && (it & 15) == 0) cst[it >> 4] = make_float4(-off, sum, 0.f, 0.f);
+      __half h[8];
+      if (valid) load8_as_half(static_cast<const uint8_t*>(S.x) + static_cast<int64_t>(it) * 16, p.x_bf16, h);
+      table_chunk(h, valid, it, xs, cst);
     }
   }
 }
@@ -401,6 +436,8 @@ __global__ void __maxnreg__(kMaxRegs) gemv_int4_multi_kernel(const __grid_consta
     c.ib = (local_tiles_below(tile_end, cta, C) - c.jlo) * c.ipt;  // this entry's items; prefix-summed below
     c.mag_ipt = div_magic(c.ipt);
     c.mag_p = div_magic(c.P);
+    c.epi = E.epi;
+    c.ep = E.ep;
     entc[i] = c;
   }
   __syncthreads();
@@ -501,14 +538,31 @@ __global__ void __maxnreg__(kMaxRegs) gemv_int4_multi_kernel(const __grid_consta
     // the whole tile is reclaimed). The arrive has release semantics: it waits until this thread's earlier
     // memory operations are performed, so the global store of y comes after it.
     if (lane == 0) mbar_arrive_cnt(&empty[j % kWindow], it == E.ipt - 1 ? kRelease - (E.ipt - 1) : 1);
-    if (store && qd == 0 && row < E.N) store_out(E.y, row, out, p.y_bf16);
+    if (E.epi == RB_EPI_STORE) {
+      if (store && qd == 0 && row < E.N) store_out(E.y, row, out, p.y_bf16);
+    } else if (store) {  // routed as the engine's post kernel would (engine/fused.py:43-84); store is warp-uniform
+      const EpiP& P = p.epis[E.ep];
+      const float rr = round_act(out, p.y_bf16);             // what the engine's y buffer would hold
+      const float pr = __shfl_xor_sync(0xffffffffu, rr, 8);  // row ^ 1 is MMA row r ^ 2: lane ^ 8
+      int64_t pos = 0;
+      bool pos_ok = true;
+      if (E.epi == RB_EPI_ROPE_KV) {
+        pos = *P.pos;
+        pos_ok = pos >= 0 && pos < P.S;
+        if (!pos_ok && lane == 0) atomicOr(&g_device_error, ERR_ARG);
+      }
+      if (qd == 0 && row < E.N) {
+        if (E.y) store_out(E.y, row, out, p.y_bf16);
+        if (pos_ok) route_row(P, E.epi, row, rr, pr, pos, p.y_bf16);
+      }
+    }
   }
 }
 
 }  // namespace g4m
 
 int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, const rb_gemv_epi* epi, const rb_add_ln* ln) {
   using namespace g4m;
   constexpr uint32_t kSmemMax = 227 * 1024;
   // 16-row tiles halve the per-tile producer work; lists with a K too large for two 16-row tiles (plus
@@ -531,27 +585,44 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
     p.k64 = 0x54005400u;
     // distinct activation vectors -> slots; stop adding entries when the next one would not fit
     // (activation tables + two of the largest tiles must fit in shared memory)
-    constexpr uint32_t kFixed = 64 + 16 + kMaxEntries * (sizeof(EntryP) + sizeof(EntryC)) + sizeof(EntryC) +
+    constexpr uint32_t kFixed = 64 + 16 + 2 * kLnMaxGroups * 4 + kMaxEntries * (sizeof(EntryP) + sizeof(EntryC)) + sizeof(EntryC) +
                                 kWindow * 4 + 16 + kRedSlots * 2 * 4 + kRedSlots * 2 * kMaxP * 8 * 4 +
                                 2 * kWindow * 8 + 128;
-    int nslots = 0, tiles = 0;
+    int nslots = 0, tiles = 0, nepis = 0;
     uint32_t x_bytes = 0, max_tile = 0;
     int take = 0;
     for (; take < n; ++take) {
       const rb_gemv_desc& D = d[done + take];
       const uint32_t G = static_cast<uint32_t>(D.K / 128);
       const uint32_t tb = tile_bytes(TR, static_cast<int>(D.K), static_cast<int>(G));
+      const bool from_ln = D.x == nullptr;  // multiplies the prologue's normalised vector
+      const int kind = epi ? epi[done + take].kind : RB_EPI_STORE;
+      if (from_ln && !ln) return RB_ERR_NULL;
       int slot = -1;
       for (int i = 0; i < nslots; ++i)
-        if (p.slots[i].x == D.x && p.slots[i].K == static_cast<int>(D.K)) slot = i;
+        if (p.slots[i].ln == (from_ln ? 1 : 0) && (from_ln || p.slots[i].x == D.x) &&
+            p.slots[i].K == static_cast<int>(D.K))
+          slot = i;
       const uint32_t add_x = slot < 0 ? G * (256u + 16u) : 0u;
       if (slot < 0 && nslots == kMaxSlots) break;
       if (x_bytes + add_x + kFixed + 2u * std::max(max_tile, tb) > kSmemMax) break;
+      if (kind != RB_EPI_STORE && nepis == 4) break;
       if (slot < 0) {
         slot = nslots++;
-        p.slots[slot].x = D.x;
-        p.slots[slot].K = static_cast<int>(D.K);
-        p.slots[slot].G = static_cast<int>(G);
+        Slot& S = p.slots[slot];
+        S = Slot{};
+        S.x = from_ln ? ln->x : D.x;
+        if (from_ln) {
+          S.ln = 1;
+          S.a = ln->a;
+          S.b = ln->b;
+          S.w = ln->w;
+          S.x_out = ln->x_out;
+          S.h_out = ln->h_out;
+          S.eps = ln->eps;
+        }
+        S.K = static_cast<int>(D.K);
+        S.G = static_cast<int>(G);
         x_bytes += add_x;
       }
       Entry& E = p.e[take];
@@ -564,10 +635,30 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
       E.G = static_cast<int>(G);
       E.slot = slot;
       E.tile_begin = tiles;
+      E.epi = kind;
+      E.ep = 0;
+      if (kind != RB_EPI_STORE) {
+        const rb_gemv_epi& X = epi[done + take];
+        EpiP& P = p.epis[nepis];
+        P.pos = X.pos;
+        P.cos = X.cos;
+        P.sin = X.sin;
+        P.q_out = X.q_out;
+        P.k_cache = X.k_cache;
+        P.v_cache = X.v_cache;
+        P.act = X.act_out;
+        P.S = X.cache_len;
+        P.rope = X.rope;
+        P.nq = X.n_q_heads;
+        P.nkv = X.n_kv_heads;
+        P.hd = X.head_dim;
+        E.ep = nepis++;
+      }
       tiles += static_cast<int>((D.N + TR - 1) / TR);
       max_tile = std::max(max_tile, tb);
     }
     if (take == 0) return RB_ERR_SHAPE;
+    if ((epi || ln) && take < count) return RB_ERR_SHAPE;  // the fused glue needs the whole list in one launch
     p.count = take;
     p.nslots = nslots;
     p.total_tiles = tiles;
@@ -584,6 +675,8 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
     }
     p.zero_off = off;
     off += 64;
+    p.ln_off = off;  // the prologue's group sums (2 x kLnMaxGroups floats)
+    off += 2 * kLnMaxGroups * 4;
     off = (off + 15) & ~15u;
     p.ent_off = off;
     off += static_cast<uint32_t>(take) * sizeof(EntryP) + static_cast<uint32_t>(take + 1) * sizeof(EntryC);

@@ -22,6 +22,7 @@
 // 2e-5 of the group's largest activation); the weights are used exactly. All mbarrier waits are bounded;
 // no multicast, no clusters.
 #include "common.cuh"
+#include "glue.cuh"
 #include "kernels.h"
 
 namespace rb {
@@ -63,19 +64,6 @@ struct Entry {
   int ks, ppk, item_begin;
 };
 
-// Where the rows of a routed entry go (rb_gemv_epi).
-struct EpiP {
-  const int64_t* pos;
-  const void* cos;
-  const void* sin;
-  void* q_out;
-  void* k_cache;
-  void* v_cache;
-  void* act;
-  int64_t S;
-  int rope, nq, nkv, hd;
-};
-
 struct Slot {
   const void* x;  // activations; for the prologue slot the residual stream
   const void* a;  // prologue (ln != 0): x + a + b -> LayerNorm with weight w
@@ -101,9 +89,8 @@ struct __align__(64) TcParams {
 };
 static_assert(sizeof(TcParams) <= 32000, "kernel parameter block too large");
 
-// Auxiliary shared memory: the prologue's two reduction arrays, per set two 64-float exchange buffers of the
-// SwiGLU epilogue (up values handed to the gate rows), then per set the split-K "last slice" flag.
-constexpr uint32_t kAuxBytes = 2 * kConvWarps * 4 + kSets * 2 * 64 * 4 + 16;
+// Auxiliary shared memory: the prologue's two arrays of group sums, then per set the split-K "last slice" flag.
+constexpr uint32_t kAuxBytes = 2 * kLnMaxGroups * 4 + 16;
 
 // Split-K workspace: one completion counter per 128-row block (rounded up to 256 bytes), then the partials.
 inline int64_t split_ticket_bytes(int blocks) { return (static_cast<int64_t>(blocks) * 4 + 255) / 256 * 256; }
@@ -184,107 +171,26 @@ __device__ __forceinline__ void quant_chunk(const float (&v)[8], bool valid, int
   }
 }
 
-// Sum of one value per converter thread, the same fp32 result in every thread (fixed order).
-__device__ __forceinline__ float conv_sum(float v, float* red, int ct, int nthreads) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  if ((ct & 31) == 0) red[ct >> 5] = v;
-  named_bar_sync(kBarLn, nthreads);
-  float t = 0.f;
-  for (int i = 0; i < nthreads / 32; ++i) t += red[i];
-  return t;
+__device__ __forceinline__ LnSrc ln_src(const Slot& S) {
+  LnSrc L;
+  L.x = S.x;
+  L.a = S.a;
+  L.b = S.b;
+  L.w = S.w;
+  L.x_out = S.x_out;
+  L.h_out = S.h_out;
+  L.eps = S.eps;
+  L.K = S.K;
+  return L;
 }
 
-__device__ __forceinline__ void store8_act(void* p, const float (&v)[8], bool is_bf16) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if (is_bf16) {
-      w[i] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i]))) |
-             (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1]))) << 16);
-    } else {
-      w[i] = pack_half2(__float2half_rn(v[2 * i]), __float2half_rn(v[2 * i + 1]));
-    }
-  }
-  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-// The add + LayerNorm prologue of rumik-fast's add_ln (engine/fused.py:29-40), computed by every CTA from
-// global memory: s = (x + a) + b in fp32 rounded to the activation type, h = (s - mean) * rsqrt(var + eps) * w
-// rounded likewise (mean and var over the H elements, two passes as the reference), then tabulated like any
-// other activation vector. CTA 0 also writes s (the new residual) and h.
-template <bool kTab>
-__device__ void stage_ln_slot(const Slot& S, bool bf, uint8_t* tab, float2* cst, float* red, int ct, int nthreads) {
-  const int chunks = S.K / 8;
-  const bool writer = blockIdx.x == 0;
-  float v[kLnIter][8];
-  uint4 wraw[kLnIter];  // the LayerNorm weight, loaded with x, a and b
-  float part = 0.f;
-#pragma unroll
-  for (int it = 0; it < kLnIter; ++it) {
-    const int c = it * nthreads + ct;
-    wraw[it] = c < chunks ? ldg_cg_128(static_cast<const uint8_t*>(S.w) + static_cast<int64_t>(c) * 16)
-                          : make_uint4(0u, 0u, 0u, 0u);
-    if (c < chunks) {
-      load8_f32(static_cast<const uint8_t*>(S.x) + static_cast<int64_t>(c) * 16, bf, v[it]);
-      float t[8];
-      if (S.a) {
-        load8_f32(static_cast<const uint8_t*>(S.a) + static_cast<int64_t>(c) * 16, bf, t);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[it][i] += t[i];
-      }
-      if (S.b) {
-        load8_f32(static_cast<const uint8_t*>(S.b) + static_cast<int64_t>(c) * 16, bf, t);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[it][i] += t[i];
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[it][i] = round_act(v[it][i], bf);
-        part += v[it][i];
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[it][i] = 0.f;
-    }
-  }
-  const float inv_h = 1.f / static_cast<float>(S.K);
-  const float mean = conv_sum(part, red, ct, nthreads) * inv_h;
-  float sq = 0.f;
-#pragma unroll
-  for (int it = 0; it < kLnIter; ++it)
-    if (it * nthreads + ct < chunks) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float d = v[it][i] - mean;
-        sq += d * d;
-      }
-    }
-  const float rstd = rsqrtf(conv_sum(sq, red + nthreads / 32, ct, nthreads) * inv_h + S.eps);
-#pragma unroll
-  for (int it = 0; it < kLnIter; ++it) {
-    if (it * nthreads >= chunks) break;  // uniform over the converter threads
-    const int c = it * nthreads + ct;
-    const bool valid = c < chunks;
-    float h[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (valid) {
-      float w[8];
-      raw_to_f32(wraw[it], bf, w);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) h[i] = round_act((v[it][i] - mean) * rstd * w[i], bf);
-      if (writer && S.x_out) store8_act(static_cast<uint8_t*>(S.x_out) + static_cast<int64_t>(c) * 16, v[it], bf);
-      if (writer && S.h_out) store8_act(static_cast<uint8_t*>(S.h_out) + static_cast<int64_t>(c) * 16, h, bf);
-    }
-    if (kTab) quant_chunk(h, valid, c, tab, cst);
-  }
-}
-
-// The same add + LayerNorm on its own (the final norm in front of the head): one CTA of the converter
-// threads' shape, so that its results are bit-identical to the fused prologue's.
+// The same add + LayerNorm on its own (the final norm in front of the head): one CTA; bit-identical to the
+// prologue of the fused launches (the prologue's sums do not depend on the thread count).
 __global__ void __launch_bounds__(kConvWarps * 32, 1) add_ln_kernel(const __grid_constant__ Slot S, int bf) {
-  __shared__ float red[2 * kConvWarps];
+  __shared__ float gsum[2 * kLnMaxGroups];
   griddep_wait();
-  stage_ln_slot<false>(S, bf != 0, nullptr, nullptr, red, threadIdx.x, kConvWarps * 32);
+  stage_ln<kLnIter>(ln_src(S), bf != 0, gsum, 1, threadIdx.x, kConvWarps * 32, true,
+                    [](const float (&)[8], bool, int) {});
   griddep_launch_dependents();
 }
 
@@ -319,7 +225,8 @@ __device__ void stage_x_tables(const TcParams& p, uint8_t* xs, float* red, int c
     uint8_t* tab = xs + S.tab_off;
     float2* cst = reinterpret_cast<float2*>(xs + S.cst_off);
     if (S.ln) {
-      stage_ln_slot<true>(S, p.x_bf16 != 0, tab, cst, red, ct, nthreads);
+      stage_ln<kLnIter>(ln_src(S), p.x_bf16 != 0, red, kBarLn, ct, nthreads, blockIdx.x == 0,
+                        [&](const float (&h)[8], bool valid, int c) { quant_chunk(h, valid, c, tab, cst); });
     } else {
       const int chunks = S.K / 8;  // 16 per group
       for (int base = 0; base < chunks; base += nthreads, ++n) {
@@ -370,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
   auto afull = [&](int s, int b) { return bars + s * per_set + 2 * nst + b; };
   auto mdone = [&](int s, int b) { return bars + s * per_set + 2 * nst + kNP + b; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kSets * per_set);
-  float* aux = reinterpret_cast<float*>(smem + p.aux_off);  // [2 x kConvWarps] reduction, then SwiGLU exchange
+  float* aux = reinterpret_cast<float*>(smem + p.aux_off);  // prologue group sums, then split-K flags
 
   if (tid == 0) {
     for (int s = 0; s < kSets; ++s) {
@@ -650,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
         p.ws_part[static_cast<int64_t>(gi) * kRows + rib] = acc;
         __threadfence();
         named_bar_sync(2 + s, 128);
-        volatile int* last = reinterpret_cast<volatile int*>(aux + 2 * kConvWarps + kSets * 2 * 64) + s;
+        volatile int* last = reinterpret_cast<volatile int*>(aux + 2 * kLnMaxGroups) + s;
         if (rib == 0)
           *last = atomicAdd(p.ws_ticket + E.block_begin + blk, 1u) == static_cast<unsigned int>(E.ks - 1) ? 1 : 0;
         named_bar_sync(2 + s, 128);
@@ -668,37 +575,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
       } else {
         const EpiP& P = p.epis[E.ep];
         if (E.y && ok && row_ok) store_out(E.y, row, acc, p.y_bf16);
-        const float r = round_act(acc, p.y_bf16);  // what the engine's y buffer would hold
+        const float r = round_act(acc, p.y_bf16);               // what the engine's y buffer would hold
+        const float pr = __shfl_xor_sync(0xffffffffu, r, 1);    // the partner row (rotary pair / up channel)
+        int64_t pos = 0;
+        bool pos_ok = true;
         if (E.epi == kEpiRopeKv) {
-          const float pr = __shfl_xor_sync(0xffffffffu, r, 1);  // the other element of the rotary pair
-          const int64_t pos = *P.pos;
-          const bool pos_ok = pos >= 0 && pos < P.S;
+          pos = *P.pos;
+          pos_ok = pos >= 0 && pos < P.S;
           if (!pos_ok && rib == 0) atomicOr(&g_device_error, ERR_ARG);
-          if (ok && row_ok && pos_ok) {
-            const int head = row / P.hd, dd = row - head * P.hd;
-            float o = r;
-            if (P.rope && head < P.nq + P.nkv) {  // pairs (2j, 2j + 1) rotated by pos * theta_j
-              const int64_t ci = pos * P.hd + (dd & ~1);
-              const float c = load_act(P.cos, ci, p.y_bf16), sn = load_act(P.sin, ci, p.y_bf16);
-              o = (dd & 1) ? r * c + pr * sn : r * c - pr * sn;
-            }
-            if (head < P.nq)
-              store_out(P.q_out, static_cast<int64_t>(head) * P.hd + dd, o, p.y_bf16);
-            else if (head < P.nq + P.nkv)
-              store_out(P.k_cache, (static_cast<int64_t>(head - P.nq) * P.S + pos) * P.hd + dd, o, p.y_bf16);
-            else
-              store_out(P.v_cache, (static_cast<int64_t>(head - P.nq - P.nkv) * P.S + pos) * P.hd + dd, o,
-                        p.y_bf16);
-          }
-        } else {  // kEpiSwiglu: rows 0..63 of the block are gate channels, rows 64..127 the matching up channels
-          float* xch = aux + 2 * kConvWarps + (s * 2 + (((jj - s) / kSets) & 1)) * 64;  // double-buffered per set
-          if (rib >= 64) xch[rib - 64] = r;
-          named_bar_sync(2 + s, 128);
-          if (rib < 64 && ok && row_ok) {
-            const float a = r / (1.f + __expf(-r)) * xch[rib];
-            store_out(P.act, static_cast<int64_t>(blk) * 64 + rib, a, p.y_bf16);
-          }
         }
+        if (ok && row_ok && pos_ok) route_row(P, E.epi, row, r, pr, pos, p.y_bf16);
       }
     }
   }

@@ -15,9 +15,9 @@ side of a layer is one kernel:
     layer()                       # add_ln + QKV GEMV + gate_up GEMV + rope + KV write + silu(gate) * up
 
 Weights: the engine's fused w_in rows [q | k | v | gate | up] (engine/rumik_int4.py:95-100) are split with
-split_w_in into the q|k|v rows (unchanged) and the gate|up rows re-ordered by interleave_gate_up (tiles of 64
-gate rows followed by the 64 matching up rows), so that a gate channel and its up channel land in one
-128-row block of the kernel. Both are one-time permutations at load; the codes themselves are unchanged.
+split_w_in into the q|k|v rows (unchanged) and the gate|up rows re-ordered by interleave_gate_up (gate channel
+c at row 2c, its up channel at row 2c + 1), so that the two rows of a channel finish in the same warp, like the
+two elements of a rotary pair. Both are one-time permutations at load; the codes themselves are unchanged.
 
 The residual stream alternates between two buffers (every CTA reads x while one CTA writes x + o + down).
 """
@@ -30,21 +30,19 @@ from .cuda_gemv import _on_device, _require
 from .gemv_set import _ws_len, _ws_ptr, workspace
 
 G = 128
-TILE = 64  # gate (or up) channels per 128-row block of the SwiGLU epilogue
 
 
 # ---------------------------------------------------------------------------------------------- weight layout
 def gate_up_order(inter, device=None):
     """Row permutation of interleave_gate_up: new row r reads old row order[r] of [gate (inter) | up (inter)]."""
-    _require(inter % TILE == 0, f"MLP width {inter} must be a multiple of {TILE}")
-    c = torch.arange(inter, device=device).view(-1, TILE)
+    c = torch.arange(inter, device=device)
     return torch.stack([c, c + inter], 1).reshape(-1)
 
 
 def interleave_gate_up(q, s, m):
-    """[gate; up] int4 rows (q [2I, K/2], s/m [2I, K/128]) -> the SwiGLU epilogue's order: per 128-row block,
-    64 gate channels then the same 64 up channels."""
-    _require(q.shape[0] % (2 * TILE) == 0, f"gate_up rows {q.shape[0]} must be a multiple of {2 * TILE}")
+    """[gate; up] int4 rows (q [2I, K/2], s/m [2I, K/128]) -> the SwiGLU epilogue's order: gate channel c at row
+    2c, its up channel at row 2c + 1."""
+    _require(q.shape[0] % 2 == 0, f"gate_up rows {q.shape[0]} must be even")
     order = gate_up_order(q.shape[0] // 2, q.device)
     return q[order].contiguous(), s[order].contiguous(), m[order].contiguous()
 
@@ -109,11 +107,12 @@ class AddLnGemvPost:
     k_cache, v_cache  [n_kv_heads, cache_len, head_dim];  q_out [n_q_heads * head_dim];  act [inter]
     rope     False for the layers without position embedding
     y_qkv, y_gate_up  optional buffers that also receive the plain GEMV results
+    kernel   None (by size: the warp-MMA kernel for a layer's projections), "tc" or "mma"
     Built once (graph-capture safe to call); every tensor must stay alive.
     """
 
     def __init__(self, qkv, gate_up, *, pos, cos, sin, k_cache, v_cache, q_out, act, n_q_heads, n_kv_heads,
-                 add_ln=None, h=None, rope=True, y_qkv=None, y_gate_up=None):
+                 add_ln=None, h=None, rope=True, y_qkv=None, y_gate_up=None, kernel=None):
         _require((add_ln is None) != (h is None), "give exactly one of add_ln and h")
         src = add_ln.tensors[0] if add_ln is not None else h
         self.device, self.x_dtype = src.device, src.dtype
@@ -131,7 +130,7 @@ class AddLnGemvPost:
         qq, qs, qm, Nqkv, K1 = _int4(qkv, H)
         gq, gs, gm, Ngu, K2 = _int4(gate_up, H)
         _require(Nqkv == (n_q_heads + 2 * n_kv_heads) * hd, "qkv rows must be (n_q_heads + 2 n_kv_heads) head_dim")
-        _require(Ngu % (2 * TILE) == 0 and act.numel() == Ngu // 2, "act must hold the N/2 MLP channels")
+        _require(Ngu % 2 == 0 and act.numel() == Ngu // 2, "act must hold the N/2 MLP channels")
         for y, N in ((y_qkv, Nqkv), (y_gate_up, Ngu)):
             _require(y is None or (y.dtype == dt and y.numel() == N and y.is_contiguous()), "bad y buffer")
         xp = None if add_ln is not None else h.data_ptr()
@@ -145,7 +144,8 @@ class AddLnGemvPost:
                                v_cache.data_ptr(), None)
         epis[1] = _lib.GemvEpi(_lib.EPI_SWIGLU, 0, 0, 0, 0, 0, None, None, None, None, None, None, act.data_ptr())
         self._descs, self._epis, self._ln = descs, epis, add_ln
-        self.ws = workspace(descs, 2, self.device)
+        self.kflags = _lib.KERNEL_FLAGS[kernel]
+        self.ws = workspace(descs, 2, self.device, self.kflags)
         self._keep = (qkv, gate_up, pos, cos, sin, k_cache, v_cache, q_out, act, h, y_qkv, y_gate_up)
         self.y_dtype = dt
         self.bytes = sum(t.numel() for t in (qq, gq)) + 4 * (qs.numel() + gs.numel())
@@ -155,6 +155,6 @@ class AddLnGemvPost:
         lnp = ctypes.byref(self._ln.c) if self._ln is not None else None
         with _on_device(self.device):
             st = L.rb_gemv_int4_fused(self._descs, self._epis, 2, lnp, _ws_ptr(self.ws), _ws_len(self.ws),
-                                      _lib.dtype_code(self.x_dtype), _lib.dtype_code(self.y_dtype), config.flags(),
-                                      _lib.stream_ptr(self.device))
+                                      _lib.dtype_code(self.x_dtype), _lib.dtype_code(self.y_dtype),
+                                      config.flags() | self.kflags, _lib.stream_ptr(self.device))
         _lib.check("rb_gemv_int4_fused", st)

@@ -22,7 +22,10 @@ G = 128
 
 
 class Int4GemvSet:
-    def __init__(self, entries):
+    """kernel: None (by the list's size: a decode layer's projections on the warp-MMA kernel, a whole step's on
+    the tcgen05 kernel), "tc" or "mma"."""
+
+    def __init__(self, entries, kernel=None):
         _require(len(entries) > 0, "empty GEMV list")
         self.entries = list(entries)
         x0, y0 = self.entries[0][0], self.entries[0][4]
@@ -45,22 +48,24 @@ class Int4GemvSet:
             descs[i] = _lib.GemvDesc(x.data_ptr(), y.data_ptr(), q.data_ptr(), s.data_ptr(), m.data_ptr(), N, K)
         self._descs = descs
         self.bytes = sum(q.numel() + 4 * s.numel() + 2 * x.numel() + 2 * y.numel() for x, q, s, m, y in self.entries)
-        self.ws = workspace(descs, len(self.entries), self.device)
+        self.kflags = _lib.KERNEL_FLAGS[kernel]
+        self.ws = workspace(descs, len(self.entries), self.device, self.kflags)
 
     def __call__(self):
         L = _lib.lib()
         with _on_device(self.device):
             st = L.rb_gemv_int4_multi_ws(self._descs, len(self.entries), _ws_ptr(self.ws), _ws_len(self.ws),
-                                         _lib.dtype_code(self.x_dtype), _lib.dtype_code(self.y_dtype), config.flags(),
-                                         _lib.stream_ptr(self.device))
+                                         _lib.dtype_code(self.x_dtype), _lib.dtype_code(self.y_dtype),
+                                         config.flags() | self.kflags, _lib.stream_ptr(self.device))
         _lib.check("rb_gemv_int4_multi_ws", st)
 
 
-def workspace(descs, count, device):
-    """The zeroed split-K workspace of a GEMV list (None when its launches do not split K): a list with fewer
-    128-row blocks than 3 x the SM count spreads each block over several converter sets."""
+def workspace(descs, count, device, kflags=0):
+    """The zeroed split-K workspace of a GEMV list (None when its launches do not split K): on the tcgen05
+    kernel a list with fewer 128-row blocks than 3 x the SM count spreads each block over several converter
+    sets."""
     with _on_device(device):
-        need = _lib.lib().rb_gemv_int4_workspace(descs, count)
+        need = _lib.lib().rb_gemv_int4_workspace(descs, count, kflags)
     if need < 0:
         _lib.check("rb_gemv_int4_workspace", -need)
     return torch.zeros(need, dtype=torch.uint8, device=device) if need > 0 else None

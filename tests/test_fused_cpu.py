@@ -53,7 +53,7 @@ def test_fused_argument_checks(native_lib):
     assert call(L, [desc(N=192)], [epi_rope(cos=None)]) == _lib.ERR_NULL      # rope needs the tables
     assert call(L, [desc(N=192)], [epi_rope(k=None)]) == _lib.ERR_NULL
     # SwiGLU epilogue
-    assert call(L, [desc(N=192)], [epi_swiglu()]) == _lib.ERR_SHAPE           # N % 128
+    assert call(L, [desc(N=191)], [epi_swiglu()]) == _lib.ERR_SHAPE           # N odd
     assert call(L, [desc(N=256)], [epi_swiglu(act=None)]) == _lib.ERR_NULL
     assert call(L, [desc(N=256)] * 5, [epi_swiglu()] * 5) == _lib.ERR_SHAPE   # at most 4 routed entries
     bad = epi_swiglu()
@@ -62,10 +62,11 @@ def test_fused_argument_checks(native_lib):
     assert call(L, [desc()], ws=0x50008, ws_bytes=1024) == _lib.ERR_ALIGN       # split-K workspace alignment
     d = (_lib.GemvDesc * 1)(desc())
     assert L.rb_gemv_int4_multi_ws(d, 1, 0x50008, 1024, _lib.F16, _lib.F16, 0, None) == _lib.ERR_ALIGN
-    assert L.rb_gemv_int4_workspace(d, 0) == 0
-    assert L.rb_gemv_int4_workspace(None, 1) == -_lib.ERR_NULL
+    assert L.rb_gemv_int4_workspace(d, 0, 0) == 0
+    assert L.rb_gemv_int4_workspace(None, 1, 0) == -_lib.ERR_NULL
+    assert L.rb_gemv_int4_workspace(d, 1, 0) == 0                   # a small list: warp-MMA kernel, no workspace
     d[0].K = 200
-    assert L.rb_gemv_int4_workspace(d, 1) == -_lib.ERR_SHAPE
+    assert L.rb_gemv_int4_workspace(d, 1, 0) == -_lib.ERR_SHAPE
 
 
 def test_prologue_argument_checks(native_lib):
@@ -88,7 +89,7 @@ def test_prologue_argument_checks(native_lib):
 
 
 def test_gate_up_order_matches_oracle():
-    for inter in (64, 256, 8192):
+    for inter in (1, 64, 256, 8192):
         assert np.array_equal(fused.gate_up_order(inter).numpy(), O.gate_up_order(inter))
 
 
@@ -103,8 +104,8 @@ def test_interleave_and_split_w_in_on_host_tensors():
     assert torch.equal(qq, q[:nqkv]) and torch.equal(qs, s[:nqkv]) and torch.equal(qm, m[:nqkv])
     order = O.gate_up_order(inter) + nqkv
     assert torch.equal(gs[:, 0], s[order, 0]) and torch.equal(gm, m[order]) and torch.equal(gq, q[order])
-    # block t of the interleaved matrix: rows 0..63 = gate channels 64t.., rows 64..127 = up channels 64t..
-    assert gs[64, 0].item() == nqkv + inter and gs[128, 0].item() == nqkv + 64
+    # row 2c = gate channel c, row 2c + 1 = up channel c
+    assert gs[1, 0].item() == nqkv + inter and gs[2, 0].item() == nqkv + 1
 
 
 def test_attention_argument_checks(native_lib):

@@ -60,20 +60,25 @@ def ln_inputs(H, g, dt):
     return x, a, b, w
 
 
-def run_fused(entries, epis=None, ln=None, x_dtype=torch.float16, y_dtype=torch.float16, split=True):
-    """One rb_gemv_int4_fused call; with split, through the split-K workspace the list would use."""
+KERNELS = ["tc", "mma"]  # the glue runs in both GEMV kernels (tcgen05 with split K, and warp-MMA)
+
+
+def run_fused(entries, epis=None, ln=None, x_dtype=torch.float16, y_dtype=torch.float16, kernel="tc"):
+    """One rb_gemv_int4_fused call on the given kernel (tc: through the split-K workspace the list uses)."""
+    kf = _lib.KERNEL_FLAGS[kernel]
     d = (_lib.GemvDesc * len(entries))(*entries)
     e = (_lib.GemvEpi * len(entries))(*epis) if epis else None
-    ws = workspace(d, len(entries), torch.device(DEV)) if split else None
+    ws = workspace(d, len(entries), torch.device(DEV), kf)
     st = _lib.lib().rb_gemv_int4_fused(d, e, len(entries), ctypes.byref(ln.c) if ln else None, _ws_ptr(ws),
                                        _ws_len(ws), _lib.dtype_code(x_dtype), _lib.dtype_code(y_dtype),
-                                       rb.config.flags(), _lib.stream_ptr(torch.device(DEV)))
+                                       rb.config.flags() | kf, _lib.stream_ptr(torch.device(DEV)))
     _lib.check("rb_gemv_int4_fused", st)
     return ws
 
 
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("dt", DTYPES)
-def test_add_ln_prologue_then_gemvs(dt):
+def test_add_ln_prologue_then_gemvs(dt, kernel):
     g = syn.generator(1, "cpu")
     H = 3072
     x, a, b, w = ln_inputs(H, g, dt)
@@ -85,7 +90,7 @@ def test_add_ln_prologue_then_gemvs(dt):
     W = [weights(n, k, g) for n, k in shapes]
     ys = [torch.full((n,), float("nan"), device=DEV, dtype=dt) for n, _ in shapes]
     run_fused([_lib.GemvDesc(None, y.data_ptr(), *(t.data_ptr() for t in wd), n, H)
-               for (n, _), (_, wd), y in zip(shapes, W, ys)], ln=ln, x_dtype=dt, y_dtype=dt)
+               for (n, _), (_, wd), y in zip(shapes, W, ys)], ln=ln, x_dtype=dt, y_dtype=dt, kernel=kernel)
     torch.cuda.synchronize()
     s_ref, h_ref = O.add_ln_ref(np_act(x)[0], np_act(a)[0], np_act(b)[0], np_act(w)[0], 1e-5, tag(dt))
     assert np.array_equal(vals(x_out), s_ref)
@@ -123,9 +128,10 @@ def rope_setup(dt, nq, nkv, hd, S, g):
     return cos_n, sin_n, cos, sin, kc, vc
 
 
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("dt", DTYPES)
 @pytest.mark.parametrize("hd,rope", [(128, True), (128, False), (64, True)])
-def test_rope_kv_epilogue(dt, hd, rope):
+def test_rope_kv_epilogue(dt, hd, rope, kernel):
     g = syn.generator(3, "cpu")
     nq, nkv, S, pos, K = 4, 2, 48, 37, 1024
     N = (nq + 2 * nkv) * hd
@@ -139,7 +145,7 @@ def test_rope_kv_epilogue(dt, hd, rope):
     epi = _lib.GemvEpi(_lib.EPI_ROPE_KV, int(rope), nq, nkv, hd, S, pos_t.data_ptr(), cos.data_ptr(), sin.data_ptr(),
                        q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), None)
     run_fused([_lib.GemvDesc(xin.data_ptr(), y.data_ptr(), *(t.data_ptr() for t in wd), N, K)], [epi],
-              x_dtype=dt, y_dtype=dt)
+              x_dtype=dt, y_dtype=dt, kernel=kernel)
     torch.cuda.synchronize()
     assert_close(y, int4_ref(xin.cpu(), *wh), "QKV GEMV")
     q_ref, k_ref, v_ref = O.rope_kv_ref(vals(y), pos, cos_n, sin_n, nq, nkv, hd, rope, tag(dt))
@@ -150,8 +156,9 @@ def test_rope_kv_epilogue(dt, hd, rope):
     assert torch.equal(kc[:, others], kc0[:, others]) and torch.equal(vc[:, others], vc0[:, others])
 
 
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("dt", DTYPES)
-def test_swiglu_epilogue(dt):
+def test_swiglu_epilogue(dt, kernel):
     g = syn.generator(4, "cpu")
     inter, K = 640, 1024
     q, s, m = syn.int4_weights(2 * inter, K, g, "cpu")           # rows [gate (inter) | up (inter)]
@@ -161,7 +168,7 @@ def test_swiglu_epilogue(dt):
     y = torch.empty(2 * inter, device=DEV, dtype=dt)
     epi = _lib.GemvEpi(_lib.EPI_SWIGLU, 0, 0, 0, 0, 0, None, None, None, None, None, None, act.data_ptr())
     run_fused([_lib.GemvDesc(xin.data_ptr(), y.data_ptr(), gq.data_ptr(), gs.data_ptr(), gm.data_ptr(), 2 * inter,
-                             K)], [epi], x_dtype=dt, y_dtype=dt)
+                             K)], [epi], x_dtype=dt, y_dtype=dt, kernel=kernel)
     torch.cuda.synchronize()
     order = O.gate_up_order(inter)
     y_nat = np.empty(2 * inter, np.float32)
@@ -171,8 +178,9 @@ def test_swiglu_epilogue(dt):
     assert O.ulp_diff(vals(act), act_ref, tag(dt)).max() <= 1
 
 
+@pytest.mark.parametrize("kernel", [None, "tc"])
 @pytest.mark.parametrize("dt", DTYPES)
-def test_layer_input_launch_at_benchmark_shapes(dt):
+def test_layer_input_launch_at_benchmark_shapes(dt, kernel):
     """add_ln + QKV (24 query / 8 key-value heads of 128) + gate_up (2 x 8192) + post as ONE launch, against the
     oracle's unfused chain add_ln -> fp32 GEMV -> round -> rope / KV / silu * up."""
     g = syn.generator(5, "cpu")
@@ -189,7 +197,7 @@ def test_layer_input_launch_at_benchmark_shapes(dt):
     pos_t = torch.tensor([pos], device=DEV, dtype=torch.int64)
     layer = fused.AddLnGemvPost(qkv_d, gu_d, add_ln=fused.AddLn(xd, ad, bd, wd, x_out, eps=1e-5), pos=pos_t,
                                 cos=cos, sin=sin, k_cache=kc, v_cache=vc, q_out=q_out, act=act, n_q_heads=nq,
-                                n_kv_heads=nkv, rope=True)
+                                n_kv_heads=nkv, rope=True, kernel=kernel)
     layer()
     torch.cuda.synchronize()
     t = tag(dt)
@@ -240,7 +248,8 @@ def test_layer_input_in_a_cuda_graph_follows_the_position():
     assert torch.count_nonzero(vc[:, 3:]) == 0 and torch.count_nonzero(kc[:, 3:]) == 0
 
 
-def test_position_outside_the_cache_stores_nothing():
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_position_outside_the_cache_stores_nothing(kernel):
     dt = torch.float16
     g = syn.generator(7, "cpu")
     nq, nkv, hd, S, K = 2, 1, 128, 16, 512
@@ -254,6 +263,6 @@ def test_position_outside_the_cache_stores_nothing():
         pos = torch.tensor([bad], device=DEV, dtype=torch.int64)
         epi = _lib.GemvEpi(_lib.EPI_ROPE_KV, 0, nq, nkv, hd, S, pos.data_ptr(), None, None, q_out.data_ptr(),
                            kc.data_ptr(), vc.data_ptr(), None)
-        run_fused([_lib.GemvDesc(xin.data_ptr(), None, *(t.data_ptr() for t in wd), N, K)], [epi])
+        run_fused([_lib.GemvDesc(xin.data_ptr(), None, *(t.data_ptr() for t in wd), N, K)], [epi], kernel=kernel)
         assert rb.device_error() & _lib.DEVERR_ARG
         assert torch.count_nonzero(kc) == 0 and torch.count_nonzero(vc) == 0 and torch.count_nonzero(q_out) == 0
