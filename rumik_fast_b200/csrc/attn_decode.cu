@@ -6,7 +6,8 @@
 //
 // Grid = n_kv_heads x nsplit CTAs (nsplit ~ SMs / n_kv_heads); the filled slots 0..pos are cut into nsplit
 // chunks whose length is computed from *pos on the device (one CUDA graph serves every position). A CTA reads
-// its chunk of K and V once for all `rep` query heads of its key-value head. Each warp takes 8 slots per step:
+// its chunk of K and V once for all `rep` query heads of its key-value head. Each warp takes 8 slots per step
+// (the next step's rows are loaded during this step's math):
 // every lane holds 4 of the 128 dimensions of each row (8-byte loads, one 256-byte row per warp-load), the 8
 // x rep partial dot products are reduced across the warp with a butterfly that sums 8 values in 9 shuffles,
 // and an online softmax (running max, running sum, rescaled accumulator) folds them in. The CTA merges its
@@ -120,14 +121,19 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
   const uint8_t* kb = static_cast<const uint8_t*>(p.kc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
   const uint8_t* vb = static_cast<const uint8_t*>(p.vc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
   const int jl = lane >> 2;  // the slot of the step whose score this lane ends up holding
-  for (int64_t t0 = start + warp * kStep; t0 < end; t0 += kWarps * kStep) {
-    uint2 kr[kStep], vr[kStep];
+  uint2 kr[kStep], vr[kStep];  // this step's K and V rows; the next step's are loaded before this one's math
+  auto load_rows = [&](int64_t t, uint2 (&kk)[kStep], uint2 (&vv)[kStep]) {
 #pragma unroll
     for (int j = 0; j < kStep; ++j) {
-      const bool in = t0 + j < end;
-      kr[j] = in ? __ldg(reinterpret_cast<const uint2*>(kb + (t0 + j) * kHd * 2)) : make_uint2(0u, 0u);
-      vr[j] = in ? __ldg(reinterpret_cast<const uint2*>(vb + (t0 + j) * kHd * 2)) : make_uint2(0u, 0u);
+      const bool in = t + j < end;
+      kk[j] = in ? __ldg(reinterpret_cast<const uint2*>(kb + (t + j) * kHd * 2)) : make_uint2(0u, 0u);
+      vv[j] = in ? __ldg(reinterpret_cast<const uint2*>(vb + (t + j) * kHd * 2)) : make_uint2(0u, 0u);
     }
+  };
+  load_rows(start + warp * kStep, kr, vr);
+  for (int64_t t0 = start + warp * kStep; t0 < end; t0 += kWarps * kStep) {
+    uint2 kn[kStep], vn[kStep];
+    load_rows(t0 + kWarps * kStep, kn, vn);  // past the end: nothing loaded
     float kf[kStep][4];
 #pragma unroll
     for (int j = 0; j < kStep; ++j) unpack4(kr[j], bf, kf[j]);
@@ -158,6 +164,11 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
         for (int i = 0; i < 4; ++i) o[r][i] = fmaf(pb, vf[i], o[r][i]);
       }
       m[r] = m_new;
+    }
+#pragma unroll
+    for (int j = 0; j < kStep; ++j) {
+      kr[j] = kn[j];
+      vr[j] = vn[j];
     }
   }
   // merge the warps of this CTA
@@ -205,24 +216,59 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  // The last CTA of key-value head g merges the active partials of its query heads in split order, each
-  // thread for its dimension, with an online rescale (running max) so that every load of the merge - maxima,
-  // sums and accumulators of all splits - is independent of the others and issued at once.
+  // The last CTA of key-value head g merges the active partials of its query heads. Warp w takes splits
+  // w, w + 4, ... and every lane 4 dimensions (16-byte loads), merging with an online rescale (running max) so
+  // that all loads of a warp - maxima, sums and accumulators of its splits for every head - are independent
+  // and in flight together; the four warps' results are then merged through shared memory in warp order.
   const int64_t hg = static_cast<int64_t>(g * REP) * p.nsplit;
+  {
+    float Mw[REP], Lw[REP], Ow[REP][4];
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      Mw[r] = -INFINITY;
+      Lw[r] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) Ow[r][i] = 0.f;
+    }
+#pragma unroll 4
+    for (int s = warp; s < active; s += kWarps) {
+#pragma unroll
+      for (int r = 0; r < REP; ++r) {
+        const int64_t hs = hg + r * p.nsplit + s;
+        const float ms = __ldcg(p.pm + hs), ls = __ldcg(p.pl + hs);
+        const float4 os = __ldcg(reinterpret_cast<const float4*>(p.po + hs * kHd) + lane);
+        const float Mn = fmaxf(Mw[r], ms);
+        const float a = __expf(Mw[r] - Mn), w = __expf(ms - Mn);  // a = 0 for the warp's first split
+        Lw[r] = fmaf(Lw[r], a, w * ls);
+        Ow[r][0] = fmaf(Ow[r][0], a, w * os.x);
+        Ow[r][1] = fmaf(Ow[r][1], a, w * os.y);
+        Ow[r][2] = fmaf(Ow[r][2], a, w * os.z);
+        Ow[r][3] = fmaf(Ow[r][3], a, w * os.w);
+        Mw[r] = Mn;
+      }
+    }
+    __syncthreads();  // the CTA-merge arrays are free again
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      if (lane == 0) {
+        sm_m[warp][r] = Mw[r];
+        sm_l[warp][r] = Lw[r];
+      }
+      *reinterpret_cast<float4*>(&sm_o[warp][r][4 * lane]) = make_float4(Ow[r][0], Ow[r][1], Ow[r][2], Ow[r][3]);
+    }
+  }
+  __syncthreads();
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
-    const float* pm = p.pm + hg + r * p.nsplit;
-    const float* pl = p.pl + hg + r * p.nsplit;
-    const float* po = p.po + (hg + r * p.nsplit) * kHd + tid;
-    float M = -INFINITY, O = 0.f, L = 0.f;
-#pragma unroll 6
-    for (int s = 0; s < active; ++s) {
-      const float ms = __ldcg(pm + s), ls = __ldcg(pl + s), os = __ldcg(po + s * kHd);
-      const float Mn = fmaxf(M, ms);
-      const float a = __expf(M - Mn), w = __expf(ms - Mn);  // a = 0 for the first split (M = -inf)
-      O = fmaf(O, a, w * os);
-      L = fmaf(L, a, w * ls);
-      M = Mn;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w][r]);
+    float O = 0.f, L = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float e = sm_m[w][r] == -INFINITY ? 0.f : __expf(sm_m[w][r] - M);  // a warp without splits
+      O = fmaf(e, sm_o[w][r][tid], O);
+      L = fmaf(e, sm_l[w][r], L);
     }
     store_out(p.out, static_cast<int64_t>(g * REP + r) * kHd + tid, O / L, bf);
   }
