@@ -210,12 +210,16 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
     }
   }
   if (active == 1) return;
-  __threadfence();  // this CTA's partial is visible device-wide before its ticket
+  // The counter add releases this CTA's partial (the barrier orders every thread's stores before thread 0's
+  // release) and, for the last CTA, acquires the others' (its loads follow the barrier after the acquire).
   __syncthreads();
-  if (tid == 0) is_last = atomicAdd(&p.ticket[g], 1u) == static_cast<unsigned int>(active - 1);
+  if (tid == 0) {
+    unsigned int prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.ticket + g) : "memory");
+    is_last = prev == static_cast<unsigned int>(active - 1);
+  }
   __syncthreads();
   if (!is_last) return;
-  __threadfence();
   // The last CTA of key-value head g merges the active partials of its query heads. Warp w takes splits
   // w, w + 4, ... and every lane 4 dimensions (16-byte loads), merging with an online rescale (running max) so
   // that all loads of a warp - maxima, sums and accumulators of its splits for every head - are independent
