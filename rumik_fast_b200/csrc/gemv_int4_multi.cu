@@ -393,11 +393,9 @@ __global__ void __maxnreg__(kMaxRegs) gemv_int4_multi_kernel(const __grid_consta
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   uint64_t* empty = full + kWindow;
   uint32_t* start = reinterpret_cast<uint32_t*>(smem + p.start_off);
-  if (tid == 0) {
-    for (int i = 0; i < kWindow; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kRelease);
-    }
+  if (tid < kWindow) {  // one barrier pair per thread: 256 serial inits would cost a microsecond per launch
+    mbar_init(&full[tid], 1);
+    mbar_init(&empty[tid], kRelease);
     fence_mbar_init();
   }
   if (tid < 16) reinterpret_cast<uint32_t*>(smem + p.zero_off)[tid] = 0u;
