@@ -532,7 +532,10 @@ def build_step(dev, seed, nlayers, pos):
     assert 0 <= pos < S
     gen = syn.generator(seed, dev)
     f16 = torch.float16
-    x_emb = syn.activations((H,), gen, dev)
+    vocab = 32768  # int8 token-embedding table (engine/fused.py:18-27); layer 0 gathers the token's row
+    emb_q = torch.randint(-127, 128, (vocab, H), generator=gen, device=dev, dtype=torch.int16).to(torch.int8)
+    emb_s = torch.rand(vocab, generator=gen, device=dev) * 0.02 + 0.001
+    tok = torch.tensor([1234], device=dev, dtype=torch.int64)
     lnw = [(1 + 0.1 * syn.activations((H,), gen, dev).float()).to(f16) for _ in range(nlayers + 1)]
     inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=dev).float() / hd))
     ang = torch.outer(torch.arange(S, device=dev).float(), inv).repeat_interleave(2, -1)
@@ -546,10 +549,11 @@ def build_step(dev, seed, nlayers, pos):
     logits = torch.empty(syn.HEAD_SHAPE[0], device=dev, dtype=f16)
     pos_t = torch.tensor([pos], device=dev, dtype=torch.int64)
     layer_in, attn, layer_out = [], [], []
-    xin = x_emb
+    xin = None
     for L in range(nlayers):
         xout = xr[L % 2]
-        ln = fused.AddLn(xin, buf_o if L else None, buf_d if L else None, lnw[L], xout, eps=c["eps"])
+        ln = (fused.AddLn(xin, buf_o, buf_d, lnw[L], xout, eps=c["eps"]) if L else
+              fused.AddLn.from_embedding(emb_q, emb_s, tok, lnw[0], xout, eps=c["eps"]))
         qkv = syn.int4_weights((nq + 2 * nkv) * hd, H, gen, dev)
         gu = fused.interleave_gate_up(*syn.int4_weights(2 * inter, H, gen, dev))
         layer_in.append(fused.AddLnGemvPost(qkv, gu, add_ln=ln, pos=pos_t, cos=cos, sin=sin, k_cache=kc[L],
@@ -574,8 +578,8 @@ def build_step(dev, seed, nlayers, pos):
     shapes = [((nq + 2 * nkv) * hd, H), (2 * inter, H), (H, nq * hd), (H, inter)]
     wbytes = nlayers * sum(syn.int4_bytes(n, k) for n, k in shapes) + syn.int8_bytes(*syn.HEAD_SHAPE)
     kvbytes = nlayers * attn[0].bytes_read(pos)
-    return dict(step=step, x_emb=x_emb, logits=logits, wbytes=wbytes, kvbytes=kvbytes,
-                launches=3 * nlayers + 2, keep=(layer_in, attn, layer_out, final, head, kc, vc))
+    return dict(step=step, tok=tok, logits=logits, wbytes=wbytes + H, kvbytes=kvbytes,
+                launches=3 * nlayers + 2, keep=(layer_in, attn, layer_out, final, head, kc, vc, emb_q, emb_s))
 
 
 def run_step(a):
@@ -598,11 +602,11 @@ def run_step(a):
         ms = timed(g.replay, a.steps, a.warmup, world)
         m1 = clk.mark()
     ms_step = ms / a.steps
-    hx = w["x_emb"].cpu().pin_memory()
+    hx = w["tok"].cpu().pin_memory()
     hy = torch.empty(w["logits"].shape, dtype=torch.float16).pin_memory()
 
     def e2e_step():
-        w["x_emb"].copy_(hx, non_blocking=True)
+        w["tok"].copy_(hx, non_blocking=True)
         g.replay()
         hy.copy_(w["logits"], non_blocking=True)
     e2e_steps = max(1, a.steps // 2)
@@ -615,7 +619,8 @@ def run_step(a):
             "metric": "full decode step tok/s", "value": round(world * 1e3 / ms_step, 1), "unit": "tok/s",
             "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": f"{a.layers}-layer decode step at position {a.pos}: per layer add_ln + QKV "
+            "config": {"workload": f"{a.layers}-layer decode step at position {a.pos}: token id -> int8 embedding row "
+                                   "(layer 0's prologue); per layer add_ln + QKV "
                                    "5120x3072 + gate_up 16384x3072 + rope/KV write/silu*up (one launch), attention "
                                    "24/8 heads x 128 (one launch), o_proj 3072x3072 + down 3072x8192 (one launch); "
                                    "final add_ln + int8 head 16385x3072; one CUDA graph",
@@ -624,7 +629,7 @@ def run_step(a):
                        "l2": "no flush: 2.0 GB of weights per step > 126 MB L2"},
             "hbm_gbs": round(gbs, 1),
             "e2e": {"value": round(world * 1e3 / ms_e2e, 1), "unit": "tok/s",
-                    "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2,
+                    "h2d_bytes_per_step": hx.numel() * 8, "d2h_bytes_per_step": hy.numel() * 2,
                     "ms_per_step": round(ms_e2e, 5)},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_kind": kind, "kernel": "whole decode step",

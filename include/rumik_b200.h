@@ -203,6 +203,15 @@ typedef struct rb_add_ln {
   void* h_out;          /* the normalised vector [H], or NULL */
   int64_t H;
   float eps;
+  /* Token-embedding source (engine/fused.py:18-27, embed_ln): with emb_q non-NULL the residual is the token's
+   * int8 embedding row times its scale, s = round(emb_q[tok, :] * emb_s[tok]), instead of x + a + b (x, a, b
+   * must then be NULL). emb_q int8 [vocab, H]; emb_s [vocab] of dtype emb_s_dtype (RB_F32 or RB_F16); tok a
+   * device pointer to the int64 token id. A token outside [0, vocab) reads row 0 and sets RB_DEVERR_ARG. */
+  const int8_t* emb_q;
+  const void* emb_s;
+  const int64_t* tok;
+  int64_t vocab;
+  int emb_s_dtype;
 } rb_add_ln;
 
 enum rb_epi_kind { RB_EPI_STORE = 0, RB_EPI_ROPE_KV = 1, RB_EPI_SWIGLU = 2 };

@@ -31,7 +31,8 @@ class GemvDesc(ctypes.Structure):
 class AddLn(ctypes.Structure):
     """struct rb_add_ln (include/rumik_b200.h)."""
     _fields_ = [("x", _vp), ("a", _vp), ("b", _vp), ("w", _vp), ("x_out", _vp), ("h_out", _vp), ("H", _i64),
-                ("eps", _c.c_float)]
+                ("eps", _c.c_float), ("emb_q", _vp), ("emb_s", _vp), ("tok", _vp), ("vocab", _i64),
+                ("emb_s_dtype", _int)]
 
 
 class GemvEpi(ctypes.Structure):

@@ -207,7 +207,15 @@ static bool ranges_overlap(const void* a, int64_t abytes, const void* b, int64_t
 }
 
 static int check_add_ln(const rb_add_ln* ln) {
-  if (!ln->x || !ln->w) return RB_ERR_NULL;
+  if (ln->emb_q) {  // the token-embedding source replaces x + a + b
+    if (ln->x || ln->a || ln->b) return RB_ERR_SHAPE;
+    if (!ln->emb_s || !ln->tok || !ln->w) return RB_ERR_NULL;
+    if (ln->vocab < 1) return RB_ERR_SHAPE;
+    if (ln->emb_s_dtype != RB_F32 && ln->emb_s_dtype != RB_F16) return RB_ERR_DTYPE;
+    if (!aligned16(ln->emb_q)) return RB_ERR_ALIGN;
+  } else if (!ln->x || !ln->w) {
+    return RB_ERR_NULL;
+  }
   if (ln->H < 128 || ln->H % 128 != 0 || ln->H > 12288) return RB_ERR_SHAPE;
   if (!(ln->eps >= 0.f)) return RB_ERR_SHAPE;
   const void* in[4] = {ln->x, ln->a, ln->b, ln->w};

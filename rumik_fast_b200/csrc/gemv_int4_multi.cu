@@ -73,6 +73,11 @@ struct Slot {
   int ln;
   int K, G;
   uint32_t tab_off, cst_off;
+  const int8_t* emb_q;  // prologue from a token's embedding row (rb_add_ln::emb_q)
+  const void* emb_s;
+  const int64_t* tok;
+  int64_t vocab;
+  int emb_f16;
 };
 
 // Per-entry data kept in shared memory for the whole launch (per-tile lookups must not go to the
@@ -273,6 +278,11 @@ __device__ void stage_all_x(const MultiParams& p, uint8_t* smem, int tid) {
       L.h_out = S.h_out;
       L.eps = S.eps;
       L.K = S.K;
+      L.emb_q = S.emb_q;
+      L.emb_s = S.emb_s;
+      L.tok = S.tok;
+      L.vocab = S.vocab;
+      L.emb_f16 = S.emb_f16;
       stage_ln<4>(L, p.x_bf16 != 0, reinterpret_cast<float*>(smem + p.ln_off), 2, tid, kConsumerWarps * 32,
                   blockIdx.x == 0, [&](const float (&v)[8], bool valid, int it) {
                     __half h[8];
@@ -618,6 +628,11 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
           S.x_out = ln->x_out;
           S.h_out = ln->h_out;
           S.eps = ln->eps;
+          S.emb_q = ln->emb_q;
+          S.emb_s = ln->emb_s;
+          S.tok = ln->tok;
+          S.vocab = ln->vocab;
+          S.emb_f16 = ln->emb_s_dtype == RB_F16;
         }
         S.K = static_cast<int>(D.K);
         S.G = static_cast<int>(G);

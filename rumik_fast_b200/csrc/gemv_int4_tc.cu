@@ -75,6 +75,11 @@ struct Slot {
   int ln;
   int K, G;
   uint32_t tab_off, cst_off;
+  const int8_t* emb_q;  // prologue from a token's embedding row (rb_add_ln::emb_q)
+  const void* emb_s;
+  const int64_t* tok;
+  int64_t vocab;
+  int emb_f16;
 };
 
 struct __align__(64) TcParams {
@@ -181,6 +186,11 @@ __device__ __forceinline__ LnSrc ln_src(const Slot& S) {
   L.h_out = S.h_out;
   L.eps = S.eps;
   L.K = S.K;
+  L.emb_q = S.emb_q;
+  L.emb_s = S.emb_s;
+  L.tok = S.tok;
+  L.vocab = S.vocab;
+  L.emb_f16 = S.emb_f16;
   return L;
 }
 
@@ -608,6 +618,11 @@ int launch_add_ln(const rb_add_ln* ln, int dtype, int flags, cudaStream_t stream
   S.x_out = ln->x_out;
   S.h_out = ln->h_out;
   S.eps = ln->eps;
+  S.emb_q = ln->emb_q;
+  S.emb_s = ln->emb_s;
+  S.tok = ln->tok;
+  S.vocab = ln->vocab;
+  S.emb_f16 = ln->emb_s_dtype == RB_F16;
   S.ln = 1;
   S.K = static_cast<int>(ln->H);
   S.G = static_cast<int>(ln->H / 128);
@@ -716,6 +731,11 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
           S.x_out = ln->x_out;
           S.h_out = ln->h_out;
           S.eps = ln->eps;
+          S.emb_q = ln->emb_q;
+          S.emb_s = ln->emb_s;
+          S.tok = ln->tok;
+          S.vocab = ln->vocab;
+          S.emb_f16 = ln->emb_s_dtype == RB_F16;
         }
         S.K = static_cast<int>(D.K);
         S.G = static_cast<int>(G);

@@ -30,6 +30,11 @@ struct LnSrc {
   void* h_out;
   float eps;
   int K;
+  const int8_t* emb_q;  // token-embedding source (x, a, b unused): round(emb_q[tok] * emb_s[tok])
+  const void* emb_s;
+  const int64_t* tok;
+  int64_t vocab;
+  int emb_f16;          // emb_s is fp16 (else fp32)
 };
 
 constexpr int kLnMaxGroups = 96;  // H <= 12288: 128-element groups of the prologue vector
@@ -73,6 +78,19 @@ __device__ void stage_ln(const LnSrc& S, bool bf, float* gsum, int bar_id, int c
   const int chunks = S.K / 8, G = S.K / 128;
   float v[kIter][8];
   uint4 wraw[kIter];  // the LayerNorm weight, loaded with x, a and b
+  // token-embedding source (engine/fused.py:18-27): the token's int8 row and its scale
+  const int8_t* erow = nullptr;
+  float escale = 0.f;
+  if (S.emb_q) {
+    int64_t tok = *S.tok;
+    if (tok < 0 || tok >= S.vocab) {
+      if (ct == 0 && writer_cta) atomicOr(&g_device_error, ERR_ARG);
+      tok = 0;
+    }
+    erow = S.emb_q + tok * S.K;
+    escale = S.emb_f16 ? __half2float(reinterpret_cast<const __half*>(S.emb_s)[tok])
+                       : reinterpret_cast<const float*>(S.emb_s)[tok];
+  }
 #pragma unroll
   for (int it = 0; it < kIter; ++it) {
     const int c = it * nthreads + ct;
@@ -80,7 +98,16 @@ __device__ void stage_ln(const LnSrc& S, bool bf, float* gsum, int bar_id, int c
     wraw[it] = valid ? ldg_cg_128(static_cast<const uint8_t*>(S.w) + static_cast<int64_t>(c) * 16)
                      : make_uint4(0u, 0u, 0u, 0u);
     float cs = 0.f;
-    if (valid) {
+    if (valid && erow) {
+      const uint2 q8 = __ldg(reinterpret_cast<const uint2*>(erow + static_cast<int64_t>(c) * 8));
+      const uint32_t qw[2] = {q8.x, q8.y};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int8_t qi = static_cast<int8_t>((qw[i >> 2] >> (8 * (i & 3))) & 0xFFu);
+        v[it][i] = round_act(static_cast<float>(qi) * escale, bf);
+        cs += v[it][i];
+      }
+    } else if (valid) {
       load8_f32(static_cast<const uint8_t*>(S.x) + static_cast<int64_t>(c) * 16, bf, v[it]);
       float t[8];
       if (S.a) {

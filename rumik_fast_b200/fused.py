@@ -60,7 +60,25 @@ def split_w_in(q, s, m, n_q_heads, n_kv_heads, head_dim):
 # ---------------------------------------------------------------------------------------------- descriptors
 class AddLn:
     """The add + LayerNorm prologue: x_out = x + a + b (fp32 sum, rounded once), h = LayerNorm(x_out) * w
-    (engine/fused.py:29-40). a and b may be None; h_out (optional) receives h."""
+    (engine/fused.py:29-40). a and b may be None; h_out (optional) receives h. AddLn.from_embedding builds the
+    layer-0 form (engine/fused.py:18-27): the residual is the token's int8 embedding row times its scale."""
+
+    @classmethod
+    def from_embedding(cls, emb_q, emb_s, tok, w, x_out, eps=1e-5, h_out=None):
+        """emb_q int8 [vocab, H], emb_s [vocab] fp32/fp16, tok an int64 device tensor holding the token id."""
+        _require(emb_q.dtype == torch.int8 and emb_q.dim() == 2 and emb_q.is_contiguous() and emb_q.is_cuda,
+                 "emb_q must be a contiguous CUDA int8 [vocab, H] tensor")
+        _require(emb_s.dtype in (torch.float32, torch.float16) and emb_s.numel() == emb_q.shape[0],
+                 "emb_s must hold one fp32/fp16 scale per embedding row")
+        _require(tok.dtype == torch.int64 and tok.device == emb_q.device, "tok must be an int64 device tensor")
+        self = cls(w, None, None, w, x_out, eps=eps, h_out=h_out)  # w stands in for x to check shapes
+        self.c.x = None
+        self.c.emb_q, self.c.emb_s, self.c.tok = emb_q.data_ptr(), emb_s.data_ptr(), tok.data_ptr()
+        self.c.vocab = emb_q.shape[0]
+        self.c.emb_s_dtype = _lib.dtype_code(emb_s.dtype)
+        self.tensors = (None, None, None, w, x_out, h_out)
+        self.embedding = (emb_q, emb_s, tok)
+        return self
 
     def __init__(self, x, a, b, w, x_out, eps=1e-5, h_out=None):
         H = x.numel()
@@ -114,7 +132,7 @@ class AddLnGemvPost:
     def __init__(self, qkv, gate_up, *, pos, cos, sin, k_cache, v_cache, q_out, act, n_q_heads, n_kv_heads,
                  add_ln=None, h=None, rope=True, y_qkv=None, y_gate_up=None, kernel=None):
         _require((add_ln is None) != (h is None), "give exactly one of add_ln and h")
-        src = add_ln.tensors[0] if add_ln is not None else h
+        src = add_ln.tensors[3] if add_ln is not None else h  # the norm weight: the activations' dtype
         self.device, self.x_dtype = src.device, src.dtype
         H = src.numel()
         dt = act.dtype

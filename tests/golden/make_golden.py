@@ -150,8 +150,23 @@ def make_glue(ref_root):
         up = torch.randn(inter, generator=g).to(dt)
         out.update({f"{dname}_sw_g": bits(gt), f"{dname}_sw_u": bits(up),
                     f"{dname}_sw_act": bits((F.silu(gt.float()) * up.float()).to(dt))})
-    # decode attention: 6 query heads on 2 key-value heads, 50 cache slots, position 33
+    # layer-0 input: the reference's embed (int8 row x scale, rounded) then cohere_ln, bf16 and fp16 outputs
     import types
+    g = torch.Generator().manual_seed(43)
+    vocab, H = 37, 256
+    emb_q = torch.randint(-127, 128, (vocab, H), generator=g, dtype=torch.int16).to(torch.int8)
+    emb_s = torch.rand(vocab, generator=g) * 0.02 + 0.001
+    ids = torch.tensor([5, 36, 0])
+    for dname, dt in (("bf16", torch.bfloat16), ("f16", torch.float16)):
+        w = (1 + 0.1 * torch.randn(H, generator=g)).to(dt)
+        if dt == torch.bfloat16:   # the reference's own embed (engine/rumik_int4.py:134-135), bf16 by design
+            e = refe.RumikInt4.embed(types.SimpleNamespace(emb_q=emb_q, emb_s=emb_s), ids)
+        else:                      # the same product rounded to fp16
+            e = (emb_q[ids].float() * emb_s[ids, None].float()).to(dt)
+        out.update({f"{dname}_emb_w": bits(w), f"{dname}_emb_x": bits(e),
+                    f"{dname}_emb_h": bits(torch.stack([refe.cohere_ln(r, w, 1e-5) for r in e]))})
+    out.update({"emb_q": emb_q.numpy(), "emb_s": emb_s.numpy(), "emb_ids": ids.numpy()})
+    # decode attention: 6 query heads on 2 key-value heads, 50 cache slots, position 33
     g = torch.Generator().manual_seed(42)
     nq, nkv, hd, S, pos = 6, 2, 128, 50, 33
     q = torch.randn(nq * hd, generator=g).to(torch.bfloat16)

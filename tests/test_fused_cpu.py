@@ -132,3 +132,23 @@ def test_attention_argument_checks(native_lib):
     assert with_(dt=_lib.F32) == _lib.ERR_DTYPE
     assert with_(out=0x50008) == _lib.ERR_ALIGN
     assert with_(scale=float("nan")) == _lib.ERR_SHAPE
+
+
+def test_embedding_prologue_argument_checks(native_lib):
+    L = native_lib
+
+    def emb(**kw):
+        ln = add_ln(x=None, a=None, b=None)
+        ln.emb_q, ln.emb_s, ln.tok, ln.vocab, ln.emb_s_dtype = 0xA0000, 0xB0000, 0xC0000, 100, _lib.F32
+        for k, v in kw.items():
+            setattr(ln, k, v)
+        return ln
+
+    assert L.rb_add_layernorm(ctypes.byref(emb(x=0x50000)), _lib.F16, 0, None) == _lib.ERR_SHAPE   # x and emb
+    assert L.rb_add_layernorm(ctypes.byref(emb(a=0x60000)), _lib.F16, 0, None) == _lib.ERR_SHAPE
+    assert L.rb_add_layernorm(ctypes.byref(emb(tok=None)), _lib.F16, 0, None) == _lib.ERR_NULL
+    assert L.rb_add_layernorm(ctypes.byref(emb(emb_s=None)), _lib.F16, 0, None) == _lib.ERR_NULL
+    assert L.rb_add_layernorm(ctypes.byref(emb(vocab=0)), _lib.F16, 0, None) == _lib.ERR_SHAPE
+    assert L.rb_add_layernorm(ctypes.byref(emb(emb_s_dtype=_lib.BF16)), _lib.F16, 0, None) == _lib.ERR_DTYPE
+    assert L.rb_add_layernorm(ctypes.byref(emb(emb_q=0xA0008)), _lib.F16, 0, None) == _lib.ERR_ALIGN
+    assert call(L, [desc(x=None)], ln=emb(tok=None)) == _lib.ERR_NULL

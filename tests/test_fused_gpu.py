@@ -266,3 +266,38 @@ def test_position_outside_the_cache_stores_nothing(kernel):
         run_fused([_lib.GemvDesc(xin.data_ptr(), None, *(t.data_ptr() for t in wd), N, K)], [epi], kernel=kernel)
         assert rb.device_error() & _lib.DEVERR_ARG
         assert torch.count_nonzero(kc) == 0 and torch.count_nonzero(vc) == 0 and torch.count_nonzero(q_out) == 0
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("dt", DTYPES)
+def test_embedding_prologue(dt, kernel):
+    """Layer 0: the residual is the token's int8 embedding row times its scale (engine/fused.py:18-27), read on the
+    device from the token id; then the LayerNorm and the GEMVs, and the standalone kernel gives the same bits."""
+    g = syn.generator(8, "cpu")
+    vocab, H = 1000, 3072
+    emb_q = torch.randint(-127, 128, (vocab, H), generator=g, dtype=torch.int16).to(torch.int8)
+    emb_s = torch.rand(vocab, generator=g) * 0.02 + 0.001
+    w = rand(H, g, dt, 0.1, 1.0)
+    eq, es, wd = emb_q.to(DEV), emb_s.to(DEV), w.to(DEV)
+    tok = torch.tensor([731], device=DEV, dtype=torch.int64)
+    x_out = torch.empty(H, device=DEV, dtype=dt)
+    h_out = torch.empty(H, device=DEV, dtype=dt)
+    ln = fused.AddLn.from_embedding(eq, es, tok, wd, x_out, eps=1e-5, h_out=h_out)
+    (wh, wdd) = weights(640, H, g)
+    y = torch.empty(640, device=DEV, dtype=dt)
+    run_fused([_lib.GemvDesc(None, y.data_ptr(), *(t.data_ptr() for t in wdd), 640, H)], ln=ln, x_dtype=dt,
+              y_dtype=dt, kernel=kernel)
+    torch.cuda.synchronize()
+    s_ref, h_ref = O.embed_ln_ref(731, emb_q.numpy(), emb_s.numpy(), np_act(w)[0], 1e-5, tag(dt))
+    assert np.array_equal(vals(x_out), s_ref)
+    assert O.ulp_diff(vals(h_out), h_ref, tag(dt)).max() <= 1
+    assert_close(y, int4_ref(h_out.cpu(), *wh), "GEMV of the embedded, normalised token")
+    x2, h2 = torch.empty_like(x_out), torch.empty_like(h_out)
+    fused.add_layernorm(fused.AddLn.from_embedding(eq, es, tok, wd, x2, eps=1e-5, h_out=h2))
+    torch.cuda.synchronize()
+    assert torch.equal(x2, x_out) and torch.equal(h2, h_out)
+    tok.fill_(vocab)                                   # outside the table: row 0, error bit set
+    fused.add_layernorm(fused.AddLn.from_embedding(eq, es, tok, wd, x2, eps=1e-5, h_out=h2))
+    assert rb.device_error() & _lib.DEVERR_ARG
+    s0, _ = O.embed_ln_ref(0, emb_q.numpy(), emb_s.numpy(), np_act(w)[0], 1e-5, tag(dt))
+    assert np.array_equal(vals(x2), s0)

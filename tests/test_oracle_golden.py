@@ -154,3 +154,11 @@ def test_attention_matches_reference(gg):
     nq, nkv, hd, S, pos = (int(v) for v in gg["attn_meta"])
     o = O.attention_ref(gg["attn_q"], gg["attn_k"], gg["attn_v"], pos, nq, nkv, hd, hd ** -0.5, "bf16")
     assert O.ulp_diff(o, _stored(gg["attn_o"], "bf16"), "bf16").max() <= 1
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_embed_ln_matches_reference(gg, dt):
+    for i, tok in enumerate(gg["emb_ids"]):
+        s, h = O.embed_ln_ref(int(tok), gg["emb_q"], gg["emb_s"], gg[f"{dt}_emb_w"], 1e-5, dt)
+        assert np.array_equal(s, _stored(gg[f"{dt}_emb_x"][i], dt))     # one product, one rounding: exact
+        assert O.ulp_diff(h, _stored(gg[f"{dt}_emb_h"][i], dt), dt).max() <= 1
