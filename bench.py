@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers in the step (36 = config 1; fewer only for small profiling cases)")
     ap.add_argument("--pos", type=int, default=511, help="step workload: position of the token (cache slots read)")
+    ap.add_argument("--attn", default="separate", choices=["fused", "separate"],
+                    help="step workload: attention in its own launch (default, faster at the config shapes), or "
+                         "inside the o_proj/down_proj launch")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "step"],
                     help="decode: config 1 + 2 (the headline); prefill: config 3, the int4-weight matmul over the "
                          "36-layer projection set for --tokens prompt tokens")
@@ -517,7 +520,7 @@ def run_prefill(a):
 STEP_SHAPE = dict(H=3072, nq=24, nkv=8, hd=128, inter=8192, S=2048, eps=1e-5)
 
 
-def build_step(dev, seed, nlayers, pos):
+def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
     """A whole decode step at the config-1 shapes (3072 hidden, 24 query / 8 key-value heads of 128, MLP 8192,
     36 layers, int8 head), laid out as rumik-fast's fused engine runs it (engine/rumik_fused.py:83-118), with the
     glue fused: per layer [add_ln + QKV + gate_up + rope/KV/silu*up] (one launch), attention (one launch),
@@ -559,10 +562,14 @@ def build_step(dev, seed, nlayers, pos):
         layer_in.append(fused.AddLnGemvPost(qkv, gu, add_ln=ln, pos=pos_t, cos=cos, sin=sin, k_cache=kc[L],
                                             v_cache=vc[L], q_out=q_out, act=act, n_q_heads=nq, n_kv_heads=nkv,
                                             rope=L % 4 != 3))
-        attn.append(DecodeAttention(q_out, kc[L], vc[L], pos_t, ob, nq, nkv))
         wo = syn.int4_weights(H, nq * hd, gen, dev)
         wd = syn.int4_weights(H, inter, gen, dev)
-        layer_out.append(rb.Int4GemvSet([(ob, *wo, buf_o), (act, *wd, buf_d)]))
+        if attn_mode == "fused":  # attention inside the o_proj/down_proj launch
+            layer_out.append(fused.AttnGemvSet([(act, *wd, buf_d), (ob, *wo, buf_o)], q=q_out, k_cache=kc[L],
+                                               v_cache=vc[L], pos=pos_t, out=ob, n_q_heads=nq, n_kv_heads=nkv))
+        else:
+            attn.append(DecodeAttention(q_out, kc[L], vc[L], pos_t, ob, nq, nkv))
+            layer_out.append(rb.Int4GemvSet([(ob, *wo, buf_o), (act, *wd, buf_d)]))
         xin = xout
     final = fused.AddLn(xin, buf_o, buf_d, lnw[nlayers], None, eps=c["eps"], h_out=hn)
     head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
@@ -570,16 +577,17 @@ def build_step(dev, seed, nlayers, pos):
     def step():
         for L in range(nlayers):
             layer_in[L]()
-            attn[L]()
+            if attn:
+                attn[L]()
             layer_out[L]()
         fused.add_layernorm(final)
         rb.gemv_int8_cuda(hn, *head, out=logits)
 
     shapes = [((nq + 2 * nkv) * hd, H), (2 * inter, H), (H, nq * hd), (H, inter)]
     wbytes = nlayers * sum(syn.int4_bytes(n, k) for n, k in shapes) + syn.int8_bytes(*syn.HEAD_SHAPE)
-    kvbytes = nlayers * attn[0].bytes_read(pos)
+    kvbytes = nlayers * (2 * nkv * (pos + 1) * hd * 2 + 2 * nq * hd * 2)
     return dict(step=step, tok=tok, logits=logits, wbytes=wbytes + H, kvbytes=kvbytes,
-                launches=3 * nlayers + 2, keep=(layer_in, attn, layer_out, final, head, kc, vc, emb_q, emb_s))
+                launches=(2 if attn_mode == "fused" else 3) * nlayers + 2, keep=(layer_in, attn, layer_out, final, head, kc, vc, emb_q, emb_s))
 
 
 def run_step(a):
@@ -595,7 +603,7 @@ def run_step(a):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     rb.set_weight_prefetch(not a.no_prefetch)
-    w = build_step(dev, 777 + rank, a.layers, a.pos)
+    w = build_step(dev, 777 + rank, a.layers, a.pos, a.attn)
     g = capture(w["step"])
     with ClockSampler(local_gpu_index(local)) as clk:
         m0 = clk.mark()
@@ -619,11 +627,13 @@ def run_step(a):
             "metric": "full decode step tok/s", "value": round(world * 1e3 / ms_step, 1), "unit": "tok/s",
             "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": f"{a.layers}-layer decode step at position {a.pos}: token id -> int8 embedding row "
+            "config": {"attention": a.attn,
+                       "workload": f"{a.layers}-layer decode step at position {a.pos}: token id -> int8 embedding row "
                                    "(layer 0's prologue); per layer add_ln + QKV "
                                    "5120x3072 + gate_up 16384x3072 + rope/KV write/silu*up (one launch), attention "
-                                   "24/8 heads x 128 (one launch), o_proj 3072x3072 + down 3072x8192 (one launch); "
-                                   "final add_ln + int8 head 16385x3072; one CUDA graph",
+                                   "24/8 heads x 128 with o_proj 3072x3072 + down 3072x8192 ("
+                                   + ("one launch" if a.attn == "fused" else "two launches") +
+                                   "); final add_ln + int8 head 16385x3072; one CUDA graph",
                        "pos": a.pos, "bytes_per_step": total, "weight_bytes": w["wbytes"], "kv_bytes": w["kvbytes"],
                        "parallelism": f"replica x{world}", "weight_prefetch": not a.no_prefetch,
                        "l2": "no flush: 2.0 GB of weights per step > 126 MB L2"},

@@ -233,11 +233,35 @@ typedef struct rb_gemv_epi {
 /* Device error bit set by rb_gemv_int4_fused when *pos is outside [0, cache_len). */
 #define RB_DEVERR_ARG (1u << 9)
 
-/* descs[i], epis[i] (epis may be NULL: all RB_EPI_STORE); ln may be NULL (no entry may then have x == NULL).
- * ws / ws_bytes: the split-K workspace of rb_gemv_int4_multi_ws (rb_gemv_int4_workspace(descs, count) bytes),
- * or NULL / 0. A split entry runs its epilogue in the last slice of each block. */
+/*
+ * Decode attention fused into a GEMV launch (the o_proj input of a layer; rb_attn_decode's attention, in the
+ * same launch as the layer's o_proj and down_proj). Entries whose `x` equals `out` read the attention output,
+ * which the launch computes and also stores to `out`; they must come last in the list. The other entries (the
+ * down_proj of the layer, whose input is ready at launch) stream while the attention runs. Fields as
+ * rb_attn_decode; ws: rb_attn_decode_workspace(...) bytes, its first 512 bytes zero before the first use (every
+ * launch leaves them zero). 1 <= n_q_heads / n_kv_heads <= 4. Such a launch always runs on the warp-MMA kernel
+ * (RB_FLAG_KERNEL_TC: RB_ERR_SHAPE) and the whole list must fit one launch.
+ */
+typedef struct rb_attn_src {
+  const void* q;
+  const void* k_cache;
+  const void* v_cache;
+  const int64_t* pos;
+  void* out;
+  int n_q_heads, n_kv_heads, head_dim;
+  int64_t cache_len;
+  float scale;
+  void* ws;
+  int64_t ws_bytes;
+} rb_attn_src;
+
+/* descs[i], epis[i] (epis may be NULL: all RB_EPI_STORE); ln may be NULL (no entry may then have x == NULL);
+ * attn may be NULL. ws / ws_bytes: the split-K workspace of rb_gemv_int4_multi_ws
+ * (rb_gemv_int4_workspace(descs, count, flags) bytes), or NULL / 0. A split entry runs its epilogue in the last
+ * slice of each block. */
 int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int count, const rb_add_ln* ln,
-                       void* ws, int64_t ws_bytes, int x_dtype, int y_dtype, int flags, void* stream);
+                       const rb_attn_src* attn, void* ws, int64_t ws_bytes, int x_dtype, int y_dtype, int flags,
+                       void* stream);
 
 /* The add + LayerNorm alone (engine/fused.py:29-40 as launched at engine/rumik_fused.py:115-116 for the final
  * norm in front of the head): one CTA; results bit-identical to rb_gemv_int4_fused's prologue. dtype is the

@@ -42,6 +42,13 @@ class GemvEpi(ctypes.Structure):
                 ("v_cache", _vp), ("act_out", _vp)]
 
 
+class AttnSrc(ctypes.Structure):
+    """struct rb_attn_src (include/rumik_b200.h)."""
+    _fields_ = [("q", _vp), ("k_cache", _vp), ("v_cache", _vp), ("pos", _vp), ("out", _vp), ("n_q_heads", _int),
+                ("n_kv_heads", _int), ("head_dim", _int), ("cache_len", _i64), ("scale", _c.c_float), ("ws", _vp),
+                ("ws_bytes", _i64)]
+
+
 EPI_STORE, EPI_ROPE_KV, EPI_SWIGLU = 0, 1, 2
 DEVERR_ARG = 1 << 9
 
@@ -53,8 +60,8 @@ SIGNATURES = {
     "rb_mm_int4_static": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
     "rb_mm_int4_ws": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _vp, _i64, _int, _vp]),
     "rb_gemv_int4_multi": (_int, [_c.POINTER(GemvDesc), _int, _int, _int, _int, _vp]),
-    "rb_gemv_int4_fused": (_int, [_c.POINTER(GemvDesc), _c.POINTER(GemvEpi), _int, _c.POINTER(AddLn), _vp, _i64,
-                                  _int, _int, _int, _vp]),
+    "rb_gemv_int4_fused": (_int, [_c.POINTER(GemvDesc), _c.POINTER(GemvEpi), _int, _c.POINTER(AddLn),
+                                  _c.POINTER(AttnSrc), _vp, _i64, _int, _int, _int, _vp]),
     "rb_gemv_int4_workspace": (_i64, [_c.POINTER(GemvDesc), _int, _int]),
     "rb_gemv_int4_multi_ws": (_int, [_c.POINTER(GemvDesc), _int, _vp, _i64, _int, _int, _int, _vp]),
     "rb_add_layernorm": (_int, [_c.POINTER(AddLn), _int, _int, _vp]),

@@ -14,272 +14,23 @@
 // warps and writes an fp32 partial (acc, max, sum); the last CTA of each key-value head to finish (an atomic
 // ticket) merges the nsplit partials in split order and writes the heads' outputs, so no second launch.
 // HBM-bound at long contexts: 2 x (pos + 1) x 256 bytes per key-value head.
-#include "common.cuh"
+#include "attn.cuh"
 #include "kernels.h"
 
 namespace rb {
 
 namespace attn {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kHd = 128;       // head_dim: 4 dimensions per lane
-constexpr int kStep = 8;       // slots per warp step
-constexpr int kMaxRep = 8;
-constexpr int kMaxSplit = 64;
-constexpr int kMaxKv = 64;
-constexpr int64_t kTicketBytes = kMaxKv * 4;
-
-struct AttnParams {
-  const void* q;
-  const void* kc;
-  const void* vc;
-  const int64_t* pos;
-  void* out;
-  unsigned int* ticket;  // [n_kv_heads], zero between calls
-  float* po;             // [n_q_heads, nsplit, 128] partial accumulators
-  float* pm;             // [n_q_heads, nsplit] partial maxima
-  float* pl;             // [n_q_heads, nsplit] partial sums
-  int64_t S;
-  float scale;
-  int nsplit, bf16;
-};
-
-__device__ __forceinline__ void unpack4(uint2 u, bool bf, float (&f)[4]) {
-  if (bf) {
-    f[0] = __uint_as_float(u.x << 16);
-    f[1] = __uint_as_float(u.x & 0xffff0000u);
-    f[2] = __uint_as_float(u.y << 16);
-    f[3] = __uint_as_float(u.y & 0xffff0000u);
-  } else {
-    f[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(u.x & 0xffffu)));
-    f[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(u.x >> 16)));
-    f[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(u.y & 0xffffu)));
-    f[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(u.y >> 16)));
-  }
-}
-
-// Sum of s[j] over the 32 lanes for 8 values at once: afterwards lane l holds the sum for slot j = l >> 2.
-__device__ __forceinline__ float reduce8(const float (&s)[8], int lane) {
-  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
-  float k1[4], k2[2];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float send = b4 ? s[i] : s[i + 4];
-    k1[i] = (b4 ? s[i + 4] : s[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float send = b3 ? k1[i] : k1[i + 2];
-    k2[i] = (b3 ? k1[i + 2] : k1[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-  const float send = b2 ? k2[0] : k2[1];
-  float v = (b2 ? k2[1] : k2[0]) + __shfl_xor_sync(0xffffffffu, send, 4);
-  v += __shfl_xor_sync(0xffffffffu, v, 2);
-  v += __shfl_xor_sync(0xffffffffu, v, 1);
-  return v;
-}
-
 template <int REP>
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
   __shared__ float sm_m[kWarps][REP], sm_l[kWarps][REP];
   __shared__ __align__(16) float sm_o[kWarps][REP][kHd];
   __shared__ int is_last;
-  const int g = blockIdx.x / p.nsplit, sp = blockIdx.x - g * p.nsplit;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const bool bf = p.bf16 != 0;
   griddep_launch_dependents();
   griddep_wait();  // q and the cache slot of this token come from the previous kernel
-  uint2 qraw[REP];  // issued together with the position load: one round trip for both
-#pragma unroll
-  for (int r = 0; r < REP; ++r)
-    qraw[r] = __ldcg(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(p.q) +
-                                                    (static_cast<int64_t>(g * REP + r) * kHd + 4 * lane) * 2));
-  const int64_t pos = __ldcg(p.pos);
-  if (pos < 0 || pos >= p.S) {  // the same decision in every CTA: none takes a ticket
-    if (tid == 0 && blockIdx.x == 0) atomicOr(&g_device_error, ERR_ARG);
-    return;
-  }
-  const int64_t n = pos + 1;
-  const int64_t ch = ((n + p.nsplit - 1) / p.nsplit + kWarps * kStep - 1) / (kWarps * kStep) * (kWarps * kStep);
-  const int active = static_cast<int>((n + ch - 1) / ch);  // splits with slots; the others leave at once
-  if (sp >= active) return;
-  const int64_t start = static_cast<int64_t>(sp) * ch, end = start + ch < n ? start + ch : n;
-
-  float qv[REP][4], m[REP], l[REP], o[REP][4];
-#pragma unroll
-  for (int r = 0; r < REP; ++r) {
-    unpack4(qraw[r], bf, qv[r]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      qv[r][i] *= p.scale;
-      o[r][i] = 0.f;
-    }
-    m[r] = -INFINITY;
-    l[r] = 0.f;
-  }
-  const uint8_t* kb = static_cast<const uint8_t*>(p.kc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
-  const uint8_t* vb = static_cast<const uint8_t*>(p.vc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
-  const int jl = lane >> 2;  // the slot of the step whose score this lane ends up holding
-  uint2 kr[kStep], vr[kStep];  // this step's K and V rows; the next step's are loaded before this one's math
-  auto load_rows = [&](int64_t t, uint2 (&kk)[kStep], uint2 (&vv)[kStep]) {
-#pragma unroll
-    for (int j = 0; j < kStep; ++j) {
-      const bool in = t + j < end;
-      kk[j] = in ? __ldg(reinterpret_cast<const uint2*>(kb + (t + j) * kHd * 2)) : make_uint2(0u, 0u);
-      vv[j] = in ? __ldg(reinterpret_cast<const uint2*>(vb + (t + j) * kHd * 2)) : make_uint2(0u, 0u);
-    }
-  };
-  load_rows(start + warp * kStep, kr, vr);
-  for (int64_t t0 = start + warp * kStep; t0 < end; t0 += kWarps * kStep) {
-    uint2 kn[kStep], vn[kStep];
-    load_rows(t0 + kWarps * kStep, kn, vn);  // past the end: nothing loaded
-    float kf[kStep][4];
-#pragma unroll
-    for (int j = 0; j < kStep; ++j) unpack4(kr[j], bf, kf[j]);
-    const bool mine_in = t0 + jl < end;
-#pragma unroll
-    for (int r = 0; r < REP; ++r) {
-      float s[kStep];
-#pragma unroll
-      for (int j = 0; j < kStep; ++j)
-        s[j] = qv[r][0] * kf[j][0] + qv[r][1] * kf[j][1] + qv[r][2] * kf[j][2] + qv[r][3] * kf[j][3];
-      float sc = reduce8(s, lane);
-      if (!mine_in) sc = -INFINITY;
-      float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 4));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float m_new = fmaxf(m[r], mx);         // finite: slot t0 is always in range
-      const float alpha = __expf(m[r] - m_new);    // 0 on the first step (m = -inf)
-      const float pj = __expf(sc - m_new);         // 0 for slots past the end
-      l[r] = l[r] * alpha + pj;                    // per lane; the 4 lanes of a slot hold the same value
-#pragma unroll
-      for (int i = 0; i < 4; ++i) o[r][i] *= alpha;
-#pragma unroll
-      for (int j = 0; j < kStep; ++j) {
-        const float pb = __shfl_sync(0xffffffffu, pj, 4 * j);
-        float vf[4];
-        unpack4(vr[j], bf, vf);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o[r][i] = fmaf(pb, vf[i], o[r][i]);
-      }
-      m[r] = m_new;
-    }
-#pragma unroll
-    for (int j = 0; j < kStep; ++j) {
-      kr[j] = kn[j];
-      vr[j] = vn[j];
-    }
-  }
-  // merge the warps of this CTA
-#pragma unroll
-  for (int r = 0; r < REP; ++r) {
-    float lt = l[r] + __shfl_xor_sync(0xffffffffu, l[r], 4);  // one lane per slot group of the step
-    lt += __shfl_xor_sync(0xffffffffu, lt, 8);
-    lt += __shfl_xor_sync(0xffffffffu, lt, 16);
-    if (lane == 0) {
-      sm_m[warp][r] = m[r];
-      sm_l[warp][r] = lt;
-    }
-    *reinterpret_cast<float4*>(&sm_o[warp][r][4 * lane]) = make_float4(o[r][0], o[r][1], o[r][2], o[r][3]);
-  }
-  __syncthreads();
-#pragma unroll
-  for (int r = 0; r < REP; ++r) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w][r]);
-    float O = 0.f, L = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        const float e = __expf(sm_m[w][r] - M);
-        O = fmaf(e, sm_o[w][r][tid], O);
-        L = fmaf(e, sm_l[w][r], L);
-      }
-    }
-    if (active == 1) {  // one split holds every slot: no partials, no merge
-      store_out(p.out, static_cast<int64_t>(g * REP + r) * kHd + tid, O / L, bf);
-      continue;
-    }
-    const int64_t hs = static_cast<int64_t>(g * REP + r) * p.nsplit + sp;
-    p.po[hs * kHd + tid] = O;
-    if (tid == 0) {
-      p.pm[hs] = M;
-      p.pl[hs] = L;
-    }
-  }
-  if (active == 1) return;
-  // The counter add releases this CTA's partial (the barrier orders every thread's stores before thread 0's
-  // release) and, for the last CTA, acquires the others' (its loads follow the barrier after the acquire).
-  __syncthreads();
-  if (tid == 0) {
-    unsigned int prev;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.ticket + g) : "memory");
-    is_last = prev == static_cast<unsigned int>(active - 1);
-  }
-  __syncthreads();
-  if (!is_last) return;
-  // The last CTA of key-value head g merges the active partials of its query heads. Warp w takes splits
-  // w, w + 4, ... and every lane 4 dimensions (16-byte loads), merging with an online rescale (running max) so
-  // that all loads of a warp - maxima, sums and accumulators of its splits for every head - are independent
-  // and in flight together; the four warps' results are then merged through shared memory in warp order.
-  const int64_t hg = static_cast<int64_t>(g * REP) * p.nsplit;
-  {
-    float Mw[REP], Lw[REP], Ow[REP][4];
-#pragma unroll
-    for (int r = 0; r < REP; ++r) {
-      Mw[r] = -INFINITY;
-      Lw[r] = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) Ow[r][i] = 0.f;
-    }
-#pragma unroll 4
-    for (int s = warp; s < active; s += kWarps) {
-#pragma unroll
-      for (int r = 0; r < REP; ++r) {
-        const int64_t hs = hg + r * p.nsplit + s;
-        const float ms = __ldcg(p.pm + hs), ls = __ldcg(p.pl + hs);
-        const float4 os = __ldcg(reinterpret_cast<const float4*>(p.po + hs * kHd) + lane);
-        const float Mn = fmaxf(Mw[r], ms);
-        const float a = __expf(Mw[r] - Mn), w = __expf(ms - Mn);  // a = 0 for the warp's first split
-        Lw[r] = fmaf(Lw[r], a, w * ls);
-        Ow[r][0] = fmaf(Ow[r][0], a, w * os.x);
-        Ow[r][1] = fmaf(Ow[r][1], a, w * os.y);
-        Ow[r][2] = fmaf(Ow[r][2], a, w * os.z);
-        Ow[r][3] = fmaf(Ow[r][3], a, w * os.w);
-        Mw[r] = Mn;
-      }
-    }
-    __syncthreads();  // the CTA-merge arrays are free again
-#pragma unroll
-    for (int r = 0; r < REP; ++r) {
-      if (lane == 0) {
-        sm_m[warp][r] = Mw[r];
-        sm_l[warp][r] = Lw[r];
-      }
-      *reinterpret_cast<float4*>(&sm_o[warp][r][4 * lane]) = make_float4(Ow[r][0], Ow[r][1], Ow[r][2], Ow[r][3]);
-    }
-  }
-  __syncthreads();
-#pragma unroll
-  for (int r = 0; r < REP; ++r) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w][r]);
-    float O = 0.f, L = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float e = sm_m[w][r] == -INFINITY ? 0.f : __expf(sm_m[w][r] - M);  // a warp without splits
-      O = fmaf(e, sm_o[w][r][tid], O);
-      L = fmaf(e, sm_l[w][r], L);
-    }
-    store_out(p.out, static_cast<int64_t>(g * REP + r) * kHd + tid, O / L, bf);
-  }
-  if (tid == 0) p.ticket[g] = 0u;  // ready for the next call
+  attn_cta<REP, false>(p, blockIdx.x / p.nsplit, blockIdx.x % p.nsplit, threadIdx.x, 0, sm_m, sm_l, sm_o, &is_last);
 }
 
-int64_t nsplit_for(int nkv, int sms) { return std::max(1, std::min(kMaxSplit, sms / nkv)); }
 
 }  // namespace attn
 
@@ -304,6 +55,7 @@ int launch_attn_decode(const void* q, const void* kc, const void* vc, const int6
   p.nsplit = static_cast<int>(nsplit_for(nkv, num_sms));
   uint8_t* w = static_cast<uint8_t*>(ws);
   p.ticket = reinterpret_cast<unsigned int*>(w);
+  p.heads_done = nullptr;
   p.po = reinterpret_cast<float*>(w + kTicketBytes);
   p.pm = p.po + static_cast<int64_t>(nq) * p.nsplit * kHd;
   p.pl = p.pm + static_cast<int64_t>(nq) * p.nsplit;

@@ -269,7 +269,8 @@ int rb_attn_decode(const void* q, const void* k_cache, const void* v_cache, cons
 }
 
 int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int count, const rb_add_ln* ln,
-                       void* ws, int64_t ws_bytes, int x_dtype, int y_dtype, int flags, void* stream) {
+                       const rb_attn_src* attn, void* ws, int64_t ws_bytes, int x_dtype, int y_dtype, int flags,
+                       void* stream) {
   if (count < 0 || count > 160) return RB_ERR_SHAPE;
   if (count == 0) return RB_OK;
   if (!descs) return RB_ERR_NULL;
@@ -309,11 +310,30 @@ int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int c
   }
   if (routed > 4) return RB_ERR_SHAPE;
   if (ws && !aligned16(ws)) return RB_ERR_ALIGN;
+  if (attn) {
+    const int64_t need = rb::attn_decode_workspace(attn->n_q_heads, attn->n_kv_heads, attn->head_dim);
+    if (need < 0 || attn->n_q_heads / attn->n_kv_heads > 4) return RB_ERR_SHAPE;
+    if (attn->cache_len < 1 || attn->cache_len > (int64_t(1) << 31) || !(attn->scale == attn->scale))
+      return RB_ERR_SHAPE;
+    if (!attn->q || !attn->k_cache || !attn->v_cache || !attn->pos || !attn->out || !attn->ws) return RB_ERR_NULL;
+    if (!aligned16(attn->q) || !aligned16(attn->k_cache) || !aligned16(attn->v_cache) || !aligned16(attn->out) ||
+        !aligned16(attn->ws))
+      return RB_ERR_ALIGN;
+    if (attn->ws_bytes < need) return RB_ERR_SHAPE;
+    if (flags & RB_FLAG_KERNEL_TC) return RB_ERR_SHAPE;  // fused attention runs on the warp-MMA kernel
+    bool any = false;
+    for (int i = 0; i < count; ++i) {
+      if (descs[i].x != attn->out) continue;
+      any = true;
+      if (descs[i].K != static_cast<int64_t>(attn->n_q_heads) * attn->head_dim) return RB_ERR_SHAPE;
+    }
+    if (!any) return RB_ERR_SHAPE;
+  }
   int sms = 0, st = device_sms(&sms);
   if (st != RB_OK) return st;
-  if (small_list(descs, count, flags))
+  if (attn || small_list(descs, count, flags))
     st = rb::launch_gemv_int4_multi(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream), epis,
-                                    ln);
+                                    ln, attn);
   else
     st = rb::launch_gemv_int4_tc(descs, count, x_dtype, y_dtype, flags, sms, static_cast<cudaStream_t>(stream), epis,
                                  ln, ws, ws_bytes);

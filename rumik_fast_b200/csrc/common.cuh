@@ -28,6 +28,7 @@ enum : unsigned int {
   ERR_TC_WAIT = 1u << 7,      // tensor-core multi-GEMV timed out on an mbarrier
   ERR_TP_WAIT = 1u << 8,      // tensor-parallel reduction timed out waiting for a peer's flag
   ERR_ARG = 1u << 9,          // a device-side argument (a decode position) was out of range; nothing stored
+  ERR_ATT_WAIT = 1u << 10,    // a fused-attention launch timed out waiting for the attention outputs
 };
 
 // Upper bound on the wall time of one mbarrier wait. Healthy waits here last microseconds (at most the

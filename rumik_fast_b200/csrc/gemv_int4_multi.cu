@@ -17,6 +17,7 @@
 //    lead over the oldest unreleased tile, so a waiting warp can never see a stale phase.
 #include "common.cuh"
 #include "glue.cuh"
+#include "attn.cuh"
 #include "kernels.h"
 
 namespace rb {
@@ -78,6 +79,7 @@ struct Slot {
   const int64_t* tok;
   int64_t vocab;
   int emb_f16;
+  int att;  // the vector is the attention output computed inside the launch (staged once it is complete)
 };
 
 // Per-entry data kept in shared memory for the whole launch (per-tile lookups must not go to the
@@ -113,6 +115,11 @@ struct MultiParams {
   Slot slots[kMaxSlots];
   Entry e[kMaxEntries];
   EpiP epis[4];
+  // decode attention fused into the launch (rb_attn_src): CTAs < att_ctas compute key-value head
+  // cta / att.nsplit, split cta % att.nsplit with consumer warps 0-3; entries from att_entry on read its output
+  attn::AttnParams att;
+  int att_on, att_ctas, att_rep, att_entry, att_nkv;
+  uint32_t att_off;
 };
 
 // A tile of TR rows (16, or 8 when the largest K needs smaller tiles) arrives as two contiguous copies of
@@ -262,9 +269,11 @@ __device__ __forceinline__ void table_chunk(const __half (&h)[8], bool valid, in
   if (valid && (it & 15) == 0) cst[it >> 4] = make_float4(-off, sum, 0.f, 0.f);
 }
 
-__device__ void stage_all_x(const MultiParams& p, uint8_t* smem, int tid) {
+// Tabulate the slots' activations: att_phase 0 every slot except the fused attention's output, 1 only that one.
+__device__ void stage_all_x(const MultiParams& p, uint8_t* smem, int tid, int att_phase) {
   for (int sl = 0; sl < p.nslots; ++sl) {
     const Slot& S = p.slots[sl];
+    if (S.att != att_phase) continue;
     const int items = S.G * 16;
     uint8_t* xs = smem + S.tab_off;
     float4* cst = reinterpret_cast<float4*>(smem + S.cst_off);
@@ -394,7 +403,7 @@ __host__ __device__ __forceinline__ uint32_t div_magic(uint32_t d) {
   return d <= 1 ? 0u : static_cast<uint32_t>((0xFFFFFFFFull + d) / d);
 }
 
-template <int TR>
+template <int TR, bool kAtt>  // kAtt: the launch computes the fused decode attention (rb_attn_src)
 __global__ void __maxnreg__(kMaxRegs) gemv_int4_multi_kernel(const __grid_constant__ MultiParams p) {
   constexpr int ST = TR / 8, H = TR / 2;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -476,8 +485,30 @@ __global__ void __maxnreg__(kMaxRegs) gemv_int4_multi_kernel(const __grid_consta
     }
   }
   griddep_wait();
-  stage_all_x(p, smem, tid);
+  stage_all_x(p, smem, tid, 0);
   named_bar_sync(1, kConsumerWarps * 32);
+  if (kAtt && warp < attn::kWarps && cta < p.att_ctas) {
+    // the fused decode attention: this CTA's (key-value head, split) with warps 0-3, while warps 4.. start
+    // streaming the entries that do not need it
+    float* sa = reinterpret_cast<float*>(smem + p.att_off);
+    int* last = reinterpret_cast<int*>(sa + attn::kWarps * 4 * (2 + attn::kHd));
+    const int g = cta / p.att.nsplit, sp = cta - g * p.att.nsplit;
+    switch (p.att_rep) {
+#define RB_ATT_CASE(R)                                                                                          \
+  case R:                                                                                                       \
+    attn::attn_cta<R, true>(p.att, g, sp, tid, 3, reinterpret_cast<float(*)[R]>(sa),                            \
+                            reinterpret_cast<float(*)[R]>(sa + attn::kWarps * R),                               \
+                            reinterpret_cast<float(*)[R][attn::kHd]>(sa + 2 * attn::kWarps * R), last);         \
+    break;
+      RB_ATT_CASE(1)
+      RB_ATT_CASE(2)
+      RB_ATT_CASE(3)
+      RB_ATT_CASE(4)
+#undef RB_ATT_CASE
+      default:
+        break;
+    }
+  }
 
   const int r = lane >> 2, qd = lane & 3;
   const int prow0 = (r & 1) * H + (r >> 1);  // tile row of this lane's MMA row in step 0 (step t: + 4t)
@@ -491,7 +522,49 @@ __global__ void __maxnreg__(kMaxRegs) gemv_int4_multi_kernel(const __grid_consta
   // CTA-local work items in order (tile by tile, item it = step * P + slice within a tile); warp w takes
   // items w, w + kConsumerWarps, ...; the entry of an item is found by scanning forward (items only grow)
   int e = -1, next_ib = 0;
-  for (int I = warp; I < total_items; I += kConsumerWarps) {
+  // items of the entries that read the fused attention's output come last: they start once every CTA has seen
+  // all key-value heads complete and has tabulated that output
+  const int n_pre = kAtt ? entc[p.att_entry].ib : total_items;
+  // in the CTAs that compute attention, warps 0-3 (the attention warps) leave the entries that do not need it
+  // to warps 4.. and go straight to the wait
+  const bool att_cta = kAtt && cta < p.att_ctas;
+  const int w0 = att_cta ? attn::kWarps : 0, nw0 = kConsumerWarps - w0;
+  int I = warp >= w0 ? warp - w0 : n_pre;
+  int stride = nw0;
+  for (int phase = 0; phase < 2; ++phase) {
+    if (phase == 1) {
+      if (!kAtt) break;
+      if (tid == 0) {
+        const int64_t pos = *p.att.pos;
+        if (pos >= 0 && pos < p.att.S) {  // otherwise no head completes (the attention reported ERR_ARG)
+          const unsigned long long t0 = globaltimer_ns();
+          unsigned int done = 0;
+          for (;;) {
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(done) : "l"(p.att.heads_done) : "memory");
+            if (done >= static_cast<unsigned int>(p.att_nkv)) break;
+            if (globaltimer_ns() - t0 > kMaxWaitNs) {
+              atomicOr(&g_device_error, ERR_ATT_WAIT);
+              break;
+            }
+            __nanosleep(64);
+          }
+        }
+        // the launch's last CTA past this point resets the counters for the next launch (which starts after
+        // this one has completed)
+        unsigned int* passed = p.att.heads_done + 1;
+        if (atomicAdd(passed, 1u) == gridDim.x - 1) {
+          *p.att.heads_done = 0u;
+          *passed = 0u;
+        }
+      }
+      named_bar_sync(1, kConsumerWarps * 32);
+      stage_all_x(p, smem, tid, 1);
+      named_bar_sync(1, kConsumerWarps * 32);
+      I = n_pre + warp;
+      stride = kConsumerWarps;
+    }
+    const int i_end = phase == 0 ? n_pre : total_items;
+  for (; I < i_end; I += stride) {
     while (I >= next_ib) {
       ++e;
       next_ib = entc[e + 1].ib;
@@ -565,14 +638,17 @@ __global__ void __maxnreg__(kMaxRegs) gemv_int4_multi_kernel(const __grid_consta
       }
     }
   }
+  }
 }
 
 }  // namespace g4m
 
 int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,
-                           cudaStream_t stream, const rb_gemv_epi* epi, const rb_add_ln* ln) {
+                           cudaStream_t stream, const rb_gemv_epi* epi, const rb_add_ln* ln, const rb_attn_src* attn) {
   using namespace g4m;
   constexpr uint32_t kSmemMax = 227 * 1024;
+  // shared memory of the fused attention's CTA merge: max, sum and 128 outputs per warp and head (rep <= 4)
+  const uint32_t att_bytes = attn ? attn::kWarps * 4 * (2 + attn::kHd) * 4 + 16 : 0u;
   // 16-row tiles halve the per-tile producer work; lists with a K too large for two 16-row tiles (plus
   // the activation tables) in shared memory use 8-row tiles
   int64_t kmax = 0;
@@ -613,13 +689,14 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
           slot = i;
       const uint32_t add_x = slot < 0 ? G * (256u + 16u) : 0u;
       if (slot < 0 && nslots == kMaxSlots) break;
-      if (x_bytes + add_x + kFixed + 2u * std::max(max_tile, tb) > kSmemMax) break;
+      if (x_bytes + add_x + kFixed + att_bytes + 2u * std::max(max_tile, tb) > kSmemMax) break;
       if (kind != RB_EPI_STORE && nepis == 4) break;
       if (slot < 0) {
         slot = nslots++;
         Slot& S = p.slots[slot];
         S = Slot{};
         S.x = from_ln ? ln->x : D.x;
+        S.att = attn && !from_ln && D.x == attn->out ? 1 : 0;
         if (from_ln) {
           S.ln = 1;
           S.a = ln->a;
@@ -671,10 +748,46 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
       max_tile = std::max(max_tile, tb);
     }
     if (take == 0) return RB_ERR_SHAPE;
-    if ((epi || ln) && take < count) return RB_ERR_SHAPE;  // the fused glue needs the whole list in one launch
+    if ((epi || ln || attn) && take < count) return RB_ERR_SHAPE;  // the fused glue needs one launch
     p.count = take;
     p.nslots = nslots;
     p.total_tiles = tiles;
+    p.att_on = 0;
+    p.att_ctas = p.att_rep = p.att_entry = p.att_nkv = 0;
+    if (attn) {
+      // entries reading the attention output must be the last ones (their items run after the wait)
+      int first = -1;
+      for (int i = 0; i < take; ++i) {
+        const bool a = p.slots[p.e[i].slot].att != 0;
+        if (a && first < 0) first = i;
+        if (!a && first >= 0) return RB_ERR_SHAPE;
+      }
+      const int grid = std::min(num_sms, std::max(1, tiles));
+      const int nkv = attn->n_kv_heads;
+      const int nsplit = std::min(static_cast<int>(attn::nsplit_for(nkv, num_sms)), grid / nkv);
+      if (first < 0 || nsplit < 1) return RB_ERR_SHAPE;
+      attn::AttnParams& A = p.att;
+      uint8_t* w = static_cast<uint8_t*>(attn->ws);
+      A.q = attn->q;
+      A.kc = attn->k_cache;
+      A.vc = attn->v_cache;
+      A.pos = attn->pos;
+      A.out = attn->out;
+      A.ticket = reinterpret_cast<unsigned int*>(w);
+      A.heads_done = reinterpret_cast<unsigned int*>(w + attn::kHeadsDoneOff);  // the passed counter follows
+      A.po = reinterpret_cast<float*>(w + attn::kTicketBytes);
+      A.pm = A.po + static_cast<int64_t>(attn->n_q_heads) * nsplit * attn::kHd;
+      A.pl = A.pm + static_cast<int64_t>(attn->n_q_heads) * nsplit;
+      A.S = attn->cache_len;
+      A.scale = attn->scale;
+      A.nsplit = nsplit;
+      A.bf16 = x_dtype == RB_BF16;
+      p.att_on = 1;
+      p.att_ctas = nkv * nsplit;
+      p.att_rep = attn->n_q_heads / nkv;
+      p.att_entry = first;
+      p.att_nkv = nkv;
+    }
     p.maxp = 1;
     for (int i = 0; i < take; ++i)
       p.maxp = std::max(p.maxp, std::min(kMaxP, (p.e[i].G + kSliceGroups - 1) / kSliceGroups));
@@ -691,6 +804,8 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
     p.ln_off = off;  // the prologue's group sums (2 x kLnMaxGroups floats)
     off += 2 * kLnMaxGroups * 4;
     off = (off + 15) & ~15u;
+    p.att_off = off;
+    off += att_bytes;
     p.ent_off = off;
     off += static_cast<uint32_t>(take) * sizeof(EntryP) + static_cast<uint32_t>(take + 1) * sizeof(EntryC);
     p.start_off = off;
@@ -705,7 +820,8 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
     p.ring_off = off;
     if (off + 2 * max_tile > kSmemMax) return RB_ERR_SHAPE;
     p.ring_bytes = kSmemMax - off;
-    void (*kern)(MultiParams) = TR == 16 ? gemv_int4_multi_kernel<16> : gemv_int4_multi_kernel<8>;
+    void (*kern)(MultiParams) = p.att_on ? (TR == 16 ? gemv_int4_multi_kernel<16, true> : gemv_int4_multi_kernel<8, true>)
+                                         : (TR == 16 ? gemv_int4_multi_kernel<16, false> : gemv_int4_multi_kernel<8, false>);
     cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemMax);
     if (e != cudaSuccess) return RB_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};

@@ -53,7 +53,8 @@ int launch_mm_int4_tc_static(MmArgs a, int num_sms, cudaStream_t stream);
 int launch_tp_allreduce(const __half* a, const __half* b, __half* out, int64_t n, void* const* bufs, int rank,
                         int world, uint32_t flag_off, uint32_t counter_off, int flags, cudaStream_t stream);
 int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,
-                           cudaStream_t stream, const rb_gemv_epi* epi = nullptr, const rb_add_ln* ln = nullptr);
+                           cudaStream_t stream, const rb_gemv_epi* epi = nullptr, const rb_add_ln* ln = nullptr,
+                           const rb_attn_src* attn = nullptr);
 // Decode attention (attn_decode.cu): workspace bytes (-1: unsupported shape) and the launch.
 int64_t attn_decode_workspace(int nq, int nkv, int hd);
 int launch_attn_decode(const void* q, const void* kc, const void* vc, const int64_t* pos, void* out, int nq, int nkv,

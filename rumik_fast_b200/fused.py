@@ -172,7 +172,53 @@ class AddLnGemvPost:
         L = _lib.lib()
         lnp = ctypes.byref(self._ln.c) if self._ln is not None else None
         with _on_device(self.device):
-            st = L.rb_gemv_int4_fused(self._descs, self._epis, 2, lnp, _ws_ptr(self.ws), _ws_len(self.ws),
+            st = L.rb_gemv_int4_fused(self._descs, self._epis, 2, lnp, None, _ws_ptr(self.ws), _ws_len(self.ws),
                                       _lib.dtype_code(self.x_dtype), _lib.dtype_code(self.y_dtype),
                                       config.flags() | self.kflags, _lib.stream_ptr(self.device))
+        _lib.check("rb_gemv_int4_fused", st)
+
+
+class AttnGemvSet:
+    """A decode layer's output side as ONE launch: the decode attention over the KV cache (as
+    attention.DecodeAttention) fused with the GEMVs that read its output (o_proj) and the ones that do not
+    (down_proj, whose input is ready at launch and streams while the attention runs).
+
+    entries  (x, q, s, m, y) as Int4GemvSet; entries whose x is `out` read the attention output, which the launch
+             also stores to `out` (they are run after the others)
+    q, k_cache, v_cache, pos, out, n_q_heads, n_kv_heads, scale: as DecodeAttention (1..4 query heads per
+             key-value head)
+    Runs on the warp-MMA GEMV kernel. Built once (graph-capture safe to call); every tensor must stay alive.
+    """
+
+    def __init__(self, entries, *, q, k_cache, v_cache, pos, out, n_q_heads, n_kv_heads, scale=None):
+        from .gemv_set import Int4GemvSet
+        reads = [e[0].data_ptr() == out.data_ptr() for e in entries]
+        _require(any(reads), "no entry reads the attention output")
+        ordered = [e for e, r in zip(entries, reads) if not r] + [e for e, r in zip(entries, reads) if r]
+        self.set = Int4GemvSet(ordered, kernel="mma")  # validation and descriptors
+        nkv, S, hd = k_cache.shape
+        _require(nkv == n_kv_heads and tuple(v_cache.shape) == (nkv, S, hd), "caches must be [n_kv_heads, S, 128]")
+        _require(n_q_heads % n_kv_heads == 0 and 1 <= n_q_heads // n_kv_heads <= 4,
+                 "fused attention takes 1..4 query heads per key-value head")
+        for t, nm in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache"), (out, "out")):
+            _require(t.is_cuda and t.dtype == self.set.x_dtype and t.is_contiguous(),
+                     f"{nm} must be a contiguous {self.set.x_dtype} CUDA tensor")
+        _require(q.numel() == n_q_heads * hd and out.numel() == n_q_heads * hd, "q/out must be [n_q_heads * hd]")
+        _require(pos.dtype == torch.int64 and pos.device == q.device, "pos must be an int64 tensor on the device")
+        need = _lib.lib().rb_attn_decode_workspace(n_q_heads, n_kv_heads, hd)
+        _require(need > 0, f"unsupported heads {n_q_heads}/{n_kv_heads} x {hd}")
+        self.ws = torch.zeros(need, dtype=torch.uint8, device=q.device)
+        scale = float(hd ** -0.5 if scale is None else scale)
+        self.src = _lib.AttnSrc(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), pos.data_ptr(), out.data_ptr(),
+                                n_q_heads, n_kv_heads, hd, S, scale, self.ws.data_ptr(), need)
+        self._keep = (q, k_cache, v_cache, pos, out)
+        self.device = q.device
+        self.bytes = self.set.bytes
+
+    def __call__(self):
+        s = self.set
+        with _on_device(self.device):
+            st = _lib.lib().rb_gemv_int4_fused(s._descs, None, len(s.entries), None, ctypes.byref(self.src), None, 0,
+                                               _lib.dtype_code(s.x_dtype), _lib.dtype_code(s.y_dtype),
+                                               config.flags() | _lib.FLAG_KERNEL_MMA, _lib.stream_ptr(self.device))
         _lib.check("rb_gemv_int4_fused", st)

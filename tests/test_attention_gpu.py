@@ -101,3 +101,85 @@ def test_position_outside_the_cache_writes_nothing():
         DecodeAttention(q, kc, vc, pos, out, nq, nkv)()
         assert rb.device_error() & _lib.DEVERR_ARG
         assert torch.count_nonzero(out) == 0
+
+
+def output_side(nq, nkv, S, dt, seed, inter=1024, H=3072):
+    """Attention inputs plus an o_proj [H, nq * 128] and a down_proj [H, inter] with its input vector."""
+    from rumik_fast_b200 import synthetic as syn
+    q, kc, vc = setup(nq, nkv, S, dt, seed=seed)
+    g = syn.generator(seed + 100, "cpu")
+    wo = syn.int4_weights(H, nq * 128, g, "cpu")
+    wd = syn.int4_weights(H, inter, g, "cpu")
+    act = syn.activations((inter,), g, "cpu", dtype=dt)
+    return q, kc, vc, wo, wd, act
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("nq,nkv", [(24, 8), (16, 4), (8, 8)])
+def test_attention_fused_into_the_output_gemvs(dt, nq, nkv):
+    """AttnGemvSet: the attention computed inside the o_proj/down_proj launch (warp-MMA kernel) matches the
+    oracle, o_proj multiplies exactly what it computed, down_proj is unaffected, the counters return to zero
+    and repeated calls give the same bits."""
+    from rumik_fast_b200 import fused
+    from tests.helpers import int4_ref
+    S, H = 2048, 3072
+    q, kc, vc, wo, wd, act = output_side(nq, nkv, S, dt, seed=nq + 7 * nkv)
+    qd, kd, vd, actd = q.to(DEV), kc.to(DEV), vc.to(DEV), act.to(DEV)
+    wod, wdd = tuple(t.to(DEV) for t in wo), tuple(t.to(DEV) for t in wd)
+    pos = torch.zeros(1, dtype=torch.int64, device=DEV)
+    ob = torch.full((nq * 128,), float("nan"), device=DEV, dtype=dt)
+    bo = torch.empty(H, device=DEV, dtype=dt)
+    bd = torch.empty(H, device=DEV, dtype=dt)
+    layer = fused.AttnGemvSet([(ob, *wod, bo), (actd, *wdd, bd)], q=qd, k_cache=kd, v_cache=vd, pos=pos, out=ob,
+                              n_q_heads=nq, n_kv_heads=nkv)
+    for p in (0, 40, 511, S - 1):
+        pos.fill_(p)
+        layer()
+        torch.cuda.synchronize()
+        assert_close(ob, oracle(q, kc, vc, p, nq, nkv), f"fused attention at position {p}")
+        assert_close(bo, int4_ref(ob.cpu(), *wo), f"o_proj of the fused attention at {p}")
+        assert_close(bd, int4_ref(act, *wd), f"down_proj beside the attention at {p}")
+        assert torch.count_nonzero(layer.ws[:512]) == 0
+        first = (ob.clone(), bo.clone(), bd.clone())
+        layer()
+        torch.cuda.synchronize()
+        assert torch.equal(ob, first[0]) and torch.equal(bo, first[1]) and torch.equal(bd, first[2])
+
+
+def test_fused_attention_in_a_cuda_graph_and_out_of_range():
+    from rumik_fast_b200 import fused
+    from tests.helpers import int4_ref
+    dt, nq, nkv, S, H = torch.float16, 16, 4, 256, 3072
+    q, kc, vc, wo, wd, act = output_side(nq, nkv, S, dt, seed=9)
+    qd, kd, vd, actd = q.to(DEV), kc.to(DEV), vc.to(DEV), act.to(DEV)
+    wod, wdd = tuple(t.to(DEV) for t in wo), tuple(t.to(DEV) for t in wd)
+    pos = torch.zeros(1, dtype=torch.int64, device=DEV)
+    ob = torch.empty(nq * 128, device=DEV, dtype=dt)
+    bo = torch.empty(H, device=DEV, dtype=dt)
+    bd = torch.empty(H, device=DEV, dtype=dt)
+    outs = torch.empty(3, H, device=DEV, dtype=dt)
+    idx = torch.zeros(1, dtype=torch.int64, device=DEV)
+    layer = fused.AttnGemvSet([(actd, *wdd, bd), (ob, *wod, bo)], q=qd, k_cache=kd, v_cache=vd, pos=pos, out=ob,
+                              n_q_heads=nq, n_kv_heads=nkv)
+    layer()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layer()
+        outs.index_copy_(0, idx, bo.view(1, -1))
+        pos.add_(50)
+        idx.add_(1)
+    pos.fill_(3)
+    idx.zero_()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    for i in range(3):
+        o_ref = oracle(q, kc, vc, 3 + 50 * i, nq, nkv)
+        assert_close(outs[i], int4_ref(torch.from_numpy(o_ref).to(dt), *wo), f"graph replay {i}")
+    # a position outside the cache: the attention writes nothing and the launch does not wait for it
+    pos.fill_(S)
+    layer()
+    torch.cuda.synchronize()
+    assert rb.device_error() & _lib.DEVERR_ARG
+    assert torch.count_nonzero(layer.ws[:512]) == 0

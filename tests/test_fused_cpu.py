@@ -31,7 +31,7 @@ def call(L, descs, epis=None, ln=None, xd=_lib.F16, yd=_lib.F16, count=None, ws=
     d = (_lib.GemvDesc * max(n, 1))(*descs)
     e = (_lib.GemvEpi * max(n, 1))(*epis) if epis is not None else None
     return L.rb_gemv_int4_fused(d, e, n if count is None else count, ctypes.byref(ln) if ln is not None else None,
-                                ws, ws_bytes, xd, yd, 0, None)
+                                None, ws, ws_bytes, xd, yd, 0, None)
 
 
 def add_ln(x=0x50000, a=0x60000, b=0x70000, w=0x80000, x_out=0x90000, h_out=None, H=256, eps=1e-5):

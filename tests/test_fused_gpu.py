@@ -69,7 +69,7 @@ def run_fused(entries, epis=None, ln=None, x_dtype=torch.float16, y_dtype=torch.
     d = (_lib.GemvDesc * len(entries))(*entries)
     e = (_lib.GemvEpi * len(entries))(*epis) if epis else None
     ws = workspace(d, len(entries), torch.device(DEV), kf)
-    st = _lib.lib().rb_gemv_int4_fused(d, e, len(entries), ctypes.byref(ln.c) if ln else None, _ws_ptr(ws),
+    st = _lib.lib().rb_gemv_int4_fused(d, e, len(entries), ctypes.byref(ln.c) if ln else None, None, _ws_ptr(ws),
                                        _ws_len(ws), _lib.dtype_code(x_dtype), _lib.dtype_code(y_dtype),
                                        rb.config.flags() | kf, _lib.stream_ptr(torch.device(DEV)))
     _lib.check("rb_gemv_int4_fused", st)
