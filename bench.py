@@ -22,6 +22,7 @@ import subprocess
 import sys
 import threading
 import time
+import types
 
 import numpy as np
 import torch
@@ -573,6 +574,19 @@ def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
         xin = xout
     final = fused.AddLn(xin, buf_o, buf_d, lnw[nlayers], None, eps=c["eps"], h_out=hn)
     head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
+    # the sampling tail (engine/sample.py): stop predictor (LayerNorm, 512 x H bf16, GELU, 1 x 512), top-30,
+    # Gumbel-max with in-graph uniforms; the sampled head row's id (< vocab) is the next step's token
+    from rumik_fast_b200.sample import FusedSampler
+    nz = 512
+    eng = types.SimpleNamespace(
+        hn=hn, H=H, dev=dev, audio_ids=torch.arange(syn.HEAD_SHAPE[0], device=dev, dtype=torch.int64),
+        end_id=syn.HEAD_SHAPE[0] - 1, step_i=torch.zeros(1, dtype=torch.int64, device=dev), tok=tok,
+        out=torch.zeros(4096, dtype=torch.int64, device=dev), temperature=0.8, top_k=30, min_new=8,
+        stop={"0.weight": torch.ones(H, device=dev), "0.bias": torch.zeros(H, device=dev),
+              "1.weight": (0.02 * torch.randn(nz, H, generator=gen, device=dev)).to(torch.bfloat16),
+              "1.bias": torch.zeros(nz, device=dev), "3.weight": 0.05 * torch.randn(1, nz, generator=gen, device=dev),
+              "3.bias": torch.full((1,), -100.0, device=dev)})  # never stops: every step draws a token
+    sampler = FusedSampler(eng, lambda: logits)
 
     def step():
         for L in range(nlayers):
@@ -582,12 +596,14 @@ def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
             layer_out[L]()
         fused.add_layernorm(final)
         rb.gemv_int8_cuda(hn, *head, out=logits)
+        sampler()
 
     shapes = [((nq + 2 * nkv) * hd, H), (2 * inter, H), (H, nq * hd), (H, inter)]
-    wbytes = nlayers * sum(syn.int4_bytes(n, k) for n, k in shapes) + syn.int8_bytes(*syn.HEAD_SHAPE)
+    wbytes = nlayers * sum(syn.int4_bytes(n, k) for n, k in shapes) + syn.int8_bytes(*syn.HEAD_SHAPE) + nz * H * 2
     kvbytes = nlayers * (2 * nkv * (pos + 1) * hd * 2 + 2 * nq * hd * 2)
     return dict(step=step, tok=tok, logits=logits, wbytes=wbytes + H, kvbytes=kvbytes,
-                launches=(2 if attn_mode == "fused" else 3) * nlayers + 2, keep=(layer_in, attn, layer_out, final, head, kc, vc, emb_q, emb_s))
+                launches=(2 if attn_mode == "fused" else 3) * nlayers + 4,
+                keep=(layer_in, attn, layer_out, final, head, kc, vc, emb_q, emb_s, sampler, eng))
 
 
 def run_step(a):
@@ -611,12 +627,12 @@ def run_step(a):
         m1 = clk.mark()
     ms_step = ms / a.steps
     hx = w["tok"].cpu().pin_memory()
-    hy = torch.empty(w["logits"].shape, dtype=torch.float16).pin_memory()
+    hy = torch.empty(1, dtype=torch.int64).pin_memory()
 
-    def e2e_step():
+    def e2e_step():  # token id in, next token id out
         w["tok"].copy_(hx, non_blocking=True)
         g.replay()
-        hy.copy_(w["logits"], non_blocking=True)
+        hy.copy_(w["tok"], non_blocking=True)
     e2e_steps = max(1, a.steps // 2)
     ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
     if rank == 0:
@@ -633,13 +649,14 @@ def run_step(a):
                                    "5120x3072 + gate_up 16384x3072 + rope/KV write/silu*up (one launch), attention "
                                    "24/8 heads x 128 with o_proj 3072x3072 + down 3072x8192 ("
                                    + ("one launch" if a.attn == "fused" else "two launches") +
-                                   "); final add_ln + int8 head 16385x3072; one CUDA graph",
+                                   "); final add_ln + int8 head 16385x3072; sampler (stop predictor, top-30, "
+                                   "Gumbel-max; the drawn token feeds the next step); one CUDA graph",
                        "pos": a.pos, "bytes_per_step": total, "weight_bytes": w["wbytes"], "kv_bytes": w["kvbytes"],
                        "parallelism": f"replica x{world}", "weight_prefetch": not a.no_prefetch,
                        "l2": "no flush: 2.0 GB of weights per step > 126 MB L2"},
             "hbm_gbs": round(gbs, 1),
             "e2e": {"value": round(world * 1e3 / ms_e2e, 1), "unit": "tok/s",
-                    "h2d_bytes_per_step": hx.numel() * 8, "d2h_bytes_per_step": hy.numel() * 2,
+                    "h2d_bytes_per_step": hx.numel() * 8, "d2h_bytes_per_step": hy.numel() * 8,
                     "ms_per_step": round(ms_e2e, 5)},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_kind": kind, "kernel": "whole decode step",

@@ -281,6 +281,51 @@ int rb_add_layernorm(const rb_add_ln* ln, int dtype, int flags, void* stream);
  *   completion counters) must be zero before the first call and are zero again after each call. Calls that
  *   share a workspace must not overlap in time (one stream).
  */
+/*
+ * The sampling tail of a decode step (rumik-fast engine/sample.py, the same maths as
+ * engine/rumik_int4.py:174-198): the stop predictor, top-k over the audio head's logits, a Gumbel-max draw and the
+ * device-side counters, in two launches:
+ *   stop  = W2 . gelu(W1 . LayerNorm(h; ln_w, ln_b, eps 1e-5) + b1) + b2 > 0    (counted once *step >= min_new)
+ *   token = ids[argmax_{j < top_k}(top_j * inv_temp - log(-log(clamp(u_j, 1e-10, 1))))]
+ * where top_j is the j-th largest logit (ties: the higher row first) with row end_idx masked to -inf while
+ * *step < min_new; then out[*step] = token (if *step < out_len), *tok = token, *step += 1. The first of equal
+ * scores wins. u: top_k uniforms drawn by the caller (the reference draws them with torch.rand).
+ * logits [n_vocab] (RB_F16 / RB_BF16 / RB_F32), n_vocab <= 32768, 1 <= top_k <= 32; h [H] (H <= 8192);
+ * w1 [nz, H] (any of the three dtypes, 16-byte aligned); ln_w, ln_b [H], b1, w2 [nz], b2 [1] fp32;
+ * ws: rb_sample_workspace(nz) bytes of device scratch, 16-byte aligned.
+ */
+typedef struct rb_sampler {
+  const void* logits;
+  int logits_dtype;
+  int64_t n_vocab;
+  int64_t end_idx;
+  const int64_t* ids;
+  int top_k;
+  float inv_temp;
+  const float* u;
+  const void* h;
+  int h_dtype;
+  int64_t H;
+  const float* ln_w;
+  const float* ln_b;
+  const void* w1;
+  int w1_dtype;
+  int nz;
+  const float* b1;
+  const float* w2;
+  const float* b2;
+  int64_t end_id;
+  int64_t min_new;
+  int64_t* step;
+  int64_t* tok;
+  int64_t* out;
+  int64_t out_len;
+  void* ws;
+} rb_sampler;
+
+int64_t rb_sample_workspace(int nz);
+int rb_sample(const rb_sampler* s, int flags, void* stream);
+
 int64_t rb_attn_decode_workspace(int n_q_heads, int n_kv_heads, int head_dim);
 int rb_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
                    int n_q_heads, int n_kv_heads, int head_dim, int64_t cache_len, float scale, void* ws,

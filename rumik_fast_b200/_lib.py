@@ -49,6 +49,15 @@ class AttnSrc(ctypes.Structure):
                 ("ws_bytes", _i64)]
 
 
+class Sampler(ctypes.Structure):
+    """struct rb_sampler (include/rumik_b200.h)."""
+    _fields_ = [("logits", _vp), ("logits_dtype", _int), ("n_vocab", _i64), ("end_idx", _i64), ("ids", _vp),
+                ("top_k", _int), ("inv_temp", _c.c_float), ("u", _vp), ("h", _vp), ("h_dtype", _int), ("H", _i64),
+                ("ln_w", _vp), ("ln_b", _vp), ("w1", _vp), ("w1_dtype", _int), ("nz", _int), ("b1", _vp),
+                ("w2", _vp), ("b2", _vp), ("end_id", _i64), ("min_new", _i64), ("step", _vp), ("tok", _vp),
+                ("out", _vp), ("out_len", _i64), ("ws", _vp)]
+
+
 EPI_STORE, EPI_ROPE_KV, EPI_SWIGLU = 0, 1, 2
 DEVERR_ARG = 1 << 9
 
@@ -66,6 +75,8 @@ SIGNATURES = {
     "rb_gemv_int4_multi_ws": (_int, [_c.POINTER(GemvDesc), _int, _vp, _i64, _int, _int, _int, _vp]),
     "rb_add_layernorm": (_int, [_c.POINTER(AddLn), _int, _int, _vp]),
     "rb_attn_decode_workspace": (_i64, [_int, _int, _int]),
+    "rb_sample": (_int, [_c.POINTER(Sampler), _int, _vp]),
+    "rb_sample_workspace": (_i64, [_int]),
     "rb_attn_decode": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _int, _i64, _c.c_float, _vp, _i64, _int, _int,
                               _vp]),
     "rb_status_string": (_c.c_char_p, [_int]),

@@ -245,6 +245,27 @@ int rb_add_layernorm(const rb_add_ln* ln, int dtype, int flags, void* stream) {
   return st;
 }
 
+int64_t rb_sample_workspace(int nz) { return nz < 1 ? -RB_ERR_SHAPE : rb::sample_workspace(nz); }
+
+int rb_sample(const rb_sampler* s, int flags, void* stream) {
+  if (!s) return RB_ERR_NULL;
+  if (s->n_vocab < 1 || s->n_vocab > 32768 || s->top_k < 1 || s->top_k > 32 || s->top_k > s->n_vocab)
+    return RB_ERR_SHAPE;
+  if (s->H < 1 || s->H > 8192 || s->nz < 1 || s->out_len < 0 || !(s->inv_temp == s->inv_temp)) return RB_ERR_SHAPE;
+  if (!s->logits || !s->ids || !s->u || !s->h || !s->ln_w || !s->ln_b || !s->w1 || !s->b1 || !s->w2 || !s->b2 ||
+      !s->step || !s->tok || !s->ws || (s->out_len > 0 && !s->out))
+    return RB_ERR_NULL;
+  if (!aligned16(s->w1) || !aligned16(s->ws)) return RB_ERR_ALIGN;
+  const int dts[3] = {s->logits_dtype, s->h_dtype, s->w1_dtype};
+  for (int d : dts)
+    if (d != RB_F16 && d != RB_BF16 && d != RB_F32) return RB_ERR_DTYPE;
+  int sms = 0, st = device_sms(&sms);
+  if (st != RB_OK) return st;
+  st = rb::launch_sample(s, flags, static_cast<cudaStream_t>(stream));
+  if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+  return st;
+}
+
 int64_t rb_attn_decode_workspace(int n_q_heads, int n_kv_heads, int head_dim) {
   return rb::attn_decode_workspace(n_q_heads, n_kv_heads, head_dim);
 }

@@ -55,6 +55,9 @@ int launch_tp_allreduce(const __half* a, const __half* b, __half* out, int64_t n
 int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_dtype, int flags, int num_sms,
                            cudaStream_t stream, const rb_gemv_epi* epi = nullptr, const rb_add_ln* ln = nullptr,
                            const rb_attn_src* attn = nullptr);
+// The sampling tail (sample.cu): stop predictor, top-k, Gumbel-max pick, counters.
+int launch_sample(const rb_sampler* s, int flags, cudaStream_t stream);
+int64_t sample_workspace(int nz);
 // Decode attention (attn_decode.cu): workspace bytes (-1: unsupported shape) and the launch.
 int64_t attn_decode_workspace(int nq, int nkv, int hd);
 int launch_attn_decode(const void* q, const void* kc, const void* vc, const int64_t* pos, void* out, int nq, int nkv,

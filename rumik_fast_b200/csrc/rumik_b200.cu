@@ -10,3 +10,4 @@
 #include "mm_int4_tc.cu"
 #include "allreduce.cu"
 #include "attn_decode.cu"
+#include "sample.cu"

@@ -176,6 +176,34 @@ def make_glue(ref_root):
     o = refe.RumikInt4._attend(types.SimpleNamespace(hd=hd), q.view(nq, 1, hd), kc, vc, bias)[0]
     out.update({"attn_q": bits(q), "attn_k": bits(kc), "attn_v": bits(vc), "attn_o": bits(o),
                 "attn_meta": np.array([nq, nkv, hd, S, pos])})
+    # the sampling tail with the reference's eager _logits_and_stop / _pick (engine/rumik_int4.py:174-191) at the
+    # real head size; torch.rand inside _pick is reproduced by re-seeding
+    nv, hs, nz, top_k, temp, min_new = 16385, 256, 64, 30, 0.8, 8
+    ids = (1000 + 3 * torch.arange(nv)).to(torch.int64)
+    for case, (seed, step, b2) in enumerate(((50, 3, 5.0), (51, 20, -5.0), (52, 20, 5.0))):
+        g = torch.Generator().manual_seed(seed)
+        stop = {"0.weight": 1 + 0.1 * torch.randn(hs, generator=g), "0.bias": 0.1 * torch.randn(hs, generator=g),
+                "1.weight": (0.05 * torch.randn(nz, hs, generator=g)).to(torch.bfloat16),
+                "1.bias": 0.1 * torch.randn(nz, generator=g), "3.weight": 0.1 * torch.randn(1, nz, generator=g),
+                "3.bias": torch.tensor([b2])}
+        ns = types.SimpleNamespace(
+            head_w=(0.05 * torch.randn(nv, hs, generator=g)).to(torch.bfloat16),
+            hn=torch.randn(hs, generator=g).to(torch.bfloat16), stop=stop, H=hs, dev="cpu",
+            step_i=torch.tensor(step), min_new=min_new, is_end=ids == ids[-1], top_k=top_k, temperature=temp,
+            audio_ids=ids, end_id=int(ids[-1]))
+        logits, st = refe.RumikInt4._logits_and_stop(ns)
+        torch.manual_seed(1000 + case)
+        nxt = refe.RumikInt4._pick(ns, logits, st)
+        torch.manual_seed(1000 + case)
+        u = torch.rand(top_k)
+        out.update({f"smp{case}_logits": bits(logits.to(torch.bfloat16)), f"smp{case}_hn": bits(ns.hn),
+                    f"smp{case}_lnw": stop["0.weight"].numpy(), f"smp{case}_lnb": stop["0.bias"].numpy(),
+                    f"smp{case}_w1": bits(stop["1.weight"]), f"smp{case}_b1": stop["1.bias"].numpy(),
+                    f"smp{case}_w2": stop["3.weight"].reshape(-1).numpy(), f"smp{case}_b2": stop["3.bias"].numpy(),
+                    f"smp{case}_u": u.numpy(), f"smp{case}_stop": np.array(bool(st)),
+                    f"smp{case}_meta": np.array([step, min_new, top_k, nv - 1, int(ids[-1])]),
+                    f"smp{case}_next": np.array(int(nxt))})
+    out["smp_ids"] = ids.numpy()
     np.savez_compressed(os.path.join(HERE, "golden_glue.npz"), **out)
     print("golden_glue.npz", os.path.getsize(os.path.join(HERE, "golden_glue.npz")), "bytes")
 

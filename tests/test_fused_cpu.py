@@ -152,3 +152,27 @@ def test_embedding_prologue_argument_checks(native_lib):
     assert L.rb_add_layernorm(ctypes.byref(emb(emb_s_dtype=_lib.BF16)), _lib.F16, 0, None) == _lib.ERR_DTYPE
     assert L.rb_add_layernorm(ctypes.byref(emb(emb_q=0xA0008)), _lib.F16, 0, None) == _lib.ERR_ALIGN
     assert call(L, [desc(x=None)], ln=emb(tok=None)) == _lib.ERR_NULL
+
+
+def test_sampler_argument_checks(native_lib):
+    L = native_lib
+
+    def smp(**kw):
+        s = _lib.Sampler(A, _lib.F16, 16385, 16384, B, 30, 1.25, C, POS, _lib.BF16, 2048, A, B, C, _lib.BF16, 512,
+                         A, B, C, 50152, 8, 0x50000, 0x60000, 0x70000, 64, 0x80000)
+        for k, v in kw.items():
+            setattr(s, k, v)
+        return L.rb_sample(ctypes.byref(s), 0, None)
+
+    assert L.rb_sample(None, 0, None) == _lib.ERR_NULL
+    assert smp(n_vocab=0) == _lib.ERR_SHAPE
+    assert smp(n_vocab=32769) == _lib.ERR_SHAPE          # the pick CTA takes at most 32768 logits
+    assert smp(top_k=33) == _lib.ERR_SHAPE
+    assert smp(top_k=0) == _lib.ERR_SHAPE
+    assert smp(H=8193) == _lib.ERR_SHAPE
+    assert smp(inv_temp=float("nan")) == _lib.ERR_SHAPE
+    assert smp(u=None) == _lib.ERR_NULL
+    assert smp(step=None) == _lib.ERR_NULL
+    assert smp(out=None) == _lib.ERR_NULL                # out_len > 0 needs out
+    assert smp(logits_dtype=7) == _lib.ERR_DTYPE
+    assert smp(w1_dtype=9) == _lib.ERR_DTYPE

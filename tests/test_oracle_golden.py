@@ -162,3 +162,18 @@ def test_embed_ln_matches_reference(gg, dt):
         s, h = O.embed_ln_ref(int(tok), gg["emb_q"], gg["emb_s"], gg[f"{dt}_emb_w"], 1e-5, dt)
         assert np.array_equal(s, _stored(gg[f"{dt}_emb_x"][i], dt))     # one product, one rounding: exact
         assert O.ulp_diff(h, _stored(gg[f"{dt}_emb_h"][i], dt), dt).max() <= 1
+
+
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_sampling_tail_matches_reference(gg, case):
+    """The stop predictor and the top-k / Gumbel-max pick against the reference's own eager functions
+    (engine/rumik_int4.py:174-191) on the real head size, with the same uniforms."""
+    m = gg[f"smp{case}_meta"]
+    step, min_new, top_k, end_idx, end_id = (int(v) for v in m)
+    s = O.stop_logit_ref(gg[f"smp{case}_hn"], gg[f"smp{case}_lnw"], gg[f"smp{case}_lnb"],
+                         O.bf16_bits_to_f32(gg[f"smp{case}_w1"]), gg[f"smp{case}_b1"], gg[f"smp{case}_w2"],
+                         gg[f"smp{case}_b2"], "bf16")
+    assert (s > 0) == bool(gg[f"smp{case}_stop"])
+    logits = O.bf16_bits_to_f32(gg[f"smp{case}_logits"])
+    nxt = O.pick_ref(logits, step, min_new, end_idx, gg[f"smp{case}_u"], top_k, 1 / 0.8, gg["smp_ids"], s, end_id)
+    assert nxt == int(gg[f"smp{case}_next"])
