@@ -15,6 +15,10 @@
 //    product) over all groups of the row and write its 8 outputs directly;
 //  * full/empty mbarriers are per tile, reused modulo a window that is provably larger than any consumer's
 //    lead over the oldest unreleased tile, so a waiting warp can never see a stale phase.
+// Its per-launch cost is about half the tcgen05 multi-GEMV's (gemv_int4_tc.cu), so it runs the short lists: a
+// decode layer's projections with the glue of glue.cuh (the add + LayerNorm prologue, the rope / KV and SwiGLU
+// epilogues) and, optionally, the decode attention fused into the o_proj / down_proj launch (attn.cuh). The
+// tcgen05 kernel runs the long, HBM-bound lists.
 #include "common.cuh"
 #include "glue.cuh"
 #include "attn.cuh"
