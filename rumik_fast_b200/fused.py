@@ -63,34 +63,39 @@ class AddLn:
     (engine/fused.py:29-40). a and b may be None; h_out (optional) receives h. AddLn.from_embedding builds the
     layer-0 form (engine/fused.py:18-27): the residual is the token's int8 embedding row times its scale."""
 
+    def __init__(self, x, a, b, w, x_out, eps=1e-5, h_out=None):
+        _require(x is not None, "x is required (AddLn.from_embedding builds the embedding form)")
+        self._setup((x, a, b, w, x_out, h_out), eps)
+
     @classmethod
     def from_embedding(cls, emb_q, emb_s, tok, w, x_out, eps=1e-5, h_out=None):
         """emb_q int8 [vocab, H], emb_s [vocab] fp32/fp16, tok an int64 device tensor holding the token id."""
         _require(emb_q.dtype == torch.int8 and emb_q.dim() == 2 and emb_q.is_contiguous() and emb_q.is_cuda,
                  "emb_q must be a contiguous CUDA int8 [vocab, H] tensor")
-        _require(emb_s.dtype in (torch.float32, torch.float16) and emb_s.numel() == emb_q.shape[0],
-                 "emb_s must hold one fp32/fp16 scale per embedding row")
+        _require(emb_s.dtype in (torch.float32, torch.float16) and emb_s.numel() == emb_q.shape[0] and
+                 emb_s.device == emb_q.device, "emb_s must hold one fp32/fp16 scale per embedding row")
         _require(tok.dtype == torch.int64 and tok.device == emb_q.device, "tok must be an int64 device tensor")
-        self = cls(w, None, None, w, x_out, eps=eps, h_out=h_out)  # w stands in for x to check shapes
-        self.c.x = None
+        _require(emb_q.shape[1] == w.numel(), "embedding rows must have H = w.numel() elements")
+        self = cls.__new__(cls)
+        self._setup((None, None, None, w, x_out, h_out), eps)
         self.c.emb_q, self.c.emb_s, self.c.tok = emb_q.data_ptr(), emb_s.data_ptr(), tok.data_ptr()
         self.c.vocab = emb_q.shape[0]
         self.c.emb_s_dtype = _lib.dtype_code(emb_s.dtype)
-        self.tensors = (None, None, None, w, x_out, h_out)
         self.embedding = (emb_q, emb_s, tok)
         return self
 
-    def __init__(self, x, a, b, w, x_out, eps=1e-5, h_out=None):
-        H = x.numel()
-        for t, nm in ((x, "x"), (a, "a"), (b, "b"), (w, "w"), (x_out, "x_out"), (h_out, "h_out")):
+    def _setup(self, tensors, eps):
+        x, a, b, w, x_out, h_out = tensors
+        H, dt, dev = w.numel(), w.dtype, w.device
+        for t, nm in zip(tensors, ("x", "a", "b", "w", "x_out", "h_out")):
             if t is None:
                 continue
-            _require(t.is_cuda and t.device == x.device, f"{nm} must be on x's CUDA device")
-            _require(t.dtype == x.dtype and t.numel() == H and t.is_contiguous(),
-                     f"{nm} must be a contiguous [{H}] {x.dtype} vector")
+            _require(t.is_cuda and t.device == dev, f"{nm} must be on w's CUDA device")
+            _require(t.dtype == dt and t.numel() == H and t.is_contiguous(),
+                     f"{nm} must be a contiguous [{H}] {dt} vector")
         _require(H % G == 0 and H <= 12288, f"H={H} must be a multiple of {G} and <= 12288")
-        self.tensors = (x, a, b, w, x_out, h_out)
-        self.H, self.eps, self.dtype, self.device = H, float(eps), x.dtype, x.device
+        self.tensors = tensors
+        self.H, self.eps, self.dtype, self.device = H, float(eps), dt, dev
         ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
         self.c = _lib.AddLn(ptr(x), ptr(a), ptr(b), ptr(w), ptr(x_out), ptr(h_out), H, self.eps)
 
