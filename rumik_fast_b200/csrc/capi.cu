@@ -374,6 +374,9 @@ static int mm_int4_impl(const void* X, int x_dtype, int64_t ldx, const uint8_t* 
   if (!aligned16(X) || !aligned16(Y) || (ldx % 8) != 0 || (ldy % 8) != 0) return RB_ERR_ALIGN;
   if (!aligned16(q) || !aligned16(s) || !aligned16(m)) return RB_ERR_ALIGN;
   if (ws && !aligned16(ws)) return RB_ERR_ALIGN;
+  // one token is a GEMV: the GEMV kernels stream the weights faster than the prefill's per-item pipeline
+  // (measured: 1.33 against 2.06 ms for the 36-layer projection set)
+  if (M == 1 && K <= 16384) return rb_gemv_int4(X, x_dtype, K, q, s, m, Y, y_dtype, N, N, K, 1, flags, stream);
   int sms = 0, st = device_sms(&sms);
   if (st != RB_OK) return st;
   rb::MmArgs a = {};
