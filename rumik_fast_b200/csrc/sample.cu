@@ -184,12 +184,17 @@ __global__ void __launch_bounds__(32) pick_kernel(const __grid_constant__ Sample
   const int64_t step = *p.step;
   const bool early = step < p.min_new;
   const int nchunks = static_cast<int>((p.n_vocab + kChunk - 1) / kChunk);
+  // the chunk lists into shared memory first: independent, coalesced loads instead of one dependent load per round
+  __shared__ long long lists[kMaxChunks * kTop];
+#pragma unroll 8
+  for (int i = lane; i < nchunks * kTop; i += 32) lists[i] = __ldcg(p.keys + i);
+  __syncwarp();
   // lane l reads lists l and l + 32, best first; 32 rounds of "largest head"
   int ha = 0, hb = 0;
   long long mine = LLONG_MIN;  // lane j ends up holding the j-th best key
   for (int r = 0; r < kTop; ++r) {
-    const long long va = lane < nchunks && ha < kTop ? __ldcg(p.keys + lane * kTop + ha) : LLONG_MIN;
-    const long long vb = lane + 32 < nchunks && hb < kTop ? __ldcg(p.keys + (lane + 32) * kTop + hb) : LLONG_MIN;
+    const long long va = lane < nchunks && ha < kTop ? lists[lane * kTop + ha] : LLONG_MIN;
+    const long long vb = lane + 32 < nchunks && hb < kTop ? lists[(lane + 32) * kTop + hb] : LLONG_MIN;
     const long long v = va > vb ? va : vb;
     const long long best = warp_max_key(v);
     if (v == best && best != LLONG_MIN) {
