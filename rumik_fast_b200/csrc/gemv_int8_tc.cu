@@ -23,7 +23,7 @@ namespace g8t {
 constexpr int kRows = 128;
 constexpr int kThreads = 6 * 32;          // producer, MMA issuer, four epilogue warps (also stage x)
 constexpr uint32_t kStageBytes = kRows * 128;
-constexpr int kStages = 8;
+constexpr int kMaxStages = 12;  // ring depth: as many 16 KB stages as fit beside the activation table (K <= 8192: 12)
 constexpr uint32_t kXPad = 256;
 constexpr uint32_t kTmemCols = 32;        // two 8-column int32 accumulators
 
@@ -32,7 +32,7 @@ struct __align__(64) H8Params {
   const void* x;
   const void* s;
   void* y;
-  int N, K, nblocks, x_bf16, y_bf16, s_f16, q_signed, prefetch;
+  int N, K, nblocks, x_bf16, y_bf16, s_f16, q_signed, prefetch, nst;
   uint32_t xs_off, bar_off, idesc;
 };
 
@@ -52,16 +52,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int8_tc_kernel(const __grid_
   const int C = gridDim.x, cta = blockIdx.x;
   const int nlocal = (p.nblocks - cta + C - 1) / C;
   const int nk = p.K / 128;
+  const int nst = p.nst;  // ring depth of this launch
   uint8_t* xs = smem + p.xs_off;  // [K/16][32]: 16 high bytes, 16 low bytes per 16 columns; then reductions
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   uint64_t* full = bars;
-  uint64_t* empty = bars + kStages;
-  uint64_t* dready = bars + 2 * kStages;  // [2]
+  uint64_t* empty = bars + nst;
+  uint64_t* dready = bars + 2 * nst;  // [2]
   uint64_t* dfree = dready + 2;           // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfree + 2);
   float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [4] per-warp maxima, [4] per-warp integer sums
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < nst; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
@@ -91,8 +92,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int8_tc_kernel(const __grid_
       for (int j = 0; j < nlocal && ok; ++j) {
         const int row0 = (cta + j * C) * kRows;
         for (int k = 0; k < nk; ++k) {
-          const int slot = issued % kStages;
-          if (issued >= kStages && !mbar_wait(&empty[slot], ((issued / kStages) - 1) & 1, ERR_TC_WAIT)) {
+          const int slot = issued % nst;
+          if (issued >= nst && !mbar_wait(&empty[slot], ((issued / nst) - 1) & 1, ERR_TC_WAIT)) {
             ok = false;
             break;
           }
@@ -101,8 +102,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int8_tc_kernel(const __grid_
           ++issued;
         }
       }
-      for (int t = max(0, issued - kStages); t < issued; ++t)  // no retirement with copies in flight
-        if (!mbar_wait(&full[t % kStages], (t / kStages) & 1, ERR_TC_WAIT)) break;
+      for (int t = max(0, issued - nst); t < issued; ++t)  // no retirement with copies in flight
+        if (!mbar_wait(&full[t % nst], (t / nst) & 1, ERR_TC_WAIT)) break;
     }
   } else if (warp == 1) {
     named_bar_sync(1, 5 * 32);  // activation table staged
@@ -116,8 +117,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int8_tc_kernel(const __grid_
         if (j >= 2 && !mbar_wait(&dfree[b], ((j >> 1) - 1) & 1, ERR_TC_WAIT)) break;
         mm4::tc_fence_after();
         for (int k = 0; k < nk; ++k, ++used) {
-          const int slot = used % kStages;
-          if (!mbar_wait(&full[slot], (used / kStages) & 1, ERR_TC_WAIT)) {
+          const int slot = used % nst;
+          if (!mbar_wait(&full[slot], (used / nst) & 1, ERR_TC_WAIT)) {
             ok = false;
             break;
           }
@@ -243,11 +244,14 @@ int launch_gemv_int8_tc(const GemvArgs& a, int num_sms, cudaStream_t stream) {
   // instruction descriptor: D int32, A unsigned or signed 8-bit, B signed 8-bit, K-major, N = 8, M = 128
   p.idesc = (2u << 4) | ((p.q_signed ? 1u : 0u) << 7) | (1u << 10) | ((8u >> 3) << 17) |
             ((static_cast<uint32_t>(kRows) >> 4) << 24);
-  p.xs_off = kStages * kStageBytes;
-  const uint32_t xbytes = static_cast<uint32_t>(a.K / 16) * 32 + kXPad;
-  p.bar_off = (p.xs_off + xbytes + 15) & ~15u;
-  const uint32_t smem = 1024 + p.bar_off + (2 * kStages + 4) * 8 + 16 + 32;
   constexpr uint32_t kSmemMax = 227 * 1024;
+  const uint32_t xbytes = static_cast<uint32_t>(a.K / 16) * 32 + kXPad;
+  const uint32_t fixed = 1024 + xbytes + 16 + (2 * kMaxStages + 4) * 8 + 16 + 32;
+  p.nst = std::min(kMaxStages, static_cast<int>((kSmemMax - std::min(fixed, kSmemMax)) / kStageBytes));
+  if (p.nst < 2) return RB_ERR_SHAPE;
+  p.xs_off = static_cast<uint32_t>(p.nst) * kStageBytes;
+  p.bar_off = (p.xs_off + xbytes + 15) & ~15u;
+  const uint32_t smem = 1024 + p.bar_off + (2 * p.nst + 4) * 8 + 16 + 32;
   if (smem > kSmemMax) return RB_ERR_SHAPE;
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gemv_int8_tc_kernel), static_cast<int>(kSmemMax));
   if (e != cudaSuccess) return RB_ERR_LAUNCH;
