@@ -176,3 +176,30 @@ def test_sampler_argument_checks(native_lib):
     assert smp(out=None) == _lib.ERR_NULL                # out_len > 0 needs out
     assert smp(logits_dtype=7) == _lib.ERR_DTYPE
     assert smp(w1_dtype=9) == _lib.ERR_DTYPE
+
+
+def test_fused_attention_argument_checks(native_lib):
+    """rb_attn_src (attention inside the o_proj/down_proj launch) is validated before any CUDA call."""
+    L = native_lib
+    OUT = 0x90000
+    need = L.rb_attn_decode_workspace(8, 2, 128)
+
+    def run(descs, flags=0, **kw):
+        src = _lib.AttnSrc(A, B, C, POS, OUT, 8, 2, 128, 64, 0.088, 0xA0000, need)
+        for k, v in kw.items():
+            setattr(src, k, v)
+        d = (_lib.GemvDesc * len(descs))(*descs)
+        return L.rb_gemv_int4_fused(d, None, len(descs), None, ctypes.byref(src), None, 0, _lib.F16, _lib.F16,
+                                    flags, None)
+
+    o_proj = desc(x=OUT, N=256, K=8 * 128)
+    down = desc(x=A, N=256, K=256)
+    assert run([down]) == _lib.ERR_SHAPE                                   # no entry reads the attention output
+    assert run([down, desc(x=OUT, N=256, K=512)]) == _lib.ERR_SHAPE        # K != n_q_heads * head_dim
+    assert run([down, o_proj], n_q_heads=10, n_kv_heads=2) == _lib.ERR_SHAPE   # 5 query heads per key-value head
+    assert run([down, o_proj], q=None) == _lib.ERR_NULL
+    assert run([down, o_proj], ws=None) == _lib.ERR_NULL
+    assert run([down, o_proj], k_cache=0x30008) == _lib.ERR_ALIGN
+    assert run([down, o_proj], ws_bytes=need - 1) == _lib.ERR_SHAPE
+    assert run([down, o_proj], cache_len=0) == _lib.ERR_SHAPE
+    assert run([down, o_proj], flags=_lib.FLAG_KERNEL_TC) == _lib.ERR_SHAPE    # runs on the warp-MMA kernel only
