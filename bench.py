@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--attn", default="separate", choices=["fused", "separate"],
                     help="step workload: attention in its own launch (default, faster at the config shapes), or "
                          "inside the o_proj/down_proj launch")
+    ap.add_argument("--scales", default="fp16", choices=["fp16", "8bit"],
+                    help="decode workload: the reference's fp16 scales, or 8-bit double-quantised ones")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "step"],
                     help="decode: config 1 + 2 (the headline); prefill: config 3, the int4-weight matmul over the "
                          "36-layer projection set for --tokens prompt tokens")
@@ -132,16 +134,23 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------- workload
-def build_workload(dev, seed, nlayers=LAYERS):
+def build_workload(dev, seed, nlayers=LAYERS, scales="fp16"):
+    """scales "8bit": every projection's fp16 scale / min repacked as 8-bit double-quantised scales
+    (rumik_fast_b200.scales8), entries (q, Scales8, None)."""
     from rumik_fast_b200 import synthetic as syn
     gen = syn.generator(seed, dev)
     layers = [[syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES] for _ in range(nlayers)]
+    if scales == "8bit":
+        from rumik_fast_b200 import scales8
+        layers = [[(q, scales8.pack(s, m), None) for q, s, m in L] for L in layers]
     head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
     xh = syn.activations((3072,), gen, dev)
     xi = syn.activations((8192,), gen, dev)
     outs = [torch.empty(n, device=dev, dtype=torch.float16) for _, n, _ in syn.LAYER_SHAPES]
     logits = torch.empty(syn.HEAD_SHAPE[0], device=dev, dtype=torch.float16)
     int4_bytes = nlayers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES)
+    if scales == "8bit":  # 2 bytes per group instead of 4, plus a 4-byte factor per row
+        int4_bytes -= nlayers * sum(2 * n * (k // 128) - 4 * n for _, n, k in syn.LAYER_SHAPES)
     head_bytes = syn.int8_bytes(*syn.HEAD_SHAPE)
     return dict(layers=layers, head=head, xh=xh, xi=xi, outs=outs, logits=logits, int4_bytes=int4_bytes,
                 head_bytes=head_bytes)
@@ -363,7 +372,9 @@ def run_ours(a):
             dist.barrier()
             dist.destroy_process_group()
         return rc
-    w = build_workload(dev, seed=1234 + rank, nlayers=a.layers)
+    if a.scales == "8bit" and a.mode != "set":
+        raise SystemExit("--scales 8bit runs on the projection-set kernel (--mode set)")
+    w = build_workload(dev, seed=1234 + rank, nlayers=a.layers, scales=a.scales)
     step = step_fn(w, a.mode)
     g_step = capture(step)
     g_int4 = capture(step_fn(w, a.mode, with_head=False))
@@ -413,7 +424,9 @@ def run_ours(a):
                        else "145 stream-ordered launches",
                        "batch": 1, "bytes_per_step": step_bytes, "parallelism": f"replica x{world}",
                        "weight_prefetch": not a.no_prefetch,
-                       "l2": "no flush: 1.98 GB of weights per step > 126 MB L2"},
+                       "l2": "no flush: 1.98 GB of weights per step > 126 MB L2",
+                       "scales": "fp16 scale + min per group (the reference format)" if a.scales == "fp16" else
+                       "8-bit double-quantised scales (rumik_fast_b200.scales8): 2 bytes per group + 4 per row"},
             "tok_s": round(world * 1e3 / ms_step, 1),
             "pct_of_peak": round(100 * gbs / world / peak, 1),
             "e2e": {"value": round(world * step_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": UNIT,

@@ -131,9 +131,17 @@ typedef struct rb_gemv_desc {
   void* y;              /* output [N] (dtype y_dtype of the call) */
   const uint8_t* q;     /* codes [N, K/2] */
   const uint16_t* s;    /* fp16 scales [N, K/128] */
-  const uint16_t* m;    /* fp16 mins [N, K/128] */
+  const uint16_t* m;    /* fp16 mins [N, K/128]; unused (may be NULL) when s_row is set */
   int64_t N;            /* >= 1 */
   int64_t K;            /* multiple of 128, <= 16384 */
+  /* NULL: s and m are the reference's fp16 scales and mins. Set: 8-bit double-quantised scales - s holds one
+   * 16-bit word per group [N, K/128] (low byte b: scale code, high byte z: zero point in 1/16 steps) and s_row
+   * the fp32 per-row scale factors [N] (4-byte aligned). They decode to the fp16 scale and min of the fp16
+   * format: scale = fp16(2^((b >> 4) - 15) * (1 + (b & 15) / 16) * s_row[n]), min = fp16(-(z / 16) * scale)
+   * (rumik_fast_b200/scales8.py packs them). Such entries run on the tcgen05
+   * kernel only (with RB_FLAG_KERNEL_MMA or fused attention: RB_ERR_SHAPE). No reference counterpart: the
+   * byte saving rumik-fast names as its next step (engine/README.md:192-193). */
+  const float* s_row;
 } rb_gemv_desc;
 
 /*

@@ -26,7 +26,8 @@ _vp, _i64, _int = _c.c_void_p, _c.c_int64, _c.c_int
 
 class GemvDesc(ctypes.Structure):
     """struct rb_gemv_desc (include/rumik_b200.h)."""
-    _fields_ = [("x", _vp), ("y", _vp), ("q", _vp), ("s", _vp), ("m", _vp), ("N", _i64), ("K", _i64)]
+    _fields_ = [("x", _vp), ("y", _vp), ("q", _vp), ("s", _vp), ("m", _vp), ("N", _i64), ("K", _i64),
+                ("s_row", _vp)]
 
 class AddLn(ctypes.Structure):
     """struct rb_add_ln (include/rumik_b200.h)."""

@@ -114,14 +114,26 @@ int rb_gemv_int8(const void* x, int x_dtype, int64_t ldx, const uint8_t* q, int 
   return st;
 }
 
+// The min / per-row-factor pointer of a descriptor: fp16 mins 16-byte aligned, or (8-bit scales) fp32 factors
+// 4-byte aligned.
+static bool scales_aligned(const rb_gemv_desc& d) {
+  return d.s_row ? (reinterpret_cast<uintptr_t>(d.s_row) & 3u) == 0 : aligned16(d.m);
+}
+
+static bool any_scales8(const rb_gemv_desc* d, int count) {
+  for (int i = 0; i < count; ++i)
+    if (d[i].s_row) return true;
+  return false;
+}
+
 static int check_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_dtype) {
   if (!descs) return RB_ERR_NULL;
   if (!act_dtype_ok(x_dtype) || !act_dtype_ok(y_dtype)) return RB_ERR_DTYPE;
   for (int i = 0; i < count; ++i) {
     const rb_gemv_desc& d = descs[i];
     if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.K > 16384 || d.N > (int64_t(1) << 30)) return RB_ERR_SHAPE;
-    if (!d.x || !d.y || !d.q || !d.s || !d.m) return RB_ERR_NULL;
-    if (!aligned16(d.x) || !aligned16(d.q) || !aligned16(d.s) || !aligned16(d.m)) return RB_ERR_ALIGN;
+    if (!d.x || !d.y || !d.q || !d.s || (!d.m && !d.s_row)) return RB_ERR_NULL;
+    if (!aligned16(d.x) || !aligned16(d.q) || !aligned16(d.s) || !scales_aligned(d)) return RB_ERR_ALIGN;
   }
   return RB_OK;
 }
@@ -132,6 +144,11 @@ static int check_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_
 #ifndef RB_SMALL_LIST_BYTES
 #define RB_SMALL_LIST_BYTES (int64_t(128) << 20)
 #endif
+// A list with 8-bit scales cannot be forced onto the warp-MMA kernel, which has no decoder for them.
+static bool kernel_ok(const rb_gemv_desc* d, int count, int flags) {
+  return !((flags & RB_FLAG_KERNEL_MMA) && any_scales8(d, count));
+}
+
 static bool small_list(const rb_gemv_desc* d, int count, int flags) {
 #ifdef RB_MULTI_LEGACY  // comparison builds: every list on the warp-MMA kernel
   (void)d;
@@ -140,6 +157,7 @@ static bool small_list(const rb_gemv_desc* d, int count, int flags) {
   return true;
 #else
   if (flags & RB_FLAG_KERNEL_TC) return false;
+  if (any_scales8(d, count)) return false;  // 8-bit scales: the tcgen05 kernel only (kernel_ok refuses MMA)
   if (flags & RB_FLAG_KERNEL_MMA) return true;
   int64_t bytes = 0;
   for (int i = 0; i < count; ++i) bytes += d[i].N * (d[i].K / 2);
@@ -153,6 +171,7 @@ static int multi_impl(const rb_gemv_desc* descs, int count, void* ws, int64_t ws
   if (count == 0) return RB_OK;
   int st = check_multi(descs, count, x_dtype, y_dtype);
   if (st != RB_OK) return st;
+  if (!kernel_ok(descs, count, flags)) return RB_ERR_SHAPE;
   if (ws && !aligned16(ws)) return RB_ERR_ALIGN;
   int sms = 0;
   st = device_sms(&sms);
@@ -184,6 +203,7 @@ int64_t rb_gemv_int4_workspace(const rb_gemv_desc* descs, int count, int flags) 
     if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.K > 16384 || d.N > (int64_t(1) << 30)) return -RB_ERR_SHAPE;
     if (!d.q) return -RB_ERR_NULL;
   }
+  if (!kernel_ok(descs, count, flags)) return -RB_ERR_SHAPE;
   if (small_list(descs, count, flags)) return 0;  // the warp-MMA kernel splits K inside each CTA
   int sms = 0, st = device_sms(&sms);
   if (st != RB_OK) return -st;
@@ -305,10 +325,10 @@ int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int c
     const rb_gemv_desc& d = descs[i];
     const int kind = epis ? epis[i].kind : RB_EPI_STORE;
     if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.K > 16384 || d.N > (int64_t(1) << 30)) return RB_ERR_SHAPE;
-    if (!d.q || !d.s || !d.m) return RB_ERR_NULL;
+    if (!d.q || !d.s || (!d.m && !d.s_row)) return RB_ERR_NULL;
     if (!d.x && !ln) return RB_ERR_NULL;
     if (!d.x && d.K != ln->H) return RB_ERR_SHAPE;
-    if ((d.x && !aligned16(d.x)) || !aligned16(d.q) || !aligned16(d.s) || !aligned16(d.m)) return RB_ERR_ALIGN;
+    if ((d.x && !aligned16(d.x)) || !aligned16(d.q) || !aligned16(d.s) || !scales_aligned(d)) return RB_ERR_ALIGN;
     if (kind == RB_EPI_STORE) {
       if (!d.y) return RB_ERR_NULL;
       continue;
@@ -330,6 +350,7 @@ int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int c
     }
   }
   if (routed > 4) return RB_ERR_SHAPE;
+  if (!kernel_ok(descs, count, flags)) return RB_ERR_SHAPE;
   if (ws && !aligned16(ws)) return RB_ERR_ALIGN;
   if (attn) {
     const int64_t need = rb::attn_decode_workspace(attn->n_q_heads, attn->n_kv_heads, attn->head_dim);
@@ -342,6 +363,7 @@ int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int c
       return RB_ERR_ALIGN;
     if (attn->ws_bytes < need) return RB_ERR_SHAPE;
     if (flags & RB_FLAG_KERNEL_TC) return RB_ERR_SHAPE;  // fused attention runs on the warp-MMA kernel
+    if (any_scales8(descs, count)) return RB_ERR_SHAPE;  // which has no 8-bit scales
     bool any = false;
     for (int i = 0; i < count; ++i) {
       if (descs[i].x != attn->out) continue;

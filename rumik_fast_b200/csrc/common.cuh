@@ -298,6 +298,25 @@ __device__ __forceinline__ void load8_f32(const void* p, bool is_bf16, float (&v
 }
 
 // v rounded to the 16-bit activation type (nearest even), back in fp32: the value a bf16/fp16 buffer holds.
+// 8-bit double-quantised scales (rb_gemv_desc::s_row): a group's 16-bit word holds the scale code b (low byte)
+// and the zero point z in 1/16 steps (high byte). They decode to the fp16 scale and min of the reference format:
+// s = fp16(sc8(b) * s_row) with sc8(b) = 2^((b >> 4) - 15) * (1 + (b & 15) / 16), the fp32 whose bits are
+// (b << 19) + 0x38000000 (exact), and m = fp16(-(z / 16) * s), each rounded to nearest even once.
+// Two groups' words (low half first) -> their fp16 scales (s2) and mins (m2), packed the same way.
+__device__ __forceinline__ void dq_scales8_f16x2(uint32_t words, float s_row, uint32_t& s2, uint32_t& m2) {
+  uint32_t s_out = 0u, m_out = 0u;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t w = (words >> (16 * i)) & 0xFFFFu;
+    const __half s = __float2half_rn(__uint_as_float(((w & 0xFFu) << 19) + 0x38000000u) * s_row);
+    const __half m = __float2half_rn(-(static_cast<float>(w >> 8) * 0.0625f) * __half2float(s));
+    s_out |= static_cast<uint32_t>(__half_as_ushort(s)) << (16 * i);
+    m_out |= static_cast<uint32_t>(__half_as_ushort(m)) << (16 * i);
+  }
+  s2 = s_out;
+  m2 = m_out;
+}
+
 __device__ __forceinline__ float round_act(float v, bool is_bf16) {
   return is_bf16 ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
 }

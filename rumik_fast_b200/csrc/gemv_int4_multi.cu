@@ -656,7 +656,10 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
   // 16-row tiles halve the per-tile producer work; lists with a K too large for two 16-row tiles (plus
   // the activation tables) in shared memory use 8-row tiles
   int64_t kmax = 0;
-  for (int i = 0; i < count; ++i) kmax = std::max(kmax, d[i].K);
+  for (int i = 0; i < count; ++i) {
+    if (d[i].s_row) return RB_ERR_SHAPE;  // 8-bit double-quantised scales: the tcgen05 kernel only
+    kmax = std::max(kmax, d[i].K);
+  }
   const int TR = (2u * tile_bytes(16, static_cast<int>(kmax), static_cast<int>(kmax / 128)) +
                   static_cast<uint32_t>(kmax / 128) * 272u + 48u * 1024u <= kSmemMax) ? 16 : 8;
   int done = 0;

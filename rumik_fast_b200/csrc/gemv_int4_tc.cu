@@ -9,15 +9,17 @@
 //  * warp 0 (producer) streams each block's int4 codes two groups (128 columns x 2) at a time with 2-D TMA
 //    (box 128 bytes x 128 rows, 128-byte swizzle, 16 KB) into a ring per converter set;
 //  * each converter set (four warps, one per tensor-memory lane quadrant, thread = weight row) unpacks one
-//    group of its row to unsigned 8-bit codes (three instructions per eight codes: no dequantisation at all,
-//    the codes 0..15 are the integer A operand) and writes the 32 columns to tensor memory (tcgen05.st);
+//    group of its row to unsigned 8-bit codes (even columns as the code, odd columns as 16 x the code: two
+//    instructions per eight codes, no dequantisation at all) and writes the 32 columns to tensor memory
+//    (tcgen05.st);
 //  * one thread per set issues four tcgen05.mma.kind::i8 per group (K = 32 each), eight per pair of groups
 //    (one TMA stage, the unit in which converters and MMA issuers synchronise): A = the codes in tensor
 //    memory (128 rows), B = the group's activations quantised to 16-bit integers and split into a signed
-//    high byte (B row 0) and a signed low byte (B row 1), read from shared memory by a K-major, no-swizzle
-//    descriptor; D = 128 x 8 int32 in tensor memory (columns 0 and 1 used), exact;
-//  * two pairs later the converter reads its row's two accumulator columns per group (tcgen05.ld) and adds
-//    s * delta * (256 * D0 + D1) in fp32; m * sum(x) is added when the group is unpacked.
+//    high byte and a signed low byte, each in one B row for the even columns and one for the odd columns
+//    (B rows 0-3), read from shared memory by a K-major, no-swizzle descriptor; D = 128 x 8 int32 in tensor
+//    memory (columns 0-3 used), exact;
+//  * two pairs later the converter reads its row's four accumulator columns per group (tcgen05.ld) and adds
+//    s * delta / 16 * (4096 D0 + 16 D1 + 256 D2 + D3) in fp32; m * sum(x) is added when the group is unpacked.
 // The activations are quantised per 128-column group with delta = max|x| / 32639 (relative error below
 // 2e-5 of the group's largest activation); the weights are used exactly. All mbarrier waits are bounded;
 // no multicast, no clusters.
@@ -46,7 +48,11 @@ constexpr int kNP = 2;  // tensor-memory buffers per set, each for a PAIR of gro
 constexpr uint32_t kACols = 64, kDCols = 16, kSetCols = kNP * (kACols + kDCols);  // group 0 | group 1 halves
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kXPad = 256;            // bytes the B descriptor's unused rows read past a table
-constexpr uint32_t kXGroupBytes = 256;     // per group: 8 chunks of (16 high bytes, 16 low bytes)
+// Activation table per group: 8 chunks of 16 positions, each 4 B rows of 16 bytes: the high and low bytes of x at
+// the even-column positions (zero at the odd ones), then those at the odd-column positions. The odd-column codes
+// then stay in their high nibble (16 x code): one instruction per 8 codes fewer than shifting them down.
+constexpr uint32_t kXGroupBytes = 512;
+constexpr uint32_t kXChunkBytes = 64;
 
 constexpr int kMaxEpis = 4;                // routed (non-store) epilogues per launch
 constexpr int kLnIter = 4;                 // prologue: 8-element chunks per converter thread (H <= 4 x 384 x 8)
@@ -54,14 +60,15 @@ constexpr int kBarLn = 2 + kSets;          // named barriers: 1 = tables staged,
 enum : int { kEpiStore = RB_EPI_STORE, kEpiRopeKv = RB_EPI_ROPE_KV, kEpiSwiglu = RB_EPI_SWIGLU };
 
 struct Entry {
-  const uint16_t* s;
-  const uint16_t* m;
+  const uint16_t* s;  // fp16 scales [N, G]; 8-bit scales (s8): the packed (scale code, zero point) pairs [N, G]
+  const void* m;      // fp16 mins [N, G]; s8: the fp32 per-row scale factors [N]
   void* y;
   int N, G, slot, block_begin;
   int epi, ep;  // epilogue kind, index into TcParams::epis
   // K split: each 128-row block is cut into `ks` slices of `ppk` pairs of groups (the last may be shorter);
   // work item i of this entry (i from item_begin) is block i / ks, slice i % ks
   int ks, ppk, item_begin;
+  int s8;  // 8-bit double-quantised scales (rb_gemv_desc::s_row set); fills the struct's padding
 };
 
 struct Slot {
@@ -100,11 +107,13 @@ constexpr uint32_t kAuxBytes = 2 * kLnMaxGroups * 4 + 16;
 // Split-K workspace: one completion counter per 128-row block (rounded up to 256 bytes), then the partials.
 inline int64_t split_ticket_bytes(int blocks) { return (static_cast<int64_t>(blocks) * 4 + 255) / 256 * 256; }
 
-// B operand descriptor over an activation table: K-major, no swizzle, 16-byte rows at a 16-byte pitch (row 0
-// = 16 high bytes, row 1 = the 16 matching low bytes), the next 16 K-elements of a row 32 bytes further on
-// (leading byte offset 32), 8-row groups 128 bytes apart (unused with N = 8), descriptor version 1 (sm_100).
+// B operand descriptor over an activation table: K-major, no swizzle, 16-byte rows at a 16-byte pitch, the next
+// 16 K-elements of a row kChunk bytes further on (leading byte offset), 8-row groups 128 bytes apart (unused with
+// N = 8), descriptor version 1 (sm_100). This kernel's tables: kChunk = 64 (rows 0-3 of a chunk; B rows 4-7 read
+// the next chunk, their D columns are never read). The int8 head's: kChunk = 32 (rows 0-1).
+template <uint32_t kChunk = kXChunkBytes>
 __device__ __forceinline__ uint64_t x_desc(uint32_t saddr) {
-  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(32 >> 4) << 16) |
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(kChunk >> 4) << 16) |
          (static_cast<uint64_t>(128 >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
 }
 
@@ -127,19 +136,36 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 __device__ __forceinline__ void tmem_ld2(uint32_t taddr, int& h, int& l) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(h), "=r"(l) : "r"(taddr) : "memory");
 }
+// Accumulator columns 0-3 (rows 0-3 of B: even-column high / low, odd-column high / low) of this lane; valid only
+// after tmem_wait_ld4, which takes them as operands so that no use can be scheduled before it.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, int (&d)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+               : "r"(taddr)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld4(int (&d)[4]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3]) : : "memory");
+}
+// 16 x a group's integer dot product from its accumulators; exact in int32 (|value| < 1.02e9).
+__device__ __forceinline__ float group_dot16(const int (&d)[4]) {
+  return static_cast<float>((d[0] << 12) + (d[1] << 4) + (d[2] << 8) + d[3]);
+}
+__device__ __forceinline__ float h2f_lo(uint32_t w) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)));
+}
+__device__ __forceinline__ float h2f_hi(uint32_t w) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+}
 __device__ __forceinline__ void tmem_wait_ld(int& h, int& l) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(h), "+r"(l) : : "memory");
-}
-__device__ __forceinline__ float half_at(const uint4& v, int i) {  // i: compile-time 0..7
-  const uint32_t w = i < 2 ? v.x : i < 4 ? v.y : i < 6 ? v.z : v.w;
-  return __half2float(__ushort_as_half(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xFFFFu))));
 }
 
 // Activation tables: for every slot and 128-column group, x quantised to 16-bit integers
 // xi = rint(x / delta), delta = max|x| / 32639, split as xi = 256 * hi + lo with hi, lo signed bytes, in the
 // order in which a converter thread writes a group's codes to tensor memory (within each 8 columns: the four
-// even columns, then the four odd ones), stored per 16 positions as 16 high bytes then 16 low bytes; plus per
-// group {delta, sum(x)}.
+// even columns, then the four odd ones), stored per 16 positions as four 16-byte B rows (kXChunkBytes); plus per
+// group {delta / 16, sum(x)}.
 //
 // One chunk: positions 8c .. 8c + 7 of a slot. All 32 lanes call this together (a group is 16 chunks = 16
 // consecutive threads, reduced with shuffles); lanes with valid == false contribute zeros and write nothing.
@@ -169,10 +195,13 @@ __device__ __forceinline__ void quant_chunk(const float (&v)[8], bool valid, int
       lo[jp >> 2] |= (static_cast<uint32_t>(l) & 255u) << (8 * (jp & 3));
     }
     // positions 8 * (c % 16) .. + 7 of the group: 16-position chunk (c % 16) / 2, half (c & 1)
-    uint8_t* dst = tab + (c >> 4) * kXGroupBytes + ((c & 15) >> 1) * 32 + (c & 1) * 8;
-    *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], hi[1]);
-    *reinterpret_cast<uint2*>(dst + 16) = make_uint2(lo[0], lo[1]);
-    if ((c & 15) == 0) cst[c >> 4] = make_float2(delta, sum);
+    uint8_t* dst = tab + (c >> 4) * kXGroupBytes + ((c & 15) >> 1) * kXChunkBytes + (c & 1) * 8;
+    *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], 0u);       // B row 0: even-column x, high bytes
+    *reinterpret_cast<uint2*>(dst + 16) = make_uint2(lo[0], 0u);  // B row 1: even-column x, low bytes
+    *reinterpret_cast<uint2*>(dst + 32) = make_uint2(0u, hi[1]);  // B row 2: odd-column x, high bytes
+    *reinterpret_cast<uint2*>(dst + 48) = make_uint2(0u, lo[1]);  // B row 3: odd-column x, low bytes
+    // 4096 D0 + 16 D1 + 256 D2 + D3 is 16 x the group's dot product in units of delta
+    if ((c & 15) == 0) cst[c >> 4] = make_float2(delta * 0.0625f, sum);
   }
 }
 
@@ -395,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
 #pragma unroll
             for (int i = 0; i < 4; ++i)
               umma_ts(tmem + dcol + 8 * h, tmem + acol + 32 * h + 8 * i,
-                      x_desc(xtab + (g + h) * kXGroupBytes + 64 * i), p.idesc, i > 0);
+                      x_desc(xtab + (g + h) * kXGroupBytes + 2 * kXChunkBytes * i), p.idesc, i > 0);
           mm4::umma_commit(mdone(s, b));
         }
       }
@@ -422,7 +451,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
       const int row = blk * kRows + rib;
       const bool row_ok = row < E.N;
       const uint16_t* srow = E.s + static_cast<int64_t>(row_ok ? row : 0) * G;
-      const uint16_t* mrow = E.m + static_cast<int64_t>(row_ok ? row : 0) * G;
       const float2* cst = reinterpret_cast<const float2*>(xs + p.slots[E.slot].cst_off);
       float acc = 0.f;
       // s * delta of the two groups of each pair whose results are pending, oldest pair first (0 for a missing
@@ -450,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
             o[c * 8 + t * 2 + 0] = wv[t] & 0x0F0F0F0Fu;         // even columns of these 8
-            o[c * 8 + t * 2 + 1] = (wv[t] >> 4) & 0x0F0F0F0Fu;  // odd columns
+            o[c * 8 + t * 2 + 1] = wv[t] & 0xF0F0F0F0u;         // odd columns, as 16 x code
           }
         }
       };
@@ -468,15 +496,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
         if (two) acc = fmaf(m1, cb.y, acc);
         const int qq = qp0 + k, b = qq % kNP;
         const bool epi = k >= kNP;
-        int h0 = 0, l0 = 0, h1 = 0, l1 = 0;
+        int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
         ok = __all_sync(0xffffffffu, ok);  // tcgen05 loads / stores are warp-collective
         if (epi && ok) {  // the pair kNP back used this buffer: fetch its results once its MMAs are done
           ok = __all_sync(0xffffffffu, mbar_wait(mdone(s, b), ((qq / kNP) - 1) & 1, ERR_TC_WAIT));
-          if (ok) {
-            mm4::tc_fence_after();
-            tmem_ld2(d_set + b * kDCols, h0, l0);
-            tmem_ld2(d_set + b * kDCols + 8, h1, l1);
-          }
+          if (ok) mm4::tc_fence_after();
         }
         if (ok) {
           uint32_t o[32];
@@ -484,14 +508,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
           tmem_st32(a_set + b * kACols, o);
           unpack(w + 4, o);
           tmem_st32(a_set + b * kACols + 32, o);
+          if (epi) {  // issued after the codes, so that the accumulators are not live across the unpack
+            tmem_ld4(d_set + b * kDCols, d0);
+            tmem_ld4(d_set + b * kDCols + 8, d1);
+          }
         }
         if (k + 1 < npairs) load_codes(k + 1);  // overlaps the tensor-memory traffic above
         ok = __all_sync(0xffffffffu, ok);
         if (epi && ok) {
-          tmem_wait_ld(h0, l0);
-          tmem_wait_ld(h1, l1);
-          acc = fmaf(pa[0], static_cast<float>(h0 * 256 + l0), acc);
-          acc = fmaf(pb[0], static_cast<float>(h1 * 256 + l1), acc);
+          tmem_wait_ld4(d0);
+          tmem_wait_ld4(d1);
+          acc = fmaf(pa[0], group_dot16(d0), acc);
+          acc = fmaf(pb[0], group_dot16(d1), acc);
         }
         if (epi) {
           pa[0] = pa[1];
@@ -514,29 +542,45 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
       };
       load_codes(0);
       const int g0 = 2 * p0, g1 = min(2 * p1, G);  // this item's groups
+      // 8-bit scales: each chunk of (scale code, zero point) words is expanded to the fp16 scale / min pairs that
+      // the fp16 format stores, and both formats then run the same code. The format, the mins' row and the row's
+      // scale factor are read from the kernel parameters when used, not held in registers across the chunk.
+      const int64_t r0 = row_ok ? row : 0;
+      auto mins_at = [&](int g) { return static_cast<const uint16_t*>(E.m) + r0 * G + g; };
+      auto expand = [&](uint32_t& sw, uint32_t& mw) {
+        dq_scales8_f16x2(sw, __ldg(static_cast<const float*>(E.m) + r0), sw, mw);
+      };
       if ((G & 7) == 0) {
         // scales and mins of 8 groups (4 pairs) per 16-byte load, fetched one chunk ahead. With G % 8 == 0 every
         // item starts on a multiple of 8 groups and holds a multiple of 8 groups (slices are a multiple of 4
         // pairs), so all four pairs of a chunk exist.
-        uint4 s8n = __ldg(reinterpret_cast<const uint4*>(srow + g0)), m8n = __ldg(reinterpret_cast<const uint4*>(mrow + g0));
+        uint4 s8n = __ldg(reinterpret_cast<const uint4*>(srow + g0));
+        uint4 m8n = E.s8 ? s8n : __ldg(reinterpret_cast<const uint4*>(mins_at(g0)));
         for (int g8 = g0; g8 < g1; g8 += 8) {
-          const uint4 s8 = s8n, m8 = m8n;
+          uint32_t sw[4] = {s8n.x, s8n.y, s8n.z, s8n.w}, mw[4] = {m8n.x, m8n.y, m8n.z, m8n.w};
           if (g8 + 8 < g1) {
             s8n = __ldg(reinterpret_cast<const uint4*>(srow + g8 + 8));
-            m8n = __ldg(reinterpret_cast<const uint4*>(mrow + g8 + 8));
+            m8n = E.s8 ? s8n : __ldg(reinterpret_cast<const uint4*>(mins_at(g8 + 8)));
+          }
+          if (E.s8) {
+#pragma unroll
+            for (int h = 0; h < 4; ++h) expand(sw[h], mw[h]);
           }
           const int k0 = (g8 - g0) >> 1;
 #pragma unroll
           for (int h = 0; h < 4; ++h)
-            step(k0 + h, half_at(s8, 2 * h), half_at(m8, 2 * h), half_at(s8, 2 * h + 1), half_at(m8, 2 * h + 1));
+            step(k0 + h, h2f_lo(sw[h]), h2f_lo(mw[h]), h2f_hi(sw[h]), h2f_hi(mw[h]));
         }
       } else {
         for (int k = 0; k < npairs; ++k) {
           const int g = 2 * (p0 + k);
           const bool two = g + 1 < G;
-          step(k, __half2float(__ushort_as_half(__ldg(srow + g))), __half2float(__ushort_as_half(__ldg(mrow + g))),
-               two ? __half2float(__ushort_as_half(__ldg(srow + g + 1))) : 0.f,
-               two ? __half2float(__ushort_as_half(__ldg(mrow + g + 1))) : 0.f);
+          uint32_t sw = __ldg(srow + g) | (two ? static_cast<uint32_t>(__ldg(srow + g + 1)) << 16 : 0u), mw = sw;
+          if (E.s8)
+            expand(sw, mw);
+          else
+            mw = __ldg(mins_at(g)) | (two ? static_cast<uint32_t>(__ldg(mins_at(g + 1))) << 16 : 0u);
+          step(k, h2f_lo(sw), h2f_lo(mw), two ? h2f_hi(sw) : 0.f, two ? h2f_hi(mw) : 0.f);
         }
       }
       q += npairs;
@@ -551,13 +595,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
             mm4::tc_fence_after();
-            int h0, l0, h1, l1;
-            tmem_ld2(d_set + b * kDCols, h0, l0);
-            tmem_ld2(d_set + b * kDCols + 8, h1, l1);
-            tmem_wait_ld(h0, l0);
-            tmem_wait_ld(h1, l1);
-            acc = fmaf(pa[i], static_cast<float>(h0 * 256 + l0), acc);
-            acc = fmaf(pb[i], static_cast<float>(h1 * 256 + l1), acc);
+            int d0[4], d1[4];
+            tmem_ld4(d_set + b * kDCols, d0);
+            tmem_ld4(d_set + b * kDCols + 8, d1);
+            tmem_wait_ld4(d0);
+            tmem_wait_ld4(d1);
+            acc = fmaf(pa[i], group_dot16(d0), acc);
+            acc = fmaf(pb[i], group_dot16(d1), acc);
           }
         }
       }
@@ -743,7 +787,8 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
       }
       Entry& E = p.e[take];
       E.s = D.s;
-      E.m = D.m;
+      E.s8 = D.s_row != nullptr;
+      E.m = E.s8 ? static_cast<const void*>(D.s_row) : static_cast<const void*>(D.m);
       E.y = D.y;
       E.N = static_cast<int>(D.N);
       E.G = static_cast<int>(G);

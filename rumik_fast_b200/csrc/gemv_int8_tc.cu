@@ -126,8 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int8_tc_kernel(const __grid_
           const uint32_t a_base = smem_u32(smem + static_cast<size_t>(slot) * kStageBytes);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            umma_ss_i8(tmem + b * 8, mm4::sw128_desc(a_base + 32 * i), g4t::x_desc(xtab + k * 256 + 64 * i), p.idesc,
-                       (k | i) != 0);
+            umma_ss_i8(tmem + b * 8, mm4::sw128_desc(a_base + 32 * i), g4t::x_desc<32>(xtab + k * 256 + 64 * i),
+                       p.idesc, (k | i) != 0);
           mm4::umma_commit(&empty[slot]);  // the tile may be refilled once these MMAs have read it
         }
         if (ok) mm4::umma_commit(&dready[b]);

@@ -10,12 +10,14 @@ of their weights through one persistent kernel instead:
 
 Entries are (x, q, s, m, y) with the layout of gemv_int4_cuda (x [K] fp16/bf16, q uint8 [N, K/2], s and m
 fp16 [N, K/128], y [N]); all x share one dtype and all y share one dtype. Calling is graph-capture safe.
+An entry may carry 8-bit double-quantised scales instead (s = scales8.Scales8, m = None); a list with such an
+entry runs on the tcgen05 kernel.
 """
 import ctypes
 
 import torch
 
-from . import _lib, config
+from . import _lib, config, scales8
 from .cuda_gemv import _on_device, _require
 
 G = 128
@@ -42,12 +44,12 @@ class Int4GemvSet:
             _require(y.numel() == N and y.is_contiguous(), f"entry {i}: y must be a contiguous [{N}] vector")
             _require(q.dtype == torch.uint8 and q.is_contiguous(), f"entry {i}: q must be contiguous uint8 [N, K/2]")
             _require(K % G == 0, f"entry {i}: K={K} must be a multiple of {G}")
-            for t, nm in ((s, "s"), (m, "m")):
-                _require(t.dtype == torch.float16 and t.is_contiguous() and tuple(t.shape) == (N, K // G),
-                         f"entry {i}: {nm} must be a contiguous fp16 [{N}, {K // G}] tensor")
-            descs[i] = _lib.GemvDesc(x.data_ptr(), y.data_ptr(), q.data_ptr(), s.data_ptr(), m.data_ptr(), N, K)
+            sp, mp = _scale_ptrs(s, m, N, K, i, self.device)
+            descs[i] = _lib.GemvDesc(x.data_ptr(), y.data_ptr(), q.data_ptr(), sp, mp, N, K)
+            if isinstance(s, scales8.Scales8):
+                descs[i].s_row = s.s_row.data_ptr()
         self._descs = descs
-        self.bytes = sum(q.numel() + 4 * s.numel() + 2 * x.numel() + 2 * y.numel() for x, q, s, m, y in self.entries)
+        self.bytes = sum(entry_bytes(q, s, x, y) for x, q, s, m, y in self.entries)
         self.kflags = _lib.KERNEL_FLAGS[kernel]
         self.ws = workspace(descs, len(self.entries), self.device, self.kflags)
 
@@ -58,6 +60,25 @@ class Int4GemvSet:
                                          _lib.dtype_code(self.x_dtype), _lib.dtype_code(self.y_dtype),
                                          config.flags() | self.kflags, _lib.stream_ptr(self.device))
         _lib.check("rb_gemv_int4_multi_ws", st)
+
+
+def _scale_ptrs(s, m, N, K, i, device):
+    """(s, m) pointers of an entry: fp16 scale and min tensors, or a scales8.Scales8 as s with m None."""
+    if isinstance(s, scales8.Scales8):
+        _require(m is None, f"entry {i}: with 8-bit scales m must be None")
+        scales8.check(s, N, K // G, device, where=f"entry {i}: ")
+        return s.sz.data_ptr(), None
+    for t, nm in ((s, "s"), (m, "m")):
+        _require(isinstance(t, torch.Tensor) and t.dtype == torch.float16 and t.is_contiguous()
+                 and tuple(t.shape) == (N, K // G), f"entry {i}: {nm} must be a contiguous fp16 [{N}, {K // G}] tensor")
+    return s.data_ptr(), m.data_ptr()
+
+
+def entry_bytes(q, s, x, y):
+    """HBM bytes one GEMV must move: codes, scales (fp16 pair or 8-bit word per group, plus the row factors),
+    x and y."""
+    sb = 2 * s.sz.numel() + 4 * s.s_row.numel() if isinstance(s, scales8.Scales8) else 4 * s.numel()
+    return q.numel() + sb + x.element_size() * x.numel() + y.element_size() * y.numel()
 
 
 def workspace(descs, count, device, kflags=0):
