@@ -34,8 +34,8 @@ LAYERS = 36
 METRIC = "decode-step GEMV HBM GB/s"
 UNIT = "GB/s"
 # DRAM bytes (read + write) per launch of gemv_int4_tc_kernel on the 36-layer set: ncu capture of the 3-layer
-# case (160.53 MB read + 4.80 MB written) scaled x12 by blocks streamed
-NCU_TRAFFIC_PER_LAUNCH = 1983999984
+# case (160.590336 MB read + 3.537920 MB written) scaled x12 by blocks streamed
+NCU_TRAFFIC_PER_LAUNCH = 1969539072
 
 
 def parse():

@@ -203,3 +203,31 @@ def test_fused_attention_argument_checks(native_lib):
     assert run([down, o_proj], ws_bytes=need - 1) == _lib.ERR_SHAPE
     assert run([down, o_proj], cache_len=0) == _lib.ERR_SHAPE
     assert run([down, o_proj], flags=_lib.FLAG_KERNEL_TC) == _lib.ERR_SHAPE    # runs on the warp-MMA kernel only
+
+
+def test_scales8_descriptor_checks(native_lib):
+    """rb_gemv_desc::s_row (8-bit scales) is validated before any CUDA call: m may then be NULL, s_row must be
+    4-byte aligned, and such a list cannot be forced onto the warp-MMA kernel or run with fused attention."""
+    L = native_lib
+
+    def d8(s_row=0xB0000, m=None, **kw):
+        d = desc(**kw)
+        d.m = m
+        d.s_row = s_row
+        return d
+
+    one = lambda d: (_lib.GemvDesc * 1)(d)  # noqa: E731
+    plain = desc()
+    plain.m = None
+    assert L.rb_gemv_int4_multi(one(plain), 1, _lib.F16, _lib.F16, 0, None) == _lib.ERR_NULL  # fp16 needs m
+    assert L.rb_gemv_int4_multi(one(d8(s_row=0xB0002)), 1, _lib.F16, _lib.F16, 0, None) == _lib.ERR_ALIGN
+    assert L.rb_gemv_int4_multi(one(d8()), 1, _lib.F16, _lib.F16, _lib.FLAG_KERNEL_MMA, None) == _lib.ERR_SHAPE
+    assert L.rb_gemv_int4_workspace(one(d8()), 1, _lib.FLAG_KERNEL_MMA) == -_lib.ERR_SHAPE
+    assert L.rb_gemv_int4_fused(one(d8()), None, 1, None, None, None, 0, _lib.F16, _lib.F16,
+                                _lib.FLAG_KERNEL_MMA, None) == _lib.ERR_SHAPE
+    OUT = 0x90000
+    need = L.rb_attn_decode_workspace(8, 2, 128)
+    src = _lib.AttnSrc(A, B, C, POS, OUT, 8, 2, 128, 64, 0.088, 0xA0000, need)
+    two = (_lib.GemvDesc * 2)(desc(x=A), d8(x=OUT, K=8 * 128))
+    assert L.rb_gemv_int4_fused(two, None, 2, None, ctypes.byref(src), None, 0, _lib.F16, _lib.F16, 0,
+                                None) == _lib.ERR_SHAPE                   # fused attention: warp-MMA kernel only
