@@ -25,7 +25,7 @@ import ctypes
 
 import torch
 
-from . import _lib, config
+from . import _lib, config, scales8
 from .cuda_gemv import _on_device, _require
 from .gemv_set import _ws_len, _ws_ptr, workspace
 
@@ -109,21 +109,31 @@ def add_layernorm(ln: AddLn):
 
 
 def _int4(w, K=None):
+    """(q, s, m) with fp16 scale and min, or (q, scales8.Scales8, None) -> (descriptor of the GEMV with x and y
+    unset, HBM bytes of its weights)."""
     q, s, m = w
     N, Kq = q.shape[0], q.shape[1] * 2
     _require(q.dtype == torch.uint8 and q.is_contiguous() and q.is_cuda, "q must be contiguous CUDA uint8 [N, K/2]")
     _require(K is None or Kq == K, f"weights have K={Kq}, activations {K}")
+    if isinstance(s, scales8.Scales8):
+        _require(m is None, "with 8-bit scales m must be None")
+        scales8.check(s, N, Kq // G, q.device)
+        d = _lib.GemvDesc(None, None, q.data_ptr(), s.sz.data_ptr(), None, N, Kq)
+        d.s_row = s.s_row.data_ptr()
+        return d, q.numel() + 2 * s.sz.numel() + 4 * s.s_row.numel()
     for t, nm in ((s, "s"), (m, "m")):
         _require(t.dtype == torch.float16 and t.is_contiguous() and tuple(t.shape) == (N, Kq // G),
                  f"{nm} must be a contiguous fp16 [{N}, {Kq // G}] tensor")
-    return q, s, m, N, Kq
+    return _lib.GemvDesc(None, None, q.data_ptr(), s.data_ptr(), m.data_ptr(), N, Kq), q.numel() + 4 * s.numel()
 
 
 class AddLnGemvPost:
     """One decode layer's input side as ONE launch: [add_ln ->] gemv(w_qkv), gemv(w_gate_up) -> post.
 
-    qkv      (q, s, m) of the q|k|v rows, N = (n_q_heads + 2 n_kv_heads) head_dim
-    gate_up  (q, s, m) of the gate|up rows in interleave_gate_up order
+    qkv      (q, s, m) of the q|k|v rows, N = (n_q_heads + 2 n_kv_heads) head_dim; or (q, Scales8, None) with
+             8-bit scales (rumik_fast_b200.scales8: the launch then runs on the tcgen05 kernel)
+    gate_up  (q, s, m) of the gate|up rows in interleave_gate_up order (or (q, Scales8, None), packed after
+             interleaving)
     add_ln   an AddLn (its h is the GEMV input), or None with h = the input vector
     pos      int64 [1] device tensor: the position (cache slot) of this token
     cos, sin [cache_len, head_dim] rotary tables (engine/rumik_int4.py:107-109)
@@ -150,17 +160,18 @@ class AddLnGemvPost:
         _require(nkv == n_kv_heads and tuple(v_cache.shape) == (nkv, S, hd), "caches must be [n_kv_heads, S, hd]")
         _require(tuple(cos.shape) == (S, hd) and tuple(sin.shape) == (S, hd), f"cos/sin must be [{S}, {hd}]")
         _require(q_out.numel() == n_q_heads * hd, "q_out must hold n_q_heads * head_dim elements")
-        qq, qs, qm, Nqkv, K1 = _int4(qkv, H)
-        gq, gs, gm, Ngu, K2 = _int4(gate_up, H)
+        d_qkv, b_qkv = _int4(qkv, H)
+        d_gu, b_gu = _int4(gate_up, H)
+        Nqkv, Ngu = d_qkv.N, d_gu.N
         _require(Nqkv == (n_q_heads + 2 * n_kv_heads) * hd, "qkv rows must be (n_q_heads + 2 n_kv_heads) head_dim")
         _require(Ngu % 2 == 0 and act.numel() == Ngu // 2, "act must hold the N/2 MLP channels")
         for y, N in ((y_qkv, Nqkv), (y_gate_up, Ngu)):
             _require(y is None or (y.dtype == dt and y.numel() == N and y.is_contiguous()), "bad y buffer")
         xp = None if add_ln is not None else h.data_ptr()
         yp = lambda y: y.data_ptr() if y is not None else None  # noqa: E731
-        descs = (_lib.GemvDesc * 2)()
-        descs[0] = _lib.GemvDesc(xp, yp(y_qkv), qq.data_ptr(), qs.data_ptr(), qm.data_ptr(), Nqkv, H)
-        descs[1] = _lib.GemvDesc(xp, yp(y_gate_up), gq.data_ptr(), gs.data_ptr(), gm.data_ptr(), Ngu, H)
+        descs = (_lib.GemvDesc * 2)(d_qkv, d_gu)
+        for d, y in ((descs[0], y_qkv), (descs[1], y_gate_up)):
+            d.x, d.y = xp, yp(y)
         epis = (_lib.GemvEpi * 2)()
         epis[0] = _lib.GemvEpi(_lib.EPI_ROPE_KV, int(bool(rope)), n_q_heads, n_kv_heads, hd, S, pos.data_ptr(),
                                cos.data_ptr(), sin.data_ptr(), q_out.data_ptr(), k_cache.data_ptr(),
@@ -171,7 +182,7 @@ class AddLnGemvPost:
         self.ws = workspace(descs, 2, self.device, self.kflags)
         self._keep = (qkv, gate_up, pos, cos, sin, k_cache, v_cache, q_out, act, h, y_qkv, y_gate_up)
         self.y_dtype = dt
-        self.bytes = sum(t.numel() for t in (qq, gq)) + 4 * (qs.numel() + gs.numel())
+        self.bytes = b_qkv + b_gu
 
     def __call__(self):
         L = _lib.lib()

@@ -213,6 +213,47 @@ def test_layer_input_launch_at_benchmark_shapes(dt, kernel):
         assert_close(got, ref, what)
 
 
+@pytest.mark.parametrize("dt", DTYPES)
+def test_layer_input_launch_with_8bit_scales(dt):
+    """The same layer-input launch with both weight sets carrying 8-bit double-quantised scales (the launch runs
+    on the tcgen05 kernel), against the oracle's unfused chain on the fp16 scale / min those scales decode to."""
+    from rumik_fast_b200 import scales8
+    g = syn.generator(15, "cpu")
+    H, nq, nkv, hd, inter, S, pos = 3072, 24, 8, 128, 8192, 64, 9
+    x, a, b, w = ln_inputs(H, g, dt)
+    xd, ad, bd, wd = (t.to(DEV) for t in (x, a, b, w))
+    qkv_q, qkv_s, qkv_m = syn.int4_weights((nq + 2 * nkv) * hd, H, g, "cpu")
+    gu_q, gu_s, gu_m = fused.interleave_gate_up(*syn.int4_weights(2 * inter, H, g, "cpu"))
+    sc_qkv, sc_gu = scales8.pack(qkv_s, qkv_m), scales8.pack(gu_s, gu_m)
+    cos_n, sin_n, cos, sin, kc, vc = rope_setup(dt, nq, nkv, hd, S, g)
+    x_out = torch.empty(H, device=DEV, dtype=dt)
+    q_out = torch.empty(nq * hd, device=DEV, dtype=dt)
+    act = torch.empty(inter, device=DEV, dtype=dt)
+    pos_t = torch.tensor([pos], device=DEV, dtype=torch.int64)
+    on_dev = lambda sc: scales8.Scales8(sc.sz.to(DEV), sc.s_row.to(DEV))  # noqa: E731
+    layer = fused.AddLnGemvPost((qkv_q.to(DEV), on_dev(sc_qkv), None), (gu_q.to(DEV), on_dev(sc_gu), None),
+                                add_ln=fused.AddLn(xd, ad, bd, wd, x_out, eps=1e-5), pos=pos_t, cos=cos, sin=sin,
+                                k_cache=kc, v_cache=vc, q_out=q_out, act=act, n_q_heads=nq, n_kv_heads=nkv,
+                                rope=True)
+    layer()
+    torch.cuda.synchronize()
+    t = tag(dt)
+    s_ref, h_ref = O.add_ln_ref(np_act(x)[0], np_act(a)[0], np_act(b)[0], np_act(w)[0], 1e-5, t)
+    assert np.array_equal(vals(x_out), s_ref)
+    h_st = O.from_f32(h_ref, t)
+
+    def gemv(q, sc):
+        s16, m16 = O.unpack_scales8(sc.sz.numpy().view(np.uint16), sc.s_row.numpy())
+        return O.round_act(O.gemv_int4_ref(h_st, q.numpy(), s16, m16, x_dtype=t), t)
+    y_qkv = gemv(qkv_q, sc_qkv)
+    q_ref, k_ref, v_ref = O.rope_kv_ref(y_qkv, pos, cos_n, sin_n, nq, nkv, hd, True, t)
+    y_gu = gemv(gu_q, sc_gu)                          # interleaved rows: gate c at 2c, up c at 2c + 1
+    act_ref = O.swiglu_ref(y_gu[0::2], y_gu[1::2], t)
+    for got, ref, what in ((q_out, q_ref, "q"), (kc[:, pos], k_ref, "k"), (vc[:, pos], v_ref, "v"),
+                           (act, act_ref, "act")):
+        assert_close(got, ref, what)
+
+
 def test_layer_input_in_a_cuda_graph_follows_the_position():
     """Captured once, replayed with pos advanced on the device: each replay writes the next cache slot."""
     dt = torch.float16
