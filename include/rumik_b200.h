@@ -7,6 +7,9 @@
  * cudaStream_t passed as void*. They never allocate, never synchronise, and are safe to call while a CUDA
  * graph is being captured on `stream`. Every function returns an rb_status code (0 = success); argument
  * checks run before any CUDA call, so a bad argument is reported without touching the device.
+ * Several host threads may call them at once (for example one per GPU): the library's only process-wide host
+ * state, a per-kernel cache of the shared-memory attribute and the static scratch's address per device, is
+ * guarded. Device buffers that two calls share (a workspace, the static scratch) must be ordered by the caller.
  *
  * Weight format (kernels/int4_gemv.py:1-3, modal_export_int4.py:48-59):
  *   q  uint8 [N, K/2]   two 4-bit codes per byte, low nibble = even column, high nibble = odd column

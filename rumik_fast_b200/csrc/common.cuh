@@ -9,6 +9,8 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 
 namespace rb {
 
@@ -340,9 +342,11 @@ __device__ __forceinline__ void store_out(void* y, int64_t idx, float v, bool is
 inline cudaError_t ensure_smem_limit(const void* kern, int bytes) {
   static const void* keys[64] = {};
   static unsigned long long done[64] = {};
+  static std::mutex lock;  // host threads (e.g. one per GPU) may launch at the same time
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> hold(lock);
   int slot = -1;
   for (int i = 0; i < 64; ++i) {
     if (keys[i] == kern || keys[i] == nullptr) {

@@ -451,18 +451,18 @@ int launch_mm_int4_tc_static(MmArgs a, int num_sms, cudaStream_t stream) {
   a.ws_bytes = 0;
   if (need > 0) {
     // the symbol's device address, looked up once per device (return code checked)
-    static void* addr[64] = {};
+    static std::atomic<void*> addr[64] = {};  // host threads may race here; they all store the same address
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return RB_ERR_DEVICE;
-    if (!addr[dev]) {
-      void* p = nullptr;
+    void* p = addr[dev].load(std::memory_order_acquire);
+    if (!p) {
       if (cudaGetSymbolAddress(&p, g_mm_scratch) != cudaSuccess || !p) {
         (void)cudaGetLastError();
         return RB_ERR_DEVICE;
       }
-      addr[dev] = p;
+      addr[dev].store(p, std::memory_order_release);
     }
-    a.ws = static_cast<float*>(addr[dev]);
+    a.ws = static_cast<float*>(p);
     a.ws_bytes = kStaticScratchBytes;
   }
   return launch_mm_int4_tc(a, num_sms, stream);
