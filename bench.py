@@ -260,12 +260,16 @@ def run_reference(a):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
+    from rumik_fast_b200 import synthetic as syn
     gbs, threads, desc, n = cpu_oracle_sample(a.cpu_seconds)
+    step_bytes = LAYERS * sum(syn.int4_bytes(nn, k) for _, nn, k in syn.LAYER_SHAPES) + syn.int8_bytes(*syn.HEAD_SHAPE)
     line = {"metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "n_gpus": a.gpus, "steps": n, "warmup": 1,
-            "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp32", "data": "synthetic", "impl": "reference",
+            "ms_per_step": round(step_bytes / (gbs * 1e9) * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
             "config": {"workload": "config-1 decode-step projection set (36 x QKV/o/gate_up/down, int4 g128), "
-                                   "CPU dequantise-then-matvec sample", "batch": 1},
+                                   "CPU dequantise-then-matvec sample", "batch": 1,
+                       "ms_per_step": "extrapolated: the full step's bytes (projections + head) at the sampled "
+                                      "rate; steps = GEMVs in the sample"},
             "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": desc},
             "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
