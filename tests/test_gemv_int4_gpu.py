@@ -73,7 +73,7 @@ def test_config0_full_size():
 
 @pytest.mark.parametrize("N,K", [(1, 128), (7, 256), (8, 384), (9, 128), (100, 1024), (1000, 2048), (3072, 3072),
                                  (5120, 3072), (16384, 3072), (3072, 8192), (2048, 11008), (300, 16384), (25088, 2048),
-                                 (16400, 2048)])
+                                 (16400, 2048), (21504, 3072)])  # the last: the engine's fused [q|k|v|gate|up] w_in
 def test_shapes(N, K):
     q, s, m = weights(N, K, seed=N * 7 + K)
     x = syn.activations((K,), syn.generator(K, "cpu"), "cpu")
