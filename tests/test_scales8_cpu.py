@@ -99,3 +99,30 @@ def test_descriptor_layout():
     assert ctypes.sizeof(_lib.GemvDesc) == 64
     assert _lib.GemvDesc.s_row.offset == 56
     assert _lib.GemvDesc(1, 2, 3, 4, 5, 6, 7).s_row is None
+
+
+try:
+    from hypothesis import given, settings, strategies as st
+    from hypothesis.extra import numpy as hnp
+except ImportError:  # pragma: no cover
+    given = None
+
+if given is not None:
+    _f16 = hnp.arrays(np.float16, st.tuples(st.integers(1, 6), st.integers(1, 9)),
+                      elements=st.floats(min_value=0, max_value=65504, width=16, allow_nan=False))
+
+    @settings(max_examples=60, deadline=None)
+    @given(_f16, st.data())
+    def test_pack_matches_oracle_on_arbitrary_grids(s, data):
+        """Any finite non-negative fp16 scales (zeros, subnormals, the fp16 maximum) and any finite fp16 mins:
+        the torch packer and decoder agree with the oracle bit for bit (overflowing products included)."""
+        m = data.draw(hnp.arrays(np.float16, s.shape,
+                                 elements=st.floats(min_value=-65504, max_value=65504, width=16, allow_nan=False)))
+        sc = scales8.pack(torch.from_numpy(s), torch.from_numpy(m))
+        sz_o, row_o = O.pack_scales8(s, m)
+        sz, row = _np(sc)
+        assert np.array_equal(row, row_o) and np.array_equal(sz, sz_o)
+        s16, m16 = scales8.unpack(sc)
+        s16_o, m16_o = O.unpack_scales8(sz_o, row_o)
+        assert np.array_equal(s16.numpy().view(np.uint16), s16_o.view(np.uint16))
+        assert np.array_equal(m16.numpy().view(np.uint16), m16_o.view(np.uint16))
