@@ -692,6 +692,8 @@ def run_step(a):
 
 def main():
     a = parse()
+    if a.scales != "fp16" and (a.workload != "decode" or a.parallel != "replica"):
+        raise SystemExit("--scales 8bit applies to the decode workload's projection set (replicas)")
     if a.impl == "reference":
         return run_reference(a)
     if a.workload == "prefill":
