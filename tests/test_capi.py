@@ -12,7 +12,8 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 
 
 def declared_functions():
-    txt = open(HEADER).read()
+    with open(HEADER) as f:
+        txt = f.read()
     txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
     return sorted(set(re.findall(r"\b(rb_[a-z0-9_]+)\s*\(", txt)))
 
