@@ -1,15 +1,24 @@
 #!/usr/bin/env python
 """Decode-step GEMV benchmark of rumik_fast_b200 on B200 (the 36-layer decode-step projection set + the int8 audio head).
 
-One step = the 36-layer decode-step projection set (per layer: QKV 5120x3072, o_proj 3072x3072,
-gate_up 16384x3072, down 3072x8192, int4 group-128) followed by the int8 audio head (16385x3072), replayed
-from one CUDA graph, the way rumik-fast's engine and its full-step benchmark run it (engine/rumik_int4.py:225-245,
-kernels/bench_gemv.py:83-113). Inputs follow the reference benchmark: fixed activations (x_h for
-QKV/o/gate_up/head, x_i for down). --mode set (default) runs the 144 projections as one persistent
-rb_gemv_int4_multi launch plus the head; --mode chain runs 145 stream-ordered launches, one per matrix. The
-weights (1.98 GB) are larger than L2 (126 MB), so no L2 flush is needed between steps.
+Headline (the BASELINE metric, decode-step GEMV HBM GB/s): one step = the 36-layer config-1 projection set (per
+layer: QKV 5120x3072, o_proj 3072x3072, gate_up 16384x3072, down 3072x8192, int4 group-128) followed by the int8
+audio head (16385x3072), replayed from one CUDA graph, the way rumik-fast's full-step benchmark runs it
+(kernels/bench_gemv.py:83-113; engine/rumik_int4.py:225-245). Inputs follow the reference benchmark: fixed
+activations (x_h for QKV/o/gate_up/head, x_i for down). The 144 projections run as one persistent
+rb_gemv_int4_multi launch plus the head. The weights (1.98 GB) are larger than L2 (126 MB), so no L2 flush is
+needed between steps.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-prefetch]
+The same JSON line carries sub-records, each timed by its own CUDA events:
+  step      the real token-to-token decode step at position 511 (embedding row, 36 fused layers with attention,
+            final norm, head, sampler; engine/rumik_fused.py:97-121): its tok/s is the line's "tok_s"
+  prefill   config 3: the int4-weight matmul over the projection set at M = 34, 256, 1024 tokens
+  gemv_c0   config 0: 36 distinct 8192x3072 GEMVs through gemv_int4_cuda in one CUDA graph, best of 3 rounds of
+            20 replays (kernels/bench_cuda.py:18-32)
+  chain     the headline step as an unmodified engine issues it: 145 stream-ordered gemv_int4_cuda/gemv_int8_cuda
+            launches
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extras]
 
 Prints one JSON line (rank 0). value = algorithmic HBM bytes of a step / device time of a step, summed over
 ranks (each rank runs an independent replica of the step: weak scaling).
@@ -24,7 +33,6 @@ import threading
 import time
 import types
 
-import numpy as np
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -33,18 +41,20 @@ sys.path.insert(0, ROOT)
 LAYERS = 36
 METRIC = "decode-step GEMV HBM GB/s"
 UNIT = "GB/s"
+PREFILL_TOKENS = (34, 256, 1024)
 # DRAM bytes (read + write) per launch of gemv_int4_tc_kernel on the 36-layer set: ncu capture of the 3-layer
-# case (160.590336 MB read + 3.537920 MB written) scaled x12 by blocks streamed
+# case scaled x12 by blocks streamed (profiles/gemv_int4_tc_3layer_full.md)
 NCU_TRAFFIC_PER_LAUNCH = 1969539072
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefetch", action="store_true", help="do not stream weights before the PDL wait")
+    ap.add_argument("--no-extras", action="store_true", help="headline only: no step/prefill/gemv_c0/chain records")
     ap.add_argument("--mode", default="set", choices=["set", "chain"],
                     help="set: the 144 projections as one persistent launch (Int4GemvSet); chain: one launch each")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -59,7 +69,7 @@ def parse():
                     help="decode workload: the reference's fp16 scales, or 8-bit double-quantised ones")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "step"],
                     help="decode: config 1 + 2 (the headline); prefill: config 3, the int4-weight matmul over the "
-                         "36-layer projection set for --tokens prompt tokens")
+                         "36-layer projection set for --tokens prompt tokens; step: the full decode step alone")
     ap.add_argument("--tokens", type=int, default=256, help="prefill prompt length M (config 3: 34, 256, 1024)")
     ap.add_argument("--collective", default="nccl", choices=["peer", "nccl"],
                     help="tp only: per-layer reduction by the peer-memory kernel or by add + NCCL all-reduce")
@@ -74,63 +84,115 @@ def dist_env():
 
 
 def peaks():
+    """(HBM GB/s, kind, bf16 TFLOP/s burst) from MEASURED_PEAKS.json, else the pool's fallback figures."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         j = json.load(open(p))
-        return float(j["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(j["hbm_gbs"]), "measured", float(j.get("bf16_tflops", 1590.0))
+    return 6650.0, "fallback", 1590.0
 
 
 # ---------------------------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples every 200 ms while the timed region runs (read-only queries)."""
+    """SM clock, power and clock-event reasons of this GPU, polled through NVML about every millisecond while
+    the timed regions run (read-only queries), so that even a timed region of a few milliseconds holds samples.
+    Falls back to nvidia-smi at 200 ms when NVML is unavailable."""
 
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
+               ("hw_power_brake_slowdown", 0x80), ("sw_power_cap", 0x4))
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        self.rows, self.proc, self.thread = [], None, None
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.rows, self.proc, self.thread, self.stop, self.nvml = [], None, None, False, None
+        self.max_mhz = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        try:
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(props.uuid))
+        except Exception:  # noqa: BLE001
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
 
     def __enter__(self):
         try:
+            nv, h = self._nvml_handle()
+            self.nvml = (nv, h)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:  # noqa: BLE001
+            self.nvml = None
+        try:
+            idx = self.device.index or 0
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+            if vis.replace(",", "").isdigit():
+                idx = int(vis.split(",")[idx])
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                          "-i", str(idx), "-lms", "200"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread = threading.Thread(target=self._read_smi, daemon=True)
             self.thread.start()
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
-    def _read(self):
+    def _poll(self):
+        nv, h = self.nvml
+        while not self.stop:
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                reasons = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.rows.append((sm, reasons))
+            except Exception:  # noqa: BLE001
+                return
+            time.sleep(0.001)
+
+    def _read_smi(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+            r = [c.strip() for c in line.split(",")]
+            if len(r) < 9:
+                continue
+            bits = 0
+            for nm, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    bits |= dict(self.REASONS)[nm]
+            try:
+                self.max_mhz = float(r[2])
+                self.rows.append((float(r[1]), bits))
+            except ValueError:
+                pass
 
     def mark(self):
         return len(self.rows)
 
     def __exit__(self, *a):
+        self.stop = True
         if self.proc:
             self.proc.terminate()
             self.proc.wait()
+        if self.thread:
             self.thread.join(timeout=2)
+        if self.nvml:
+            try:
+                self.nvml[0].nvmlShutdown()
+            except Exception:  # noqa: BLE001
+                pass
 
     def summary(self, start=0, end=None):
         rows = self.rows[start:end]
         if not rows:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for nm, v in zip(names, r[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
-                "samples": len(rows), "reasons": sorted(reasons)}
+        reasons = sorted({nm for _, bits in rows for nm, b in self.REASONS if bits & b})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": self.max_mhz,
+                "samples": len(rows), "reasons": reasons, "source": "nvml" if self.nvml else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------------------------- workload
@@ -215,326 +277,119 @@ def timed(run, steps, warmup, world):
     return ms
 
 
+def free():
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+
 # ---------------------------------------------------------------------------------------------- CPU side
-def cpu_oracle_sample(seconds, threads=None):
-    """The reference's CPU path (fp32 dequantise-then-matvec, restated in numpy by oracle/) on the config-1
-    layer shapes, timed on the host cores for about `seconds`. Returns (GB/s, threads, description, n)."""
-    from concurrent.futures import ThreadPoolExecutor
-    from oracle import oracle as O
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def host_layers(nlayers, seed):
+    """Distinct config-1 layers, the int8 head and the two activation vectors as host torch tensors."""
     from rumik_fast_b200 import synthetic as syn
-    threads = threads or os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    mats = []
-    for _, n, k in syn.LAYER_SHAPES:
-        q = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
-        s = rng.uniform(0.002, 0.02, size=(n, k // 128)).astype(np.float16)
-        m = (-7.5 * s.astype(np.float32) + rng.normal(0, 1e-3, size=s.shape)).astype(np.float16)
-        x = rng.normal(0, 1, size=k).astype(np.float16)
-        mats.append((q, s, m, x, syn.int4_bytes(n, k)))
-    pool = ThreadPoolExecutor(threads)
+    g = torch.Generator().manual_seed(seed)
+    layers = [[syn.int4_weights(n, k, g, "cpu") for _, n, k in syn.LAYER_SHAPES] for _ in range(nlayers)]
+    head = syn.int8_weights(*syn.HEAD_SHAPE, g, "cpu")
+    return layers, head, syn.activations((3072,), g, "cpu"), syn.activations((8192,), g, "cpu")
 
-    def gemv(q, s, m, x):
-        rows = q.shape[0]
-        chunk = max(64, (rows + threads - 1) // threads)
-        parts = pool.map(lambda r0: O.gemv_int4_ref(x, q[r0:r0 + chunk], s[r0:r0 + chunk], m[r0:r0 + chunk]),
-                         range(0, rows, chunk))
-        return np.concatenate(list(parts))
 
-    gemv(*mats[1][:4])                                   # warm the pool / BLAS
+def cpu_layer(L, xh, xi):
+    """One layer's four projections by the reference's CPU path (oracle/reference_cpu.py)."""
+    from oracle import reference_cpu as R
+    R.gemv_int4_torch(xh, *L[0])
+    R.gemv_int4_torch(xh, *L[1])
+    R.gemv_int4_torch(xh, *L[2])
+    R.gemv_int4_torch(xi, *L[3])
+
+
+def cpu_head(head, xh):
+    from oracle import reference_cpu as R
+    R.gemv_int8_torch(xh, *head, signed=True)
+
+
+def cpu_baseline_sample(seconds):
+    """The reference's CPU dequantise-then-matvec (torch on all host threads) over 8 distinct config-1 layers,
+    cycled for about `seconds`, plus the head once: GB/s of algorithmic bytes."""
+    from rumik_fast_b200 import synthetic as syn
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    layers, head, xh, xi = host_layers(8, 99)
+    layer_bytes = sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES)
+    cpu_layer(layers[0], xh, xi)  # warm the allocator and the thread pool
     t0 = time.perf_counter()
-    nbytes, n = 0, 0
-    while True:
-        q, s, m, x, b = mats[n % len(mats)]
-        gemv(q, s, m, x)
-        nbytes += b
+    cpu_head(head, xh)
+    nbytes, n = syn.int8_bytes(*syn.HEAD_SHAPE), 0
+    while time.perf_counter() - t0 < seconds:
+        cpu_layer(layers[n % len(layers)], xh, xi)
+        nbytes += layer_bytes
         n += 1
-        if time.perf_counter() - t0 >= seconds and n % len(mats) == 0:
-            break
     dt = time.perf_counter() - t0
-    pool.shutdown()
-    return nbytes / dt / 1e9, threads, f"{n} int4 GEMVs over the 4 config-1 layer shapes ({n // 4} layers), {dt:.1f} s", n
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"reference CPU path (torch dequantize(q, s, m) @ x.float(), kernels/int4_gemv.py:27-30, "
+                      f"on {threads} threads): the int8 head + {n} config-1 layers cycled over 8 distinct layers, "
+                      f"{dt:.1f} s"}
 
 
-# ---------------------------------------------------------------------------------------------- arms
 def run_reference(a):
+    """The reference's own CPU path for the headline step, timed on the host cores: each step is the whole
+    decode-step projection set (36 distinct layers) plus the int8 head, by torch dequantise-then-matvec on all
+    host threads. Rank 0 only."""
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
     from rumik_fast_b200 import synthetic as syn
-    gbs, threads, desc, n = cpu_oracle_sample(a.cpu_seconds)
-    step_bytes = LAYERS * sum(syn.int4_bytes(nn, k) for _, nn, k in syn.LAYER_SHAPES) + syn.int8_bytes(*syn.HEAD_SHAPE)
-    line = {"metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "n_gpus": a.gpus, "steps": n, "warmup": 1,
-            "ms_per_step": round(step_bytes / (gbs * 1e9) * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+    threads = cpu_threads()
+    torch.set_num_threads(threads)  # torchrun sets OMP_NUM_THREADS=1 for N > 1: override it
+    layers, head, xh, xi = host_layers(a.layers, 4242)
+    step_bytes = a.layers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES) + syn.int8_bytes(*syn.HEAD_SHAPE)
+
+    def step():
+        for L in layers:
+            cpu_layer(L, xh, xi)
+        cpu_head(head, xh)
+    # every step is a whole step; the counts are capped so that the run stays within a few minutes
+    warm_budget, timed_budget = 30.0, 150.0
+    t0 = time.perf_counter()
+    step()
+    est = time.perf_counter() - t0
+    warmup = 1
+    while warmup < a.warmup and (warmup + 1) * est <= warm_budget:
+        step()
+        warmup += 1
+    steps = max(1, min(a.steps, int(timed_budget // max(est, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = time.perf_counter() - t0
+    ms = dt / steps * 1e3
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    note = "" if (steps, warmup) == (a.steps, a.warmup) else (
+        f"; {steps} timed / {warmup} warm-up steps of the {a.steps} / {a.warmup} asked, to stay within a few minutes")
+    line = {"metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "n_gpus": a.gpus, "steps": steps,
+            "warmup": warmup, "ms_per_step": round(ms, 1), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "config-1 decode-step projection set (36 x QKV/o/gate_up/down, int4 g128), "
-                                   "CPU dequantise-then-matvec sample", "batch": 1,
-                       "ms_per_step": "extrapolated: the full step's bytes (projections + head) at the sampled "
-                                      "rate; steps = GEMVs in the sample"},
+            "config": {"workload": f"config-1 {a.layers}-layer decode-step projection set (QKV 5120x3072, o "
+                                   "3072x3072, gate_up 16384x3072, down 3072x8192; int4 g128) + config-2 int8 head "
+                                   "16385x3072, batch 1: the reference's CPU path, torch dequantize(q, s, m) @ x.float() "
+                                   "(kernels/int4_gemv.py:27-30, kernels/bench_cuda.py:38) per matrix" + note,
+                       "batch": 1, "bytes_per_step": step_bytes, "threads": threads},
+            "tok_s": round(1e3 / ms, 4),
             "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": desc},
+                             "sample": f"{steps} whole decode steps ({4 * a.layers} int4 GEMVs + the int8 head "
+                                       "each), "
+                                       f"{dt:.1f} s"},
             "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
-def run_tp(a, rank, world, dev):
-    """Tensor-parallel decode step (config 4): every rank holds 1/world of each projection (column-parallel
-    QKV/gate_up, row-parallel o/down, row-split int8 head); per layer one multi-GEMV launch of the rank's
-    shards and one NCCL all-reduce of the 6 KB hidden vector, then the head and an all-gather of the logits."""
-    import rumik_fast_b200 as rb
-    from rumik_fast_b200 import synthetic as syn
-    from rumik_fast_b200.tensor_parallel import TPDecodeStep
-    gen = syn.generator(1234, dev)                    # the same full model on every rank; each keeps its shards
-    layers = []
-    for _ in range(a.layers):
-        full = [syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES]
-        layers.append((full[0], full[1], full[2], full[3]))
-    head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
-    x_h = syn.activations((3072,), gen, dev)
-    x_attn = syn.activations((3072,), gen, dev)
-    x_act = syn.activations((8192,), gen, dev)
-    step = TPDecodeStep(layers, x_attn, x_act, head, rank, world, collective=a.collective)
-    del layers, head
-    torch.cuda.empty_cache()
-    step.h[0].copy_(x_h)
-    g = capture(step)
-    full_bytes = a.layers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES) + syn.int8_bytes(*syn.HEAD_SHAPE)
-    gpu_index = local_gpu_index(dev.index)
-    with ClockSampler(gpu_index) as clk:
-        m0 = clk.mark()
-        ms = timed(g.replay, a.steps, a.warmup, world)
-        m1 = clk.mark()
-    clocks = clk.summary(m0, m1)
-    ms_step = ms / a.steps
-    hx = x_h.cpu().pin_memory()
-    hl = torch.empty(step.logits_all.numel(), dtype=torch.float16).pin_memory()
-
-    def e2e_step():
-        step.h[0].copy_(hx, non_blocking=True)
-        g.replay()
-        hl.copy_(step.logits_all, non_blocking=True)
-    e2e_steps = max(1, a.steps // 2)
-    ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
-    peak, peak_kind = peaks()
-    rank_gbs = step.bytes / (ms_step * 1e-3) / 1e9
-    if rank == 0:
-        gbs = full_bytes / (ms_step * 1e-3) / 1e9
-        line = {
-            "metric": METRIC, "value": round(gbs, 1), "unit": UNIT, "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": "config-4 tensor-parallel decode step: config-1 36-layer projection set + "
-                                   "int8 head sharded over the GPUs (column-parallel QKV/gate_up, row-parallel "
-                                   "o/down), one NCCL all-reduce of the hidden vector per layer, batch 1",
-                       "batch": 1, "bytes_per_step": full_bytes, "parallelism": f"tp{world}",
-                       "launches": "per layer: one multi-GEMV launch + " + (
-                           "one peer-memory reduction kernel" if a.collective == "peer" else "add + NCCL all-reduce")
-                       + "; head + all-gather", "collective": a.collective,
-                       "l2": "no flush: 1.98 GB of weights per step over all ranks > 126 MB L2 per GPU"},
-            "tok_s": round(1e3 / ms_step, 1),
-            "e2e": {"value": round(full_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": UNIT,
-                    "h2d_bytes_per_step": 3072 * 2, "d2h_bytes_per_step": hl.numel() * 2,
-                    "ms_per_step": round(ms_e2e, 5)},
-            "roofline": {"bound": "hbm", "achieved": round(rank_gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(rank_gbs / peak, 4), "peak_kind": peak_kind,
-                         "kernel": "whole tensor-parallel step per rank (GEMVs + all-reduces)", "traffic": None,
-                         "algorithmic_bytes_per_launch": None},
-            "cpu_baseline": None, "clocks": clocks,
-            "gpu_launches": a.steps * (a.layers + 1), "mode": "tp",
-        }
-        print(json.dumps(line), flush=True)
-    del g
-    torch.cuda.synchronize()
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-    step.close()
-    return 0
-
-
-def local_gpu_index(local):
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    if vis.replace(",", "").isdigit():
-        return int(vis.split(",")[local])
-    return local
-
-
-def run_ours(a):
-    import rumik_fast_b200 as rb
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    rb.set_weight_prefetch(not a.no_prefetch)
-    if a.parallel == "tp":
-        rc = run_tp(a, rank, world, dev)
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-            dist.destroy_process_group()
-        return rc
-    if a.scales == "8bit" and a.mode != "set":
-        raise SystemExit("--scales 8bit runs on the projection-set kernel (--mode set)")
-    w = build_workload(dev, seed=1234 + rank, nlayers=a.layers, scales=a.scales)
-    step = step_fn(w, a.mode)
-    g_step = capture(step)
-    g_int4 = capture(step_fn(w, a.mode, with_head=False))
-    step_bytes = w["int4_bytes"] + w["head_bytes"]
-    gpu_index = local_gpu_index(local)
-
-    with ClockSampler(gpu_index) as clk:
-        m0 = clk.mark()
-        ms = timed(g_step.replay, a.steps, a.warmup, world)
-        m1 = clk.mark()
-    clocks = clk.summary(m0, m1)
-    ms_step = ms / a.steps
-
-    # dominant kernel: the int4 projections (97 % of the step's bytes), timed alone over the same steps
-    ms4 = timed(g_int4.replay, max(1, a.steps // 2), a.warmup, world) / max(1, a.steps // 2)
-    launches4 = 1 if a.mode == "set" else a.layers * 4
-    achieved = (w["int4_bytes"] / launches4) / (ms4 / launches4 * 1e-3) / 1e9
-    peak, peak_kind = peaks()
-
-    # end to end through the public API: pinned host inputs -> device, step, logits -> pinned host
-    hx, hi = w["xh"].cpu().pin_memory(), w["xi"].cpu().pin_memory()
-    hl = torch.empty_like(w["logits"], device="cpu").pin_memory()
-
-    def e2e_step():
-        w["xh"].copy_(hx, non_blocking=True)
-        w["xi"].copy_(hi, non_blocking=True)
-        g_step.replay()
-        hl.copy_(w["logits"], non_blocking=True)
-    e2e_steps = max(1, a.steps // 2)
-    ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
-
-    line = None
-    if rank == 0:
-        gbs = world * step_bytes / (ms_step * 1e-3) / 1e9
-        cpu = None
-        if world == 1 and a.cpu_seconds > 0:
-            c_gbs, c_threads, c_desc, _ = cpu_oracle_sample(a.cpu_seconds)
-            cpu = {"value": round(c_gbs, 3), "unit": UNIT, "cores": c_threads, "kind": "port", "sample": c_desc}
-        line = {
-            "metric": METRIC, "value": round(gbs, 1), "unit": UNIT, "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": "config-1 36-layer decode-step projection set (QKV 5120x3072, o 3072x3072, "
-                                   "gate_up 16384x3072, down 3072x8192; int4 g128) + config-2 int8 head "
-                                   "16385x3072, batch 1, in one CUDA graph",
-                       "launches": "144 projections in one persistent launch + the head" if a.mode == "set"
-                       else "145 stream-ordered launches",
-                       "batch": 1, "bytes_per_step": step_bytes, "parallelism": f"replica x{world}",
-                       "weight_prefetch": not a.no_prefetch,
-                       "l2": "no flush: 1.98 GB of weights per step > 126 MB L2",
-                       "scales": "fp16 scale + min per group (the reference format)" if a.scales == "fp16" else
-                       "8-bit double-quantised scales (rumik_fast_b200.scales8): 2 bytes per group + 4 per row"},
-            "tok_s": round(world * 1e3 / ms_step, 1),
-            "pct_of_peak": round(100 * gbs / world / peak, 1),
-            "e2e": {"value": round(world * step_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": UNIT,
-                    "h2d_bytes_per_step": (3072 + 8192) * 2, "d2h_bytes_per_step": w["logits"].numel() * 2,
-                    "ms_per_step": round(ms_e2e, 5)},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "kernel": "gemv_int4_tc_kernel" if a.mode == "set" else "gemv_int4_kernel",
-                         "traffic": NCU_TRAFFIC_PER_LAUNCH if a.mode == "set" and a.layers == LAYERS else None,
-                         "algorithmic_bytes_per_launch": w["int4_bytes"] // launches4},
-            "cpu_baseline": cpu,
-            "clocks": clocks,
-            "gpu_launches": a.steps * (launches4 + 1),
-            "mode": a.mode,
-        }
-        print(json.dumps(line), flush=True)
-    del g_step, g_int4
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
-
-
-def run_prefill(a):
-    """Config 3: Y = X W^T for the 36-layer projection set (QKV, o_proj, gate_up, down) with X fp16 [M, K],
-    one mm_int4 call per matrix, replayed from one CUDA graph. value = 2 M sum(N K) / step time."""
-    import rumik_fast_b200 as rb
-    from rumik_fast_b200 import synthetic as syn
-    from rumik_fast_b200.mm_int4 import mm_int4
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    M = a.tokens
-    gen = syn.generator(4321 + rank, dev)
-    layers = [[syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES] for _ in range(a.layers)]
-    xs = {k: syn.activations((M, k), gen, dev) for k in (3072, 8192)}
-    ys = [torch.empty(M, n, device=dev, dtype=torch.float16) for _, n, _ in syn.LAYER_SHAPES]
-
-    def step():
-        for L in layers:
-            for i, ((_, n, k), w) in enumerate(zip(syn.LAYER_SHAPES, L)):
-                mm_int4(xs[k], *w, out=ys[i])
-    g = capture(step)
-    flops = 2 * M * a.layers * sum(n * k for _, n, k in syn.LAYER_SHAPES)
-    wbytes = a.layers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES)
-    with ClockSampler(local_gpu_index(local)) as clk:
-        m0 = clk.mark()
-        ms = timed(g.replay, a.steps, a.warmup, world)
-        m1 = clk.mark()
-    ms_step = ms / a.steps
-    hx = {k: v.cpu().pin_memory() for k, v in xs.items()}
-    hy = torch.empty(ys[0].shape, dtype=torch.float16).pin_memory()
-
-    def e2e_step():
-        for k, v in xs.items():
-            v.copy_(hx[k], non_blocking=True)
-        g.replay()
-        hy.copy_(ys[0], non_blocking=True)
-    e2e_steps = max(1, a.steps // 2)
-    ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
-    bound = "hbm" if M < 64 else "tensor"
-    j = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
-        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
-    if rank == 0:
-        tf = world * flops / (ms_step * 1e-3) / 1e12
-        if bound == "hbm":
-            peak, kind = peaks()
-            achieved, unit = wbytes / (ms_step * 1e-3) / 1e9, "GB/s"
-        else:
-            peak, kind = float(j.get("bf16_tflops", 1590.0)), "measured" if j else "fallback"
-            achieved, unit = flops / (ms_step * 1e-3) / 1e12, "TFLOP/s"
-        line = {
-            "metric": "prefill int4-weight matmul TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s",
-            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": f"config-3 prefill: X fp16 [{M}, K] against the 36-layer projection set "
-                                   "(QKV 5120x3072, o 3072x3072, gate_up 16384x3072, down 3072x8192; int4 g128), "
-                                   "one mm_int4 launch per matrix, in one CUDA graph",
-                       "tokens": M, "flops_per_step": flops, "weight_bytes_per_step": wbytes,
-                       "parallelism": f"replica x{world}", "l2": "no flush: 1.93 GB of weights per step > 126 MB L2"},
-            "e2e": {"value": round(world * flops / (ms_e2e * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": sum(v.numel() * 2 for v in xs.values()),
-                    "d2h_bytes_per_step": hy.numel() * 2, "ms_per_step": round(ms_e2e, 5)},
-            "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": peak, "unit": unit,
-                         "frac": round(achieved / peak, 4), "peak_kind": kind, "kernel": "whole prefill step",
-                         "traffic": None},
-            "cpu_baseline": None, "clocks": clk.summary(m0, m1),
-            "gpu_launches": a.steps * a.layers * 4, "mode": "prefill",
-        }
-        print(json.dumps(line), flush=True)
-    del g
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
-
-
-# ---------------------------------------------------------------------------------------------- full decode step
+# ---------------------------------------------------------------------------------------------- sub-records
 STEP_SHAPE = dict(H=3072, nq=24, nkv=8, hd=128, inter=8192, S=2048, eps=1e-5)
 
 
@@ -623,26 +478,15 @@ def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
                 keep=(layer_in, attn, layer_out, final, head, kc, vc, emb_q, emb_s, sampler, eng))
 
 
-def run_step(a):
-    """The whole decode step (fused glue + attention + head) replayed from one CUDA graph. value = tokens/s
-    (one token per step per GPU, replicas); the roofline is HBM over the step's algorithmic bytes (int4 weights,
-    int8 head, K/V slots read)."""
-    import rumik_fast_b200 as rb
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    rb.set_weight_prefetch(not a.no_prefetch)
-    w = build_step(dev, 777 + rank, a.layers, a.pos, a.attn)
+def measure_step(dev, seed, nlayers, pos, attn_mode, steps, warmup, world, clk=None):
+    """The whole decode step (fused glue + attention + head + sampler) from one CUDA graph, token id in and the
+    drawn token out. Returns the record (tokens/s per GPU and the HBM roofline over the step's bytes)."""
+    w = build_step(dev, seed, nlayers, pos, attn_mode)
     g = capture(w["step"])
-    with ClockSampler(local_gpu_index(local)) as clk:
-        m0 = clk.mark()
-        ms = timed(g.replay, a.steps, a.warmup, world)
-        m1 = clk.mark()
-    ms_step = ms / a.steps
+    m0 = clk.mark() if clk else 0
+    ms = timed(g.replay, steps, warmup, world)
+    m1 = clk.mark() if clk else 0
+    ms_step = ms / steps
     hx = w["tok"].cpu().pin_memory()
     hy = torch.empty(1, dtype=torch.int64).pin_memory()
 
@@ -650,43 +494,335 @@ def run_step(a):
         w["tok"].copy_(hx, non_blocking=True)
         g.replay()
         hy.copy_(w["tok"], non_blocking=True)
+    e2e_steps = max(1, steps // 2)
+    ms_e2e = timed(e2e_step, e2e_steps, warmup, world) / e2e_steps
+    peak, kind, _ = peaks()
+    total = w["wbytes"] + w["kvbytes"]
+    gbs = total / (ms_step * 1e-3) / 1e9
+    rec = {"tok_s": round(world * 1e3 / ms_step, 1), "ms_per_step": round(ms_step, 5), "pos": pos, "layers": nlayers,
+           "attention": attn_mode, "bytes_per_step": total, "weight_bytes": w["wbytes"], "kv_bytes": w["kvbytes"],
+           "hbm_gbs": round(gbs, 1), "roofline_frac": round(gbs / peak, 4), "peak_gbs": peak, "peak_kind": kind,
+           "e2e_tok_s": round(world * 1e3 / ms_e2e, 1), "e2e_h2d_bytes": 8, "e2e_d2h_bytes": 8,
+           "launches_per_step": w["launches"],
+           "clocks": clk.summary(m0, m1) if clk else None,
+           "workload": f"{nlayers}-layer decode step at position {pos}: token id -> int8 embedding row (layer 0's "
+                       "prologue); per layer add_ln + QKV 5120x3072 + gate_up 16384x3072 + rope/KV write/silu*up "
+                       "(one launch), attention 24/8 heads x 128, o_proj 3072x3072 + down 3072x8192; final add_ln "
+                       "+ int8 head 16385x3072; sampler (stop predictor, top-30, Gumbel-max; the drawn token feeds "
+                       "the next step); one CUDA graph"}
+    del g, w
+    free()
+    return rec
+
+
+def measure_prefill(dev, seed, tokens, nlayers, steps, warmup, world, clk=None):
+    """Config 3: Y = X W^T over the 36-layer projection set with X fp16 [M, K], one mm_int4 launch per matrix,
+    replayed from one CUDA graph, for each M in `tokens`. Returns {M: record}."""
+    from rumik_fast_b200 import synthetic as syn
+    from rumik_fast_b200.mm_int4 import mm_int4
+    gen = syn.generator(seed, dev)
+    layers = [[syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES] for _ in range(nlayers)]
+    wbytes = nlayers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES)
+    hbm, hkind, tf_peak = peaks()
+    tf_kind = hkind
+    out = {}
+    for M in tokens:
+        xs = {k: syn.activations((M, k), gen, dev) for k in (3072, 8192)}
+        ys = [torch.empty(M, n, device=dev, dtype=torch.float16) for _, n, _ in syn.LAYER_SHAPES]
+
+        def step():
+            for L in layers:
+                for i, ((_, n, k), w) in enumerate(zip(syn.LAYER_SHAPES, L)):
+                    mm_int4(xs[k], *w, out=ys[i])
+        g = capture(step)
+        m0 = clk.mark() if clk else 0
+        ms = timed(g.replay, steps, warmup, world) / steps
+        m1 = clk.mark() if clk else 0
+        flops = 2 * M * nlayers * sum(n * k for _, n, k in syn.LAYER_SHAPES)
+        tf = flops / (ms * 1e-3) / 1e12
+        gbs = wbytes / (ms * 1e-3) / 1e9
+        bound = "hbm" if M < 64 else "tensor"
+        frac = gbs / hbm if bound == "hbm" else tf / tf_peak
+        out[str(M)] = {"tflops": round(world * tf, 1), "weight_gbs": round(gbs, 1), "ms_per_step": round(ms, 4),
+                       "bound": bound, "roofline_frac": round(frac, 4),
+                       "peak": hbm if bound == "hbm" else tf_peak,
+                       "peak_unit": "GB/s" if bound == "hbm" else "TFLOP/s (bf16 dense, cuBLAS burst)",
+                       "peak_kind": hkind if bound == "hbm" else tf_kind, "flops_per_step": flops,
+                       "launches_per_step": 4 * nlayers, "clocks": clk.summary(m0, m1) if clk else None}
+        del g, xs, ys
+        free()
+    del layers
+    free()
+    return out
+
+
+def measure_c0(dev, seed, steps, warmup, world):
+    """Config 0 the reference's way (kernels/bench_cuda.py:18-32): 36 distinct 8192x3072 int4 GEMVs through
+    gemv_int4_cuda, captured in one CUDA graph; best of 3 rounds of max(steps, 20) replays (CUDA events)."""
+    import rumik_fast_b200 as rb
+    from rumik_fast_b200 import synthetic as syn
+    gen = syn.generator(seed, dev)
+    mats = [syn.int4_weights(8192, 3072, gen, dev) for _ in range(LAYERS)]
+    x = syn.activations((3072,), gen, dev)
+    y = torch.empty(8192, device=dev, dtype=torch.float16)
+    g = capture(lambda: [rb.gemv_int4_cuda(x, *w, out=y) for w in mats])
+    reps = max(steps, 20)
+    best = min(timed(g.replay, reps, warmup if r == 0 else 3, world) / reps for r in range(3))
+    per = best / LAYERS
+    nb = syn.int4_bytes(8192, 3072)
+    hbm, kind, _ = peaks()
+    gbs = nb / (per * 1e-3) / 1e9
+    rec = {"gbs": round(world * gbs, 1), "us_per_gemv": round(per * 1e3, 3), "bytes_per_gemv": nb,
+           "roofline_frac": round(gbs / hbm, 4), "peak_gbs": hbm, "peak_kind": kind,
+           "method": "36 distinct 8192x3072 matrices, one gemv_int4_cuda each, in one CUDA graph; best of 3 rounds "
+                     f"x {reps} replays"}
+    del g, mats
+    free()
+    return rec
+
+
+def measure_chain(w, steps, warmup, world):
+    """The headline step as an unmodified engine issues it: one gemv_int4_cuda per projection + the head."""
+    g = capture(step_fn(w, "chain"))
+    ms = timed(g.replay, steps, warmup, world) / steps
+    hbm, kind, _ = peaks()
+    nb = w["int4_bytes"] + w["head_bytes"]
+    gbs = nb / (ms * 1e-3) / 1e9
+    rec = {"gbs": round(world * gbs, 1), "ms_per_step": round(ms, 5), "launches_per_step": 4 * len(w["layers"]) + 1,
+           "roofline_frac": round(gbs / hbm, 4)}
+    del g
+    free()
+    return rec
+
+
+# ---------------------------------------------------------------------------------------------- arms
+def run_tp(a, rank, world, dev):
+    """Tensor-parallel decode step (config 4): every rank holds 1/world of each projection (column-parallel
+    QKV/gate_up, row-parallel o/down, row-split int8 head); per layer one multi-GEMV launch of the rank's
+    shards and one NCCL all-reduce of the 6 KB hidden vector, then the head and an all-gather of the logits."""
+    from rumik_fast_b200 import synthetic as syn
+    from rumik_fast_b200.tensor_parallel import TPDecodeStep
+    gen = syn.generator(1234, dev)                    # the same full model on every rank; each keeps its shards
+    layers = []
+    for _ in range(a.layers):
+        full = [syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES]
+        layers.append((full[0], full[1], full[2], full[3]))
+    head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
+    x_h = syn.activations((3072,), gen, dev)
+    x_attn = syn.activations((3072,), gen, dev)
+    x_act = syn.activations((8192,), gen, dev)
+    step = TPDecodeStep(layers, x_attn, x_act, head, rank, world, collective=a.collective)
+    del layers, head
+    torch.cuda.empty_cache()
+    step.h[0].copy_(x_h)
+    g = capture(step)
+    full_bytes = a.layers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES) + syn.int8_bytes(*syn.HEAD_SHAPE)
+    with ClockSampler(dev) as clk:
+        m0 = clk.mark()
+        ms = timed(g.replay, a.steps, a.warmup, world)
+        m1 = clk.mark()
+    clocks = clk.summary(m0, m1)
+    ms_step = ms / a.steps
+    hx = x_h.cpu().pin_memory()
+    hl = torch.empty(step.logits_all.numel(), dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        step.h[0].copy_(hx, non_blocking=True)
+        g.replay()
+        hl.copy_(step.logits_all, non_blocking=True)
     e2e_steps = max(1, a.steps // 2)
     ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
+    peak, peak_kind, _ = peaks()
+    rank_gbs = step.bytes / (ms_step * 1e-3) / 1e9
     if rank == 0:
-        peak, kind = peaks()
-        total = w["wbytes"] + w["kvbytes"]
-        gbs = total / (ms_step * 1e-3) / 1e9
+        gbs = full_bytes / (ms_step * 1e-3) / 1e9
         line = {
-            "metric": "full decode step tok/s", "value": round(world * 1e3 / ms_step, 1), "unit": "tok/s",
-            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"attention": a.attn,
-                       "workload": f"{a.layers}-layer decode step at position {a.pos}: token id -> int8 embedding row "
-                                   "(layer 0's prologue); per layer add_ln + QKV "
-                                   "5120x3072 + gate_up 16384x3072 + rope/KV write/silu*up (one launch), attention "
-                                   "24/8 heads x 128 with o_proj 3072x3072 + down 3072x8192 ("
-                                   + ("one launch" if a.attn == "fused" else "two launches") +
-                                   "); final add_ln + int8 head 16385x3072; sampler (stop predictor, top-30, "
-                                   "Gumbel-max; the drawn token feeds the next step); one CUDA graph",
-                       "pos": a.pos, "bytes_per_step": total, "weight_bytes": w["wbytes"], "kv_bytes": w["kvbytes"],
-                       "parallelism": f"replica x{world}", "weight_prefetch": not a.no_prefetch,
-                       "l2": "no flush: 2.0 GB of weights per step > 126 MB L2"},
-            "hbm_gbs": round(gbs, 1),
-            "e2e": {"value": round(world * 1e3 / ms_e2e, 1), "unit": "tok/s",
-                    "h2d_bytes_per_step": hx.numel() * 8, "d2h_bytes_per_step": hy.numel() * 8,
+            "metric": METRIC, "value": round(gbs, 1), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "config-4 tensor-parallel decode step: config-1 36-layer projection set + "
+                                   "int8 head sharded over the GPUs (column-parallel QKV/gate_up, row-parallel "
+                                   "o/down), one NCCL all-reduce of the hidden vector per layer, batch 1",
+                       "batch": 1, "bytes_per_step": full_bytes, "parallelism": f"tp{world}",
+                       "launches": "per layer: one multi-GEMV launch + " + (
+                           "one peer-memory reduction kernel" if a.collective == "peer" else "add + NCCL all-reduce")
+                       + "; head + all-gather", "collective": a.collective,
+                       "l2": "no flush: 1.98 GB of weights per step over all ranks > 126 MB L2 per GPU"},
+            "tok_s": round(1e3 / ms_step, 1),
+            "e2e": {"value": round(full_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": UNIT,
+                    "h2d_bytes_per_step": 3072 * 2, "d2h_bytes_per_step": hl.numel() * 2,
                     "ms_per_step": round(ms_e2e, 5)},
-            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 4), "peak_kind": kind, "kernel": "whole decode step",
-                         "traffic": None},
-            "cpu_baseline": None, "clocks": clk.summary(m0, m1),
-            "gpu_launches": a.steps * w["launches"], "mode": "step",
+            "roofline": {"bound": "hbm", "achieved": round(rank_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(rank_gbs / peak, 4), "peak_kind": peak_kind,
+                         "kernel": "whole tensor-parallel step per rank (GEMVs + all-reduces)", "traffic": None,
+                         "algorithmic_bytes_per_launch": None},
+            "cpu_baseline": None, "clocks": clocks,
+            "gpu_launches": a.steps * (a.layers + 1), "mode": "tp",
         }
         print(json.dumps(line), flush=True)
     del g
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    step.close()
+    return 0
+
+
+def init_dist(dev, world):
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+
+def end_dist(world):
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_ours(a):
+    import rumik_fast_b200 as rb
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    init_dist(dev, world)
+    rb.set_weight_prefetch(not a.no_prefetch)
+    if a.parallel == "tp":
+        rc = run_tp(a, rank, world, dev)
+        end_dist(world)
+        return rc
+    if a.scales == "8bit" and a.mode != "set":
+        raise SystemExit("--scales 8bit runs on the projection-set kernel (--mode set)")
+    w = build_workload(dev, seed=1234 + rank, nlayers=a.layers, scales=a.scales)
+    g_step = capture(step_fn(w, a.mode))
+    g_int4 = capture(step_fn(w, a.mode, with_head=False))
+    int4_bytes = w["int4_bytes"]
+    step_bytes = int4_bytes + w["head_bytes"]
+    logits_bytes = w["logits"].numel() * 2
+
+    with ClockSampler(dev) as clk:
+        m0 = clk.mark()
+        ms = timed(g_step.replay, a.steps, a.warmup, world)
+        m1 = clk.mark()
+        ms_step = ms / a.steps
+
+        # dominant kernel: the int4 projections (97 % of the step's bytes), timed alone over the same steps
+        ms4 = timed(g_int4.replay, max(1, a.steps // 2), a.warmup, world) / max(1, a.steps // 2)
+        launches4 = 1 if a.mode == "set" else a.layers * 4
+        achieved = (int4_bytes / launches4) / (ms4 / launches4 * 1e-3) / 1e9
+        peak, peak_kind, _ = peaks()
+
+        # end to end through the public API: pinned host inputs -> device, step, logits -> pinned host
+        hx, hi = w["xh"].cpu().pin_memory(), w["xi"].cpu().pin_memory()
+        hl = torch.empty_like(w["logits"], device="cpu").pin_memory()
+
+        def e2e_step():
+            w["xh"].copy_(hx, non_blocking=True)
+            w["xi"].copy_(hi, non_blocking=True)
+            g_step.replay()
+            hl.copy_(w["logits"], non_blocking=True)
+        e2e_steps = max(1, a.steps // 2)
+        ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
+        del g_step, g_int4, e2e_step
+        free()
+
+        extras = {}
+        if not a.no_extras and a.layers == LAYERS and a.scales == "fp16" and a.mode == "set":
+            extras["chain"] = measure_chain(w, a.steps, a.warmup, world)
+            del w
+            free()
+            extras["gemv_c0"] = measure_c0(dev, 5 + rank, a.steps, a.warmup, world)
+            extras["step"] = measure_step(dev, 777 + rank, LAYERS, 511, "separate", a.steps, a.warmup, world, clk)
+            extras["prefill"] = measure_prefill(dev, 4321 + rank, PREFILL_TOKENS, LAYERS, a.steps, a.warmup, world,
+                                                clk)
+    clocks = clk.summary(m0, m1)
+
+    if rank == 0:
+        gbs = world * step_bytes / (ms_step * 1e-3) / 1e9
+        cpu = cpu_baseline_sample(a.cpu_seconds) if world == 1 and a.cpu_seconds > 0 else None
+        line = {
+            "metric": METRIC, "value": round(gbs, 1), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "config-1 36-layer decode-step projection set (QKV 5120x3072, o 3072x3072, "
+                                   "gate_up 16384x3072, down 3072x8192; int4 g128) + config-2 int8 head "
+                                   "16385x3072, batch 1, in one CUDA graph",
+                       "launches": "144 projections in one persistent launch + the head" if a.mode == "set"
+                       else "145 stream-ordered launches",
+                       "batch": 1, "bytes_per_step": step_bytes, "parallelism": f"replica x{world}",
+                       "weight_prefetch": not a.no_prefetch,
+                       "l2": "no flush: 1.98 GB of weights per step > 126 MB L2",
+                       "scales": "fp16 scale + min per group (the reference format)" if a.scales == "fp16" else
+                       "8-bit double-quantised scales (rumik_fast_b200.scales8): 2 bytes per group + 4 per row"},
+            "tok_s": extras["step"]["tok_s"] if "step" in extras else None,
+            "tok_s_independent_set": round(world * 1e3 / ms_step, 1),
+            "pct_of_peak": round(100 * gbs / world / peak, 1),
+            "e2e": {"value": round(world * step_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": UNIT,
+                    "h2d_bytes_per_step": (3072 + 8192) * 2, "d2h_bytes_per_step": logits_bytes,
+                    "ms_per_step": round(ms_e2e, 5)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "kernel": "gemv_int4_tc_kernel" if a.mode == "set" else "gemv_int4_kernel",
+                         "traffic": NCU_TRAFFIC_PER_LAUNCH if a.mode == "set" and a.layers == LAYERS else None,
+                         "algorithmic_bytes_per_launch": int4_bytes // launches4},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": a.steps * (launches4 + 1),
+            "mode": a.mode,
+        }
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    end_dist(world)
+    return 0
+
+
+def run_prefill(a):
+    """Config 3 alone (--workload prefill --tokens M): the prefill record as the line's value."""
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    init_dist(dev, world)
+    M = a.tokens
+    with ClockSampler(dev) as clk:
+        rec = measure_prefill(dev, 4321 + rank, (M,), a.layers, a.steps, a.warmup, world, clk)[str(M)]
+    if rank == 0:
+        line = {"metric": "prefill int4-weight matmul TFLOP/s", "value": rec["tflops"], "unit": "TFLOP/s",
+                "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": rec["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+                "data": "synthetic",
+                "config": {"workload": f"config-3 prefill: X fp16 [{M}, K] against the {a.layers}-layer projection "
+                                       "set, one mm_int4 launch per matrix, in one CUDA graph", "tokens": M,
+                           "parallelism": f"replica x{world}", "l2": "no flush: weights per step > 126 MB L2"},
+                "prefill": rec, "clocks": rec["clocks"], "gpu_launches": a.steps * rec["launches_per_step"],
+                "mode": "prefill"}
+        print(json.dumps(line), flush=True)
+    end_dist(world)
+    return 0
+
+
+def run_step(a):
+    """The full decode step alone (--workload step): the step record as the line's value."""
+    import rumik_fast_b200 as rb
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    init_dist(dev, world)
+    rb.set_weight_prefetch(not a.no_prefetch)
+    with ClockSampler(dev) as clk:
+        rec = measure_step(dev, 777 + rank, a.layers, a.pos, a.attn, a.steps, a.warmup, world, clk)
+    if rank == 0:
+        line = {"metric": "full decode step tok/s", "value": rec["tok_s"], "unit": "tok/s", "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": rec["ms_per_step"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+                "config": {"workload": rec["workload"], "pos": a.pos, "parallelism": f"replica x{world}",
+                           "l2": "no flush: 2.0 GB of weights per step > 126 MB L2"},
+                "step": rec, "clocks": rec["clocks"], "gpu_launches": a.steps * rec["launches_per_step"],
+                "mode": "step"}
+        print(json.dumps(line), flush=True)
+    end_dist(world)
     return 0
 
 

@@ -83,7 +83,8 @@ int rb_gemv_int4(const void* x, int x_dtype, int64_t ldx,
  * Python wrapper gemv_int8_cuda (:245-249) calls this. s_dtype RB_F32 (engine) or RB_F16 (configs).
  *   N >= 1 (no padding to 16 required), K % 64 == 0, 64 <= K <= 16384, 1 <= batch <= 16
  * Batch 1 with K % 128 == 0 runs on the tcgen05 tensor cores (the codes are the 8-bit A operand, x is
- * quantised once to 16-bit integers, delta = max|x| / 32639); other shapes on the warp-level MMA kernel.
+ * quantised per 128-column group to 16-bit integers, delta_g = max_g|x| / 32639, each group's integer dot
+ * product combined exactly in int32); other shapes on the warp-level MMA kernel.
  */
 int rb_gemv_int8(const void* x, int x_dtype, int64_t ldx,
                  const uint8_t* q, int q_signed, const void* s, int s_dtype,
@@ -94,7 +95,11 @@ int rb_gemv_int8(const void* x, int x_dtype, int64_t ldx,
  * int4-weight matrix product (prefill) on tcgen05 tensor cores:  Y[t, n] = sum_k X[t, k] * w[n, k].
  * Replaces mm_int4(x, q, s, m) (kernels/mm_int4.py:59-73) and its Triton kernel _mm_int4 (:24-46).
  *   X [M, K] fp16 or bf16, row stride ldx;  Y [M, N] fp16 or bf16, row stride ldy.
- *   The weights are dequantised to fp16 in shared memory (never stored wider than int4 in HBM).
+ *   Each 128-row weight block is dequantised per group to fp16 straight into tensor memory, the A operand of
+ *   tcgen05.mma.kind::f16 (the weights never exist wider than int4 in HBM or shared memory); X tiles arrive by
+ *   TMA and a bf16 X is converted to fp16 in shared memory (exact for |x| <= 65504). fp32 accumulation.
+ *   M == 1 is a GEMV and runs as rb_gemv_int4. This entry point never splits K (no workspace); see
+ *   rb_mm_int4_ws and rb_mm_int4_static for the split that fills idle SMs on calls with few tiles.
  *   M >= 1, N >= 1, K % 128 == 0.
  */
 int rb_mm_int4(const void* X, int x_dtype, int64_t ldx,
@@ -117,7 +122,9 @@ int64_t rb_mm_int4_workspace(int64_t M, int64_t N, int64_t K);
  * nothing. Returns RB_ERR_SHAPE when the split it would use needs more than 8 MiB
  * (rb_mm_int4_workspace(M, N, K) > 8 MiB); nothing in the scratch needs to start at zero. The scratch is one
  * per device and shared by every call: calls that overlap in time (on two streams, or otherwise not ordered
- * one after the other) race on it. Consecutive calls on one stream are safe.
+ * one after the other) race on it. Consecutive calls on one stream are safe. The scratch's device address is
+ * looked up (cudaGetSymbolAddress) on the first call that splits on each device and kept for the life of the
+ * process: do not use this entry point across a cudaDeviceReset of that device.
  */
 int rb_mm_int4_static(const void* X, int x_dtype, int64_t ldx,
                       const uint8_t* q, const uint16_t* s, const uint16_t* m,

@@ -70,7 +70,6 @@ int rb_gemv_int4(const void* x, int x_dtype, int64_t ldx, const uint8_t* q, cons
   a.q = q; a.s = s; a.m = m;
   a.y = y; a.y_dtype = y_dtype; a.ldy = batch > 1 ? ldy : N;
   a.N = N; a.K = K; a.batch = batch; a.flags = flags;
-#ifndef RB_MULTI_LEGACY
   // batch 1 with at least one 128-row block per SM: the tensor-core kernel (a one-entry list). Smaller
   // matrices keep the warp-MMA kernel, which spreads 8-row stages over every SM.
   if (batch == 1 && N >= static_cast<int64_t>(sms) * 128) {
@@ -79,7 +78,6 @@ int rb_gemv_int4(const void* x, int x_dtype, int64_t ldx, const uint8_t* q, cons
     if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
     return st;
   }
-#endif
   st = rb::launch_gemv_int4(a, sms, static_cast<cudaStream_t>(stream));
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
@@ -103,13 +101,9 @@ int rb_gemv_int8(const void* x, int x_dtype, int64_t ldx, const uint8_t* q, int 
   a.q = q; a.q_signed = q_signed; a.s_row = s; a.s_dtype = s_dtype;
   a.y = y; a.y_dtype = y_dtype; a.ldy = batch > 1 ? ldy : N;
   a.N = N; a.K = K; a.batch = batch; a.flags = flags;
-#ifdef RB_INT8_LEGACY  // the warp-MMA kernel for every call (comparison builds)
-  st = rb::launch_gemv_int8(a, sms, static_cast<cudaStream_t>(stream));
-#else
   // batch 1 with K % 128 == 0 runs on the tensor cores; other shapes on the warp-MMA kernel
   st = rb::launch_gemv_int8_tc(a, sms, static_cast<cudaStream_t>(stream));
   if (st == RB_ERR_SHAPE) st = rb::launch_gemv_int8(a, sms, static_cast<cudaStream_t>(stream));
-#endif
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
 }
@@ -150,19 +144,12 @@ static bool kernel_ok(const rb_gemv_desc* d, int count, int flags) {
 }
 
 static bool small_list(const rb_gemv_desc* d, int count, int flags) {
-#ifdef RB_MULTI_LEGACY  // comparison builds: every list on the warp-MMA kernel
-  (void)d;
-  (void)count;
-  (void)flags;
-  return true;
-#else
   if (flags & RB_FLAG_KERNEL_TC) return false;
   if (any_scales8(d, count)) return false;  // 8-bit scales: the tcgen05 kernel only (kernel_ok refuses MMA)
   if (flags & RB_FLAG_KERNEL_MMA) return true;
   int64_t bytes = 0;
   for (int i = 0; i < count; ++i) bytes += d[i].N * (d[i].K / 2);
   return bytes < RB_SMALL_LIST_BYTES;
-#endif
 }
 
 static int multi_impl(const rb_gemv_desc* descs, int count, void* ws, int64_t ws_bytes, int x_dtype, int y_dtype,
@@ -412,11 +399,7 @@ static int mm_int4_impl(const void* X, int x_dtype, int64_t ldx, const uint8_t* 
     if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
     return st;
   }
-#ifdef RB_MM_LEGACY  // dequantisation into shared memory, one CTA per tile (comparison builds)
-  st = rb::launch_mm_int4(a, sms, static_cast<cudaStream_t>(stream));
-#else
   st = rb::launch_mm_int4_tc(a, sms, static_cast<cudaStream_t>(stream));
-#endif
   if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
   return st;
 }

@@ -24,6 +24,7 @@
 // 2e-5 of the group's largest activation); the weights are used exactly. All mbarrier waits are bounded;
 // no multicast, no clusters.
 #include "common.cuh"
+#include "tc.cuh"
 #include "glue.cuh"
 #include "kernels.h"
 

@@ -5,15 +5,19 @@
 // kernels/cuda_gemv.py:234-242) or (int8)q for signed storage.
 //
 // The codes are already 8-bit integers, so they are the A operand of tcgen05.mma.kind::i8 as they arrive:
-//  * warp 0 streams 128-row x 128-column tiles of q with 2-D TMA (128-byte swizzle, 16 KB) into a ring;
-//  * warp 1 issues four tcgen05.mma (M=128, N=8, K=32) per tile straight from shared memory, accumulating a
-//    whole row block in tensor memory (int32, exact), and frees each tile with tcgen05.commit;
-//  * x is quantised once per CTA to 16-bit integers xi = rint(x / delta), delta = max|x| / 32639, split into
-//    signed high and low bytes (B rows 0 and 1, as in gemv_int4_tc.cu);
-//  * four warps read the row's two accumulator columns and write
-//    y = s * delta * (256 * D0 + D1 - 128 * sum(xi))  (the last term only for uint8 storage).
+//  * warp 0 streams 128-row x 128-column tiles of q (one 128-column group each) with 2-D TMA (128-byte swizzle,
+//    16 KB) into a ring;
+//  * warp 1 issues four tcgen05.mma (M=128, N=8, K=32) per tile straight from shared memory into one of kDBufs
+//    int32 accumulators in tensor memory (one per group, exact), frees the tile with tcgen05.commit and signals
+//    the accumulator with another;
+//  * x is quantised per 128-column group g to 16-bit integers xi = rint(x / delta_g), delta_g = max_g|x| / 32639,
+//    split into signed high and low bytes (B rows 0 and 1): an outlier channel coarsens only its own group;
+//  * four warps (thread = row) read each group's two accumulator columns and add
+//    delta_g * (256 * D0 + D1 - 128 * sum_g(xi)) (the last term only for uint8 storage), combined in int32 so
+//    that both storages give the same bits; y = s * sum.
 // No dequantisation instruction runs at all; the kernel is a pure HBM stream. All waits are bounded.
 #include "common.cuh"
+#include "tc.cuh"
 #include "kernels.h"
 
 namespace rb {
@@ -25,7 +29,8 @@ constexpr int kThreads = 6 * 32;          // producer, MMA issuer, four epilogue
 constexpr uint32_t kStageBytes = kRows * 128;
 constexpr int kMaxStages = 12;  // ring depth: as many 16 KB stages as fit beside the activation table (K <= 8192: 12)
 constexpr uint32_t kXPad = 256;
-constexpr uint32_t kTmemCols = 32;        // two 8-column int32 accumulators
+constexpr int kDBufs = 8;                 // per-group accumulators in flight between the MMA issuer and epilogue
+constexpr uint32_t kTmemCols = 64;        // kDBufs x 8 int32 columns
 
 struct __align__(64) H8Params {
   CUtensorMap qmap;                       // [N rows, K bytes], box 128 x 128, 128-byte swizzle
@@ -33,7 +38,7 @@ struct __align__(64) H8Params {
   const void* s;
   void* y;
   int N, K, nblocks, x_bf16, y_bf16, s_f16, q_signed, prefetch, nst;
-  uint32_t xs_off, bar_off, idesc;
+  uint32_t xs_off, cst_off, bar_off, idesc;
 };
 
 __device__ __forceinline__ void umma_ss_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
@@ -53,20 +58,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int8_tc_kernel(const __grid_
   const int nlocal = (p.nblocks - cta + C - 1) / C;
   const int nk = p.K / 128;
   const int nst = p.nst;  // ring depth of this launch
-  uint8_t* xs = smem + p.xs_off;  // [K/16][32]: 16 high bytes, 16 low bytes per 16 columns; then reductions
+  uint8_t* xs = smem + p.xs_off;  // [K/16][32]: 16 high bytes, 16 low bytes per 16 columns
+  int2* cst = reinterpret_cast<int2*>(smem + p.cst_off);  // per group: {delta_g bits, sum_g(xi)}
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   uint64_t* full = bars;
   uint64_t* empty = bars + nst;
-  uint64_t* dready = bars + 2 * nst;  // [2]
-  uint64_t* dfree = dready + 2;           // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfree + 2);
-  float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [4] per-warp maxima, [4] per-warp integer sums
+  uint64_t* dready = bars + 2 * nst;       // [kDBufs]
+  uint64_t* dfree = dready + kDBufs;       // [kDBufs]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfree + kDBufs);
   if (tid == 0) {
     for (int i = 0; i < nst; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kDBufs; ++b) {
       mbar_init(&dready[b], 1);
       mbar_init(&dfree[b], 4);
     }
@@ -110,15 +115,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int8_tc_kernel(const __grid_
     if (lane == 0) {
       mm4::tc_fence_after();
       const uint32_t xtab = smem_u32(xs);
-      int used = 0;
+      int u = 0;  // groups issued by this CTA: tile u % nst, accumulator u % kDBufs
       bool ok = true;
       for (int j = 0; j < nlocal && ok; ++j) {
-        const int b = j & 1;
-        if (j >= 2 && !mbar_wait(&dfree[b], ((j >> 1) - 1) & 1, ERR_TC_WAIT)) break;
-        mm4::tc_fence_after();
-        for (int k = 0; k < nk; ++k, ++used) {
-          const int slot = used % nst;
-          if (!mbar_wait(&full[slot], (used / nst) & 1, ERR_TC_WAIT)) {
+        for (int k = 0; k < nk; ++k, ++u) {
+          const int slot = u % nst, d = u % kDBufs;
+          if (u >= kDBufs && !mbar_wait(&dfree[d], ((u / kDBufs) - 1) & 1, ERR_TC_WAIT)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&full[slot], (u / nst) & 1, ERR_TC_WAIT)) {
             ok = false;
             break;
           }
@@ -126,81 +132,84 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int8_tc_kernel(const __grid_
           const uint32_t a_base = smem_u32(smem + static_cast<size_t>(slot) * kStageBytes);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            umma_ss_i8(tmem + b * 8, mm4::sw128_desc(a_base + 32 * i), g4t::x_desc<32>(xtab + k * 256 + 64 * i),
-                       p.idesc, (k | i) != 0);
+            umma_ss_i8(tmem + d * 8, mm4::sw128_desc(a_base + 32 * i), g4t::x_desc<32>(xtab + k * 256 + 64 * i),
+                       p.idesc, i != 0);
           mm4::umma_commit(&empty[slot]);  // the tile may be refilled once these MMAs have read it
+          mm4::umma_commit(&dready[d]);    // and the group's accumulator read
         }
-        if (ok) mm4::umma_commit(&dready[b]);
       }
     }
   } else {
     // ---------------- activation table, then epilogue ----------------
     const int et = tid - 64;  // 0..127
     griddep_wait();           // x may come from the previous kernel; y is written below
-    // delta = max|x| / 32639 over the whole vector
-    float mx = 0.f;
-    for (int k = et * 8; k < p.K; k += 128 * 8) {
-      __half h[8];
-      load8_as_half(static_cast<const uint8_t*>(p.x) + static_cast<int64_t>(k) * 2, p.x_bf16, h);
+    // chunk c = 8 columns; the 16 chunks of a group sit on 16 consecutive lanes (reduced with shuffles)
+    const int nchunks = p.K / 8;
+    for (int base = 0; base < nchunks; base += 128) {
+      const int c = base + et;
+      const bool valid = c < nchunks;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (valid) load8_f32(static_cast<const uint8_t*>(p.x) + static_cast<int64_t>(c) * 16, p.x_bf16, v);
+      float mx = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(__half2float(h[i])));
-    }
+      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[i]));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[warp - 2] = mx;
-    named_bar_sync(2, 128);
-    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    const float delta = mx > 0.f ? mx / 32639.f : 1.f;
-    const float inv = 1.f / delta;
-    int isum = 0;
-    for (int k = et * 8; k < p.K; k += 128 * 8) {
-      __half h[8];
-      load8_as_half(static_cast<const uint8_t*>(p.x) + static_cast<int64_t>(k) * 2, p.x_bf16, h);
+      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float delta = mx > 0.f ? mx / 32639.f : 1.f;
+      const float inv = 1.f / delta;
+      int isum = 0;
       uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int xi = __float2int_rn(fminf(fmaxf(__half2float(h[i]) * inv, -32639.f), 32639.f));
+        const int xi = __float2int_rn(fminf(fmaxf(v[i] * inv, -32639.f), 32639.f));
         isum += xi;
         const int l = ((xi + 128) & 255) - 128;
         const int hh = (xi - l) >> 8;
         hi[i >> 2] |= (static_cast<uint32_t>(hh) & 255u) << (8 * (i & 3));
         lo[i >> 2] |= (static_cast<uint32_t>(l) & 255u) << (8 * (i & 3));
       }
-      uint8_t* dst = xs + (k >> 4) * 32 + (k & 8);
-      *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], hi[1]);
-      *reinterpret_cast<uint2*>(dst + 16) = make_uint2(lo[0], lo[1]);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
+      if (valid) {
+        uint8_t* dst = xs + (c >> 1) * 32 + (c & 1) * 8;
+        *reinterpret_cast<uint2*>(dst) = make_uint2(hi[0], hi[1]);
+        *reinterpret_cast<uint2*>(dst + 16) = make_uint2(lo[0], lo[1]);
+        if ((c & 15) == 0) cst[c >> 4] = make_int2(__float_as_int(delta), isum);
+      }
     }
     for (int i = et; i < static_cast<int>(kXPad / 16); i += 128)
       reinterpret_cast<uint4*>(xs + (p.K / 16) * 32)[i] = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
-    named_bar_sync(2, 128);  // everyone has read red[] (the maxima) before it is reused
-    if (lane == 0) reinterpret_cast<int*>(red)[warp - 2] = isum;
     fence_proxy_async_smem();  // generic writes of the table -> visible to the tensor core
     named_bar_sync(1, 5 * 32);
-    const int* ired = reinterpret_cast<const int*>(red);
-    const float offset = p.q_signed ? 0.f : 128.f * static_cast<float>(ired[0] + ired[1] + ired[2] + ired[3]);
     const int quad = warp & 3;
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const int off_mul = p.q_signed ? 0 : 128;
     bool ok = true;
-    for (int j = 0; j < nlocal; ++j) {
-      const int b = j & 1;
-      if (ok) ok = mbar_wait(&dready[b], (j >> 1) & 1, ERR_TC_WAIT);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      mm4::tc_fence_after();
-      int dh, dl;
-      g4t::tmem_ld2(tq + b * 8, dh, dl);
-      g4t::tmem_wait_ld(dh, dl);
-      mm4::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&dfree[b]);
+    int u = 0;
+    for (int j = 0; j < nlocal && ok; ++j) {
+      float acc = 0.f;
+      for (int k = 0; k < nk; ++k, ++u) {
+        const int d = u % kDBufs;
+        if (ok) ok = mbar_wait(&dready[d], (u / kDBufs) & 1, ERR_TC_WAIT);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        mm4::tc_fence_after();
+        int dh, dl;
+        g4t::tmem_ld2(tq + d * 8, dh, dl);
+        g4t::tmem_wait_ld(dh, dl);
+        mm4::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dfree[d]);
+        const int2 cg = cst[k];
+        // sum over the group of v(q) * xi, exact in int32 (|value| <= 128 * 255 * 32639 < 2^31)
+        const int t = dh * 256 + dl - off_mul * cg.y;
+        acc = fmaf(__int_as_float(cg.x), static_cast<float>(t), acc);
+      }
       const int row = (cta + j * C) * kRows + quad * 32 + lane;
-      if (row < p.N) {
+      if (ok && row < p.N) {
         const float sr = p.s_f16 ? __half2float(reinterpret_cast<const __half*>(p.s)[row])
                                  : reinterpret_cast<const float*>(p.s)[row];
-        const float v = sr * delta * ((256.f * static_cast<float>(dh) + static_cast<float>(dl)) - offset);
-        store_out(p.y, row, v, p.y_bf16);
+        store_out(p.y, row, sr * acc, p.y_bf16);
       }
     }
   }
@@ -246,12 +255,14 @@ int launch_gemv_int8_tc(const GemvArgs& a, int num_sms, cudaStream_t stream) {
             ((static_cast<uint32_t>(kRows) >> 4) << 24);
   constexpr uint32_t kSmemMax = 227 * 1024;
   const uint32_t xbytes = static_cast<uint32_t>(a.K / 16) * 32 + kXPad;
-  const uint32_t fixed = 1024 + xbytes + 16 + (2 * kMaxStages + 4) * 8 + 16 + 32;
+  const uint32_t cbytes = static_cast<uint32_t>(a.K / 128) * 8;
+  const uint32_t fixed = 1024 + xbytes + cbytes + 32 + (2 * kMaxStages + 2 * kDBufs) * 8 + 16;
   p.nst = std::min(kMaxStages, static_cast<int>((kSmemMax - std::min(fixed, kSmemMax)) / kStageBytes));
   if (p.nst < 2) return RB_ERR_SHAPE;
   p.xs_off = static_cast<uint32_t>(p.nst) * kStageBytes;
-  p.bar_off = (p.xs_off + xbytes + 15) & ~15u;
-  const uint32_t smem = 1024 + p.bar_off + (2 * p.nst + 4) * 8 + 16 + 32;
+  p.cst_off = (p.xs_off + xbytes + 15) & ~15u;
+  p.bar_off = (p.cst_off + cbytes + 15) & ~15u;
+  const uint32_t smem = 1024 + p.bar_off + (2 * p.nst + 2 * kDBufs) * 8 + 16;
   if (smem > kSmemMax) return RB_ERR_SHAPE;
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gemv_int8_tc_kernel), static_cast<int>(kSmemMax));
   if (e != cudaSuccess) return RB_ERR_LAUNCH;

@@ -46,7 +46,6 @@ struct MmArgs {
 int launch_gemv_int4(const GemvArgs& a, int num_sms, cudaStream_t stream);
 int launch_gemv_int8(const GemvArgs& a, int num_sms, cudaStream_t stream);
 int launch_gemv_int8_tc(const GemvArgs& a, int num_sms, cudaStream_t stream);
-int launch_mm_int4(const MmArgs& a, int num_sms, cudaStream_t stream);
 int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream);
 int64_t mm_int4_tc_workspace(int64_t M, int64_t N, int64_t K, int num_sms);
 int launch_mm_int4_tc_static(MmArgs a, int num_sms, cudaStream_t stream);

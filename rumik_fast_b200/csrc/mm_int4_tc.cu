@@ -2,7 +2,11 @@
 // the dequantised weights in tensor memory (sm_100a).
 //
 // The operation of rumik-fast's Triton kernel _mm_int4 (kernels/mm_int4.py:24-46) and its wrapper mm_int4
-// (:59-73): w = code * s + m in the int4 group-128 layout, X fp16 [M, K], fp32 accumulation.
+// (:59-73): w = code * s + m in the int4 group-128 layout, X fp16 or bf16 [M, K], fp32 accumulation. Both
+// operands of a kind::f16 MMA share one type, and fp16 keeps the dequantised weight's rounding ~8x smaller than
+// bf16, so a bf16 X is converted to fp16 in shared memory (the kernel instance with kBf16X: each converter set
+// rewrites its stage's X atoms in place before it releases the group to the MMA issuer; exact for |x| <= 65504,
+// as a torch cast of X to fp16 would be).
 //
 // Work items are (128-row weight block, token chunk of BT <= 128 tokens, K slice), block-major so that the CTAs working
 // at the same time on the chunks of one block share its codes through L2; items are dealt round-robin to one
@@ -20,6 +24,7 @@
 //    partial into a caller-provided workspace; mm_int4_reduce then adds the slices in slice order.
 // All mbarrier waits are bounded; no multicast, no clusters.
 #include "common.cuh"
+#include "tc.cuh"
 #include "kernels.h"
 
 namespace rb {
@@ -63,6 +68,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// bf16 -> fp16 of a pair of activations held in one 32-bit word (round to nearest even).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
+  const __half2 h = __floats2half2_rn(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <bool kBf16X>
 __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_constant__ MmtParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -229,6 +241,22 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
 #pragma unroll
           for (int c = 0; c < 4; ++c) w4[c] = lds128(rowp + ((c ^ ((rib >> 1) & 3)) << 4));
         }
+        if constexpr (kBf16X) {
+          // the stage's two X atoms (BT rows x 128 bytes each), bf16 -> fp16 in place; the MMA issuer reads them
+          // only after this set's afull arrival below, and the proxy fence makes the writes visible to it
+          if (ok) {
+            uint8_t* xa = stage_of(s, slot) + kCodeBytes;
+            for (int c = rib; c < BT * 16; c += 128) {
+              uint4 v = *reinterpret_cast<const uint4*>(xa + c * 16);
+              v.x = bf16x2_to_f16x2(v.x);
+              v.y = bf16x2_to_f16x2(v.y);
+              v.z = bf16x2_to_f16x2(v.z);
+              v.w = bf16x2_to_f16x2(v.w);
+              *reinterpret_cast<uint4*>(xa + c * 16) = v;
+            }
+            fence_proxy_async_smem();
+          }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty(s, slot));  // codes are in registers
         const uint32_t s2 = static_cast<uint32_t>(s16) * 0x10001u, m2 = static_cast<uint32_t>(m16) * 0x10001u;
@@ -325,14 +353,14 @@ struct MmPlan {
 };
 inline MmPlan mm_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
   MmPlan pl;
-  const int nch = static_cast<int>((M + 127) / 128);
-  int BT = static_cast<int>((M + nch - 1) / nch);
-  pl.BT = std::max(16, (BT + 15) / 16 * 16);
+  const int64_t nch = (M + 127) / 128;
+  const int64_t BT = (M + nch - 1) / nch;
+  pl.BT = static_cast<int>(std::max<int64_t>(16, (BT + 15) / 16 * 16));
   pl.nchunks = static_cast<int>((M + pl.BT - 1) / pl.BT);
   const int G = static_cast<int>(K / 128);
-  const int items = static_cast<int>((N + kRows - 1) / kRows) * pl.nchunks;
+  const int64_t items = (N + kRows - 1) / kRows * pl.nchunks;  // int64: M and N may each be up to 2^30
   int ks = 1;
-  if (2 * items <= num_sms) ks = std::min(num_sms / items, G / 2);  // at most one wave of items
+  if (2 * items <= num_sms) ks = std::min(static_cast<int>(num_sms / items), G / 2);  // at most one wave of items
   ks = std::max(ks, 1);
   pl.gps = (G + ks - 1) / ks;
   pl.kslices = (G + pl.gps - 1) / pl.gps;
@@ -356,7 +384,9 @@ int64_t mm_int4_tc_workspace(int64_t M, int64_t N, int64_t K, int num_sms) {
 
 int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   using namespace mm4t;
-  if (a.x_dtype != RB_F16) return RB_ERR_DTYPE;
+  if (a.x_dtype != RB_F16 && a.x_dtype != RB_BF16) return RB_ERR_DTYPE;
+  // the work-item count must fit the kernel's int arithmetic
+  if ((a.N + kRows - 1) / kRows * ((a.M + 15) / 16) > (int64_t(1) << 30)) return RB_ERR_SHAPE;
   auto encode = mm4::encode_fn();
   if (!encode) return RB_ERR_DEVICE;
   const int M = static_cast<int>(a.M), N = static_cast<int>(a.N), K = static_cast<int>(a.K);
@@ -408,12 +438,15 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.ldx) * 2};
     const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(BT)};
     const cuuint32_t es[2] = {1, 1};
-    if (encode(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.X), dims, strides, box, es,
+    const CUtensorMapDataType xt =
+        a.x_dtype == RB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (encode(&p.xmap, xt, 2, const_cast<void*>(a.X), dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return RB_ERR_SHAPE;
   }
-  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(mm_int4_tc_kernel), kSmemMax);
+  void (*kern)(MmtParams) = a.x_dtype == RB_BF16 ? mm_int4_tc_kernel<true> : mm_int4_tc_kernel<false>;
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemMax);
   if (e != cudaSuccess) return RB_ERR_LAUNCH;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(std::min(num_sms, p.nitems));
@@ -425,7 +458,7 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = (a.flags & RB_FLAG_PDL) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, mm_int4_tc_kernel, p);
+  e = cudaLaunchKernelEx(&cfg, kern, p);
   if (e != cudaSuccess) return RB_ERR_LAUNCH;
   if (p.kslices > 1) {
     cudaLaunchConfig_t rc = {};

@@ -4,7 +4,6 @@
 #include "gemv_int4.cu"
 #include "gemv_int8.cu"
 #include "gemv_int4_multi.cu"
-#include "mm_int4.cu"
 #include "gemv_int4_tc.cu"
 #include "gemv_int8_tc.cu"
 #include "mm_int4_tc.cu"

@@ -6,9 +6,13 @@
 Y[T, N] = X[T, K] @ W^T with W in the int4 group-128 layout. X may be fp16 or bf16 and strided in its
 first dimension; y has X's dtype and is newly allocated, as in the reference. The tensor-core operands are
 fp16 (both operands of a kind::f16 MMA must share a type, and fp16 keeps the dequantised weight's rounding
-~8x smaller than bf16), so a bf16 X is first cast to fp16 on the device. The Triton tile knobs are accepted
-and ignored. The kernel is compiled ahead of time, so warmup() only performs one tiny call per shape (it
-makes the first call inside a CUDA-graph capture cheap).
+~8x smaller than bf16): the kernel converts a bf16 X to fp16 in shared memory, so a call launches the kernel
+(and, when K is split over the SMs, its reduction) and no torch op. The split-K workspace is kept per (device,
+stream) and only grows; calls on one stream are ordered, so they can share it. The Triton tile knobs are
+accepted and ignored. (While a CUDA graph is being captured each call takes its own workspace from the
+graph's pool instead, so that graphs replayed on different streams never share one.) The kernel is compiled
+ahead of time, so warmup() only performs one tiny call per shape
+(it makes the first call inside a CUDA-graph capture cheap).
 """
 import torch
 
@@ -28,8 +32,6 @@ def mm_int4(x, q, s, m, BM=None, BN=64, num_warps=4, num_stages=3, out=None):
         _require(t.dtype == torch.float16 and t.is_contiguous() and tuple(t.shape) == (N, K // G),
                  f"{nm} must be a contiguous fp16 [{N}, {K // G}] tensor")
     out_dtype = x.dtype
-    if x.dtype == torch.bfloat16:
-        x = x.to(torch.float16)
     if x.stride(1) != 1 or x.stride(0) % 8 != 0 or x.data_ptr() % 16 != 0:
         x = x.contiguous()
     T = x.shape[0]
@@ -39,13 +41,31 @@ def mm_int4(x, q, s, m, BM=None, BN=64, num_warps=4, num_stages=3, out=None):
     with _on_device(x.device):
         # a call with few 128-row x token-chunk tiles splits K over the idle SMs through an fp32 workspace
         ws_bytes = L.rb_mm_int4_workspace(T, N, K)
-        ws = torch.empty(ws_bytes // 4, device=x.device, dtype=torch.float32) if ws_bytes > 0 else None
+        ws = _workspace(x.device, ws_bytes) if ws_bytes > 0 else None
         st = L.rb_mm_int4_ws(x.data_ptr(), _lib.dtype_code(x.dtype), x.stride(0), q.data_ptr(), s.data_ptr(),
                              m.data_ptr(), y.data_ptr(), _lib.dtype_code(y.dtype), y.stride(0), T, N, K,
                              None if ws is None else ws.data_ptr(), ws_bytes, config.flags(),
                              _lib.stream_ptr(x.device))
     _lib.check("rb_mm_int4", st)
     return y
+
+
+_WS = {}
+_RETIRED = []  # outgrown workspaces stay allocated: work already queued on the stream may still use them
+
+
+def _workspace(device, nbytes):
+    """The split-K workspace of the current stream on `device`, grown to at least nbytes."""
+    if torch.cuda.is_current_stream_capturing():
+        return torch.empty((nbytes + 3) // 4, device=device, dtype=torch.float32)
+    key = (device.index, _lib.stream_ptr(device))
+    ws = _WS.get(key)
+    if ws is None or ws.numel() * 4 < nbytes:
+        if ws is not None:
+            _RETIRED.append(ws)
+        ws = torch.empty((nbytes + 3) // 4, device=device, dtype=torch.float32)
+        _WS[key] = ws
+    return ws
 
 
 def warmup(shapes):

@@ -29,16 +29,24 @@ def bf16_round(a):
 def assert_close(y, ref, what=""):
     """North-star acceptance: rel-L2 <= 1e-3 and max-abs <= 2e-3 * max|ref| against the fp32 oracle.
 
-    For a bf16 output the oracle is first rounded to bf16: bf16 rounding alone is ~1.1e-3 rel-L2 (8-bit
-    mantissa), above the bar, so the kernel is held to the correctly rounded bf16 result instead (the
-    reference's own bf16 path reports 2.3e-3 against unrounded fp32, engine/README.md:110), and its max-abs
-    bound is widened by one bf16 rounding step at max|ref| (2**-8): an output may round the other way."""
-    abs_tol = O.MAX_ABS_TOL
+    A bf16 output carries its own rounding error, r = rel-L2(bf16(ref), ref), about 1.1e-3 (8-bit mantissa)
+    and so above the bar by itself (the reference's own bf16 path reports 2.3e-3 against unrounded fp32,
+    engine/README.md:110). The kernel's arithmetic error and that rounding are independent, so they add in
+    quadrature: a bf16 output passes when rel-L2(y, ref) <= sqrt(1e-3**2 + r**2), with r computed from the
+    oracle on the same rows, i.e. when the kernel's own error is within the 1e-3 bar. Its max-abs bound is
+    widened by the largest rounding step at max|ref| (2**-8). (Comparing with the rounded oracle instead
+    counts a full ulp for every output whose fp32 value lies near a rounding midpoint; that count grows with
+    the kernel's error and shrinks with the number of rows, so a kernel error of 3e-4 on a few hundred rows
+    reads as 1.3e-3. Simulated with the kernel's integer arithmetic and planted relative errors e, this
+    criterion gives rel / bar = 0.85, 1.0 and 1.8 for e = 0, 1e-3 and 3e-3, on 256 rows as on 3072.)"""
+    abs_tol, rel_tol = O.MAX_ABS_TOL, O.REL_L2_TOL
     if isinstance(y, torch.Tensor) and y.dtype == torch.bfloat16:
-        ref = bf16_round(ref)
+        r, _ = O.errors(bf16_round(ref), ref)
+        rel_tol = float(np.hypot(O.REL_L2_TOL, r))
         abs_tol += 2.0 ** -8
     rel, mab = O.errors(np_f32(y) if isinstance(y, torch.Tensor) else y, ref)
-    assert rel <= O.REL_L2_TOL and mab <= abs_tol, f"{what}: rel-L2 {rel:.3e}, max-abs/max {mab:.3e}"
+    assert rel <= rel_tol and mab <= abs_tol, (f"{what}: rel-L2 {rel:.3e} (bar {rel_tol:.3e}), "
+                                               f"max-abs/max {mab:.3e}")
     return rel, mab
 
 

@@ -43,12 +43,14 @@ def check(host, dev_entries, what):
         assert_close(e[4], int4_ref(x, q, s, m), f"{what} entry {i}")
 
 
-def test_layer_set():
-    """Two layers of the config-1 projection set (QKV, o, gate_up with x_h; down with x_i)."""
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
+def test_layer_set(kernel):
+    """Two layers of the config-1 projection set (QKV, o, gate_up with x_h; down with x_i), on each kernel
+    explicitly: ~100 MB of codes is below the size at which the default choice moves to the tcgen05 kernel."""
     shapes = [(n, k) for _ in range(2) for _, n, k in syn.LAYER_SHAPES]
     host, ent = build(shapes, nx=1)
-    rb.Int4GemvSet(ent)()
-    check(host, ent, "layers")
+    rb.Int4GemvSet(ent, kernel=kernel)()
+    check(host, ent, f"layers ({kernel})")
 
 
 def test_ragged_and_mixed_k():

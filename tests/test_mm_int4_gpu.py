@@ -82,3 +82,53 @@ def test_deterministic():
     q, s, m = (t.to(DEV) for t in syn.int4_weights(1024, 2048, g, "cpu"))
     X = syn.activations((100, 2048), g, "cpu").to(DEV)
     assert torch.equal(mm_int4(X, q, s, m), mm_int4(X, q, s, m))
+
+
+@pytest.mark.parametrize("M,N,K", [(34, 5120, 3072), (34, 3072, 8192), (256, 3072, 3072), (1024, 16384, 3072)])
+def test_bf16_x_through_the_c_abi(M, N, K):
+    """The engine's bf16 activations straight into rb_mm_int4 (no split) and rb_mm_int4_ws (split K where the
+    plan splits): converted to fp16 inside the kernel, so the result equals the fp16-X call bit for bit (the
+    conversion is exact) and matches the oracle."""
+    import ctypes
+    from rumik_fast_b200 import _lib
+    L = _lib.lib()
+    g = syn.generator(M + N + K, "cpu")
+    q, s, m = (t.to(DEV) for t in syn.int4_weights(N, K, g, "cpu"))
+    Xb = syn.activations((M, K), g, "cpu", dtype=torch.bfloat16).to(DEV)
+    Xh = Xb.to(torch.float16)
+    ws_bytes = L.rb_mm_int4_workspace(M, N, K)
+    ws = torch.empty(max(ws_bytes // 4, 1), device=DEV, dtype=torch.float32)
+    out = {}
+    for name, X in (("bf16", Xb), ("f16", Xh)):
+        for split in (False, True):
+            Y = torch.full((M, N), float("nan"), device=DEV, dtype=torch.float16)
+            args = [X.data_ptr(), _lib.dtype_code(X.dtype), K, q.data_ptr(), s.data_ptr(), m.data_ptr(), Y.data_ptr(),
+                    _lib.F16, N, M, N, K]
+            stream = _lib.stream_ptr(torch.device(DEV))
+            if split:
+                st = L.rb_mm_int4_ws(*args, ctypes.c_void_p(ws.data_ptr()), ws_bytes, 0, stream)
+            else:
+                st = L.rb_mm_int4(*args, 0, stream)
+            assert st == 0
+            out[(name, split)] = Y
+    torch.cuda.synchronize()
+    assert torch.equal(out[("bf16", False)], out[("f16", False)])
+    assert torch.equal(out[("bf16", True)], out[("f16", True)])
+    cols = np.sort(np.random.default_rng(K).choice(N, 512, replace=False))
+    assert_close(out[("bf16", True)].cpu()[:, cols], mm_ref(Xb.cpu(), q.cpu(), s.cpu(), m.cpu(), cols), "bf16 X")
+
+
+def test_wrapper_launches_only_the_library_kernels():
+    """mm_int4 with a bf16 X launches the prefill kernel (and its split-K reduction) and no torch op."""
+    from torch.profiler import ProfilerActivity, profile
+    g = syn.generator(13, "cpu")
+    q, s, m = (t.to(DEV) for t in syn.int4_weights(3072, 8192, g, "cpu"))
+    X = syn.activations((34, 8192), g, "cpu", dtype=torch.bfloat16).to(DEV)
+    Y = torch.empty(34, 3072, device=DEV, dtype=torch.bfloat16)
+    mm_int4(X, q, s, m, out=Y)  # first call: the workspace is allocated
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        mm_int4(X, q, s, m, out=Y)
+        torch.cuda.synchronize()
+    names = {e.name for e in prof.events() if e.device_type.name == "CUDA"}
+    assert names and all("mm_int4" in n for n in names), names

@@ -177,3 +177,27 @@ def test_sampling_tail_matches_reference(gg, case):
     logits = O.bf16_bits_to_f32(gg[f"smp{case}_logits"])
     nxt = O.pick_ref(logits, step, min_new, end_idx, gg[f"smp{case}_u"], top_k, 1 / 0.8, gg["smp_ids"], s, end_id)
     assert nxt == int(gg[f"smp{case}_next"])
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c", "d", "cfg"])
+def test_torch_cpu_path_matches_reference(g4, tag):
+    """The torch restatement timed as the CPU baseline (oracle/reference_cpu.py) gives the reference's own
+    dequantised weights bit for bit and its GEMV to fp32 round-off."""
+    import torch
+    from oracle import reference_cpu as R
+    q, s, m = (torch.from_numpy(np.ascontiguousarray(g4[f"{tag}_{k}"])) for k in "qsm")
+    deq = R.dequantize(q, s, m)
+    assert np.array_equal(deq.numpy().view(np.uint32), g4[f"{tag}_deq"].view(np.uint32))
+    y = R.gemv_int4_torch(torch.from_numpy(g4[f"{tag}_x16"]), q, s, m)
+    np.testing.assert_allclose(y.numpy(), g4[f"{tag}_y16"], rtol=2e-5, atol=2e-5)
+
+
+def test_torch_cpu_int8_matches_reference(g8):
+    import torch
+    from oracle import reference_cpu as R
+    x = torch.from_numpy(g8["cfg_x16"])
+    s = torch.from_numpy(g8["cfg_s16"])
+    y_signed = R.gemv_int8_torch(x, torch.from_numpy(g8["cfg_wi8"]), s, signed=True)
+    y_u8 = R.gemv_int8_torch(x, torch.from_numpy(g8["cfg_qu8"]), s, signed=False)
+    np.testing.assert_allclose(y_signed.numpy(), g8["cfg_y16"], rtol=2e-5, atol=2e-6)
+    np.testing.assert_allclose(y_u8.numpy(), g8["cfg_y16"], rtol=2e-5, atol=2e-6)

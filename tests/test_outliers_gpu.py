@@ -1,0 +1,143 @@
+"""Outlier-heavy activations through every kernel that quantises x to 16-bit integers.
+
+The tcgen05 GEMV-list kernel quantises each 128-column group of x with delta = max|x| / 32639 (per group); the
+tcgen05 int8 head does the same over the whole vector; the fused prologue tabulates its normalised vector the same
+way. A transformer's residual stream is not N(0, 1): a few channels run 100-1000x the rest. These cases put such
+channels, a group whose largest value is 1e4x its median, and groups of tiny values with one large one, through
+each path at the config shapes and hold them to the north-star bar (rel-L2 <= 1e-3, max-abs <= 2e-3 max|ref|)
+against the fp32 oracle.
+"""
+import numpy as np
+import pytest
+import torch
+
+import rumik_fast_b200 as rb
+from oracle import oracle as O
+from rumik_fast_b200 import _lib, fused, scales8
+from rumik_fast_b200 import synthetic as syn
+from tests.helpers import assert_close, int4_ref, int8_ref, np_act, np_f32
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+DTYPES = [torch.float16, torch.bfloat16]
+CASES = ["channels", "group_1e4", "tiny_groups"]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu(native_lib):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    rb.device_error()
+    yield
+    assert rb.device_error() == 0
+
+
+def outlier_x(K, case, seed, dtype=torch.float16):
+    """channels: six channels at +-200..1000, the rest N(0, 1). group_1e4: one value in group 0 at 1e4 x the
+    group's median |x|. tiny_groups: N(0, 1e-3) with one value of 500 at the start of every group."""
+    rng = np.random.default_rng(seed)
+    x = rng.normal(0, 1, K).astype(np.float32)
+    if case == "channels":
+        idx = rng.choice(K, 6, replace=False)
+        x[idx] = rng.choice([-1.0, 1.0], 6) * rng.uniform(200, 1000, 6)
+    elif case == "group_1e4":
+        x[5] = 1e4 * np.median(np.abs(x[:128]))
+    else:
+        x = rng.normal(0, 1e-3, K).astype(np.float32)
+        x[::128] = 500.0
+    return torch.from_numpy(x).to(dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("split", [False, True])
+@pytest.mark.parametrize("eight", [False, True])
+def test_int4_tc_list(case, dtype, split, eight):
+    """QKV, o_proj, gate_up and down shapes on the tcgen05 list kernel, fp16 or 8-bit scales, with K split over
+    converter sets (a short list, as a decode layer's) or unsplit (the same list run through rb_gemv_int4_multi
+    without a workspace)."""
+    g = syn.generator(11, "cpu")
+    xs = {k: outlier_x(k, case, 100 + k, dtype) for k in (3072, 8192)}
+    host, ent = [], []
+    for _, n, k in syn.LAYER_SHAPES:
+        q, s, m = syn.int4_weights(n, k, g, "cpu")
+        y = torch.full((n,), float("nan"), device=DEV, dtype=dtype)
+        if eight:
+            sc = scales8.pack(s.to(DEV), m.to(DEV))
+            host.append((xs[k], q, sc.sz.cpu(), sc.s_row.cpu()))
+            ent.append((xs[k].to(DEV), q.to(DEV), sc, None, y))
+        else:
+            host.append((xs[k], q, s, m))
+            ent.append((xs[k].to(DEV), q.to(DEV), s.to(DEV), m.to(DEV), y))
+    st = rb.Int4GemvSet(ent, kernel="tc")
+    if split:
+        assert st.ws is not None
+        st()
+    else:
+        L = _lib.lib()
+        _lib.check("rb_gemv_int4_multi", L.rb_gemv_int4_multi(
+            st._descs, len(ent), _lib.dtype_code(dtype), _lib.dtype_code(dtype), rb.config.flags() | _lib.FLAG_KERNEL_TC,
+            _lib.stream_ptr(torch.device(DEV))))
+    torch.cuda.synchronize()
+    for i, (h, e) in enumerate(zip(host, ent)):
+        if eight:
+            xa, tag = np_act(h[0])
+            ref = O.gemv_int4_s8_ref(xa, h[1].numpy(), h[2].numpy().view(np.uint16), h[3].numpy(), x_dtype=tag)
+        else:
+            ref = int4_ref(*h)
+        assert_close(e[4], ref, f"{case} entry {i}")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", CASES)
+def test_single_gemv_config0(case, dtype):
+    """Config 0's 8192 x 3072 GEMV through gemv_int4_cuda (a one-entry tcgen05 list at this size)."""
+    q, s, m = syn.int4_weights(8192, 3072, syn.generator(0, "cpu"), "cpu")
+    x = outlier_x(3072, case, 7, dtype)
+    y = rb.gemv_int4_cuda(x.to(DEV), q.to(DEV), s.to(DEV), m.to(DEV))
+    assert_close(y, int4_ref(x, q, s, m), f"config 0 {case}")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", CASES)
+def test_int8_head(case, dtype):
+    """Config 2's head, 16385 x 3072, on the tcgen05 int8 kernel (signed and int8+128 storage)."""
+    q, s = syn.int8_weights(16385, 3072, syn.generator(0, "cpu"), "cpu")
+    x = outlier_x(3072, case, 9, dtype)
+    y = rb.gemv_int8_cuda(x.to(DEV), q.to(DEV), s.to(DEV))
+    assert_close(y, int8_ref(x, q, s), f"head {case}")
+    qu = (q.to(torch.int16) + 128).to(torch.uint8)
+    yu = rb.gemv_int8_cuda(x.to(DEV), qu.to(DEV), s.to(DEV))
+    assert torch.equal(y, yu)
+
+
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", CASES)
+def test_prologue_outlier_residual(case, dtype, kernel):
+    """The fused add + LayerNorm prologue with an outlier-heavy residual stream, then QKV and gate_up GEMVs of
+    the normalised vector (which keeps the outlier channels) in the same launch."""
+    H = 3072
+    g = torch.Generator().manual_seed(3)
+    x = outlier_x(H, case, 21, dtype)
+    a = torch.randn(H, generator=g).to(dtype)
+    b = (0.5 * torch.randn(H, generator=g)).to(dtype)
+    w = (1 + 0.1 * torch.randn(H, generator=g)).to(dtype)
+    xd, ad, bd, wd = (t.to(DEV) for t in (x, a, b, w))
+    x_out = torch.empty(H, device=DEV, dtype=dtype)
+    h_out = torch.empty(H, device=DEV, dtype=dtype)
+    ln = fused.AddLn(xd, ad, bd, wd, x_out, eps=1e-5, h_out=h_out)
+    gw = syn.generator(4, "cpu")
+    W = [syn.int4_weights(n, H, gw, "cpu") for n in (5120, 16384)]
+    ys = [torch.full((n,), float("nan"), device=DEV, dtype=dtype) for n in (5120, 16384)]
+    keep =[[t.to(DEV) for t in wh] for wh in W]  # device copies alive for the call
+    descs = [_lib.GemvDesc(None, y.data_ptr(), *(t.data_ptr() for t in kw), y.numel(), H) for kw, y in zip(keep, ys)]
+    from tests.test_fused_gpu import run_fused
+    run_fused(descs, ln=ln, x_dtype=dtype, y_dtype=dtype, kernel=kernel)
+    torch.cuda.synchronize()
+    tag = "bf16" if dtype == torch.bfloat16 else "f16"
+    s_ref, h_ref = O.add_ln_ref(np_act(x)[0], np_act(a)[0], np_act(b)[0], np_act(w)[0], 1e-5, tag)
+    assert np.array_equal(np_f32(x_out), s_ref)
+    assert O.ulp_diff(np_f32(h_out), h_ref, tag).max() <= 1
+    for wh, y in zip(W, ys):
+        assert_close(y, int4_ref(h_out.cpu(), *wh), f"prologue {case} GEMV")
