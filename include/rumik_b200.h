@@ -357,8 +357,8 @@ int rb_attn_decode(const void* q, const void* k_cache, const void* v_cache, cons
  *   bufs       the `world` ranks' symmetric buffers (device pointers mapped into this process, bufs[rank] the
  *              local one), each at least 8 * world * n bytes of data at offset 0, `world` uint32 flags at
  *              flag_off and one uint32 counter at counter_off, all zero before the first call
- * Every rank must make the same sequence of calls. A peer that does not arrive within 4 s sets a bit in the
- * device error word (rb_get_device_error). 1 <= world <= 8.
+ * Every rank must make the same sequence of calls. A peer that does not arrive within the wait limit (4 s unless
+ * rb_set_wait_limit changed it) sets a bit in the device error word (rb_get_device_error). 1 <= world <= 8.
  */
 int rb_tp_allreduce_f16(const void* a, const void* b, void* out, int64_t n, void* const* bufs, int rank, int world,
                         uint32_t flag_off, uint32_t counter_off, int flags, void* stream);
@@ -389,6 +389,14 @@ int rb_version(void);
 /* Read and clear the device-side error word of the current device (bit set by a kernel that gave up a
  * bounded wait). Synchronises `stream`. *out receives the word; returns RB_OK or RB_ERR_DEVICE. */
 int rb_get_device_error(unsigned int* out, void* stream);
+
+/* Set the longest a kernel of this library waits on the CURRENT device for anything another thread, CTA or rank
+ * must provide (an mbarrier phase, a peer's flag, a completion counter) before it gives up: it then sets its bit
+ * in the device error word, skips the work that depended on the wait and returns, so the context stays usable.
+ * ns = 0 restores the default of 4 s; otherwise 1000 <= ns <= 6e10. Affects kernels launched after the call
+ * (it synchronises `stream`). A short limit is for tests that let a wait run out on purpose. No reference
+ * counterpart (the reference's kernels do not wait on one another). */
+int rb_set_wait_limit(uint64_t ns, void* stream);
 
 #ifdef __cplusplus
 }

@@ -60,7 +60,8 @@ class Sampler(ctypes.Structure):
 
 
 EPI_STORE, EPI_ROPE_KV, EPI_SWIGLU = 0, 1, 2
-DEVERR_ARG = 1 << 9
+# device error word bits (rb_get_device_error): a wait that ran out, or an out-of-range device-side argument
+DEVERR_TC_WAIT, DEVERR_TP_WAIT, DEVERR_ARG, DEVERR_ATT_WAIT = 1 << 7, 1 << 8, 1 << 9, 1 << 10
 
 SIGNATURES = {
     "rb_gemv_int4": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
@@ -83,6 +84,7 @@ SIGNATURES = {
     "rb_status_string": (_c.c_char_p, [_int]),
     "rb_version": (_int, []),
     "rb_get_device_error": (_int, [_c.POINTER(_c.c_uint), _vp]),
+    "rb_set_wait_limit": (_int, [_c.c_uint64, _vp]),
     "rb_ipc_alloc": (_int, [_c.c_uint64, _c.POINTER(_vp), _vp]),
     "rb_ipc_free": (_int, [_vp]),
     "rb_ipc_open": (_int, [_vp, _c.c_uint64, _c.POINTER(_vp), _c.POINTER(_vp)]),
@@ -140,3 +142,10 @@ def device_error(device=None):
     with torch.cuda.device(dev):
         check("rb_get_device_error", lib().rb_get_device_error(ctypes.byref(out), stream_ptr(dev)))
     return out.value
+
+
+def set_wait_limit(ns=0, device=None):
+    """Longest wait of a kernel on `device` before it gives up and sets its error bit (0: the default 4 s)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        check("rb_set_wait_limit", lib().rb_set_wait_limit(int(ns), stream_ptr(dev)))

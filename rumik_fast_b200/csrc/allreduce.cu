@@ -63,9 +63,9 @@ __global__ void __launch_bounds__(kThreads, 1) tp_allreduce_kernel(const __grid_
     st_release_sys(reinterpret_cast<uint32_t*>(p.buf[tid] + p.flag_off) + p.rank, e);
     const uint32_t* f = reinterpret_cast<const uint32_t*>(p.buf[p.rank] + p.flag_off) + tid;
     if (ld_acquire_sys(f) < e) {
-      const unsigned long long t0 = globaltimer_ns();
+      const unsigned long long t0 = globaltimer_ns(), lim = wait_limit_ns();
       while (ld_acquire_sys(f) < e) {
-        if (globaltimer_ns() - t0 > kMaxWaitNs) {
+        if (globaltimer_ns() - t0 > lim) {
           atomicOr(&g_device_error, ERR_TP_WAIT);
           break;
         }

@@ -488,6 +488,19 @@ int rb_ipc_close(void* base) {
   return RB_OK;
 }
 
+int rb_set_wait_limit(uint64_t ns, void* stream) {
+  if (ns == 0) ns = rb::kMaxWaitNs;
+  if (ns < 1000 || ns > 60000000000ull) return RB_ERR_SHAPE;
+  int sms = 0, st = device_sms(&sms);
+  if (st != RB_OK) return st;
+  const unsigned long long v = ns;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyToSymbolAsync(rb::g_wait_limit_ns, &v, sizeof(v), 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return RB_ERR_DEVICE;
+  return RB_OK;
+}
+
 int rb_get_device_error(unsigned int* out, void* stream) {
   if (!out) return RB_ERR_NULL;
   unsigned int zero = 0;

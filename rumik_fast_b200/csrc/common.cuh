@@ -33,9 +33,17 @@ enum : unsigned int {
   ERR_ATT_WAIT = 1u << 10,    // a fused-attention launch timed out waiting for the attention outputs
 };
 
-// Upper bound on the wall time of one mbarrier wait. Healthy waits here last microseconds (at most the
-// duration of the previous GEMV when a kernel starts early under PDL); four seconds means the wait is hung.
+// Upper bound on the wall time of one wait (an mbarrier phase, a peer's flag, a completion counter). Healthy
+// waits here last microseconds (at most the duration of the previous GEMV when a kernel starts early under PDL);
+// four seconds means the wait is hung. The limit in force is g_wait_limit_ns, per device, set by
+// rb_set_wait_limit (a test lowers it to make a wait that nothing will satisfy run out quickly).
 constexpr unsigned long long kMaxWaitNs = 4000000000ull;
+__device__ unsigned long long g_wait_limit_ns = kMaxWaitNs;
+
+// The limit, read once per wait that does not complete at its first test.
+__device__ __forceinline__ unsigned long long wait_limit_ns() {
+  return *const_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+}
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
@@ -96,12 +104,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait on an mbarrier phase. Returns false (and sets `err_bit` in g_device_error) if the phase did
-// not complete within kMaxWaitNs; the caller then skips its work and returns, so the context stays usable.
+// not complete within the wait limit; the caller then skips its work and returns, so the context stays usable.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_bit) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
+  const unsigned long long t0 = globaltimer_ns(), lim = wait_limit_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > kMaxWaitNs) {
+    if (globaltimer_ns() - t0 > lim) {
       atomicOr(&g_device_error, err_bit);
       return false;
     }

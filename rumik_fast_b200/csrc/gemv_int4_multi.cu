@@ -541,12 +541,14 @@ __global__ void __maxnreg__(kMaxRegs) gemv_int4_multi_kernel(const __grid_consta
       if (tid == 0) {
         const int64_t pos = *p.att.pos;
         if (pos >= 0 && pos < p.att.S) {  // otherwise no head completes (the attention reported ERR_ARG)
-          const unsigned long long t0 = globaltimer_ns();
+          const unsigned long long t0 = globaltimer_ns(), lim = wait_limit_ns();
           unsigned int done = 0;
           for (;;) {
             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(done) : "l"(p.att.heads_done) : "memory");
-            if (done >= static_cast<unsigned int>(p.att_nkv)) break;
-            if (globaltimer_ns() - t0 > kMaxWaitNs) {
+            // signed: a counter the caller left below zero (a workspace not zeroed) never completes, and the
+            // wait runs out instead of passing at once
+            if (static_cast<int>(done) >= p.att_nkv) break;
+            if (globaltimer_ns() - t0 > lim) {
               atomicOr(&g_device_error, ERR_ATT_WAIT);
               break;
             }
