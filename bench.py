@@ -62,9 +62,10 @@ def parse():
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers in the step (36 = config 1; fewer only for small profiling cases)")
     ap.add_argument("--pos", type=int, default=511, help="step workload: position of the token (cache slots read)")
-    ap.add_argument("--attn", default="separate", choices=["fused", "separate"],
-                    help="step workload: attention in its own launch (default, faster at the config shapes), or "
-                         "inside the o_proj/down_proj launch")
+    ap.add_argument("--attn", default="separate", choices=["fused", "separate", "persistent"],
+                    help="step workload: per layer three launches with the attention in its own launch, or inside "
+                         "the o_proj/down_proj launch (fused); or every layer in one launch of the whole-step "
+                         "kernel (persistent)")
     ap.add_argument("--scales", default="fp16", choices=["fp16", "8bit"],
                     help="decode workload: the reference's fp16 scales, or 8-bit double-quantised ones")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "step"],
@@ -424,7 +425,8 @@ def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
     buf_o, buf_d, hn = (torch.empty(H, device=dev, dtype=f16) for _ in range(3))
     logits = torch.empty(syn.HEAD_SHAPE[0], device=dev, dtype=f16)
     pos_t = torch.tensor([pos], device=dev, dtype=torch.int64)
-    layer_in, attn, layer_out = [], [], []
+    layer_in, attn, layer_out, pl_layers = [], [], [], []
+    persistent = attn_mode == "persistent"
     xin = None
     for L in range(nlayers):
         xout = xr[L % 2]
@@ -432,6 +434,12 @@ def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
               fused.AddLn.from_embedding(emb_q, emb_s, tok, lnw[0], xout, eps=c["eps"]))
         qkv = syn.int4_weights((nq + 2 * nkv) * hd, H, gen, dev)
         gu = fused.interleave_gate_up(*syn.int4_weights(2 * inter, H, gen, dev))
+        if persistent:  # every layer in one launch of the whole-step kernel (DecodeLayers)
+            wo = syn.int4_weights(H, nq * hd, gen, dev)
+            wd = syn.int4_weights(H, inter, gen, dev)
+            pl_layers.append(dict(qkv=qkv, gate_up=gu, o_proj=wo, down=wd, ln_w=lnw[L], k_cache=kc[L],
+                                  v_cache=vc[L], rope=L % 4 != 3))
+            continue
         layer_in.append(fused.AddLnGemvPost(qkv, gu, add_ln=ln, pos=pos_t, cos=cos, sin=sin, k_cache=kc[L],
                                             v_cache=vc[L], q_out=q_out, act=act, n_q_heads=nq, n_kv_heads=nkv,
                                             rope=L % 4 != 3))
@@ -444,6 +452,12 @@ def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
             attn.append(DecodeAttention(q_out, kc[L], vc[L], pos_t, ob, nq, nkv))
             layer_out.append(rb.Int4GemvSet([(ob, *wo, buf_o), (act, *wd, buf_d)]))
         xin = xout
+    layers_launch = None
+    if persistent:
+        from rumik_fast_b200.decode_step import DecodeLayers
+        layers_launch = DecodeLayers(pl_layers, pos=pos_t, cos=cos, sin=sin, emb_q=emb_q, emb_s=emb_s, tok=tok,
+                                     n_q_heads=nq, n_kv_heads=nkv, eps=c["eps"])
+        xin, buf_o, buf_d = layers_launch.last()
     final = fused.AddLn(xin, buf_o, buf_d, lnw[nlayers], None, eps=c["eps"], h_out=hn)
     head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
     # the sampling tail (engine/sample.py): stop predictor (LayerNorm, 512 x H bf16, GELU, 1 x 512), top-30,
@@ -461,7 +475,9 @@ def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
     sampler = FusedSampler(eng, lambda: logits)
 
     def step():
-        for L in range(nlayers):
+        if layers_launch is not None:
+            layers_launch()
+        for L in range(len(layer_in)):
             layer_in[L]()
             if attn:
                 attn[L]()
@@ -474,8 +490,8 @@ def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
     wbytes = nlayers * sum(syn.int4_bytes(n, k) for n, k in shapes) + syn.int8_bytes(*syn.HEAD_SHAPE) + nz * H * 2
     kvbytes = nlayers * (2 * nkv * (pos + 1) * hd * 2 + 2 * nq * hd * 2)
     return dict(step=step, tok=tok, logits=logits, wbytes=wbytes + H, kvbytes=kvbytes,
-                launches=(2 if attn_mode == "fused" else 3) * nlayers + 4,
-                keep=(layer_in, attn, layer_out, final, head, kc, vc, emb_q, emb_s, sampler, eng))
+                launches=(((nlayers + 35) // 36) if persistent else (2 if attn_mode == "fused" else 3) * nlayers) + 4,
+                keep=(layer_in, attn, layer_out, final, head, kc, vc, emb_q, emb_s, sampler, eng, layers_launch))
 
 
 def measure_step(dev, seed, nlayers, pos, attn_mode, steps, warmup, world, clk=None):

@@ -380,6 +380,62 @@ int rb_ipc_free(void* ptr);
 int rb_ipc_open(const void* handle, uint64_t offset, void** base, void** ptr);
 int rb_ipc_close(void* base);
 
+/* One transformer layer of a decode step (rb_decode_layers). The GEMV descriptors' x and y are not used. */
+typedef struct rb_decode_layer {
+  rb_gemv_desc qkv;      /* q|k|v rows: N = (n_q_heads + 2 n_kv_heads) head_dim, K = H (fp16 scales) */
+  rb_gemv_desc gate_up;  /* gate and up rows interleaved (row 2c = gate c, 2c + 1 = up c): N = 2 I, K = H */
+  rb_gemv_desc o_proj;   /* N = H, K = n_q_heads head_dim */
+  rb_gemv_desc down;     /* N = H, K = I */
+  const void* ln_w;      /* LayerNorm weight [H] of this layer's input */
+  void* k_cache;         /* [n_kv_heads, cache_len, head_dim]: slot *pos is written */
+  void* v_cache;
+  int rope;              /* rotary embedding of q and k (0: none) */
+} rb_decode_layer;
+
+/* A decode step's layers and the buffers they pass on. Buffers marked [2] alternate by layer: the layer with step
+ * index g (first_layer + its index in layers) writes copy g & 1 and reads what layer g - 1 wrote in copy
+ * (g - 1) & 1. All activation buffers have the call's dtype. */
+typedef struct rb_decode_step {
+  const rb_decode_layer* layers;
+  int n_layers;          /* 1 .. 36 per call; a longer step is several calls, first_layer advancing */
+  int first_layer;       /* step index of layers[0]; 0: its input is the token's int8 embedding row */
+  int64_t H, I;          /* hidden size, MLP channels: multiples of 256 */
+  int n_q_heads, n_kv_heads, head_dim;  /* head_dim 128; 1 .. 4 query heads per key-value head */
+  int64_t cache_len;
+  float eps;             /* LayerNorm epsilon */
+  float attn_scale;      /* softmax scale of q . k */
+  const int64_t* pos;    /* device: the token's position (its cache slot) */
+  const void* cos;       /* [cache_len, head_dim] rotary tables (engine/rumik_int4.py:107-109) */
+  const void* sin;
+  const int8_t* emb_q;   /* first_layer == 0: int8 token embeddings [vocab, H] */
+  const void* emb_s;     /* their per-row scales, dtype emb_s_dtype (RB_F32 or RB_F16) */
+  int emb_s_dtype;
+  const int64_t* tok;    /* device: the token id */
+  int64_t vocab;
+  void* resid[2];        /* residual stream x [H] */
+  void* q_out[2];        /* rotated queries [n_q_heads * head_dim] */
+  void* attn_out[2];     /* attention output [n_q_heads * head_dim] */
+  void* act[2];          /* silu(gate) * up [I] */
+  void* o_out[2];        /* o_proj output [H] */
+  void* down_out[2];     /* down_proj output [H] */
+  void* ws;              /* rb_decode_layers_workspace() bytes, zeroed once; every call leaves it zeroed */
+  int64_t ws_bytes;
+} rb_decode_step;
+
+/*
+ * A decode step's transformer layers as ONE persistent launch (one CTA per SM, cooperative): per layer
+ * h = LayerNorm(x + o_out + down_out) (layer 0: the token's embedding row), x stored to resid; QKV and gate_up
+ * of h with rope, the KV-cache write at *pos and silu(gate) * up; the decode attention; down_proj and o_proj.
+ * The same results as the per-layer launches (rb_gemv_int4_fused for the input side, rb_attn_decode,
+ * rb_gemv_int4_multi for o_proj + down_proj) up to the order of fp32 additions. Replaces the per-layer
+ * launch sequence of engine/rumik_fused.py:97-121 (the add_ln / gemv / post / attention / gemv calls). After
+ * it the step's final add + LayerNorm (rb_add_layernorm on resid, o_out, down_out of the last layer) and the
+ * head follow. dtype: RB_F16 or RB_BF16. A wait that runs out sets bit 11 (0x800) of the device error word and
+ * aborts the launch (rb_get_device_error).
+ */
+int64_t rb_decode_layers_workspace(const rb_decode_step* st);
+int rb_decode_layers(const rb_decode_step* st, int dtype, int flags, void* stream);
+
 /* Human-readable text for a status code (static storage). */
 const char* rb_status_string(int status);
 

@@ -61,7 +61,7 @@ class Sampler(ctypes.Structure):
 
 EPI_STORE, EPI_ROPE_KV, EPI_SWIGLU = 0, 1, 2
 # device error word bits (rb_get_device_error): a wait that ran out, or an out-of-range device-side argument
-DEVERR_TC_WAIT, DEVERR_TP_WAIT, DEVERR_ARG, DEVERR_ATT_WAIT = 1 << 7, 1 << 8, 1 << 9, 1 << 10
+DEVERR_TC_WAIT, DEVERR_TP_WAIT, DEVERR_ARG, DEVERR_ATT_WAIT, DEVERR_STEP_WAIT = 1 << 7, 1 << 8, 1 << 9, 1 << 10, 1 << 11
 
 SIGNATURES = {
     "rb_gemv_int4": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
@@ -85,6 +85,8 @@ SIGNATURES = {
     "rb_version": (_int, []),
     "rb_get_device_error": (_int, [_c.POINTER(_c.c_uint), _vp]),
     "rb_set_wait_limit": (_int, [_c.c_uint64, _vp]),
+    "rb_decode_layers_workspace": (_i64, [_vp]),
+    "rb_decode_layers": (_int, [_vp, _int, _int, _vp]),
     "rb_ipc_alloc": (_int, [_c.c_uint64, _c.POINTER(_vp), _vp]),
     "rb_ipc_free": (_int, [_vp]),
     "rb_ipc_open": (_int, [_vp, _c.c_uint64, _c.POINTER(_vp), _c.POINTER(_vp)]),

@@ -104,7 +104,17 @@ __device__ __forceinline__ void online_step(const float (&s)[kStep], bool mine_i
 // named barrier bar_id. Writes its partial (or, when one split holds every slot, the output); the last split of
 // the head to finish merges the partials and writes the head group's outputs (and, when p.heads_done is set,
 // adds 1 to it with release semantics). sm_*: shared memory of the CTA merge; is_last: one shared int.
-template <int REP, bool kLean>
+// Cache rows: through the read-only path, or (kCoherent) through L2 only, for a launch that itself writes the
+// token's slot (the whole-step kernel, where another CTA's epilogue stores it earlier in the same launch).
+template <bool kCoherent>
+__device__ __forceinline__ uint2 ld_row8(const uint8_t* p) {
+  if constexpr (kCoherent)
+    return __ldcg(reinterpret_cast<const uint2*>(p));
+  else
+    return __ldg(reinterpret_cast<const uint2*>(p));
+}
+
+template <int REP, bool kLean, bool kCoherent = false>
 __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id, float (*sm_m)[REP],
                          float (*sm_l)[REP], float (*sm_o)[REP][kHd], int* is_last) {
   const int warp = tid >> 5, lane = tid & 31;
@@ -146,8 +156,8 @@ __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id
 #pragma unroll
       for (int j = 0; j < kStep; ++j) {
         const bool in = t0 + j < end;
-        kr[j] = in ? __ldg(reinterpret_cast<const uint2*>(kb + (t0 + j) * kHd * 2)) : make_uint2(0u, 0u);
-        vr[j] = in ? __ldg(reinterpret_cast<const uint2*>(vb + (t0 + j) * kHd * 2)) : make_uint2(0u, 0u);
+        kr[j] = in ? ld_row8<kCoherent>(kb + (t0 + j) * kHd * 2) : make_uint2(0u, 0u);
+        vr[j] = in ? ld_row8<kCoherent>(vb + (t0 + j) * kHd * 2) : make_uint2(0u, 0u);
       }
       const bool mine_in = t0 + jl < end;
 #pragma unroll
@@ -168,8 +178,8 @@ __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id
   #pragma unroll
       for (int j = 0; j < kStep; ++j) {
         const bool in = t + j < end;
-        kk[j] = in ? __ldg(reinterpret_cast<const uint2*>(kb + (t + j) * kHd * 2)) : make_uint2(0u, 0u);
-        vv[j] = in ? __ldg(reinterpret_cast<const uint2*>(vb + (t + j) * kHd * 2)) : make_uint2(0u, 0u);
+        kk[j] = in ? ld_row8<kCoherent>(kb + (t + j) * kHd * 2) : make_uint2(0u, 0u);
+        vv[j] = in ? ld_row8<kCoherent>(vb + (t + j) * kHd * 2) : make_uint2(0u, 0u);
       }
     };
     load_rows(start + warp * kStep, kr, vr);

@@ -488,6 +488,22 @@ int rb_ipc_close(void* base) {
   return RB_OK;
 }
 
+int64_t rb_decode_layers_workspace(const rb_decode_step* st) {
+  int sms = 0, s = device_sms(&sms);
+  if (s != RB_OK) return -s;
+  return rb::decode_layers_workspace(st, sms);
+}
+
+int rb_decode_layers(const rb_decode_step* st, int dtype, int flags, void* stream) {
+  if (!st) return RB_ERR_NULL;
+  if (!act_dtype_ok(dtype)) return RB_ERR_DTYPE;
+  int sms = 0, s = device_sms(&sms);
+  if (s != RB_OK) return s;
+  s = rb::launch_decode_layers(st, dtype, flags, sms, static_cast<cudaStream_t>(stream));
+  if (s == RB_OK && cudaGetLastError() != cudaSuccess) s = RB_ERR_LAUNCH;
+  return s;
+}
+
 int rb_set_wait_limit(uint64_t ns, void* stream) {
   if (ns == 0) ns = rb::kMaxWaitNs;
   if (ns < 1000 || ns > 60000000000ull) return RB_ERR_SHAPE;

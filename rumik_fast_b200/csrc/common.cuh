@@ -31,6 +31,7 @@ enum : unsigned int {
   ERR_TP_WAIT = 1u << 8,      // tensor-parallel reduction timed out waiting for a peer's flag
   ERR_ARG = 1u << 9,          // a device-side argument (a decode position) was out of range; nothing stored
   ERR_ATT_WAIT = 1u << 10,    // a fused-attention launch timed out waiting for the attention outputs
+  ERR_STEP_WAIT = 1u << 11,   // the whole-step kernel gave up a wait (and aborted the launch)
 };
 
 // Upper bound on the wall time of one wait (an mbarrier phase, a peer's flag, a completion counter). Healthy

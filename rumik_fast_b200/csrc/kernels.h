@@ -59,6 +59,8 @@ int launch_sample(const rb_sampler* s, int flags, cudaStream_t stream);
 int64_t sample_workspace(int nz);
 // Decode attention (attn_decode.cu): workspace bytes (-1: unsupported shape) and the launch.
 int64_t attn_decode_workspace(int nq, int nkv, int hd);
+int64_t decode_layers_workspace(const rb_decode_step* d, int num_sms);
+int launch_decode_layers(const rb_decode_step* d, int dtype, int flags, int num_sms, cudaStream_t stream);
 int launch_attn_decode(const void* q, const void* kc, const void* vc, const int64_t* pos, void* out, int nq, int nkv,
                        int64_t S, float scale, void* ws, int dtype, int flags, int num_sms, cudaStream_t stream);
 // The add + LayerNorm of rb_add_layernorm (one CTA), bit-identical to the prologue of rb_gemv_int4_fused.

@@ -10,3 +10,4 @@
 #include "allreduce.cu"
 #include "attn_decode.cu"
 #include "sample.cu"
+#include "decode_step.cu"
