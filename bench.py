@@ -430,8 +430,6 @@ def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
     xin = None
     for L in range(nlayers):
         xout = xr[L % 2]
-        ln = (fused.AddLn(xin, buf_o, buf_d, lnw[L], xout, eps=c["eps"]) if L else
-              fused.AddLn.from_embedding(emb_q, emb_s, tok, lnw[0], xout, eps=c["eps"]))
         qkv = syn.int4_weights((nq + 2 * nkv) * hd, H, gen, dev)
         gu = fused.interleave_gate_up(*syn.int4_weights(2 * inter, H, gen, dev))
         if persistent:  # every layer in one launch of the whole-step kernel (DecodeLayers)
@@ -440,6 +438,8 @@ def build_step(dev, seed, nlayers, pos, attn_mode="separate"):
             pl_layers.append(dict(qkv=qkv, gate_up=gu, o_proj=wo, down=wd, ln_w=lnw[L], k_cache=kc[L],
                                   v_cache=vc[L], rope=L % 4 != 3))
             continue
+        ln = (fused.AddLn(xin, buf_o, buf_d, lnw[L], xout, eps=c["eps"]) if L else
+              fused.AddLn.from_embedding(emb_q, emb_s, tok, lnw[0], xout, eps=c["eps"]))
         layer_in.append(fused.AddLnGemvPost(qkv, gu, add_ln=ln, pos=pos_t, cos=cos, sin=sin, k_cache=kc[L],
                                             v_cache=vc[L], q_out=q_out, act=act, n_q_heads=nq, n_kv_heads=nkv,
                                             rope=L % 4 != 3))

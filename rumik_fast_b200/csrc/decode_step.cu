@@ -49,6 +49,8 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kXPad = 256;
 constexpr int kMaxLayers = 36;
 constexpr int kBarConv = 1;  // named barrier of all converter warps; 2 + s: the four warps of set s
+constexpr int kLnIter = 2;   // the prologue's 8-element chunks per converter thread: H <= 2 x 384 x 8 = 6144
+constexpr int kRegsIssue = 56, kRegsConv = 152;  // registers per thread of warpgroup 0 / the converter warpgroups
 enum : int { kQKV = 0, kGU = 1, kDown = 2, kO = 3 };
 enum : int { kPhA = 0, kPhD = 1, kPhO = 2 };
 // per-layer counters (workspace words, 8 per layer)
@@ -110,13 +112,31 @@ __device__ __forceinline__ int phase_rank(const DsParams& p, int ph, int sigma) 
   if (sigma % kSets == 0 && sigma / kSets < p.natt) return -1;
   return sigma - min(p.natt, (sigma + kSets - 1) / kSets);
 }
-// First pair of rank rho's range in phase ph (range rho = [first(rho), first(rho + 1))).
+// First pair of rank rho's range in phase ph (range rho = [first(rho), first(rho + 1))). 32-bit arithmetic: the
+// host checks T x S < 2^31.
 __device__ __forceinline__ int range_first(const DsParams& p, int ph, int rho) {
-  return static_cast<int>(static_cast<int64_t>(p.T[ph]) * rho / phase_sets(p, ph));
+  return static_cast<int>(static_cast<unsigned int>(p.T[ph] * rho) / static_cast<unsigned int>(phase_sets(p, ph)));
 }
 // Rank owning pair t of phase ph.
 __device__ __forceinline__ int owner(const DsParams& p, int ph, int t) {
-  return static_cast<int>(((static_cast<int64_t>(t) + 1) * phase_sets(p, ph) - 1) / p.T[ph]);
+  return static_cast<int>(static_cast<unsigned int>((t + 1) * phase_sets(p, ph) - 1) / static_cast<unsigned int>(p.T[ph]));
+}
+// The shares of a block whose pairs are [t0, t0 + np): with at least as many pairs as sets in the phase every range
+// is non-empty and the block's shares are the ranges of its first to last owner; with fewer, every range holds at
+// most one pair and each pair is a share. first_of(k): the first pair of share k.
+struct Shares {
+  int n, o0, t0, per_pair;
+};
+__device__ __forceinline__ Shares block_shares(const DsParams& p, int ph, int t0, int np) {
+  Shares r;
+  r.t0 = t0;
+  r.per_pair = p.T[ph] < phase_sets(p, ph);
+  r.o0 = owner(p, ph, t0);
+  r.n = r.per_pair ? np : owner(p, ph, t0 + np - 1) - r.o0 + 1;
+  return r;
+}
+__device__ __forceinline__ int share_first(const DsParams& p, int ph, const Shares& sh, int k) {
+  return sh.per_pair ? sh.t0 + k : max(sh.t0, range_first(p, ph, sh.o0 + k));
 }
 // Entry kind, block (within the entry), pair (within the block), the block's first pair in the phase, and the
 // block's index among the phase's blocks, of pair t of phase ph.
@@ -208,6 +228,24 @@ __device__ __forceinline__ void unpack_codes(const uint4* w, uint32_t* o) {
   }
 }
 
+// The MMA issuer's wait for a set's converters: between polls it sleeps, so that an idle issuer (a phase boundary,
+// the attention) takes no issue slots from the converter warps of its SM sub-partition.
+__device__ bool mbar_wait_idle(const DsParams& p, uint64_t* bar, uint32_t parity) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns(), lim = wait_limit_ns();
+  for (int n = 1;; ++n) {
+    __nanosleep(64);
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((n & 15) == 0) {
+      if (aborted(p)) return false;
+      if (globaltimer_ns() - t0 > lim) {
+        set_abort(p, ERR_STEP_WAIT);
+        return false;
+      }
+    }
+  }
+}
+
 // ---- activation tables (the layout of gemv_int4_tc.cu) ----
 __device__ void build_plain(const void* src, int K, bool bf, uint8_t* tab, float2* cst, int ct) {
   const int chunks = K / 8;
@@ -223,12 +261,6 @@ __device__ void build_plain(const void* src, int K, bool bf, uint8_t* tab, float
   for (int i = ct; i < static_cast<int>(kXPad / 16); i += kConvThreads)
     reinterpret_cast<uint4*>(tab + (K / 128) * kXGroupBytes)[i] = make_uint4(0u, 0u, 0u, 0u);
 }
-
-// One share (segment) of a block: pairs [t, t1) of phase ph in layer l.
-struct Seg {
-  int l, ph, t, t1;
-  float acc;
-};
 
 template <int REP>
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_constant__ DsParams p) {
@@ -271,18 +303,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   __syncthreads();
   mm4::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Register split: warpgroup 0 (producer + MMA issuers) gives registers to the three converter warpgroups. The
+  // shares add up to the launch's 128 per thread: 4 x 32 x kRegsIssue + 12 x 32 x kRegsConv = 512 x 128.
+  // Each role's code sits inside the branch that sets its limit, so that the compiler allocates it accordingly.
+  static_assert(4 * 32 * kRegsIssue + kConvWarps * 32 * kRegsConv == kThreads * 128, "register split");
   // the token's position: every CTA makes the same decision, so an invalid one skips the whole launch
   const int64_t pos = __ldcg(p.pos);
   const bool pos_ok = pos >= 0 && pos < p.cache_len;
   if (!pos_ok && tid == 0 && cta == 0) atomicOr(&g_device_error, ERR_ARG);
 
+  if (warp < kFirstConv) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsIssue));
   if (!pos_ok) {
     // nothing to do
   } else if (warp == 0) {
     // ---------------- producer: the codes of every set's pairs, in each set's order ----------------
     if (lane == 0) {
-      int l[kSets], ph[kSets], t[kSets], t1[kSets], issued[kSets];
-      bool live[kSets];
+      int l[kSets] = {0, 0, 0}, ph[kSets] = {0, 0, 0}, t[kSets] = {0, 0, 0}, t1[kSets] = {0, 0, 0};
+      int issued[kSets] = {0, 0, 0};
+      bool live[kSets] = {false, false, false};
       auto open = [&](int s) {  // move set s to its next non-empty range at or after (l, ph)
         const int sigma = cta * kSets + s;
         while (l[s] < p.nl) {
@@ -298,6 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
           }
         }
       };
+#pragma unroll
       for (int s = 0; s < kSets; ++s) {
         l[s] = 0;
         ph[s] = 0;
@@ -310,10 +350,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       bool ok = true;
       while (ok && (live[0] || live[1] || live[2])) {
         bool progress = false;
+#pragma unroll
         for (int s = 0; s < kSets; ++s) {
           if (!live[s]) continue;
           const int slot = issued[s] % kNst;
-          if (issued[s] >= kNst && !mbar_try_wait(empty(s, slot), ((issued[s] / kNst) - 1) & 1)) continue;
+          // non-blocking: a full ring (a set waiting for its phase's inputs) must not hold up the others
+          if (issued[s] >= kNst && !mbar_test_wait(empty(s, slot), ((issued[s] / kNst) - 1) & 1)) continue;
           const PairAt a = pair_at(p, ph[s], t[s]);
           mbar_arrive_expect_tx(full(s, slot), kStageBytes);
           mm4::tma_load_2d(smem + (static_cast<size_t>(s) * kNst + slot) * kStageBytes, &p.maps[4 * l[s] + a.e],
@@ -332,7 +374,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         // no set had ring space: bounded by the wait limit without progress, and by the abort flag
         if (progress) {
           idle_since = 0;
-        } else if ((++spins & 63) == 0) {
+        } else {
+          // every ring full: sleep rather than poll, so that this warp takes no issue slots from the converter
+          // warps of its SM sub-partition (a stage takes about a microsecond to consume)
+          __nanosleep(128);
+        }
+        if (!progress && (++spins & 15) == 0) {
           if (aborted(p)) ok = false;
           const unsigned long long now = globaltimer_ns();
           if (idle_since == 0) {
@@ -363,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
           const uint32_t xtab = smem_u32(smem + p.tab[ph]);
           for (int t = ta; t < tb; ++t, ++q) {
             const int b = q % kNP;
-            if (!mbar_wait_ab(p, afull(s, b), (q / kNP) & 1)) {
+            if (!mbar_wait_idle(p, afull(s, b), (q / kNP) & 1)) {
               ok = false;
               break;
             }
@@ -382,7 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       }
       if (q > 0) (void)mbar_wait_ab(p, mdone(s, (q - 1) % kNP), ((q - 1) / kNP) & 1);  // no MMA in flight at exit
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsConv));
+  if (pos_ok) {
     // ---------------- converters, epilogues, tables and attention ----------------
     const int ct = tid - kFirstConv * 32;  // 0 .. kConvThreads - 1
     const int cw = warp - kFirstConv;
@@ -396,50 +446,47 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     const int sbar = 2 + s;
     bool dead = false;
     int q = 0, st = 0;  // pairs of this set so far (tensor-memory buffer q % kNP), ring stages consumed
-    // pending results: the pair in buffer b belongs to segment slot pslot[b]; sa / sb = scale * delta / 16 of its
-    // two groups, mt = its min terms; plast[b]: the segment's last pair
-    int pslot[kNP] = {0, 0}, plast[kNP] = {0, 0}, npend = 0;
-    float psa[kNP] = {0.f, 0.f}, psb[kNP] = {0.f, 0.f}, pmt[kNP] = {0.f, 0.f};
-    Seg seg[2];
-    seg[0].acc = seg[1].acc = 0.f;
-    int cur = 1;  // slot of the newest segment
+    // The two pairs whose results are pending (issued, not read yet), older first: sa / sb = scale * delta / 16 of
+    // their two groups, mt = their min terms; `last`: the pair ends its segment (share) [t, t1). Results are read
+    // in pair order, so one accumulator holds the segment being read; a phase ends with a drain, so rd_l / rd_ph
+    // (the layer and phase of the pending pairs) are per phase.
+    struct Pend {
+      float sa, sb, mt;
+      int last, t, t1;
+    };
+    Pend po = {0.f, 0.f, 0.f, 0, 0, 0}, pn = po;
+    int npend = 0, rd_l = 0, rd_ph = 0;
+    float acc = 0.f;
 
-    // The end of a segment's share: its sum becomes the row's result (a whole block), or an fp32 partial whose
-    // block's last share adds all shares in order. Then the epilogue and the block's completion count.
-    auto finalize = [&](Seg& g) {
-      const int l = g.l, ph = g.ph;
-      const PairAt a = pair_at(p, ph, g.t);
+    // The end of a share [t, t1) of phase ph in layer l with sum r: the row's result (a whole block), or an fp32
+    // partial whose block's last share adds all shares in order. Then the epilogue and the block's completion count.
+    auto finalize = [&](int l, int ph, int t, int t1, float r) {
+      const PairAt a = pair_at(p, ph, t);
       const int np = p.np[a.e];
       const int N = entry_rows(p, a.e);
       const int row = a.blk * kRows + rib;
       const bool row_ok = row < N;
-      float r = g.acc;
-      g.acc = 0.f;
       bool have = true;
-      if (!(g.t == a.t0 && g.t1 == a.t0 + np)) {  // shared block
-        p.part[ph][static_cast<int64_t>(g.t) * kRows + rib] = r;
-        __threadfence();
+      if (!(t == a.t0 && t1 == a.t0 + np)) {  // shared block
+        // Every thread stores its partial; the barrier orders those stores before thread 0's acq_rel ticket add
+        // (which releases them at GPU scope), and the last share's loads follow its acquire through the barrier.
+        p.part[ph][static_cast<int64_t>(t) * kRows + rib] = r;
+        const Shares sh = block_shares(p, ph, a.t0, np);
         named_bar_sync(sbar, 128);
         if (rib == 0) {
-          // shares of the block: one starts at its first pair and at every later pair that begins a set's range
-          // (sets whose range is empty - a phase with fewer pairs than sets - own no share)
-          int shares = 1;
-          for (int u = a.t0 + 1; u < a.t0 + np; ++u) shares += range_first(p, ph, owner(p, ph, u)) == u;
           unsigned int prev;
           asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
                        : "=r"(prev)
                        : "l"(p.ticket + ticket_base(p, ph) + a.gb)
                        : "memory");
-          last_flag[s] = prev == static_cast<unsigned int>(shares - 1) ? 1 : 0;
+          last_flag[s] = prev == static_cast<unsigned int>(sh.n - 1) ? 1 : 0;
         }
         named_bar_sync(sbar, 128);
         have = last_flag[s] != 0;
         if (have) {
-          __threadfence();
           r = 0.f;
-          for (int u = a.t0; u < a.t0 + np; ++u)  // the shares in pair order, each at its first pair
-            if (u == a.t0 || range_first(p, ph, owner(p, ph, u)) == u)
-              r += __ldcg(p.part[ph] + static_cast<int64_t>(u) * kRows + rib);
+          for (int k = 0; k < sh.n; ++k)  // the shares in pair order, each stored at its first pair
+            r += __ldcg(p.part[ph] + static_cast<int64_t>(share_first(p, ph, sh, k)) * kRows + rib);
           if (rib == 0) p.ticket[ticket_base(p, ph) + a.gb] = 0u;  // ready for the next layer
         }
       }
@@ -465,16 +512,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       } else if (row_ok && !dead) {
         store_out(a.e == kDown ? p.bd[par] : p.bo[par], row, r, bf);
       }
-      named_bar_sync(sbar, 128);
+      named_bar_sync(sbar, 128);  // every row stored: the release below publishes them (barrier cumulativity)
       if (rib == 0) {
-        __threadfence();
         const int c = a.e == kQKV ? kCtrQkv : a.e == kGU ? kCtrAct : kCtrOut;
         red_release_gpu(p.ctr + l * kCtrPerLayer + c, 1u);
       }
     };
 
-    // Results of the pair in buffer b (issued kNP pairs ago): its two groups' accumulators into its segment.
-    auto read_pair = [&](int b, uint32_t qq) {
+    // Results of pending pair e, in tensor-memory buffer b and issued as this set's pair qq: its two groups'
+    // accumulators into the segment sum; the segment's last pair finalizes it.
+    auto read_pair = [&](const Pend& e, int b, uint32_t qq) {
       int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
       bool ok = !dead && mbar_wait_ab(p, mdone(s, b), (qq / kNP) & 1);
       ok = __all_sync(0xffffffffu, ok);
@@ -487,23 +534,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       } else {
         dead = true;
       }
-      Seg& g = seg[pslot[b]];
-      g.acc += pmt[b] + psa[b] * g4t::group_dot16(d0) + psb[b] * g4t::group_dot16(d1);
-      if (plast[b]) finalize(g);
+      acc += e.mt + e.sa * g4t::group_dot16(d0) + e.sb * g4t::group_dot16(d1);
+      if (e.last) {
+        finalize(rd_l, rd_ph, e.t, e.t1, acc);
+        acc = 0.f;
+      }
     };
 
     // Drain: every pending pair's results, oldest first.
     auto drain = [&]() {
-      for (int i = npend; i > 0; --i) {
-        const uint32_t qq = static_cast<uint32_t>(q - i);
-        read_pair(qq % kNP, qq);
-      }
+      if (npend >= 1) read_pair(po, (q - npend) % kNP, static_cast<uint32_t>(q - npend));
+      if (npend == 2) read_pair(pn, (q - 1) % kNP, static_cast<uint32_t>(q - 1));
       npend = 0;
     };
 
     // The set's pairs [ta, tb) of phase ph in layer l.
     auto run_pairs = [&](int l, int ph, int ta, int tb) {
       const float2* cst = reinterpret_cast<const float2*>(smem + p.cst[ph]);
+      rd_l = l;
+      rd_ph = ph;
       uint4 wn[8];
       auto load_codes = [&]() {
         const int slot = st % kNst;
@@ -516,39 +565,50 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
 #pragma unroll
         for (int c = 0; c < 8; ++c) wn[c] = lds128(rowp + ((c ^ (rib & 7)) << 4));
       };
-      if (ta < tb) load_codes();
-      for (int t = ta; t < tb; ++t) {
+      // the scale and min words of pair t (two groups each) of this thread's row; loaded a pair ahead
+      auto scale_words = [&](int t, uint32_t& sw, uint32_t& mw) {
         const PairAt a = pair_at(p, ph, t);
         const int G = p.np[a.e] * 2;
         const int row = a.blk * kRows + rib;
-        const int64_t r0 = row < entry_rows(p, a.e) ? row : 0;
-        const uint32_t sw = __ldg(reinterpret_cast<const uint32_t*>(p.L[l].s[a.e] + r0 * G + 2 * a.k));
-        const uint32_t mw = __ldg(reinterpret_cast<const uint32_t*>(p.L[l].m[a.e] + r0 * G + 2 * a.k));
+        const int64_t off = static_cast<int64_t>(row < entry_rows(p, a.e) ? row : 0) * G + 2 * a.k;
+        sw = __ldg(reinterpret_cast<const uint32_t*>(p.L[l].s[a.e] + off));
+        mw = __ldg(reinterpret_cast<const uint32_t*>(p.L[l].m[a.e] + off));
+      };
+      uint32_t sw_n = 0u, mw_n = 0u;
+      if (ta < tb) {
+        scale_words(ta, sw_n, mw_n);
+        load_codes();
+      }
+      int seg_t = ta;
+      for (int t = ta; t < tb; ++t) {
+        const PairAt a = pair_at(p, ph, t);
+        const uint32_t sw = sw_n, mw = mw_n;
+        if (t + 1 < tb) scale_words(t + 1, sw_n, mw_n);
         const uint4 w[8] = {wn[0], wn[1], wn[2], wn[3], wn[4], wn[5], wn[6], wn[7]};
         __syncwarp();
         if (lane == 0 && !dead) mbar_arrive(empty(s, st % kNst));  // both groups of this stage are in registers
         ++st;
         const int b = q % kNP;
-        // the pair kNP back used buffer b: its results first. This may finish its segment, whose slot a segment
-        // starting at this pair then takes (the slot of the segment before the current one, which ended at or
-        // before that pair).
+        // the pair kNP back used buffer b: its results first (this may finish its segment)
         if (npend == kNP) {
-          read_pair(b, static_cast<uint32_t>(q - kNP));
-          --npend;
+          read_pair(po, b, static_cast<uint32_t>(q - kNP));
+          po = pn;
+          npend = 1;
         }
-        if (t == ta || a.k == 0) {  // a new segment
-          cur ^= 1;
-          seg[cur].l = l;
-          seg[cur].ph = ph;
-          seg[cur].t = t;
-          seg[cur].t1 = min(tb, a.t0 + p.np[a.e]);
-        }
+        if (a.k == 0) seg_t = t;  // a block's first pair starts a new segment (so does the range's first pair)
         const float2 ca = cst[2 * a.k], cb = cst[2 * a.k + 1];
-        pslot[b] = cur;
-        plast[b] = t + 1 == seg[cur].t1;
-        psa[b] = g4t::h2f_lo(sw) * ca.x;
-        psb[b] = g4t::h2f_hi(sw) * cb.x;
-        pmt[b] = g4t::h2f_lo(mw) * ca.y + g4t::h2f_hi(mw) * cb.y;
+        Pend e;
+        e.sa = g4t::h2f_lo(sw) * ca.x;
+        e.sb = g4t::h2f_hi(sw) * cb.x;
+        e.mt = g4t::h2f_lo(mw) * ca.y + g4t::h2f_hi(mw) * cb.y;
+        e.t = seg_t;
+        e.t1 = min(tb, a.t0 + p.np[a.e]);
+        e.last = t + 1 == e.t1;
+        if (npend == 0)
+          po = e;
+        else
+          pn = e;
+        ++npend;
         if (!dead) {
           uint32_t o[32];
           unpack_codes(w, o);
@@ -564,7 +624,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         __syncwarp();
         if (lane == 0 && !dead) mbar_arrive(afull(s, b));
         ++q;
-        ++npend;
       }
     };
 
@@ -617,7 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         }
         uint8_t* tab = smem + p.tab[kPhA];
         float2* cstp = reinterpret_cast<float2*>(smem + p.cst[kPhA]);
-        stage_ln<g4t::kLnIter>(S, bf, aux, kBarConv, ct, kConvThreads, cta == 0,
+        stage_ln<kLnIter>(S, bf, aux, kBarConv, ct, kConvThreads, cta == 0,
                                [&](const float (&h)[8], bool valid, int c) { g4t::quant_chunk(h, valid, c, tab, cstp); });
         for (int i = ct; i < static_cast<int>(kXPad / 16); i += kConvThreads)
           reinterpret_cast<uint4*>(tab + GH * kXGroupBytes)[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -686,6 +745,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     }
     drain();
   }
+  }
 
   mm4::tc_fence_before();
   __syncthreads();
@@ -749,7 +809,7 @@ static int decode_plan(const rb_decode_step* d, int num_sms, dstep::DsParams* p,
   const int rep = d->n_q_heads / d->n_kv_heads;
   if (rep < 1 || rep > 4 || d->n_kv_heads > attn::kMaxKv) return RB_ERR_SHAPE;
   const int64_t H = d->H, I = d->I, QD = static_cast<int64_t>(d->n_q_heads) * d->head_dim;
-  if (H < 256 || H % 256 || H > 12288 || I < 256 || I % 256 || I > 16384 || QD % 256 || QD > 16384)
+  if (H < 256 || H % 256 || H > kLnIter * kConvThreads * 8 || I < 256 || I % 256 || I > 16384 || QD % 256 || QD > 16384)
     return RB_ERR_SHAPE;
   if (d->cache_len < 1 || d->cache_len > (int64_t(1) << 31) || !(d->eps >= 0.f)) return RB_ERR_SHAPE;
   int nb[4], np[4];
@@ -768,6 +828,8 @@ static int decode_plan(const rb_decode_step* d, int num_sms, dstep::DsParams* p,
   // every set takes pairs in phase A and every non-attention set in phase D: what makes the per-parity buffers
   // safe to reuse two layers later (the module comment)
   if (T[kPhA] < S || T[kPhD] < S - natt) return RB_ERR_SHAPE;
+  for (int ph = 0; ph < 3; ++ph)  // the kernel's schedule arithmetic is 32-bit
+    if (static_cast<int64_t>(T[ph] + 1) * S >= (int64_t(1) << 31)) return RB_ERR_SHAPE;
   *wl = ws_layout(d->n_layers, nb[0] + nb[1] + nb[2] + nb[3], d->n_q_heads, d->n_kv_heads, T);
   if (!p) return RB_OK;
   for (int i = 0; i < 4; ++i) {
