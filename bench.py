@@ -45,6 +45,8 @@ PREFILL_TOKENS = (34, 256, 1024)
 # DRAM bytes (read + write) per launch of gemv_int4_tc_kernel on the 36-layer set: ncu capture of the 3-layer
 # case of the current build scaled x12 by blocks streamed (profiles/gemv_int4_tc_3layer_traffic.md)
 NCU_TRAFFIC_PER_LAUNCH = 1966808064
+# The same for the one launch of the 144 projections and the int8 head's rows (the default step): not yet captured
+NCU_TRAFFIC_STEP_LAUNCH = None
 
 
 def parse():
@@ -55,9 +57,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefetch", action="store_true", help="do not stream weights before the PDL wait")
     ap.add_argument("--no-extras", action="store_true", help="headline only: no step/prefill/gemv_c0/chain records")
-    ap.add_argument("--head", default="concurrent", choices=["concurrent", "serial"],
-                    help="set mode: the int8 head on a forked branch of the step graph (concurrent with the "
-                         "projection list) or after the list in stream order")
+    ap.add_argument("--head", default="concurrent", choices=["list", "concurrent", "serial"],
+                    help="set mode: the int8 head's rows as the first entry of the projection launch (list), its "
+                         "own launch on a forked branch of the step graph (concurrent) or after the list (serial)")
     ap.add_argument("--mode", default="set", choices=["set", "chain"],
                     help="set: the 144 projections as one persistent launch (Int4GemvSet); chain: one launch each")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -222,12 +224,13 @@ def build_workload(dev, seed, nlayers=LAYERS, scales="fp16"):
                 head_bytes=head_bytes)
 
 
-def step_fn(w, mode="set", with_head=True, head="concurrent"):
+def step_fn(w, mode="set", with_head=True, head="list"):
     """One decode step's projections: 36 x (QKV, o_proj, gate_up with x_h; down with x_i) + the int8 head.
-    mode "set": the 144 int4 GEMVs as one persistent launch, with the head (independent of them) on a forked branch
-    of the step's graph, launched first: its CTAs take SMs while the projection list starts on the others, and the
-    list's dynamic schedule gives the CTAs that start late fewer blocks. "chain": one launch per GEMV, in stream
-    order, as an unmodified engine issues them."""
+    mode "set": the 144 int4 GEMVs as one persistent launch; the head (independent of them) by `head`:
+      "list"       its int8 rows are the first entry of that launch (one more kind of work item);
+      "concurrent" its own launch on a forked branch of the step's graph, launched first;
+      "serial"     its own launch after the list.
+    mode "chain": one launch per GEMV, in stream order, as an unmodified engine issues them."""
     import rumik_fast_b200 as rb
     layers, outs, xh, xi = w["layers"], w["outs"], w["xh"], w["xi"]
     side = None
@@ -235,6 +238,9 @@ def step_fn(w, mode="set", with_head=True, head="concurrent"):
         entries = []
         for L in layers:
             entries += [(xh, *L[0], outs[0]), (xh, *L[1], outs[1]), (xh, *L[2], outs[2]), (xi, *L[3], outs[3])]
+        if with_head and head == "list":
+            entries = [(xh, *w["head"], None, w["logits"])] + entries
+            with_head = False
         projections = rb.Int4GemvSet(entries)
         side = torch.cuda.Stream() if head == "concurrent" else None
     else:
@@ -732,7 +738,8 @@ def run_ours(a):
     g_step = capture(step_fn(w, a.mode, head=a.head))
     g_int4 = capture(step_fn(w, a.mode, with_head=False))
     int4_bytes = w["int4_bytes"]
-    step_bytes = int4_bytes + w["head_bytes"]
+    w_head_bytes = w["head_bytes"]
+    step_bytes = int4_bytes + w_head_bytes
     logits_bytes = w["logits"].numel() * 2
 
     with ClockSampler(dev) as clk:
@@ -741,10 +748,16 @@ def run_ours(a):
         m1 = clk.mark()
         ms_step = ms / a.steps
 
-        # dominant kernel: the int4 projections (97 % of the step's bytes), timed alone over the same steps
+        # the int4 projections alone over the same steps: the dominant kernel when the head has its own launch,
+        # and what the head costs inside the step (step - projections)
         ms4 = timed(g_int4.replay, max(1, a.steps // 2), a.warmup, world) / max(1, a.steps // 2)
         launches4 = 1 if a.mode == "set" else a.layers * 4
-        achieved = (int4_bytes / launches4) / (ms4 / launches4 * 1e-3) / 1e9
+        one_launch = a.mode == "set" and a.head == "list"  # the step IS one launch of the list kernel
+        if one_launch:
+            roof_bytes, roof_ms, roof_launches = step_bytes, ms_step, 1
+        else:
+            roof_bytes, roof_ms, roof_launches = int4_bytes, ms4, launches4
+        achieved = (roof_bytes / roof_launches) / (roof_ms / roof_launches * 1e-3) / 1e9
         peak, peak_kind, _ = peaks()
 
         # end to end through the public API: pinned host inputs -> device, step, logits -> pinned host
@@ -782,8 +795,9 @@ def run_ours(a):
             "config": {"workload": "config-1 36-layer decode-step projection set (QKV 5120x3072, o 3072x3072, "
                                    "gate_up 16384x3072, down 3072x8192; int4 g128) + config-2 int8 head "
                                    "16385x3072, batch 1, in one CUDA graph",
-                       "launches": "144 projections in one persistent launch + the head" if a.mode == "set"
-                       else "145 stream-ordered launches",
+                       "launches": ("144 projections and the int8 head's rows in one persistent launch"
+                                    if a.head == "list" else f"144 projections in one persistent launch + the "
+                                    f"head ({a.head})") if a.mode == "set" else "145 stream-ordered launches",
                        "batch": 1, "bytes_per_step": step_bytes, "parallelism": f"replica x{world}",
                        "weight_prefetch": not a.no_prefetch,
                        "l2": "no flush: 1.98 GB of weights per step > 126 MB L2",
@@ -797,12 +811,18 @@ def run_ours(a):
                     "ms_per_step": round(ms_e2e, 5)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "kernel": "gemv_int4_tc_kernel" if a.mode == "set" else "gemv_int4_kernel",
-                         "traffic": NCU_TRAFFIC_PER_LAUNCH if a.mode == "set" and a.layers == LAYERS else None,
-                         "algorithmic_bytes_per_launch": int4_bytes // launches4},
+                         "kernel": ("gemv_int4_tc_kernel (144 projections + the int8 head's rows)" if one_launch
+                                    else "gemv_int4_tc_kernel") if a.mode == "set" else "gemv_int4_kernel",
+                         "traffic": (NCU_TRAFFIC_STEP_LAUNCH if one_launch else NCU_TRAFFIC_PER_LAUNCH)
+                         if a.mode == "set" and a.layers == LAYERS else None,
+                         "algorithmic_bytes_per_launch": roof_bytes // roof_launches},
+            "head": {"placement": a.head if a.mode == "set" else "chain", "bytes": w_head_bytes,
+                     "step_minus_projections_us": round((ms_step - ms4) * 1e3, 2),
+                     "marginal_gbs": round(w_head_bytes / max(ms_step - ms4, 1e-6) / 1e6, 1),
+                     "marginal_frac": round(w_head_bytes / max(ms_step - ms4, 1e-6) / 1e6 / peak, 4)},
             "cpu_baseline": cpu,
             "clocks": clocks,
-            "gpu_launches": a.steps * (launches4 + 1),
+            "gpu_launches": a.steps * (1 if one_launch else launches4 + 1),
             "mode": a.mode,
         }
         line.update(extras)

@@ -152,7 +152,14 @@ typedef struct rb_gemv_desc {
    * kernel only (with RB_FLAG_KERNEL_MMA or fused attention: RB_ERR_SHAPE). No reference counterpart: the
    * byte saving rumik-fast names as its next step (engine/README.md:192-193). */
   const float* s_row;
+  /* 0: an int4 entry as above. RB_W8_SIGNED / RB_W8_OFFSET: an int8 entry, y = s * (q @ x) - the int8 head
+   * (gemv_int8, kernels/cuda_gemv.py:138-195) streamed as more rows of the same launch. q holds int8 codes
+   * [N, K] (RB_W8_OFFSET: uint8 = int8 + 128, quantize_int8_rows' storage), 16-byte aligned; the per-row scales
+   * [N] are s_row (fp32, 4-byte aligned) or, when s_row is NULL, s (fp16); m is unused. Such entries run on the
+   * tcgen05 kernel only, with the store epilogue (RB_FLAG_KERNEL_MMA or another epilogue: RB_ERR_SHAPE). */
+  int w8;
 } rb_gemv_desc;
+enum rb_w8 { RB_W8_NONE = 0, RB_W8_SIGNED = 1, RB_W8_OFFSET = 2 };
 
 /*
  * A list of independent int4 GEMVs (batch 1) in one persistent launch: y_i = W_i x_i for every entry.

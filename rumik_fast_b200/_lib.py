@@ -27,7 +27,10 @@ _vp, _i64, _int = _c.c_void_p, _c.c_int64, _c.c_int
 class GemvDesc(ctypes.Structure):
     """struct rb_gemv_desc (include/rumik_b200.h)."""
     _fields_ = [("x", _vp), ("y", _vp), ("q", _vp), ("s", _vp), ("m", _vp), ("N", _i64), ("K", _i64),
-                ("s_row", _vp)]
+                ("s_row", _vp), ("w8", _int)]
+
+
+W8_NONE, W8_SIGNED, W8_OFFSET = 0, 1, 2
 
 class AddLn(ctypes.Structure):
     """struct rb_add_ln (include/rumik_b200.h)."""

@@ -116,8 +116,24 @@ static bool scales_aligned(const rb_gemv_desc& d) {
 
 static bool any_scales8(const rb_gemv_desc* d, int count) {
   for (int i = 0; i < count; ++i)
-    if (d[i].s_row) return true;
+    if (d[i].s_row && d[i].w8 == RB_W8_NONE) return true;
   return false;
+}
+
+// int8 entries (rb_gemv_desc::w8): the tcgen05 list kernel only.
+static bool any_w8(const rb_gemv_desc* d, int count) {
+  for (int i = 0; i < count; ++i)
+    if (d[i].w8 != RB_W8_NONE) return true;
+  return false;
+}
+
+// An int8 entry's pointers: x, y, q (16-byte aligned) and its row scales, s_row (fp32, 4-byte aligned) or s (fp16).
+static int check_w8(const rb_gemv_desc& d) {
+  if (d.w8 != RB_W8_SIGNED && d.w8 != RB_W8_OFFSET) return RB_ERR_SHAPE;
+  if (!d.x || !d.y || !d.q || (!d.s_row && !d.s)) return RB_ERR_NULL;
+  const uintptr_t sp = d.s_row ? reinterpret_cast<uintptr_t>(d.s_row) : reinterpret_cast<uintptr_t>(d.s);
+  if (!aligned16(d.x) || !aligned16(d.q) || (sp & (d.s_row ? 3u : 1u))) return RB_ERR_ALIGN;
+  return RB_OK;
 }
 
 static int check_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_dtype) {
@@ -126,6 +142,11 @@ static int check_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_
   for (int i = 0; i < count; ++i) {
     const rb_gemv_desc& d = descs[i];
     if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.K > 16384 || d.N > (int64_t(1) << 30)) return RB_ERR_SHAPE;
+    if (d.w8 != RB_W8_NONE) {
+      const int st = check_w8(d);
+      if (st != RB_OK) return st;
+      continue;
+    }
     if (!d.x || !d.y || !d.q || !d.s || (!d.m && !d.s_row)) return RB_ERR_NULL;
     if (!aligned16(d.x) || !aligned16(d.q) || !aligned16(d.s) || !scales_aligned(d)) return RB_ERR_ALIGN;
   }
@@ -138,14 +159,15 @@ static int check_multi(const rb_gemv_desc* descs, int count, int x_dtype, int y_
 #ifndef RB_SMALL_LIST_BYTES
 #define RB_SMALL_LIST_BYTES (int64_t(128) << 20)
 #endif
-// A list with 8-bit scales cannot be forced onto the warp-MMA kernel, which has no decoder for them.
+// A list with 8-bit scales or int8 entries cannot be forced onto the warp-MMA kernel, which has no path for them.
 static bool kernel_ok(const rb_gemv_desc* d, int count, int flags) {
-  return !((flags & RB_FLAG_KERNEL_MMA) && any_scales8(d, count));
+  return !((flags & RB_FLAG_KERNEL_MMA) && (any_scales8(d, count) || any_w8(d, count)));
 }
 
 static bool small_list(const rb_gemv_desc* d, int count, int flags) {
   if (flags & RB_FLAG_KERNEL_TC) return false;
-  if (any_scales8(d, count)) return false;  // 8-bit scales: the tcgen05 kernel only (kernel_ok refuses MMA)
+  // 8-bit scales, int8 entries: the tcgen05 kernel only (kernel_ok refuses MMA)
+  if (any_scales8(d, count) || any_w8(d, count)) return false;
   if (flags & RB_FLAG_KERNEL_MMA) return true;
   int64_t bytes = 0;
   for (int i = 0; i < count; ++i) bytes += d[i].N * (d[i].K / 2);
@@ -188,6 +210,7 @@ int64_t rb_gemv_int4_workspace(const rb_gemv_desc* descs, int count, int flags) 
   for (int i = 0; i < count; ++i) {
     const rb_gemv_desc& d = descs[i];
     if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.K > 16384 || d.N > (int64_t(1) << 30)) return -RB_ERR_SHAPE;
+    if (d.w8 < RB_W8_NONE || d.w8 > RB_W8_OFFSET) return -RB_ERR_SHAPE;
     if (!d.q) return -RB_ERR_NULL;
   }
   if (!kernel_ok(descs, count, flags)) return -RB_ERR_SHAPE;
@@ -312,6 +335,7 @@ int rb_gemv_int4_fused(const rb_gemv_desc* descs, const rb_gemv_epi* epis, int c
     const rb_gemv_desc& d = descs[i];
     const int kind = epis ? epis[i].kind : RB_EPI_STORE;
     if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.K > 16384 || d.N > (int64_t(1) << 30)) return RB_ERR_SHAPE;
+    if (d.w8 != RB_W8_NONE) return RB_ERR_SHAPE;  // int8 entries: rb_gemv_int4_multi(_ws) only
     if (!d.q || !d.s || (!d.m && !d.s_row)) return RB_ERR_NULL;
     if (!d.x && !ln) return RB_ERR_NULL;
     if (!d.x && d.K != ln->H) return RB_ERR_SHAPE;

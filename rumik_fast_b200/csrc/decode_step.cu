@@ -912,7 +912,7 @@ int launch_decode_layers(const rb_decode_step* d, int dtype, int flags, int num_
     if (!Ly.ln_w || !Ly.k_cache || !Ly.v_cache) return RB_ERR_NULL;
     for (int e = 0; e < 4; ++e) {
       if (!g[e]->q || !g[e]->s || !g[e]->m) return RB_ERR_NULL;
-      if (g[e]->s_row) return RB_ERR_SHAPE;  // fp16 scales only
+      if (g[e]->s_row || g[e]->w8 != RB_W8_NONE) return RB_ERR_SHAPE;  // int4 codes with fp16 scales only
       if (g[e]->N != Ns[e] || g[e]->K != Ks[e]) return RB_ERR_SHAPE;
       if ((reinterpret_cast<uintptr_t>(g[e]->q) | reinterpret_cast<uintptr_t>(g[e]->s) |
            reinterpret_cast<uintptr_t>(g[e]->m)) & 15u)

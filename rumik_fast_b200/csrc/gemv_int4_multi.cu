@@ -659,7 +659,8 @@ int launch_gemv_int4_multi(const rb_gemv_desc* d, int count, int x_dtype, int y_
   // the activation tables) in shared memory use 8-row tiles
   int64_t kmax = 0;
   for (int i = 0; i < count; ++i) {
-    if (d[i].s_row) return RB_ERR_SHAPE;  // 8-bit double-quantised scales: the tcgen05 kernel only
+    // 8-bit double-quantised scales, int8 entries: the tcgen05 kernel only
+    if (d[i].s_row || d[i].w8 != RB_W8_NONE) return RB_ERR_SHAPE;
     kmax = std::max(kmax, d[i].K);
   }
   const int TR = (2u * tile_bytes(16, static_cast<int>(kmax), static_cast<int>(kmax / 128)) +

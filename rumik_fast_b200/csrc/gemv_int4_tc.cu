@@ -69,8 +69,15 @@ struct Entry {
   // K split: each 128-row block is cut into `ks` slices of `ppk` pairs of groups (the last may be shorter);
   // work item i of this entry (i from item_begin) is block i / ks, slice i % ks
   int ks, ppk, item_begin;
-  int s8;  // 8-bit double-quantised scales (rb_gemv_desc::s_row set); fills the struct's padding
+  int fmt;  // kFmt* bits: the weight and scale format (fills the struct's padding)
 };
+// Entry::fmt. kFmtS8: int4 codes with 8-bit double-quantised scales (rb_gemv_desc::s_row set). kFmtW8: int8
+// rows (rb_gemv_desc::w8): q int8 [N, K], one scale per row (s: fp16 [N]; m: fp32 [N] with kFmtRowF32), a stage
+// holds ONE group and the item's "pairs" are its groups. kFmtOffset: the codes are stored as uint8 = int8 + 128.
+constexpr int kFmtS8 = 1, kFmtW8 = 2, kFmtOffset = 4, kFmtRowF32 = 8;
+constexpr uint32_t kIdescASigned = 1u << 7;  // instruction descriptor, kind::i8: A signed 8-bit
+// Stages (16 KB: 128 bytes of every row) per 128-row block of an entry: two int4 groups or one int8 group each.
+__host__ __device__ __forceinline__ int entry_pairs(int G, int fmt) { return (fmt & kFmtW8) ? G : (G + 1) / 2; }
 
 struct Slot {
   const void* x;  // activations; for the prologue slot the residual stream
@@ -151,6 +158,11 @@ __device__ __forceinline__ void tmem_wait_ld4(int (&d)[4]) {
 // 16 x a group's integer dot product from its accumulators; exact in int32 (|value| < 1.02e9).
 __device__ __forceinline__ float group_dot16(const int (&d)[4]) {
   return static_cast<float>((d[0] << 12) + (d[1] << 4) + (d[2] << 8) + d[3]);
+}
+// The same for an int8 group, whose odd-column codes are not scaled by 16 in tensor memory: 16 x (256 (D0 + D2)
+// + D1 + D3). The int32 sum is exact (|value| <= 128 * 127 * 32767 < 2^29); its conversion rounds to 24 bits.
+__device__ __forceinline__ float group_dot16_w8(const int (&d)[4]) {
+  return static_cast<float>(((d[0] + d[2]) << 8) + d[1] + d[3]) * 16.f;
 }
 __device__ __forceinline__ float h2f_lo(uint32_t w) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)));
@@ -287,12 +299,13 @@ __device__ void stage_x_tables(const TcParams& p, uint8_t* xs, float* red, int c
   }
 }
 
-// Block (within its entry) and pair range [p0, p1) of global work item gi of entry E.
+// Block (within its entry) and pair range [p0, p1) of global work item gi of entry E (for int8 entries the
+// "pairs" are single groups: one stage each).
 __device__ __forceinline__ void item_range(const Entry& E, int gi, int& blk, int& p0, int& p1) {
   const int li = gi - E.item_begin;
   blk = li / E.ks;
   p0 = (li - blk * E.ks) * E.ppk;
-  p1 = min(p0 + E.ppk, (E.G + 1) / 2);
+  p1 = min(p0 + E.ppk, entry_pairs(E.G, E.fmt));
 }
 
 // The entry of global work item gi (entries hold consecutive item ranges; e only moves forward).
@@ -303,8 +316,8 @@ __device__ __forceinline__ const Entry& entry_of(const TcParams& p, int gi, int&
 
 // kS8: the launch has entries with 8-bit scales (each entry's format is then checked where its scales are read).
 // Launches without any run the instance with kS8 = false, which has no trace of the decoder: carrying it costs
-// the fp16 path about 4 % (same-box A/B).
-template <bool kS8>
+// the fp16 path about 4 % (same-box A/B). kW8: the launch has int8 entries (checked per work item).
+template <bool kS8, bool kW8>
 __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -416,7 +429,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
         int blk, p0, p1;
         item_range(E, gi, blk, p0, p1);
         const uint32_t xtab = smem_u32(xs + p.slots[E.slot].tab_off);
-        for (int g = 2 * p0; g < 2 * p1; g += 2, ++q) {
+        const bool w8 = kW8 && (E.fmt & kFmtW8);  // one group per stage, A signed
+        const uint32_t idesc = w8 ? p.idesc | kIdescASigned : p.idesc;
+        for (int pp = p0; pp < p1; ++pp, ++q) {
           const int b = q % kNP;
           if (!mbar_wait(afull(s, b), (q / kNP) & 1, ERR_TC_WAIT)) {
             ok = false;
@@ -424,12 +439,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
           }
           mm4::tc_fence_after();
           const uint32_t acol = s * kSetCols + b * kACols, dcol = s * kSetCols + kNP * kACols + b * kDCols;
-          const int ng = min(2, E.G - g);
+          const int g = w8 ? pp : 2 * pp;
+          const int ng = w8 ? 1 : min(2, E.G - g);
           for (int h = 0; h < ng; ++h)
 #pragma unroll
             for (int i = 0; i < 4; ++i)
               umma_ts(tmem + dcol + 8 * h, tmem + acol + 32 * h + 8 * i,
-                      x_desc(xtab + (g + h) * kXGroupBytes + 2 * kXChunkBytes * i), p.idesc, i > 0);
+                      x_desc(xtab + (g + h) * kXGroupBytes + 2 * kXChunkBytes * i), idesc, i > 0);
           mm4::umma_commit(mdone(s, b));
         }
       }
@@ -451,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
       const int gi = cta + jj * C;
       const Entry& E = entry_of(p, gi, e);
       const int G = E.G;
+      const bool w8 = kW8 && (E.fmt & kFmtW8);  // int8 rows: one group per stage
       int blk, p0, p1;
       item_range(E, gi, blk, p0, p1);
       const int row = blk * kRows + rib;
@@ -487,10 +504,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
           }
         }
       };
-      // the item's pair k (groups g, g + 1 of the block): codes into tensor memory, results of the pair kNP back
+      // int8 codes of one group (the stage's 128 bytes of this row) in the order unpack gives the int4 codes:
+      // within every 8 columns the four even ones, then the four odd ones (stored uint8 = int8 + 128: the top
+      // bit flipped gives the int8 code)
+      auto order8 = [&](const uint4* w, uint32_t* o) {
+        const uint32_t flip = (E.fmt & kFmtOffset) ? 0x80808080u : 0u;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t a0 = w[c].x ^ flip, a1 = w[c].y ^ flip, a2 = w[c].z ^ flip, a3 = w[c].w ^ flip;
+          o[4 * c + 0] = __byte_perm(a0, a1, 0x6420);
+          o[4 * c + 1] = __byte_perm(a0, a1, 0x7531);
+          o[4 * c + 2] = __byte_perm(a2, a3, 0x6420);
+          o[4 * c + 3] = __byte_perm(a2, a3, 0x7531);
+        }
+      };
+      auto dot16 = [&](const int (&d)[4]) { return w8 ? group_dot16_w8(d) : group_dot16(d); };
+      // the item's pair k (groups g, g + 1 of the block; for int8 rows the one group g): codes into tensor
+      // memory, results of the pair kNP back
       auto step = [&](int k, float s0, float m0, float s1, float m1) {
-        const int g = 2 * (p0 + k);
-        const bool two = g + 1 < G;
+        const int g = w8 ? p0 + k : 2 * (p0 + k);
+        const bool two = !w8 && g + 1 < G;
         const uint4 w[8] = {wn[0], wn[1], wn[2], wn[3], wn[4], wn[5], wn[6], wn[7]};
         __syncwarp();
         if (lane == 0) mbar_arrive(empty(s, st % nst));  // both groups of this stage are in registers
@@ -509,10 +542,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
         }
         if (ok) {
           uint32_t o[32];
-          unpack(w, o);
-          tmem_st32(a_set + b * kACols, o);
-          unpack(w + 4, o);
-          tmem_st32(a_set + b * kACols + 32, o);
+          if (w8) {
+            order8(w, o);
+            tmem_st32(a_set + b * kACols, o);
+          } else {
+            unpack(w, o);
+            tmem_st32(a_set + b * kACols, o);
+            unpack(w + 4, o);
+            tmem_st32(a_set + b * kACols + 32, o);
+          }
           if (epi) {  // issued after the codes, so that the accumulators are not live across the unpack
             tmem_ld4(d_set + b * kDCols, d0);
             tmem_ld4(d_set + b * kDCols + 8, d1);
@@ -523,8 +561,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
         if (epi && ok) {
           tmem_wait_ld4(d0);
           tmem_wait_ld4(d1);
-          acc = fmaf(pa[0], group_dot16(d0), acc);
-          acc = fmaf(pb[0], group_dot16(d1), acc);
+          acc = fmaf(pa[0], dot16(d0), acc);
+          acc = fmaf(pb[0], group_dot16(d1), acc);  // 0 for int8 rows
         }
         if (epi) {
           pa[0] = pa[1];
@@ -555,7 +593,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
       auto expand = [&](uint32_t& sw, uint32_t& mw) {
         dq_scales8_f16x2(sw, __ldg(static_cast<const float*>(E.m) + r0), sw, mw);
       };
-      if ((G & 7) == 0) {
+      if (w8) {
+        // int8 rows: one scale per row, no min (16 x the scale: dot16 is 16 x the dot in units of delta / 16)
+        const float sr = (E.fmt & kFmtRowF32) ? __ldg(static_cast<const float*>(E.m) + r0)
+                                              : __half2float(__ushort_as_half(__ldg(E.s + r0)));
+        for (int k = 0; k < npairs; ++k) step(k, sr, 0.f, 0.f, 0.f);
+      } else if ((G & 7) == 0) {
         // scales and mins of 4 groups (2 pairs) per 8-byte load, fetched one iteration (about 2.7 us) ahead; two
         // pair steps per iteration, so the pair step is inlined twice rather than four times (fewer
         // instruction-fetch stalls: +1.1 % on the whole-step list, same-box A/B; fully rolled, one step per
@@ -563,15 +606,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
         // G % 8 == 0 every item starts on a multiple of 8 groups and holds a multiple of 8 groups (slices are a
         // multiple of 4 pairs), so both pairs of an iteration exist and the loads are 8-byte aligned.
         uint2 sn = __ldg(reinterpret_cast<const uint2*>(srow + g0));
-        uint2 mn = (kS8 && E.s8) ? sn : __ldg(reinterpret_cast<const uint2*>(mins_at(g0)));
+        uint2 mn = (kS8 && (E.fmt & kFmtS8)) ? sn : __ldg(reinterpret_cast<const uint2*>(mins_at(g0)));
 #pragma unroll 1
         for (int g4 = g0; g4 < g1; g4 += 4) {
           uint32_t sw0 = sn.x, sw1 = sn.y, mw0 = mn.x, mw1 = mn.y;
           if (g4 + 4 < g1) {
             sn = __ldg(reinterpret_cast<const uint2*>(srow + g4 + 4));
-            mn = (kS8 && E.s8) ? sn : __ldg(reinterpret_cast<const uint2*>(mins_at(g4 + 4)));
+            mn = (kS8 && (E.fmt & kFmtS8)) ? sn : __ldg(reinterpret_cast<const uint2*>(mins_at(g4 + 4)));
           }
-          if (kS8 && E.s8) {
+          if (kS8 && (E.fmt & kFmtS8)) {
             expand(sw0, mw0);
             expand(sw1, mw1);
           }
@@ -584,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
           const int g = 2 * (p0 + k);
           const bool two = g + 1 < G;
           uint32_t sw = __ldg(srow + g) | (two ? static_cast<uint32_t>(__ldg(srow + g + 1)) << 16 : 0u), mw = sw;
-          if (kS8 && E.s8)
+          if (kS8 && (E.fmt & kFmtS8))
             expand(sw, mw);
           else
             mw = __ldg(mins_at(g)) | (two ? static_cast<uint32_t>(__ldg(mins_at(g + 1))) << 16 : 0u);
@@ -608,7 +651,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_int4_tc_kernel(const __grid_
             tmem_ld4(d_set + b * kDCols + 8, d1);
             tmem_wait_ld4(d0);
             tmem_wait_ld4(d1);
-            acc = fmaf(pa[i], group_dot16(d0), acc);
+            acc = fmaf(pa[i], dot16(d0), acc);
             acc = fmaf(pb[i], group_dot16(d1), acc);
           }
         }
@@ -702,7 +745,7 @@ int64_t plan_split(TcParams& p, int num_sms, int64_t ws_bytes) {
   int64_t pairs = 0;
   int maxnp = 1;
   for (int i = 0; i < p.count; ++i) {
-    const int np = (p.e[i].G + 1) / 2, nb = (p.e[i].N + kRows - 1) / kRows;
+    const int np = entry_pairs(p.e[i].G, p.e[i].fmt), nb = (p.e[i].N + kRows - 1) / kRows;
     pairs += static_cast<int64_t>(np) * nb;
     maxnp = std::max(maxnp, np);
   }
@@ -711,8 +754,8 @@ int64_t plan_split(TcParams& p, int num_sms, int64_t ws_bytes) {
     bool split = false;
     for (int i = 0; i < p.count; ++i) {
       Entry& E = p.e[i];
-      const int np = (E.G + 1) / 2, nb = (E.N + kRows - 1) / kRows;
-      const int pk = (E.G & 7) == 0 ? (ppk + 3) & ~3 : ppk;
+      const int np = entry_pairs(E.G, E.fmt), nb = (E.N + kRows - 1) / kRows;
+      const int pk = (E.G & 7) == 0 && !(E.fmt & kFmtW8) ? (ppk + 3) & ~3 : ppk;
       E.ks = pk >= np ? 1 : (np + pk - 1) / pk;
       E.ppk = E.ks == 1 ? np : pk;
       E.item_begin = items;
@@ -750,7 +793,8 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
     p.x_bf16 = x_dtype == RB_BF16;
     p.y_bf16 = y_dtype == RB_BF16;
     p.prefetch = (flags & RB_FLAG_PDL) && (flags & RB_FLAG_PREFETCH_WEIGHTS) ? 1 : 0;
-    // instruction descriptor: D int32, A unsigned 8-bit, B signed 8-bit, both K-major, N = 8, M = 128
+    // instruction descriptor: D int32, A unsigned 8-bit, B signed 8-bit, both K-major, N = 8, M = 128 (the int8
+    // entries' MMAs add kIdescASigned)
     p.idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((8u >> 3) << 17) | ((static_cast<uint32_t>(kRows) >> 4) << 24);
     const uint32_t kBars = kSets * (2 * kMaxStages + 2 * kNP) * 8 + 16 + 16 + kAuxBytes;
     int nslots = 0, blocks = 0, take = 0, nepis = 0;
@@ -794,9 +838,12 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
         x_bytes += add_x;
       }
       Entry& E = p.e[take];
+      const bool w8 = D.w8 != RB_W8_NONE;
+      if (w8 && kind != kEpiStore) return RB_ERR_SHAPE;  // int8 rows: the store epilogue only
       E.s = D.s;
-      E.s8 = D.s_row != nullptr;
-      E.m = E.s8 ? static_cast<const void*>(D.s_row) : static_cast<const void*>(D.m);
+      E.fmt = w8 ? kFmtW8 | (D.w8 == RB_W8_OFFSET ? kFmtOffset : 0) | (D.s_row ? kFmtRowF32 : 0)
+                 : (D.s_row ? kFmtS8 : 0);
+      E.m = D.s_row ? static_cast<const void*>(D.s_row) : static_cast<const void*>(D.m);
       E.y = D.y;
       E.N = static_cast<int>(D.N);
       E.G = static_cast<int>(G);
@@ -822,8 +869,9 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
         E.ep = nepis++;
       }
       blocks += static_cast<int>((D.N + kRows - 1) / kRows);
-      const cuuint64_t dims[2] = {static_cast<cuuint64_t>(D.K / 2), static_cast<cuuint64_t>(D.N)};
-      const cuuint64_t strides[1] = {static_cast<cuuint64_t>(D.K / 2)};
+      const int64_t row_bytes = w8 ? D.K : D.K / 2;  // int8 codes [N, K] or packed int4 codes [N, K/2]
+      const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(D.N)};
+      const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
       const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(kRows)};
       const cuuint32_t es[2] = {1, 1};
       if (encode(&p.maps[take], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(D.q), dims, strides, box, es,
@@ -861,9 +909,13 @@ int launch_gemv_int4_tc(const rb_gemv_desc* d, int count, int x_dtype, int y_dty
     p.bar_off = (p.xs_off + xtot + 15) & ~15u;
     p.aux_off = (p.bar_off + kSets * (2 * nst + 2 * kNP) * 8 + 16 + 15) & ~15u;
     const uint32_t smem = 1024 + p.aux_off + kAuxBytes;
-    bool any8 = false;
-    for (int i = 0; i < take; ++i) any8 = any8 || p.e[i].s8 != 0;
-    void (*kern)(TcParams) = any8 ? gemv_int4_tc_kernel<true> : gemv_int4_tc_kernel<false>;
+    bool any8 = false, anyw8 = false;
+    for (int i = 0; i < take; ++i) {
+      any8 = any8 || (p.e[i].fmt & kFmtS8);
+      anyw8 = anyw8 || (p.e[i].fmt & kFmtW8);
+    }
+    void (*kern)(TcParams) = any8 ? (anyw8 ? gemv_int4_tc_kernel<true, true> : gemv_int4_tc_kernel<true, false>)
+                                  : (anyw8 ? gemv_int4_tc_kernel<false, true> : gemv_int4_tc_kernel<false, false>);
     cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), static_cast<int>(kSmemMax));
     if (e != cudaSuccess) return RB_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};

@@ -89,3 +89,31 @@ def test_mm_int4_validation(native_lib):
     assert mm(ldy=60) == _lib.ERR_SHAPE
     assert mm(ldx=260) == _lib.ERR_ALIGN
     assert mm(X=None) == _lib.ERR_NULL
+
+
+def test_gemv_list_int8_entry_validation(native_lib):
+    """int8 entries of a GEMV list (rb_gemv_desc::w8) are checked before any CUDA call: the kind, the row-scale
+    pointer and alignments, and that no forced warp-MMA launch, fused epilogue or whole-step layer takes one."""
+    L = native_lib
+
+    def multi(flags=0, **kw):
+        d = _lib.GemvDesc(A, A, A, A, None, 64, 256)
+        d.w8 = _lib.W8_SIGNED
+        for k, v in kw.items():
+            setattr(d, k, v)
+        arr = (_lib.GemvDesc * 1)(d)
+        return L.rb_gemv_int4_multi(arr, 1, _lib.F16, _lib.F16, flags, None)
+
+    assert multi(w8=3) == _lib.ERR_SHAPE
+    assert multi(w8=-1) == _lib.ERR_SHAPE
+    assert multi(K=200) == _lib.ERR_SHAPE
+    assert multi(s=None) == _lib.ERR_NULL             # no row scales at all
+    assert multi(q=None) == _lib.ERR_NULL
+    assert multi(q=A + 8) == _lib.ERR_ALIGN
+    assert multi(s=A + 1) == _lib.ERR_ALIGN           # fp16 row scales: 2-byte aligned
+    assert multi(s=None, s_row=A + 2) == _lib.ERR_ALIGN  # fp32 row scales: 4-byte aligned
+    assert multi(flags=_lib.FLAG_KERNEL_MMA) == _lib.ERR_SHAPE
+    d = _lib.GemvDesc(A, A, A, A, None, 64, 256)
+    d.w8 = _lib.W8_OFFSET
+    assert L.rb_gemv_int4_fused((_lib.GemvDesc * 1)(d), None, 1, None, None, None, 0, _lib.F16, _lib.F16, 0,
+                                None) == _lib.ERR_SHAPE

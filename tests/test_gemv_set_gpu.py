@@ -132,3 +132,51 @@ def test_split_k_lists(shapes):
     _plain(ent)
     torch.cuda.synchronize()
     check(host, ent, "unsplit")
+
+
+def _int8_rows(N, K, seed, offset, s_dtype):
+    """int8 rows [N, K] (torch.int8, or the uint8 = int8 + 128 storage of quantize_int8_rows) and row scales."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int16)
+    q = (q + 128).to(torch.uint8) if offset else q.to(torch.int8)
+    s = (torch.rand(N, generator=g) * 9e-4 + 1e-4).to(s_dtype)
+    return q, s
+
+
+@pytest.mark.parametrize("offset,s_dtype", [(False, torch.float16), (True, torch.float32)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("split", [False, True])
+def test_int8_rows_in_the_list(offset, s_dtype, dtype, split):
+    """The int8 head streamed as more rows of a tcgen05 list launch (rb_gemv_desc::w8): y = s * (q @ x) against
+    the oracle's gemv_int8_ref, beside int4 entries that stay correct, with a ragged last block (N = 16385);
+    split: few enough blocks that K is split over converter sets (partials and ticket); unsplit: the whole
+    config-1 layers' projections plus the head. Two calls give the same bits; the tickets end zeroed."""
+    # split: 56 blocks; unsplit: two config-1 layers (432 blocks) + the head (129) > 3 x 148 converter sets
+    shapes = [(3072, 3072), (3072, 8192)] if split else [(n, k) for _ in range(2) for _, n, k in syn.LAYER_SHAPES]
+    host, ent = build(shapes, nx=2, seed=11, dtype=dtype)
+    q8, s8 = _int8_rows(16385 if not split else 1000, 3072, 12, offset, s_dtype)
+    xh = syn.activations((3072,), syn.generator(13, "cpu"), "cpu", dtype=dtype)
+    yh = torch.full((q8.shape[0],), float("nan"), device=DEV, dtype=dtype)
+    head = (xh.to(DEV), q8.to(DEV), s8.to(DEV), None, yh)
+    st = rb.Int4GemvSet([head] + ent, kernel="tc")
+    assert (st.ws is not None) == split
+    st()
+    torch.cuda.synchronize()
+    assert rb.device_error() == 0
+    assert_close(yh, int8_ref(xh, q8, s8), "int8 rows")
+    check(host, ent, "int4 entries beside the int8 rows")
+    first = [yh.clone()] + [e[4].clone() for e in ent]
+    st()
+    torch.cuda.synchronize()
+    assert all(torch.equal(a, b) for a, b in zip(first, [yh] + [e[4] for e in ent]))
+    if split:  # the per-block tickets (the partials after them are not cleared)
+        n_blocks = sum((n + 127) // 128 for n, _ in shapes) + (q8.shape[0] + 127) // 128
+        assert int(torch.count_nonzero(st.ws[:4 * n_blocks])) == 0
+
+
+def test_int8_rows_refused_off_the_tc_kernel():
+    host, ent = build([(256, 1024)], nx=1, seed=14)
+    q8, s8 = _int8_rows(64, 1024, 15, False, torch.float16)
+    head = (ent[0][0], q8.to(DEV), s8.to(DEV), None, torch.empty(64, device=DEV, dtype=torch.float16))
+    with pytest.raises(RuntimeError):
+        rb.Int4GemvSet([head] + ent, kernel="mma")()

@@ -1,8 +1,9 @@
 """The exact kernel instance the headline benchmark times, at the size it is timed.
 
-bench.py's decode workload runs the 36-layer config-1 projection set (144 GEMVs, 7,776 blocks of 128 rows) as
-one Int4GemvSet launch. That list is far longer than 3 x the SM count, so it runs on the tcgen05 kernel
-UNSPLIT: each CTA walks about 52 blocks and every ring slot and tensor-memory buffer wraps its phase many times.
+bench.py's decode workload runs the int8 head's rows (16385 x 3072, 129 blocks) and the 36-layer config-1
+projection set (144 GEMVs, 7,776 blocks of 128 rows) as one Int4GemvSet launch. That list is far longer than
+3 x the SM count, so it runs on the tcgen05 kernel UNSPLIT: each CTA walks about 53 blocks and every ring slot and
+tensor-memory buffer wraps its phase many times.
 These tests build that list (distinct weights per layer, as the bench does, but a distinct output per entry so
 that every entry can be checked), run it twice, and compare every output row of every entry with the fp32
 oracle (kernels/bench_cuda.py:38's check, dequantize(q, s, m) @ x.float(), in the multi-threaded torch
@@ -32,16 +33,24 @@ def _gpu(native_lib):
 
 def check_all(ent, what):
     for i, (x, q, s, m, y) in enumerate(ent):
+        if m is None:  # the int8 head's rows
+            ref = R.gemv_int8_torch(x.cpu(), q.cpu(), s.cpu(), signed=q.dtype == torch.int8).numpy()
+            assert_close(y, ref, f"{what} entry {i}: int8 rows (N={q.shape[0]}, K={q.shape[1]})")
+            continue
         ref = R.gemv_int4_torch(x.cpu(), q.cpu(), s.cpu(), m.cpu()).numpy()
         assert_close(y, ref, f"{what} entry {i} (N={q.shape[0]}, K={2 * q.shape[1]})")
 
 
-def step_list(dtype, layers=36, seed=1234):
-    """bench.py's projection set: per layer QKV, o_proj, gate_up with x_h and down with x_i."""
+def step_list(dtype, layers=36, seed=1234, head=True):
+    """bench.py's step list: the int8 head's rows (int8 codes, fp16 row scales, x_h), then per layer QKV, o_proj,
+    gate_up with x_h and down with x_i."""
     gen = syn.generator(seed, DEV)
     xh = syn.activations((3072,), gen, DEV, dtype=dtype)
     xi = syn.activations((8192,), gen, DEV, dtype=dtype)
     ent = []
+    if head:
+        q8, s8 = syn.int8_weights(*syn.HEAD_SHAPE, gen, DEV)
+        ent.append((xh, q8, s8, None, torch.full((syn.HEAD_SHAPE[0],), float("nan"), device=DEV, dtype=dtype)))
     for _ in range(layers):
         for name, n, k in syn.LAYER_SHAPES:
             q, s, m = syn.int4_weights(n, k, gen, DEV)
@@ -54,8 +63,8 @@ def step_list(dtype, layers=36, seed=1234):
 def test_whole_step_projection_set_unsplit(dtype):
     ent = step_list(dtype)
     st = rb.Int4GemvSet(ent)
-    assert st.ws is None                                  # 7,776 blocks: never split
-    assert sum((q.shape[0] + 127) // 128 for _, q, _, _, _ in ent) == 7776
+    assert st.ws is None                                  # 129 + 7,776 blocks: never split
+    assert sum((q.shape[0] + 127) // 128 for _, q, _, _, _ in ent) == 129 + 7776
     st()
     torch.cuda.synchronize()
     first = [e[4].clone() for e in ent]

@@ -141,3 +141,22 @@ def test_prologue_outlier_residual(case, dtype, kernel):
     assert O.ulp_diff(np_f32(h_out), h_ref, tag).max() <= 1
     for wh, y in zip(W, ys):
         assert_close(y, int4_ref(h_out.cpu(), *wh), f"prologue {case} GEMV")
+
+
+@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_int8_rows_in_a_tc_list(case, dtype):
+    """The int8 head as rows of the tcgen05 list launch (per-group quantisation of its x, like the int4 entries)."""
+    g = torch.Generator().manual_seed(31)
+    q8 = torch.randint(-127, 128, (16385, 3072), generator=g, dtype=torch.int16).to(torch.int8)
+    s8 = (torch.rand(16385, generator=g) * 9e-4 + 1e-4).to(torch.float16)
+    x = outlier_x(3072, case, 32, dtype)
+    q, s, m = syn.int4_weights(1024, 3072, syn.generator(33, "cpu"), "cpu")
+    y8 = torch.empty(16385, device=DEV, dtype=dtype)
+    y4 = torch.empty(1024, device=DEV, dtype=dtype)
+    xd = x.to(DEV)
+    rb.Int4GemvSet([(xd, q8.to(DEV), s8.to(DEV), None, y8), (xd, q.to(DEV), s.to(DEV), m.to(DEV), y4)],
+                   kernel="tc")()
+    torch.cuda.synchronize()
+    assert_close(y8, int8_ref(x, q8, s8), f"int8 rows, {case}")
+    assert_close(y4, int4_ref(x, q, s, m), f"int4 entry, {case}")

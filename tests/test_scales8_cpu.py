@@ -95,10 +95,12 @@ def test_pack_rejects_bad_input():
 
 
 def test_descriptor_layout():
-    """struct rb_gemv_desc: five pointers, N, K, then s_row (64 bytes)."""
-    assert ctypes.sizeof(_lib.GemvDesc) == 64
+    """struct rb_gemv_desc: five pointers, N, K, s_row, then the int8-entry kind w8 (72 bytes with padding)."""
+    assert ctypes.sizeof(_lib.GemvDesc) == 72
     assert _lib.GemvDesc.s_row.offset == 56
-    assert _lib.GemvDesc(1, 2, 3, 4, 5, 6, 7).s_row is None
+    assert _lib.GemvDesc.w8.offset == 64
+    d = _lib.GemvDesc(1, 2, 3, 4, 5, 6, 7)
+    assert d.s_row is None and d.w8 == _lib.W8_NONE == 0
 
 
 try:
