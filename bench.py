@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefetch", action="store_true", help="do not stream weights before the PDL wait")
     ap.add_argument("--no-extras", action="store_true", help="headline only: no step/prefill/gemv_c0/chain records")
-    ap.add_argument("--head", default="concurrent", choices=["list", "concurrent", "serial"],
+    ap.add_argument("--head", default="list", choices=["list", "concurrent", "serial"],
                     help="set mode: the int8 head's rows as the first entry of the projection launch (list), its "
                          "own launch on a forked branch of the step graph (concurrent) or after the list (serial)")
     ap.add_argument("--mode", default="set", choices=["set", "chain"],

@@ -5,7 +5,7 @@ import torch
 
 import rumik_fast_b200 as rb
 from rumik_fast_b200 import synthetic as syn
-from tests.helpers import assert_close, int4_ref
+from tests.helpers import assert_close, int4_ref, int8_ref
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
