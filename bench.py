@@ -42,6 +42,7 @@ LAYERS = 36
 METRIC = "decode-step GEMV HBM GB/s"
 UNIT = "GB/s"
 PREFILL_TOKENS = (34, 256, 1024)
+BATCHES = (4, 16)  # config 4: independent decode streams per GPU (batch 1 is the headline line)
 # DRAM bytes (read + write) per launch of gemv_int4_tc_kernel on the 36-layer set: ncu capture of the 3-layer
 # case of the current build scaled x12 by blocks streamed (profiles/gemv_int4_tc_3layer_traffic.md)
 NCU_TRAFFIC_PER_LAUNCH = 1966808064
@@ -594,6 +595,46 @@ def measure_prefill(dev, seed, tokens, nlayers, steps, warmup, world, clk=None):
     return out
 
 
+def measure_batched(dev, seed, batches, nlayers, steps, warmup, world, clk=None):
+    """Config 4's independent streams at batch B per GPU: one decode step's 144 projections for B tokens as
+    mm_int4 calls (M = B: the weights are dequantised once per 128-row block for all B tokens) plus the int8 head
+    at batch B (gemv_int8_cuda with x [B, K]), replayed from one CUDA graph. Returns {B: record}; batch 1 is the
+    headline line itself."""
+    from rumik_fast_b200 import synthetic as syn
+    from rumik_fast_b200.mm_int4 import mm_int4
+    import rumik_fast_b200 as rb
+    gen = syn.generator(seed, dev)
+    layers = [[syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES] for _ in range(nlayers)]
+    head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
+    wbytes = nlayers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES) + syn.int8_bytes(*syn.HEAD_SHAPE)
+    hbm, hkind, _ = peaks()
+    out = {}
+    for B in batches:
+        xs = {k: syn.activations((B, k), gen, dev) for k in (3072, 8192)}
+        ys = [torch.empty(B, n, device=dev, dtype=torch.float16) for _, n, _ in syn.LAYER_SHAPES]
+        logits = torch.empty(B, syn.HEAD_SHAPE[0], device=dev, dtype=torch.float16)
+
+        def step():
+            for L in layers:
+                for i, ((_, n, k), w) in enumerate(zip(syn.LAYER_SHAPES, L)):
+                    mm_int4(xs[k], *w, out=ys[i])
+            rb.gemv_int8_cuda(xs[3072], *head, out=logits)
+        g = capture(step)
+        m0 = clk.mark() if clk else 0
+        ms = timed(g.replay, steps, warmup, world) / steps
+        m1 = clk.mark() if clk else 0
+        gbs = wbytes / (ms * 1e-3) / 1e9
+        out[str(B)] = {"tok_s": round(world * B * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+                       "weight_gbs": round(world * gbs, 1), "roofline_frac": round(gbs / hbm, 4), "peak_gbs": hbm,
+                       "peak_kind": hkind, "launches_per_step": 4 * nlayers + 1,
+                       "clocks": clk.summary(m0, m1) if clk else None}
+        del g, xs, ys, logits
+        free()
+    del layers, head
+    free()
+    return out
+
+
 def measure_c0(dev, seed, steps, warmup, world):
     """Config 0 the reference's way (kernels/bench_cuda.py:18-32): 36 distinct 8192x3072 int4 GEMVs through
     gemv_int4_cuda, captured in one CUDA graph; best of 3 rounds of max(steps, 20) replays (CUDA events)."""
@@ -781,6 +822,7 @@ def run_ours(a):
             free()
             extras["gemv_c0"] = measure_c0(dev, 5 + rank, a.steps, a.warmup, world)
             extras["step"] = measure_step(dev, 777 + rank, LAYERS, 511, "separate", a.steps, a.warmup, world, clk)
+            extras["batched"] = measure_batched(dev, 99 + rank, BATCHES, LAYERS, a.steps, a.warmup, world, clk)
             extras["prefill"] = measure_prefill(dev, 4321 + rank, PREFILL_TOKENS, LAYERS, a.steps, a.warmup, world,
                                                 clk)
     clocks = clk.summary(m0, m1)

@@ -8,20 +8,28 @@
 // rewrites its stage's X atoms in place before it releases the group to the MMA issuer; exact for |x| <= 65504,
 // as a torch cast of X to fp16 would be).
 //
-// Work items are (128-row weight block, token chunk of BT <= 128 tokens, K slice), block-major so that the CTAs working
-// at the same time on the chunks of one block share its codes through L2; items are dealt round-robin to one
-// CTA per SM. Both converter sets work on every item, set s on its groups g = s, s + 2, ..., each into its own
-// accumulator; the epilogue adds the two in a fixed order. Per CTA:
-//  * warp 0 (producer) streams, per item and group, the block's codes (TMA box 64 bytes x 128 rows, 64-byte
-//    swizzle) and the chunk's two 64-column X atoms (TMA, 128-byte swizzle) into the set's ring;
-//  * each converter set (four warps, thread = weight row = tensor-memory lane) dequantises its row's group
-//    to fp16 (per code byte: PRMT, LOP3 to the fp16 magic numbers, HSUB2, HFMA2 with the row's scale and
-//    min, one rounding) and writes the 64 columns to tensor memory (tcgen05.st);
-//  * one thread per set issues eight tcgen05.mma.kind::f16 per group (M = 128, N = BT, K = 16): A from tensor
-//    memory, B = the X atoms in shared memory, D = 128 x BT fp32 in tensor memory accumulating over all of K;
-//  * the converter warps then read D0 + D1 (tcgen05.ld; set s takes every other 32-column chunk) and store Y,
+// Work items are (128-row weight block, token chunk of BT <= 256 tokens, K slice), block-major so that the CTAs
+// working at the same time on the chunks of one block share its codes through L2; items are dealt round-robin
+// to one CTA per SM. Per CTA, for the groups of its items in order (a CTA-wide group sequence gq):
+//  * warp 0 (producer) streams each group's codes (TMA box 64 bytes x 128 rows, 64-byte swizzle) and the chunk's
+//    two 64-column X atoms (TMA, 128-byte swizzle) into one shared ring of stages;
+//  * three converter sets (four warps each, thread = weight row = tensor-memory lane) take the groups in turn
+//    (gq % 3): each dequantises its row's group to fp16 (per code byte: PRMT, LOP3 to the fp16 magic numbers,
+//    HSUB2, HFMA2 with the row's scale and min, one rounding) and writes the 64 columns into the next of a ring
+//    of tensor-memory A buffers (gq % NA; NA = 4..7 by the accumulator's width);
+//  * ND MMA issuers (one thread each, warps 1..ND; ND = 3 for chunks of <= 64 tokens, 2 for <= 128, 1 for <= 256)
+//    take the groups in turn (gq % ND): each issues eight tcgen05.mma.kind::f16 per group (M = 128, N = BT,
+//    K = 16) in group order into ITS accumulator D_d = 128 x BT fp32 in tensor memory: A from the group's buffer,
+//    B = the X atoms in shared memory. An MMA costs about 100 cycles to issue whatever its N (measured), so short
+//    chunks spread their groups over several issuers, and up to 256 tokens share one dequantisation of the
+//    weights;
+//  * after the item's last group all twelve converter warps read D_0 + ... + D_{ND-1} in that order
+//    (deterministic; tcgen05.ld, 32-column chunks dealt over the three warps of each lane quadrant) and store Y,
 //    or, when K is split into slices (a call with fewer row-block x chunk items than SMs), the slice's fp32
-//    partial into a caller-provided workspace; mm_int4_reduce then adds the slices in slice order.
+//    partial into a caller-provided workspace; mm_int4_reduce then adds the slices in slice order. Chunks of
+//    <= 128 tokens go through a 32 KB shared staging tile and one bulk-tensor store per round (per-thread
+//    stores cost several times more); 256-token chunks store directly and keep shared memory for three stages.
+//  * the producer brings a group's codes with one TMA copy and both of its X atoms with one 3-D copy.
 // All mbarrier waits are bounded; no multicast, no clusters.
 #include "common.cuh"
 #include "tc.cuh"
@@ -31,27 +39,34 @@ namespace rb {
 
 namespace mm4t {
 
-constexpr int kSets = 2;
+constexpr int kSets = 3;
 constexpr int kRows = 128;
-constexpr int kFirstConv = 1 + kSets;
-constexpr int kThreads = (kFirstConv + 4 * kSets) * 32;
+constexpr int kMaxIssuers = 3;
+constexpr int kFirstConv = 1 + kMaxIssuers;  // warp 0 producer, warps 1..3 MMA issuers (warp 1 owns tensor memory)
+constexpr int kConvWarps = 4 * kSets;
+constexpr int kThreads = (kFirstConv + kConvWarps) * 32;
 constexpr uint32_t kCodeBytes = kRows * 64;
-constexpr int kNB = 2;                       // tensor-memory A buffers per set
-constexpr uint32_t kACols = 64;
-constexpr uint32_t kSetCols = 256;           // per set: A buffers (128 columns) + D (<= 128 columns)
+constexpr uint32_t kACols = 64;              // one group of fp16 weights: 128 lanes x 64 columns
 constexpr uint32_t kTmemCols = 512;
-constexpr int kMaxStages = 6;
+constexpr int kMaxStages = 12;
+constexpr int kMaxBT = 256;
+constexpr uint32_t kOutBytes = 32768;        // the epilogue's staging tile for bulk-tensor stores (BT <= 128)
+constexpr int kBarEpi = 1;                   // named barrier of the twelve converter warps
 
 struct __align__(64) MmtParams {
   CUtensorMap qmap;  // [N rows, K/2 bytes], box 64 x 128, 64-byte swizzle
-  CUtensorMap xmap;  // [M rows, K fp16], box 64 x BT, 128-byte swizzle
+  CUtensorMap xmap;  // x3d: {64 columns, M rows, K/64 atoms}, box 64 x BT x 2 (both atoms of a group in one copy);
+                     // else [M rows, K fp16], box 64 x BT; 128-byte swizzle
+  CUtensorMap omap;  // ostore 1: Y [M, N] (box 128 x tc); 2: the workspace [kslices, M, N] fp32 (box 128 x tc x 1)
   const uint16_t* s;
   const uint16_t* m;
   void* y;
   int64_t ldy;
   float* ws;  // [kslices][M][N] fp32 partials when kslices > 1
-  int M, N, K, G, BT, nchunks, kslices, gps, nitems, y_bf16, nst, prefetch;
-  uint32_t stage_bytes, bar_off, idesc;
+  int M, N, K, G, BT, nchunks, kslices, gps, nitems, y_bf16, nst, na, nd;
+  int ostore, tc;  // epilogue: 0 plain stores, 1 / 2 bulk-tensor stores of Y / the workspace, tc tokens a round
+  int x3d;
+  uint32_t stage_bytes, out_off, bar_off, idesc, dcols;  // dcols: columns per accumulator; A buffers from nd * dcols
 };
 
 __device__ __forceinline__ void umma_ts_f16(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -74,38 +89,68 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// Bulk-tensor stores shared -> global through a tensor map (no multicast), their bulk group, and the waits: the
+// source may be rewritten once `read` completes; the kernel ends only after the writes complete.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
+               "r"(y), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(map), "r"(x),
+               "r"(y), "r"(z), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Item `item`: its first weight row, first token and group range [g0, g1).
+struct Item {
+  int row0, t0, ks, g0, g1;
+};
+__device__ __forceinline__ Item item_of(const MmtParams& p, int item) {
+  Item it;
+  const int per_block = p.nchunks * p.kslices;
+  const int rem = item % per_block;
+  it.row0 = (item / per_block) * kRows;
+  it.t0 = (rem / p.kslices) * p.BT;
+  it.ks = rem % p.kslices;
+  it.g0 = it.ks * p.gps;
+  it.g1 = min(p.G, it.g0 + p.gps);
+  return it;
+}
+
 template <bool kBf16X>
 __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_constant__ MmtParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int C = gridDim.x, cta = blockIdx.x;
-  const int nst = p.nst, G = p.G, BT = p.BT;
+  const int nst = p.nst, na = p.na, nd = p.nd, BT = p.BT;
+  const uint32_t a_base = static_cast<uint32_t>(nd) * p.dcols;
   const int nlocal = (p.nitems - cta + C - 1) / C;  // this CTA's items: cta + j * C
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
-  const int per_set = 2 * nst + 2 * kNB + 1;
-  auto full = [&](int s, int i) { return bars + s * per_set + i; };
-  auto empty = [&](int s, int i) { return bars + s * per_set + nst + i; };
-  auto afull = [&](int s, int b) { return bars + s * per_set + 2 * nst + b; };
-  auto mdone = [&](int s, int b) { return bars + s * per_set + 2 * nst + kNB + b; };
-  auto dready = [&](int s) { return bars + s * per_set + 2 * nst + 2 * kNB; };
-  uint64_t* dfree = bars + kSets * per_set;  // both sets' epilogues have read both accumulators
+  uint64_t* full = bars;                 // [nst] producer -> converters (codes) and MMA issuer (X)
+  uint64_t* empty = bars + nst;          // [nst] four converter warps + one MMA commit
+  uint64_t* afull = bars + 2 * nst;      // [na] the converting set's four warps
+  uint64_t* mdone = afull + na;          // [na] MMA commit: the A buffer may be rewritten
+  uint64_t* dready = mdone + na;         // [kMaxIssuers] issuer d's commit after its last group of an item
+  uint64_t* dfree = dready + kMaxIssuers;  // the twelve converter warps have read the accumulators
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfree + 1);
-  auto stage_of = [&](int s, int slot) { return smem + (static_cast<size_t>(s) * nst + slot) * p.stage_bytes; };
+  auto stage_of = [&](int slot) { return smem + static_cast<size_t>(slot) * p.stage_bytes; };
 
   if (tid == 0) {
-    for (int s = 0; s < kSets; ++s) {
-      for (int i = 0; i < nst; ++i) {
-        mbar_init(full(s, i), 1);
-        mbar_init(empty(s, i), 5);  // four converter warps (codes read) + one MMA commit (X read)
-      }
-      for (int b = 0; b < kNB; ++b) {
-        mbar_init(afull(s, b), 4);
-        mbar_init(mdone(s, b), 1);
-      }
-      mbar_init(dready(s), 1);
+    for (int i = 0; i < nst; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, 5);
     }
-    mbar_init(dfree, 4 * kSets);
+    for (int b = 0; b < na; ++b) {
+      mbar_init(afull + b, 4);
+      mbar_init(mdone + b, 1);
+    }
+    for (int d = 0; d < kMaxIssuers; ++d) mbar_init(dready + d, 1);
+    mbar_init(dfree, kConvWarps);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -126,118 +171,112 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
     if (lane == 0) {
       // The codes do not depend on the previous kernel: the first stages' code loads go out before
       // griddepcontrol.wait (overlapping the previous kernel's tail); X loads only after it.
-      int pre[kSets] = {};
-      for (int j = 0; j < nlocal; ++j) {
-        const int item = cta + j * C;
-        const int rem = item % (p.nchunks * p.kslices);
-        const int row0 = (item / (p.nchunks * p.kslices)) * kRows;
-        const int g0 = (rem % p.kslices) * p.gps, g1 = min(G, g0 + p.gps);
-        bool room = false;
-        for (int g = g0; g < g1; ++g) {
-          const int s = (g - g0) % kSets;
-          if (pre[s] >= nst) continue;
-          room = true;
-          const int slot = pre[s]++;
-          mbar_arrive_expect_tx(full(s, slot), stage_tx);
-          mm4::tma_load_2d(stage_of(s, slot), &p.qmap, g * 64, row0, full(s, slot));
+      int pre = 0;
+      for (int j = 0; j < nlocal && pre < nst; ++j) {
+        const Item it = item_of(p, cta + j * C);
+        for (int g = it.g0; g < it.g1 && pre < nst; ++g, ++pre) {
+          mbar_arrive_expect_tx(full + pre, stage_tx);
+          mm4::tma_load_2d(stage_of(pre), &p.qmap, g * 64, it.row0, full + pre);
         }
-        if (!room) break;
       }
       griddep_wait();  // X may come from the previous kernel
-      int issued[kSets] = {};
+      int gq = 0;
       bool ok = true;
       for (int j = 0; j < nlocal && ok; ++j) {
-        const int item = cta + j * C;
-        const int rem = item % (p.nchunks * p.kslices);
-        const int row0 = (item / (p.nchunks * p.kslices)) * kRows, t0 = (rem / p.kslices) * BT;
-        const int g0 = (rem % p.kslices) * p.gps, g1 = min(G, g0 + p.gps);
-        for (int g = g0; g < g1 && ok; ++g) {
-          const int s = (g - g0) % kSets;
-          const int slot = issued[s] % nst;
-          uint8_t* st = stage_of(s, slot);
-          if (issued[s] >= pre[s]) {
-            if (issued[s] >= nst && !mbar_wait(empty(s, slot), ((issued[s] / nst) - 1) & 1, ERR_MM4_WAIT)) {
+        const Item it = item_of(p, cta + j * C);
+        for (int g = it.g0; g < it.g1; ++g, ++gq) {
+          const int slot = gq % nst;
+          uint8_t* st = stage_of(slot);
+          if (gq >= pre) {
+            if (!mbar_wait(empty + slot, ((gq / nst) - 1) & 1, ERR_MM4_WAIT)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(full(s, slot), stage_tx);
-            mm4::tma_load_2d(st, &p.qmap, g * 64, row0, full(s, slot));
+            mbar_arrive_expect_tx(full + slot, stage_tx);
+            mm4::tma_load_2d(st, &p.qmap, g * 64, it.row0, full + slot);
           }
-          mm4::tma_load_2d(st + kCodeBytes, &p.xmap, g * 128, t0, full(s, slot));
-          mm4::tma_load_2d(st + kCodeBytes + BT * 128, &p.xmap, g * 128 + 64, t0, full(s, slot));
-          ++issued[s];
+          if (p.x3d) {
+            mm4::tma_load_3d(st + kCodeBytes, &p.xmap, 0, it.t0, 2 * g, full + slot);
+          } else {
+            mm4::tma_load_2d(st + kCodeBytes, &p.xmap, g * 128, it.t0, full + slot);
+            mm4::tma_load_2d(st + kCodeBytes + BT * 128, &p.xmap, g * 128 + 64, it.t0, full + slot);
+          }
         }
       }
-      for (int s = 0; s < kSets; ++s)  // no retirement with copies in flight
-        for (int t = max(0, issued[s] - nst); t < issued[s]; ++t)
-          if (!mbar_wait(full(s, t % nst), (t / nst) & 1, ERR_MM4_WAIT)) break;
+      // no retirement with copies in flight
+      for (int t = max(0, gq - nst); t < gq; ++t)
+        if (!mbar_wait(full + t % nst, (t / nst) & 1, ERR_MM4_WAIT)) break;
     }
   } else if (warp < kFirstConv) {
-    // ---------------- MMA issuer of set s ----------------
-    const int s = warp - 1;
-    if (lane == 0) {
-      const uint32_t d_col = tmem + s * kSetCols + kNB * kACols;
-      int q = 0, used = 0;
+    // ---------------- MMA issuer d: the groups gq % nd == d, into accumulator d ----------------
+    const int d = warp - 1;
+    if (lane == 0 && d < nd) {
+      int gq = 0;
       bool ok = true;
+      const uint32_t dcol = tmem + static_cast<uint32_t>(d) * p.dcols;
       for (int jj = 0; jj < nlocal && ok; ++jj) {
-        if (jj >= 1 && !mbar_wait(dfree, (jj - 1) & 1, ERR_MM4_WAIT)) break;  // D read by the last epilogue
-        const int item = cta + jj * C;
-        const int g0 = (item % (p.nchunks * p.kslices) % p.kslices) * p.gps, g1 = min(G, g0 + p.gps);
-        for (int gg = g0 + s; gg < g1; gg += kSets, ++q, ++used) {
-          const int b = q % kNB, slot = used % nst;
-          if (!mbar_wait(afull(s, b), (q / kNB) & 1, ERR_MM4_WAIT) ||
-              !mbar_wait(full(s, slot), (used / nst) & 1, ERR_MM4_WAIT)) {
+        if (jj >= 1 && !mbar_wait(dfree, (jj - 1) & 1, ERR_MM4_WAIT)) break;  // read by the last epilogue
+        mm4::tc_fence_after();
+        const Item it = item_of(p, cta + jj * C);
+        bool first = true;
+        for (int g = it.g0; g < it.g1; ++g, ++gq) {
+          if (gq % nd != d) continue;
+          const int b = gq % na, slot = gq % nst;
+          if (!mbar_wait(afull + b, (gq / na) & 1, ERR_MM4_WAIT) ||
+              !mbar_wait(full + slot, (gq / nst) & 1, ERR_MM4_WAIT)) {
             ok = false;
             break;
           }
           mm4::tc_fence_after();
-          const uint32_t xb = smem_u32(stage_of(s, slot) + kCodeBytes);
+          const uint32_t xb = smem_u32(stage_of(slot) + kCodeBytes);
+          const uint32_t a = tmem + a_base + b * kACols;
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            umma_ts_f16(d_col, tmem + s * kSetCols + b * kACols + 8 * i,
-                        mm4::sw128_desc(xb + (i >> 2) * BT * 128 + (i & 3) * 32), p.idesc, (gg - g0 >= kSets) || i != 0);
-          mm4::umma_commit(mdone(s, b));     // A buffer b may be rewritten
-          mm4::umma_commit(empty(s, slot));  // the stage's X atoms may be refilled
+            umma_ts_f16(dcol, a + 8 * i, mm4::sw128_desc(xb + (i >> 2) * BT * 128 + (i & 3) * 32), p.idesc,
+                        !first || i != 0);
+          first = false;
+          mm4::umma_commit(mdone + b);     // A buffer b may be rewritten
+          mm4::umma_commit(empty + slot);  // the stage's X atoms may be refilled
         }
-        if (ok) mm4::umma_commit(dready(s));  // (with no group of this set in the item, arrives at once)
+        if (ok) mm4::umma_commit(dready + d);  // accumulator d holds its groups' sum (arrives at once if none)
       }
     }
   } else {
-    // ---------------- converters + epilogue of set s ----------------
+    // ---------------- converters (set s takes the groups gq % kSets == s) + epilogue ----------------
     const int cw = warp - kFirstConv;
     const int s = cw >> 2;
-    const int quad = warp & 3;
+    const int quad = warp & 3;  // tensor-memory lane quadrant this warp may access
     const int rib = quad * 32 + lane;
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    const uint32_t a_set = tq + s * kSetCols;
     const uint32_t magic = 0x54006400u, mask = 0x00F0000Fu;  // (1024 | low nibble, 64 | high nibble << 4)
     bool waited = false;  // griddepcontrol.wait before the first write of Y or of the workspace
-    int q = 0, used = 0;
+    int gq = 0;
     bool ok = true;
     for (int jj = 0; jj < nlocal; ++jj) {
-      const int item = cta + jj * C;
-      const int rem = item % (p.nchunks * p.kslices);
-      const int row = (item / (p.nchunks * p.kslices)) * kRows + rib, t0 = (rem / p.kslices) * BT;
-      const int ks = rem % p.kslices, g0 = ks * p.gps, g1 = min(G, g0 + p.gps);
+      const Item it = item_of(p, cta + jj * C);
+      const int row = it.row0 + rib;
       const bool row_ok = row < p.N;
-      const uint16_t* srow = p.s + static_cast<int64_t>(row_ok ? row : 0) * G;
-      const uint16_t* mrow = p.m + static_cast<int64_t>(row_ok ? row : 0) * G;
+      const uint16_t* srow = p.s + static_cast<int64_t>(row_ok ? row : 0) * p.G;
+      const uint16_t* mrow = p.m + static_cast<int64_t>(row_ok ? row : 0) * p.G;
+      // this set's first group of the item, and its scale and min fetched one of the set's groups ahead
+      int g = it.g0 + ((s - gq % kSets) + kSets) % kSets;
       uint16_t s_next = 0, m_next = 0;
-      if (g0 + s < g1) {
-        s_next = __ldg(srow + g0 + s);
-        m_next = __ldg(mrow + g0 + s);
+      if (g < it.g1) {
+        s_next = __ldg(srow + g);
+        m_next = __ldg(mrow + g);
       }
-      for (int gg = g0 + s; gg < g1; gg += kSets, ++q, ++used) {
+      for (; g < it.g1; g += kSets) {
+        const int q = gq + (g - it.g0);  // this group's place in the CTA's sequence
         const uint16_t s16 = s_next, m16 = m_next;
-        if (gg + kSets < g1) {  // the set's next group's scale and min
-          s_next = __ldg(srow + gg + kSets);
-          m_next = __ldg(mrow + gg + kSets);
+        if (g + kSets < it.g1) {
+          s_next = __ldg(srow + g + kSets);
+          m_next = __ldg(mrow + g + kSets);
         }
-        const int slot = used % nst;
-        if (ok) ok = mbar_wait(full(s, slot), (used / nst) & 1, ERR_MM4_WAIT);
+        const int slot = q % nst;
+        if (ok) ok = mbar_wait(full + slot, (q / nst) & 1, ERR_MM4_WAIT);
         uint4 w4[4];
         if (ok) {
-          const uint8_t* rowp = stage_of(s, slot) + rib * 64;
+          const uint8_t* rowp = stage_of(slot) + rib * 64;
 #pragma unroll
           for (int c = 0; c < 4; ++c) w4[c] = lds128(rowp + ((c ^ ((rib >> 1) & 3)) << 4));
         }
@@ -245,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
           // the stage's two X atoms (BT rows x 128 bytes each), bf16 -> fp16 in place; the MMA issuer reads them
           // only after this set's afull arrival below, and the proxy fence makes the writes visible to it
           if (ok) {
-            uint8_t* xa = stage_of(s, slot) + kCodeBytes;
+            uint8_t* xa = stage_of(slot) + kCodeBytes;
             for (int c = rib; c < BT * 16; c += 128) {
               uint4 v = *reinterpret_cast<const uint4*>(xa + c * 16);
               v.x = bf16x2_to_f16x2(v.x);
@@ -258,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty(s, slot));  // codes are in registers
+        if (lane == 0) mbar_arrive(empty + slot);  // codes are in registers
         const uint32_t s2 = static_cast<uint32_t>(s16) * 0x10001u, m2 = static_cast<uint32_t>(m16) * 0x10001u;
         uint32_t o[64];
 #pragma unroll
@@ -274,57 +313,105 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
             }
           }
         }
-        const int b = q % kNB;
+        const int b = q % na;
         ok = __all_sync(0xffffffffu, ok);
-        if (q >= kNB && ok) ok = __all_sync(0xffffffffu, mbar_wait(mdone(s, b), ((q / kNB) - 1) & 1, ERR_MM4_WAIT));
+        if (q >= na && ok) ok = __all_sync(0xffffffffu, mbar_wait(mdone + b, ((q / na) - 1) & 1, ERR_MM4_WAIT));
         if (ok) {
           mm4::tc_fence_after();
-          g4t::tmem_st32(a_set + b * kACols, o);
-          g4t::tmem_st32(a_set + b * kACols + 32, o + 32);
+          const uint32_t a = tq + a_base + b * kACols;
+          g4t::tmem_st32(a, o);
+          g4t::tmem_st32(a + 32, o + 32);
           g4t::tmem_wait_st();
           mm4::tc_fence_before();
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(afull(s, b));
+        if (lane == 0) mbar_arrive(afull + b);
       }
-      // ---- epilogue of this item: D0 + D1 in that order; set s stores every other 32-column chunk ----
+      gq += it.g1 - it.g0;
+      // ---- epilogue of this item: 32-column chunks of D over the three warps of each lane quadrant ----
       if (!waited) {
         griddep_wait();  // Y (and a reused workspace) may still be read by the previous kernel
         waited = true;
       }
-      for (int t = 0; t < kSets; ++t)
-        if (ok) ok = mbar_wait(dready(t), jj & 1, ERR_MM4_WAIT);
+      for (int d = 0; d < nd; ++d)
+        if (ok) ok = mbar_wait(dready + d, jj & 1, ERR_MM4_WAIT);
       ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        mm4::tc_fence_after();
+      if (ok) mm4::tc_fence_after();
+      const int gq0 = gq - (it.g1 - it.g0);  // the item's first group in the CTA's sequence
+      // D_0 + ... + D_{nd-1} (issuers without a group in this item skipped) of the 32 columns from c0
+      auto sum_d = [&](int c0, float (&acc)[32]) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+        for (int d = 0; d < nd; ++d) {
+          if ((d - gq0 % nd + nd) % nd >= it.g1 - it.g0) continue;
+          uint32_t v[32];
+          tmem_ld32(tq + static_cast<uint32_t>(d) * p.dcols + c0, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(v[i]);
+        }
+      };
+      if (p.ostore) {
+        // rounds of tc tokens: every converter warp writes its 32-column chunks of D into the staging tile
+        // [token][128 rows] in the output's type, then one thread stores the tile with one bulk-tensor copy (rows
+        // past N and tokens past M are clipped by the tensor map). Every converter warp takes every barrier,
+        // whatever `ok` is.
+        uint8_t* out = smem + p.out_off;
+        const int esz = p.ostore == 2 ? 4 : 2;
+        const int ct = cw * 32 + lane;
+        for (int tc0 = 0; tc0 < BT; tc0 += p.tc) {
+          if (ct == 0) bulk_wait_read();  // the last store has read the staging tile
+          named_bar_sync(kBarEpi, kConvWarps * 32);
+          for (int c0 = tc0 + 32 * s; c0 < min(BT, tc0 + p.tc); c0 += 32 * kSets) {
+            float acc[32];
+            if (ok) {
+              sum_d(c0, acc);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              uint8_t* dst = out + (static_cast<uint32_t>(c0 - tc0 + i) * kRows + rib) * esz;
+              if (esz == 4)
+                *reinterpret_cast<float*>(dst) = acc[i];
+              else if (p.y_bf16)
+                *reinterpret_cast<__nv_bfloat16*>(dst) = __float2bfloat16_rn(acc[i]);
+              else
+                *reinterpret_cast<__half*>(dst) = __float2half_rn(acc[i]);
+            }
+          }
+          fence_proxy_async_smem();
+          named_bar_sync(kBarEpi, kConvWarps * 32);
+          if (ct == 0) {
+            if (p.ostore == 2)
+              tma_store_3d(&p.omap, smem_u32(out), it.row0, it.t0 + tc0, it.ks);
+            else
+              tma_store_2d(&p.omap, smem_u32(out), it.row0, it.t0 + tc0);
+            bulk_commit();
+          }
+        }
+      } else if (ok) {
         for (int c0 = 32 * s; c0 < BT; c0 += 32 * kSets) {
           float acc[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-          for (int t = 0; t < kSets; ++t) {
-            if (t >= g1 - g0) break;  // that set had no group in this item
-            uint32_t v[32];
-            tmem_ld32(tq + t * kSetCols + kNB * kACols + c0, v);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(v[i]);
-          }
+          sum_d(c0, acc);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int tok = t0 + c0 + i;  // columns past BT belong to no token of this chunk
+            const int tok = it.t0 + c0 + i;  // columns past BT belong to no token of this chunk
             if (row_ok && c0 + i < BT && tok < p.M) {
               if (p.kslices == 1)
                 store_out(p.y, static_cast<int64_t>(tok) * p.ldy + row, acc[i], p.y_bf16);
               else
-                p.ws[(static_cast<int64_t>(ks) * p.M + tok) * p.N + row] = acc[i];
+                p.ws[(static_cast<int64_t>(it.ks) * p.M + tok) * p.N + row] = acc[i];
             }
           }
         }
-        mm4::tc_fence_before();
       }
+      if (ok) mm4::tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dfree);
     }
   }
+  if (warp == kFirstConv && lane == 0 && p.ostore) bulk_wait_all();  // the epilogue's stores have landed
   mm4::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -346,16 +433,24 @@ __global__ void __launch_bounds__(256) mm_int4_reduce_kernel(const float* ws, vo
   }
 }
 
-// Token chunking and K slicing of a call: chunks of <= 128 tokens; K is split into slices (>= 2 groups each)
-// when the row-block x chunk items would leave SMs idle.
+// Token chunking and K slicing of a call. Chunks of up to `width` tokens (128 or 256: one dequantisation of a
+// group then feeds up to 256 tokens); K is split into slices (>= 2 groups each) when the row-block x chunk items
+// would leave SMs idle. Of the two widths the plan takes the one with the smaller estimated time of the busiest
+// CTA: its items x (groups x the time of one group + the item's epilogue). Measured per group: about 1.05 us at
+// 128 tokens and 1.2 us at 256 (the stage ring, not the tensor rate, paces it), i.e. (BT + 750) in units of one
+// token-column; the epilogue about 1,700 units through the staging tile (BT <= 128) and 5,000 with plain stores.
 struct MmPlan {
   int BT, nchunks, kslices, gps;
+  int64_t cost;
 };
-inline MmPlan mm_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
+inline MmPlan mm_plan_width(int64_t M, int64_t N, int64_t K, int num_sms, int64_t width) {
   MmPlan pl;
-  const int64_t nch = (M + 127) / 128;
+  const int64_t nch = (M + width - 1) / width;
   const int64_t BT = (M + nch - 1) / nch;
-  pl.BT = static_cast<int>(std::max<int64_t>(16, (BT + 15) / 16 * 16));
+  // a multiple of 16 (the MMA's N); of 32 when there are several chunks, so that the epilogue's rounds of whole
+  // 32-token pieces never reach into the next chunk's tokens
+  const int64_t mult = nch > 1 ? 32 : 16;
+  pl.BT = static_cast<int>(std::max<int64_t>(16, (BT + mult - 1) / mult * mult));
   pl.nchunks = static_cast<int>((M + pl.BT - 1) / pl.BT);
   const int G = static_cast<int>(K / 128);
   const int64_t items = (N + kRows - 1) / kRows * pl.nchunks;  // int64: M and N may each be up to 2^30
@@ -364,7 +459,15 @@ inline MmPlan mm_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
   ks = std::max(ks, 1);
   pl.gps = (G + ks - 1) / ks;
   pl.kslices = (G + pl.gps - 1) / pl.gps;
+  const int64_t waves = (items * pl.kslices + num_sms - 1) / num_sms;
+  pl.cost = waves * (static_cast<int64_t>(pl.gps) * (pl.BT + 750) + (pl.BT <= 128 ? 1700 : 5000));
   return pl;
+}
+inline MmPlan mm_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
+  const MmPlan a = mm_plan_width(M, N, K, num_sms, 128);
+  if (M <= 128) return a;
+  const MmPlan b = mm_plan_width(M, N, K, num_sms, kMaxBT);
+  return b.cost < a.cost ? b : a;
 }
 
 }  // namespace mm4t
@@ -397,6 +500,12 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   }
   const int BT = pl.BT;
   MmtParams p;
+  // accumulators: 3 of 64 columns for chunks of <= 64 tokens (an MMA's issue cost, about 66 cycles, is above the
+  // tensor time of N <= 64), 2 of 128 for 65..127 tokens, 1 for 128..256 (N >= 128 runs at the full rate from
+  // one issuer); the A buffers after them
+  p.nd = BT <= 64 ? 3 : (BT < 128 ? 2 : 1);
+  p.dcols = p.nd == 3 ? 64u : (BT <= 128 ? 128u : 256u);
+  p.na = std::min(7, static_cast<int>((kTmemCols - p.nd * p.dcols) / kACols));
   p.ws = a.ws;
   p.kslices = pl.kslices;
   p.gps = pl.gps;
@@ -412,17 +521,20 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   p.nchunks = pl.nchunks;
   p.nitems = ((N + kRows - 1) / kRows) * p.nchunks * p.kslices;
   p.y_bf16 = a.y_dtype == RB_BF16;
-  p.prefetch = 0;
   p.stage_bytes = (kCodeBytes + 2u * BT * 128u + 1023u) & ~1023u;
   constexpr uint32_t kSmemMax = 227 * 1024;
-  int nst = static_cast<int>((kSmemMax - 1024 - 512) / (kSets * p.stage_bytes));
+  const uint32_t bar_bytes = (2 * kMaxStages + 2 * 7 + kMaxIssuers + 1) * 8 + 16;
+  // the staging tile only for chunks of <= 128 tokens: 256-token stages (72 KB) keep all of shared memory
+  const uint32_t out_bytes = BT <= 128 ? kOutBytes : 0u;
+  int nst = static_cast<int>((kSmemMax - 1024 - out_bytes - bar_bytes) / p.stage_bytes);
   nst = std::min(nst, kMaxStages);
   if (nst < 2) return RB_ERR_SHAPE;
   p.nst = nst;
-  p.bar_off = static_cast<uint32_t>(kSets * nst) * p.stage_bytes;
+  p.out_off = static_cast<uint32_t>(nst) * p.stage_bytes;
+  p.bar_off = p.out_off + out_bytes;
   // instruction descriptor: D f32, A f16, B f16, both K-major, N = BT, M = 128
   p.idesc = (1u << 4) | (static_cast<uint32_t>(BT >> 3) << 17) | (static_cast<uint32_t>(kRows >> 4) << 24);
-  const uint32_t smem = 1024 + p.bar_off + (kSets * (2 * nst + 2 * kNB + 1) + 1) * 8 + 16;
+  const uint32_t smem = 1024 + p.bar_off + (2 * nst + 2 * p.na + kMaxIssuers + 1) * 8 + 16;
   {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(N)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K / 2)};
@@ -434,16 +546,62 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
       return RB_ERR_SHAPE;
   }
   {
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.ldx) * 2};
-    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(BT)};
-    const cuuint32_t es[2] = {1, 1};
+    // X as {64 columns, M rows, K/64 atoms of 64 columns}: one copy brings a group's two atoms, stacked as the MMA
+    // descriptor reads them ([atom][token][64], each atom 1024-byte aligned since BT % 16 == 0). Every element
+    // it addresses lies inside X. If the driver refuses the view, two 2-D copies per group.
     const CUtensorMapDataType xt =
         a.x_dtype == RB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    if (encode(&p.xmap, xt, 2, const_cast<void*>(a.X), dims, strides, box, es,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return RB_ERR_SHAPE;
+    const cuuint64_t dims3[3] = {64, static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(K / 64)};
+    const cuuint64_t strides3[2] = {static_cast<cuuint64_t>(a.ldx) * 2, 128};
+    const cuuint32_t box3[3] = {64, static_cast<cuuint32_t>(BT), 2};
+    const cuuint32_t es3[3] = {1, 1, 1};
+    p.x3d = encode(&p.xmap, xt, 3, const_cast<void*>(a.X), dims3, strides3, box3, es3, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    if (!p.x3d) {
+      const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+      const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.ldx) * 2};
+      const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(BT)};
+      const cuuint32_t es[2] = {1, 1};
+      if (encode(&p.xmap, xt, 2, const_cast<void*>(a.X), dims, strides, box, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return RB_ERR_SHAPE;
+    }
+  }
+  // The epilogue's bulk-tensor store: Y when its rows start 16-byte aligned at a 16-byte multiple pitch, the fp32
+  // workspace [kslices, M, N] when N % 4 == 0; otherwise plain stores. Tokens past M and rows past N are clipped.
+  // A round stores tc tokens: all BT in fp16/bf16 (BT <= 128 fits the 32 KB tile); in fp32 BT when BT <= 64,
+  // else 64 or 32 (BT is then a multiple of 32, or the chunk is the call's only one and tokens past M are clipped).
+  p.ostore = 0;
+  p.tc = 0;
+  if (BT > 128) {
+    // plain stores
+  } else if (p.kslices == 1) {
+    if ((reinterpret_cast<uintptr_t>(a.Y) & 15u) == 0 && (a.ldy * 2) % 16 == 0) {
+      p.tc = BT;
+      const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+      const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.ldy) * 2};
+      const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRows), static_cast<cuuint32_t>(p.tc)};
+      const cuuint32_t es[2] = {1, 1};
+      const CUtensorMapDataType yt =
+          a.y_dtype == RB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+      if (encode(&p.omap, yt, 2, a.Y, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+        p.ostore = 1;
+    }
+  } else if (N % 4 == 0 && (reinterpret_cast<uintptr_t>(a.ws) & 15u) == 0) {
+    p.tc = BT <= 64 ? BT : (BT % 64 == 0 || p.nchunks == 1 ? 64 : 32);
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M),
+                                static_cast<cuuint64_t>(p.kslices)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(N) * 4, static_cast<cuuint64_t>(M) * N * 4};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kRows), static_cast<cuuint32_t>(p.tc), 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    if (encode(&p.omap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.ws, dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      p.ostore = 2;
   }
   void (*kern)(MmtParams) = a.x_dtype == RB_BF16 ? mm_int4_tc_kernel<true> : mm_int4_tc_kernel<false>;
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemMax);

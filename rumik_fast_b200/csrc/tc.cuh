@@ -23,6 +23,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 3-D tiled TMA load global -> shared (this CTA), completion counted on `bar` in bytes. No multicast.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Shared-memory descriptor of a K-major SWIZZLE_128B operand: 8-row groups 1024 bytes apart, descriptor
 // version 1 (sm_100).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {

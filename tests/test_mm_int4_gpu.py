@@ -46,8 +46,13 @@ def test_golden(tag):
     assert_close(Y, g[f"{tag}_Y"], f"golden mm {tag}")
 
 
+# Chunks of up to 128 tokens, or 256 where the plan estimates it faster ((512, 3072, 3072), (700, 4000, 2048),
+# (1024, 3072, 8192): one 256-column accumulator, plain stores); M <= 64: three accumulators, one MMA issuer each.
+# Chunks of <= 128 tokens store each item's tile with a bulk-tensor copy (Y, or the split-K partials: (100, 3072,
+# 3072) in two rounds of 64 tokens); (300, 1000, 1024) ends in a partial chunk after full ones.
 @pytest.mark.parametrize("M,N,K", [(1, 128, 128), (17, 200, 256), (34, 5120, 3072), (64, 3072, 8192), (300, 1000, 1024),
-                                   (256, 3072, 3072), (1024, 16384, 3072)])
+                                   (256, 3072, 3072), (1024, 16384, 3072), (512, 3072, 3072), (700, 4000, 2048),
+                                   (1024, 3072, 8192), (100, 3072, 3072)])
 def test_shapes(M, N, K):
     g = syn.generator(M * 31 + N + K, "cpu")
     q, s, m = syn.int4_weights(N, K, g, "cpu")
@@ -84,7 +89,8 @@ def test_deterministic():
     assert torch.equal(mm_int4(X, q, s, m), mm_int4(X, q, s, m))
 
 
-@pytest.mark.parametrize("M,N,K", [(34, 5120, 3072), (34, 3072, 8192), (256, 3072, 3072), (1024, 16384, 3072)])
+@pytest.mark.parametrize("M,N,K", [(34, 5120, 3072), (34, 3072, 8192), (256, 3072, 3072), (1024, 16384, 3072),
+                                   (512, 3072, 3072)])
 def test_bf16_x_through_the_c_abi(M, N, K):
     """The engine's bf16 activations straight into rb_mm_int4 (no split) and rb_mm_int4_ws (split K where the
     plan splits): converted to fp16 inside the kernel, so the result equals the fp16-X call bit for bit (the
