@@ -45,9 +45,10 @@ PREFILL_TOKENS = (34, 256, 1024)
 BATCHES = (4, 16)  # config 4: independent decode streams per GPU (batch 1 is the headline line)
 # DRAM bytes (read + write) per launch of gemv_int4_tc_kernel on the 36-layer set: ncu capture of the 3-layer
 # case of the current build scaled x12 by blocks streamed (profiles/gemv_int4_tc_3layer_traffic.md)
-NCU_TRAFFIC_PER_LAUNCH = 1966808064
-# The same for the one launch of the 144 projections and the int8 head's rows (the default step): not yet captured
-NCU_TRAFFIC_STEP_LAUNCH = None
+NCU_TRAFFIC_PER_LAUNCH = 1967102976
+# The same for the one launch of the 144 projections and the int8 head's rows (the default step): 12 x the
+# 3-layer projections + the head's share of a capture of the 3-layer list with the head (same profile)
+NCU_TRAFFIC_STEP_LAUNCH = 2018034944
 
 
 def parse():
@@ -58,7 +59,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefetch", action="store_true", help="do not stream weights before the PDL wait")
     ap.add_argument("--no-extras", action="store_true", help="headline only: no step/prefill/gemv_c0/chain records")
-    ap.add_argument("--head", default="list", choices=["list", "concurrent", "serial"],
+    ap.add_argument("--head", default="list_last", choices=["list", "list_last", "concurrent", "serial"],
                     help="set mode: the int8 head's rows as the first entry of the projection launch (list), its "
                          "own launch on a forked branch of the step graph (concurrent) or after the list (serial)")
     ap.add_argument("--mode", default="set", choices=["set", "chain"],
@@ -229,6 +230,8 @@ def step_fn(w, mode="set", with_head=True, head="list"):
     """One decode step's projections: 36 x (QKV, o_proj, gate_up with x_h; down with x_i) + the int8 head.
     mode "set": the 144 int4 GEMVs as one persistent launch; the head (independent of them) by `head`:
       "list"       its int8 rows are the first entry of that launch (one more kind of work item);
+      "list_last"  the same rows as the last entry (the default: the head's heavier blocks then fill the CTAs
+                   that the projections' static deal leaves lightest);
       "concurrent" its own launch on a forked branch of the step's graph, launched first;
       "serial"     its own launch after the list.
     mode "chain": one launch per GEMV, in stream order, as an unmodified engine issues them."""
@@ -239,8 +242,9 @@ def step_fn(w, mode="set", with_head=True, head="list"):
         entries = []
         for L in layers:
             entries += [(xh, *L[0], outs[0]), (xh, *L[1], outs[1]), (xh, *L[2], outs[2]), (xi, *L[3], outs[3])]
-        if with_head and head == "list":
-            entries = [(xh, *w["head"], None, w["logits"])] + entries
+        if with_head and head in ("list", "list_last"):
+            he = (xh, *w["head"], None, w["logits"])
+            entries = [he] + entries if head == "list" else entries + [he]
             with_head = False
         projections = rb.Int4GemvSet(entries)
         side = torch.cuda.Stream() if head == "concurrent" else None
@@ -793,7 +797,7 @@ def run_ours(a):
         # and what the head costs inside the step (step - projections)
         ms4 = timed(g_int4.replay, max(1, a.steps // 2), a.warmup, world) / max(1, a.steps // 2)
         launches4 = 1 if a.mode == "set" else a.layers * 4
-        one_launch = a.mode == "set" and a.head == "list"  # the step IS one launch of the list kernel
+        one_launch = a.mode == "set" and a.head in ("list", "list_last")  # the step IS one list launch
         if one_launch:
             roof_bytes, roof_ms, roof_launches = step_bytes, ms_step, 1
         else:
@@ -838,7 +842,7 @@ def run_ours(a):
                                    "gate_up 16384x3072, down 3072x8192; int4 g128) + config-2 int8 head "
                                    "16385x3072, batch 1, in one CUDA graph",
                        "launches": ("144 projections and the int8 head's rows in one persistent launch"
-                                    if a.head == "list" else f"144 projections in one persistent launch + the "
+                                    if a.head in ("list", "list_last") else f"144 projections in one persistent launch + the "
                                     f"head ({a.head})") if a.mode == "set" else "145 stream-ordered launches",
                        "batch": 1, "bytes_per_step": step_bytes, "parallelism": f"replica x{world}",
                        "weight_prefetch": not a.no_prefetch,
