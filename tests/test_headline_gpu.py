@@ -1,7 +1,7 @@
 """The exact kernel instance the headline benchmark times, at the size it is timed.
 
-bench.py's decode workload runs the int8 head's rows (16385 x 3072, 129 blocks) and the 36-layer config-1
-projection set (144 GEMVs, 7,776 blocks of 128 rows) as one Int4GemvSet launch. That list is far longer than
+bench.py's decode workload runs the 36-layer config-1 projection set (144 GEMVs, 7,776 blocks of 128 rows) and
+the int8 head's rows (16385 x 3072, 129 blocks, the list's last entry) as one Int4GemvSet launch. That list is far longer than
 3 x the SM count, so it runs on the tcgen05 kernel UNSPLIT: each CTA walks about 53 blocks and every ring slot and
 tensor-memory buffer wraps its phase many times.
 These tests build that list (distinct weights per layer, as the bench does, but a distinct output per entry so
@@ -42,21 +42,23 @@ def check_all(ent, what):
 
 
 def step_list(dtype, layers=36, seed=1234, head=True):
-    """bench.py's step list: the int8 head's rows (int8 codes, fp16 row scales, x_h), then per layer QKV, o_proj,
-    gate_up with x_h and down with x_i."""
+    """bench.py's step list: per layer QKV, o_proj, gate_up with x_h and down with x_i, then the int8 head's rows
+    (int8 codes, fp16 row scales, x_h)."""
     gen = syn.generator(seed, DEV)
     xh = syn.activations((3072,), gen, DEV, dtype=dtype)
     xi = syn.activations((8192,), gen, DEV, dtype=dtype)
     ent = []
+    head_entry = []
     if head:
         q8, s8 = syn.int8_weights(*syn.HEAD_SHAPE, gen, DEV)
-        ent.append((xh, q8, s8, None, torch.full((syn.HEAD_SHAPE[0],), float("nan"), device=DEV, dtype=dtype)))
+        head_entry.append((xh, q8, s8, None, torch.full((syn.HEAD_SHAPE[0],), float("nan"), device=DEV,
+                                                        dtype=dtype)))
     for _ in range(layers):
         for name, n, k in syn.LAYER_SHAPES:
             q, s, m = syn.int4_weights(n, k, gen, DEV)
             ent.append((xi if name == "down" else xh, q, s, m, torch.full((n,), float("nan"), device=DEV,
                                                                           dtype=dtype)))
-    return ent
+    return ent + head_entry
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
