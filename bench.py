@@ -562,7 +562,7 @@ def measure_prefill(dev, seed, tokens, nlayers, steps, warmup, world, clk=None):
     """Config 3: Y = X W^T over the 36-layer projection set with X fp16 [M, K], one mm_int4 launch per matrix,
     replayed from one CUDA graph, for each M in `tokens`. Returns {M: record}."""
     from rumik_fast_b200 import synthetic as syn
-    from rumik_fast_b200.mm_int4 import mm_int4
+    from rumik_fast_b200.mm_int4 import mm_int4, MmInt4Set
     gen = syn.generator(seed, dev)
     layers = [[syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES] for _ in range(nlayers)]
     wbytes = nlayers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES)
@@ -581,18 +581,28 @@ def measure_prefill(dev, seed, tokens, nlayers, steps, warmup, world, clk=None):
         m0 = clk.mark() if clk else 0
         ms = timed(g.replay, steps, warmup, world) / steps
         m1 = clk.mark() if clk else 0
+        # the same products as persistent list launches (MmInt4Set, 52 products a launch)
+        lst = MmInt4Set([(xs[k], *w, ys[i]) for L in layers for i, ((_, n, k), w) in enumerate(zip(syn.LAYER_SHAPES, L))])
+        gl = capture(lst)
+        ms_l = timed(gl.replay, steps, warmup, world) / steps
         flops = 2 * M * nlayers * sum(n * k for _, n, k in syn.LAYER_SHAPES)
         tf = flops / (ms * 1e-3) / 1e12
         gbs = wbytes / (ms * 1e-3) / 1e9
         bound = "hbm" if M < 64 else "tensor"
         frac = gbs / hbm if bound == "hbm" else tf / tf_peak
+        tf_l, gbs_l = flops / (ms_l * 1e-3) / 1e12, wbytes / (ms_l * 1e-3) / 1e9
+        frac_l = gbs_l / hbm if bound == "hbm" else tf_l / tf_peak
         out[str(M)] = {"tflops": round(world * tf, 1), "weight_gbs": round(gbs, 1), "ms_per_step": round(ms, 4),
                        "bound": bound, "roofline_frac": round(frac, 4),
                        "peak": hbm if bound == "hbm" else tf_peak,
                        "peak_unit": "GB/s" if bound == "hbm" else "TFLOP/s (bf16 dense, cuBLAS burst)",
                        "peak_kind": hkind if bound == "hbm" else tf_kind, "flops_per_step": flops,
-                       "launches_per_step": 4 * nlayers, "clocks": clk.summary(m0, m1) if clk else None}
-        del g, xs, ys
+                       "launches_per_step": 4 * nlayers, "clocks": clk.summary(m0, m1) if clk else None,
+                       "list": {"tflops": round(world * tf_l, 1), "weight_gbs": round(gbs_l, 1),
+                                "ms_per_step": round(ms_l, 4), "roofline_frac": round(frac_l, 4),
+                                "launches_per_step": -(-4 * nlayers // 52),
+                                "method": "rb_mm_int4_list: the same products in persistent launches of 52"}}
+        del g, gl, lst, xs, ys
         free()
     del layers
     free()
@@ -605,7 +615,7 @@ def measure_batched(dev, seed, batches, nlayers, steps, warmup, world, clk=None)
     at batch B (gemv_int8_cuda with x [B, K]), replayed from one CUDA graph. Returns {B: record}; batch 1 is the
     headline line itself."""
     from rumik_fast_b200 import synthetic as syn
-    from rumik_fast_b200.mm_int4 import mm_int4
+    from rumik_fast_b200.mm_int4 import mm_int4, MmInt4Set
     import rumik_fast_b200 as rb
     gen = syn.generator(seed, dev)
     layers = [[syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES] for _ in range(nlayers)]
@@ -627,12 +637,24 @@ def measure_batched(dev, seed, batches, nlayers, steps, warmup, world, clk=None)
         m0 = clk.mark() if clk else 0
         ms = timed(g.replay, steps, warmup, world) / steps
         m1 = clk.mark() if clk else 0
+        # the projections as persistent list launches (rb_mm_int4_list), the head as before
+        lst = MmInt4Set([(xs[k], *w, ys[i]) for L in layers for i, ((_, n, k), w) in enumerate(zip(syn.LAYER_SHAPES, L))])
+
+        def step_list():
+            lst()
+            rb.gemv_int8_cuda(xs[3072], *head, out=logits)
+        gl = capture(step_list)
+        ms_l = timed(gl.replay, steps, warmup, world) / steps
         gbs = wbytes / (ms * 1e-3) / 1e9
+        gbs_l = wbytes / (ms_l * 1e-3) / 1e9
         out[str(B)] = {"tok_s": round(world * B * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
                        "weight_gbs": round(world * gbs, 1), "roofline_frac": round(gbs / hbm, 4), "peak_gbs": hbm,
                        "peak_kind": hkind, "launches_per_step": 4 * nlayers + 1,
-                       "clocks": clk.summary(m0, m1) if clk else None}
-        del g, xs, ys, logits
+                       "clocks": clk.summary(m0, m1) if clk else None,
+                       "list": {"tok_s": round(world * B * 1e3 / ms_l, 1), "ms_per_step": round(ms_l, 4),
+                                "weight_gbs": round(world * gbs_l, 1), "roofline_frac": round(gbs_l / hbm, 4),
+                                "launches_per_step": -(-4 * nlayers // 52) + 1}}
+        del g, gl, lst, xs, ys, logits
         free()
     del layers, head
     free()

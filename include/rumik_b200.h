@@ -135,6 +135,31 @@ int rb_mm_int4_ws(const void* X, int x_dtype, int64_t ldx,
                   void* Y, int y_dtype, int64_t ldy,
                   int64_t M, int64_t N, int64_t K, void* ws, int64_t ws_bytes, int flags, void* stream);
 
+/* One prefill product of a list: Y [M, N] = X [M, K] * w^T, the layout of rb_mm_int4 (M is the list's). */
+typedef struct rb_mm_desc {
+  const void* X;        /* [M, K], row stride ldx elements (multiple of 8), 16-byte aligned */
+  int64_t ldx;
+  const uint8_t* q;     /* codes [N, K/2] */
+  const uint16_t* s;    /* fp16 scales [N, K/128] */
+  const uint16_t* m;    /* fp16 mins [N, K/128] */
+  void* Y;              /* [M, N], row stride ldy elements (multiple of 8), 16-byte aligned */
+  int64_t ldy;
+  int64_t N;            /* >= 1 */
+  int64_t K;            /* multiple of 128 */
+} rb_mm_desc;
+
+/*
+ * A list of independent prefill products with one token count M (one x dtype, one y dtype) in persistent
+ * launches of up to 52 products each: the work items of every product (128-row weight block x token chunk) are
+ * dealt round-robin to one CTA per SM, so the list pays one launch, one pipeline fill and one tail instead of one
+ * per product, and needs no split-K workspace. The arithmetic is rb_mm_int4's. No reference counterpart as a
+ * single call: it runs what rumik-fast's prefill benchmark issues as one mm_int4 per matrix
+ * (kernels/mm_int4.py:94-101), or a layer's products that share their input (QKV and gate_up). `descs` is a host
+ * array read during the call; every X must be ready and no Y may alias another product's inputs.
+ */
+int rb_mm_int4_list(const rb_mm_desc* descs, int count, int64_t M, int x_dtype, int y_dtype, int flags,
+                    void* stream);
+
 /* One int4 GEMV of a list (host-side description, read by rb_gemv_int4_multi during the call). */
 typedef struct rb_gemv_desc {
   const void* x;        /* activations [K] (dtype x_dtype of the call), 16-byte aligned */

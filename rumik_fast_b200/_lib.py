@@ -24,6 +24,12 @@ _c = ctypes
 _vp, _i64, _int = _c.c_void_p, _c.c_int64, _c.c_int
 
 
+class MmDesc(ctypes.Structure):
+    """struct rb_mm_desc (include/rumik_b200.h)."""
+    _fields_ = [("X", _vp), ("ldx", _i64), ("q", _vp), ("s", _vp), ("m", _vp), ("Y", _vp), ("ldy", _i64),
+                ("N", _i64), ("K", _i64)]
+
+
 class GemvDesc(ctypes.Structure):
     """struct rb_gemv_desc (include/rumik_b200.h)."""
     _fields_ = [("x", _vp), ("y", _vp), ("q", _vp), ("s", _vp), ("m", _vp), ("N", _i64), ("K", _i64),
@@ -72,6 +78,7 @@ SIGNATURES = {
     "rb_mm_int4": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
     "rb_mm_int4_workspace": (_i64, [_i64, _i64, _i64]),
     "rb_mm_int4_static": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp]),
+    "rb_mm_int4_list": (_int, [_vp, _int, _i64, _int, _int, _int, _vp]),
     "rb_mm_int4_ws": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _vp, _i64, _int, _vp]),
     "rb_gemv_int4_multi": (_int, [_c.POINTER(GemvDesc), _int, _int, _int, _int, _vp]),
     "rb_gemv_int4_fused": (_int, [_c.POINTER(GemvDesc), _c.POINTER(GemvEpi), _int, _c.POINTER(AddLn),

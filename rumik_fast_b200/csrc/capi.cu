@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include <vector>
+
 #include "kernels.h"
 
 #include <cstring>
@@ -449,6 +451,35 @@ int rb_mm_int4_static(const void* X, int x_dtype, int64_t ldx, const uint8_t* q,
                       void* Y, int y_dtype, int64_t ldy, int64_t M, int64_t N, int64_t K, int flags, void* stream) {
   if (x_dtype != RB_F16 && x_dtype != RB_BF16) return RB_ERR_DTYPE;
   return mm_int4_impl(X, x_dtype, ldx, q, s, m, Y, y_dtype, ldy, M, N, K, nullptr, 0, flags, stream, true);
+}
+
+int rb_mm_int4_list(const rb_mm_desc* descs, int count, int64_t M, int x_dtype, int y_dtype, int flags,
+                    void* stream) {
+  if (count < 0 || M < 0 || M > (int64_t(1) << 30)) return RB_ERR_SHAPE;
+  if (count == 0 || M == 0) return RB_OK;
+  if (!descs) return RB_ERR_NULL;
+  if (!act_dtype_ok(x_dtype) || !act_dtype_ok(y_dtype)) return RB_ERR_DTYPE;
+  std::vector<rb::MmArgs> args;
+  args.reserve(count);
+  for (int i = 0; i < count; ++i) {
+    const rb_mm_desc& d = descs[i];
+    if (d.N < 1 || d.K <= 0 || d.K % 128 != 0 || d.N > (int64_t(1) << 30)) return RB_ERR_SHAPE;
+    if (!d.X || !d.Y || !d.q || !d.s || !d.m) return RB_ERR_NULL;
+    if (d.ldx < d.K || d.ldy < d.N) return RB_ERR_SHAPE;
+    if (!aligned16(d.X) || !aligned16(d.Y) || (d.ldx % 8) != 0 || (d.ldy % 8) != 0) return RB_ERR_ALIGN;
+    if (!aligned16(d.q) || !aligned16(d.s) || !aligned16(d.m)) return RB_ERR_ALIGN;
+    rb::MmArgs a = {};
+    a.X = d.X; a.x_dtype = x_dtype; a.ldx = d.ldx;
+    a.q = d.q; a.s = d.s; a.m = d.m;
+    a.Y = d.Y; a.y_dtype = y_dtype; a.ldy = d.ldy;
+    a.M = M; a.N = d.N; a.K = d.K; a.flags = flags;
+    args.push_back(a);
+  }
+  int sms = 0, st = device_sms(&sms);
+  if (st != RB_OK) return st;
+  st = rb::launch_mm_int4_list(args.data(), count, sms, static_cast<cudaStream_t>(stream));
+  if (st == RB_OK && cudaGetLastError() != cudaSuccess) st = RB_ERR_LAUNCH;
+  return st;
 }
 
 int rb_tp_allreduce_f16(const void* a, const void* b, void* out, int64_t n, void* const* bufs, int rank, int world,

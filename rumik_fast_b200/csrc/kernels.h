@@ -47,6 +47,8 @@ int launch_gemv_int4(const GemvArgs& a, int num_sms, cudaStream_t stream);
 int launch_gemv_int8(const GemvArgs& a, int num_sms, cudaStream_t stream);
 int launch_gemv_int8_tc(const GemvArgs& a, int num_sms, cudaStream_t stream);
 int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream);
+// count products with one M, one x dtype and one y dtype, in persistent launches of up to 52 matrices each
+int launch_mm_int4_list(const MmArgs* a, int count, int num_sms, cudaStream_t stream);
 int64_t mm_int4_tc_workspace(int64_t M, int64_t N, int64_t K, int num_sms);
 int launch_mm_int4_tc_static(MmArgs a, int num_sms, cudaStream_t stream);
 int launch_tp_allreduce(const __half* a, const __half* b, __half* out, int64_t n, void* const* bufs, int rank,

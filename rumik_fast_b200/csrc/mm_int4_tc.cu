@@ -31,6 +31,8 @@
 //    stores cost several times more); 256-token chunks store directly and keep shared memory for three stages.
 //  * the producer brings a group's codes with one TMA copy and both of its X atoms with one 3-D copy.
 // All mbarrier waits are bounded; no multicast, no clusters.
+#include <new>
+
 #include "common.cuh"
 #include "tc.cuh"
 #include "kernels.h"
@@ -53,7 +55,8 @@ constexpr int kMaxBT = 256;
 constexpr uint32_t kOutBytes = 32768;        // the epilogue's staging tile for bulk-tensor stores (BT <= 128)
 constexpr int kBarEpi = 1;                   // named barrier of the twelve converter warps
 
-struct __align__(64) MmtParams {
+// One matrix of a launch: its tensor maps, scales, output and the range of work items it owns.
+struct __align__(64) MmEntry {
   CUtensorMap qmap;  // [N rows, K/2 bytes], box 64 x 128, 64-byte swizzle
   CUtensorMap xmap;  // x3d: {64 columns, M rows, K/64 atoms}, box 64 x BT x 2 (both atoms of a group in one copy);
                      // else [M rows, K fp16], box 64 x BT; 128-byte swizzle
@@ -61,13 +64,23 @@ struct __align__(64) MmtParams {
   const uint16_t* s;
   const uint16_t* m;
   void* y;
-  int64_t ldy;
   float* ws;  // [kslices][M][N] fp32 partials when kslices > 1
-  int M, N, K, G, BT, nchunks, kslices, gps, nitems, y_bf16, nst, na, nd;
+  int64_t ldy;
+  int N, K, G, nchunks, kslices, gps, item_begin;
   int ostore, tc;  // epilogue: 0 plain stores, 1 / 2 bulk-tensor stores of Y / the workspace, tc tokens a round
   int x3d;
+};
+
+// A launch: kE entries (1 for rb_mm_int4*, up to kListEntries for rb_mm_int4_list) sharing M, the token chunk
+// width BT and the shared-memory and tensor-memory layout.
+template <int kE>
+struct __align__(64) MmtParams {
+  MmEntry e[kE];
+  int count, M, BT, nitems, y_bf16, nst, na, nd;
   uint32_t stage_bytes, out_off, bar_off, idesc, dcols;  // dcols: columns per accumulator; A buffers from nd * dcols
 };
+constexpr int kListEntries = 52;
+static_assert(sizeof(MmtParams<kListEntries>) <= 32000, "kernel parameter block too large");
 
 __device__ __forceinline__ void umma_ts_f16(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                             uint32_t accumulate) {
@@ -105,24 +118,30 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Item `item`: its first weight row, first token and group range [g0, g1).
+// Item `item`: its entry, first weight row, first token and group range [g0, g1). Entries own consecutive item
+// ranges and a role's items only increase, so the entry cursor `cur` only moves forward.
 struct Item {
-  int row0, t0, ks, g0, g1;
+  int e, row0, t0, ks, g0, g1;
 };
-__device__ __forceinline__ Item item_of(const MmtParams& p, int item) {
+template <int kE>
+__device__ __forceinline__ Item item_of(const MmtParams<kE>& p, int item, int& cur) {
+  while (cur + 1 < p.count && item >= p.e[cur + 1].item_begin) ++cur;
+  const MmEntry& E = p.e[cur];
   Item it;
-  const int per_block = p.nchunks * p.kslices;
-  const int rem = item % per_block;
-  it.row0 = (item / per_block) * kRows;
-  it.t0 = (rem / p.kslices) * p.BT;
-  it.ks = rem % p.kslices;
-  it.g0 = it.ks * p.gps;
-  it.g1 = min(p.G, it.g0 + p.gps);
+  it.e = cur;
+  const int li = item - E.item_begin;
+  const int per_block = E.nchunks * E.kslices;
+  const int rem = li % per_block;
+  it.row0 = (li / per_block) * kRows;
+  it.t0 = (rem / E.kslices) * p.BT;
+  it.ks = rem % E.kslices;
+  it.g0 = it.ks * E.gps;
+  it.g1 = min(E.G, it.g0 + E.gps);
   return it;
 }
 
-template <bool kBf16X>
-__global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_constant__ MmtParams p) {
+template <bool kBf16X, int kE>
+__global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_constant__ MmtParams<kE> p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -171,19 +190,21 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
     if (lane == 0) {
       // The codes do not depend on the previous kernel: the first stages' code loads go out before
       // griddepcontrol.wait (overlapping the previous kernel's tail); X loads only after it.
-      int pre = 0;
+      int pre = 0, cur = 0;
       for (int j = 0; j < nlocal && pre < nst; ++j) {
-        const Item it = item_of(p, cta + j * C);
+        const Item it = item_of(p, cta + j * C, cur);
         for (int g = it.g0; g < it.g1 && pre < nst; ++g, ++pre) {
           mbar_arrive_expect_tx(full + pre, stage_tx);
-          mm4::tma_load_2d(stage_of(pre), &p.qmap, g * 64, it.row0, full + pre);
+          mm4::tma_load_2d(stage_of(pre), &p.e[it.e].qmap, g * 64, it.row0, full + pre);
         }
       }
       griddep_wait();  // X may come from the previous kernel
       int gq = 0;
       bool ok = true;
+      cur = 0;
       for (int j = 0; j < nlocal && ok; ++j) {
-        const Item it = item_of(p, cta + j * C);
+        const Item it = item_of(p, cta + j * C, cur);
+        const MmEntry& E = p.e[it.e];
         for (int g = it.g0; g < it.g1; ++g, ++gq) {
           const int slot = gq % nst;
           uint8_t* st = stage_of(slot);
@@ -193,13 +214,13 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
               break;
             }
             mbar_arrive_expect_tx(full + slot, stage_tx);
-            mm4::tma_load_2d(st, &p.qmap, g * 64, it.row0, full + slot);
+            mm4::tma_load_2d(st, &E.qmap, g * 64, it.row0, full + slot);
           }
-          if (p.x3d) {
-            mm4::tma_load_3d(st + kCodeBytes, &p.xmap, 0, it.t0, 2 * g, full + slot);
+          if (E.x3d) {
+            mm4::tma_load_3d(st + kCodeBytes, &E.xmap, 0, it.t0, 2 * g, full + slot);
           } else {
-            mm4::tma_load_2d(st + kCodeBytes, &p.xmap, g * 128, it.t0, full + slot);
-            mm4::tma_load_2d(st + kCodeBytes + BT * 128, &p.xmap, g * 128 + 64, it.t0, full + slot);
+            mm4::tma_load_2d(st + kCodeBytes, &E.xmap, g * 128, it.t0, full + slot);
+            mm4::tma_load_2d(st + kCodeBytes + BT * 128, &E.xmap, g * 128 + 64, it.t0, full + slot);
           }
         }
       }
@@ -211,13 +232,13 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
     // ---------------- MMA issuer d: the groups gq % nd == d, into accumulator d ----------------
     const int d = warp - 1;
     if (lane == 0 && d < nd) {
-      int gq = 0;
+      int gq = 0, cur = 0;
       bool ok = true;
       const uint32_t dcol = tmem + static_cast<uint32_t>(d) * p.dcols;
       for (int jj = 0; jj < nlocal && ok; ++jj) {
         if (jj >= 1 && !mbar_wait(dfree, (jj - 1) & 1, ERR_MM4_WAIT)) break;  // read by the last epilogue
         mm4::tc_fence_after();
-        const Item it = item_of(p, cta + jj * C);
+        const Item it = item_of(p, cta + jj * C, cur);
         bool first = true;
         for (int g = it.g0; g < it.g1; ++g, ++gq) {
           if (gq % nd != d) continue;
@@ -250,14 +271,15 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t magic = 0x54006400u, mask = 0x00F0000Fu;  // (1024 | low nibble, 64 | high nibble << 4)
     bool waited = false;  // griddepcontrol.wait before the first write of Y or of the workspace
-    int gq = 0;
+    int gq = 0, cur = 0;
     bool ok = true;
     for (int jj = 0; jj < nlocal; ++jj) {
-      const Item it = item_of(p, cta + jj * C);
+      const Item it = item_of(p, cta + jj * C, cur);
+      const MmEntry& E = p.e[it.e];
       const int row = it.row0 + rib;
-      const bool row_ok = row < p.N;
-      const uint16_t* srow = p.s + static_cast<int64_t>(row_ok ? row : 0) * p.G;
-      const uint16_t* mrow = p.m + static_cast<int64_t>(row_ok ? row : 0) * p.G;
+      const bool row_ok = row < E.N;
+      const uint16_t* srow = E.s + static_cast<int64_t>(row_ok ? row : 0) * E.G;
+      const uint16_t* mrow = E.m + static_cast<int64_t>(row_ok ? row : 0) * E.G;
       // this set's first group of the item, and its scale and min fetched one of the set's groups ahead
       int g = it.g0 + ((s - gq % kSets) + kSets) % kSets;
       uint16_t s_next = 0, m_next = 0;
@@ -350,18 +372,18 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
           for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(v[i]);
         }
       };
-      if (p.ostore) {
+      if (E.ostore) {
         // rounds of tc tokens: every converter warp writes its 32-column chunks of D into the staging tile
         // [token][128 rows] in the output's type, then one thread stores the tile with one bulk-tensor copy (rows
         // past N and tokens past M are clipped by the tensor map). Every converter warp takes every barrier,
         // whatever `ok` is.
         uint8_t* out = smem + p.out_off;
-        const int esz = p.ostore == 2 ? 4 : 2;
+        const int esz = E.ostore == 2 ? 4 : 2;
         const int ct = cw * 32 + lane;
-        for (int tc0 = 0; tc0 < BT; tc0 += p.tc) {
+        for (int tc0 = 0; tc0 < BT; tc0 += E.tc) {
           if (ct == 0) bulk_wait_read();  // the last store has read the staging tile
           named_bar_sync(kBarEpi, kConvWarps * 32);
-          for (int c0 = tc0 + 32 * s; c0 < min(BT, tc0 + p.tc); c0 += 32 * kSets) {
+          for (int c0 = tc0 + 32 * s; c0 < min(BT, tc0 + E.tc); c0 += 32 * kSets) {
             float acc[32];
             if (ok) {
               sum_d(c0, acc);
@@ -383,10 +405,10 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
           fence_proxy_async_smem();
           named_bar_sync(kBarEpi, kConvWarps * 32);
           if (ct == 0) {
-            if (p.ostore == 2)
-              tma_store_3d(&p.omap, smem_u32(out), it.row0, it.t0 + tc0, it.ks);
+            if (E.ostore == 2)
+              tma_store_3d(&E.omap, smem_u32(out), it.row0, it.t0 + tc0, it.ks);
             else
-              tma_store_2d(&p.omap, smem_u32(out), it.row0, it.t0 + tc0);
+              tma_store_2d(&E.omap, smem_u32(out), it.row0, it.t0 + tc0);
             bulk_commit();
           }
         }
@@ -398,10 +420,10 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
           for (int i = 0; i < 32; ++i) {
             const int tok = it.t0 + c0 + i;  // columns past BT belong to no token of this chunk
             if (row_ok && c0 + i < BT && tok < p.M) {
-              if (p.kslices == 1)
-                store_out(p.y, static_cast<int64_t>(tok) * p.ldy + row, acc[i], p.y_bf16);
+              if (E.kslices == 1)
+                store_out(E.y, static_cast<int64_t>(tok) * E.ldy + row, acc[i], p.y_bf16);
               else
-                p.ws[(static_cast<int64_t>(it.ks) * p.M + tok) * p.N + row] = acc[i];
+                E.ws[(static_cast<int64_t>(it.ks) * p.M + tok) * E.N + row] = acc[i];
             }
           }
         }
@@ -411,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1) mm_int4_tc_kernel(const __grid_co
       if (lane == 0) mbar_arrive(dfree);
     }
   }
-  if (warp == kFirstConv && lane == 0 && p.ostore) bulk_wait_all();  // the epilogue's stores have landed
+  if (warp == kFirstConv && lane == 0) bulk_wait_all();  // the epilogue's bulk stores have landed
   mm4::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -485,62 +507,59 @@ int64_t mm_int4_tc_workspace(int64_t M, int64_t N, int64_t K, int num_sms) {
   return pl.kslices > 1 ? static_cast<int64_t>(pl.kslices) * M * N * 4 : 0;
 }
 
-int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
-  using namespace mm4t;
-  if (a.x_dtype != RB_F16 && a.x_dtype != RB_BF16) return RB_ERR_DTYPE;
-  // the work-item count must fit the kernel's int arithmetic
-  if ((a.N + kRows - 1) / kRows * ((a.M + 15) / 16) > (int64_t(1) << 30)) return RB_ERR_SHAPE;
-  auto encode = mm4::encode_fn();
-  if (!encode) return RB_ERR_DEVICE;
-  const int M = static_cast<int>(a.M), N = static_cast<int>(a.N), K = static_cast<int>(a.K);
-  MmPlan pl = mm_plan(M, N, K, num_sms);
-  if (pl.kslices > 1 && (!a.ws || a.ws_bytes < static_cast<int64_t>(pl.kslices) * M * N * 4)) {
-    pl.kslices = 1;  // no (or too small a) workspace: no split
-    pl.gps = K / 128;
-  }
-  const int BT = pl.BT;
-  MmtParams p;
-  // accumulators: 3 of 64 columns for chunks of <= 64 tokens (an MMA's issue cost, about 66 cycles, is above the
-  // tensor time of N <= 64), 2 of 128 for 65..127 tokens, 1 for 128..256 (N >= 128 runs at the full rate from
-  // one issuer); the A buffers after them
+namespace mm4t {
+
+constexpr uint32_t kSmemMax = 227 * 1024;
+
+// The launch-wide layout for chunks of BT tokens: accumulators (3 of 64 columns for chunks of <= 64 tokens: an
+// MMA's issue cost, about 66 cycles, is above the tensor time of N <= 64; 2 of 128 for 65..127 tokens; 1 for
+// 128..256, where one issuer reaches the tensor rate), the A buffers after them, the stage ring, the staging tile
+// (chunks of <= 128 tokens; 256-token stages of 72 KB keep all of shared memory) and the barriers. Returns the
+// dynamic shared-memory bytes, or 0 if two stages do not fit.
+template <int kE>
+uint32_t set_layout(MmtParams<kE>& p, int M, int BT, int y_dtype) {
+  p.M = M;
+  p.BT = BT;
+  p.y_bf16 = y_dtype == RB_BF16;
   p.nd = BT <= 64 ? 3 : (BT < 128 ? 2 : 1);
   p.dcols = p.nd == 3 ? 64u : (BT <= 128 ? 128u : 256u);
   p.na = std::min(7, static_cast<int>((kTmemCols - p.nd * p.dcols) / kACols));
-  p.ws = a.ws;
-  p.kslices = pl.kslices;
-  p.gps = pl.gps;
-  p.s = a.s;
-  p.m = a.m;
-  p.y = a.Y;
-  p.ldy = a.ldy;
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.G = K / 128;
-  p.BT = BT;
-  p.nchunks = pl.nchunks;
-  p.nitems = ((N + kRows - 1) / kRows) * p.nchunks * p.kslices;
-  p.y_bf16 = a.y_dtype == RB_BF16;
   p.stage_bytes = (kCodeBytes + 2u * BT * 128u + 1023u) & ~1023u;
-  constexpr uint32_t kSmemMax = 227 * 1024;
   const uint32_t bar_bytes = (2 * kMaxStages + 2 * 7 + kMaxIssuers + 1) * 8 + 16;
-  // the staging tile only for chunks of <= 128 tokens: 256-token stages (72 KB) keep all of shared memory
   const uint32_t out_bytes = BT <= 128 ? kOutBytes : 0u;
   int nst = static_cast<int>((kSmemMax - 1024 - out_bytes - bar_bytes) / p.stage_bytes);
   nst = std::min(nst, kMaxStages);
-  if (nst < 2) return RB_ERR_SHAPE;
+  if (nst < 2) return 0;
   p.nst = nst;
   p.out_off = static_cast<uint32_t>(nst) * p.stage_bytes;
   p.bar_off = p.out_off + out_bytes;
   // instruction descriptor: D f32, A f16, B f16, both K-major, N = BT, M = 128
   p.idesc = (1u << 4) | (static_cast<uint32_t>(BT >> 3) << 17) | (static_cast<uint32_t>(kRows >> 4) << 24);
-  const uint32_t smem = 1024 + p.bar_off + (2 * nst + 2 * p.na + kMaxIssuers + 1) * 8 + 16;
+  return 1024 + p.bar_off + (2 * nst + 2 * p.na + kMaxIssuers + 1) * 8 + 16;
+}
+
+// One matrix's entry: tensor maps of its codes, of X and of its output; item range from `item_begin`.
+int set_entry(MmEntry& E, const MmArgs& a, int M, int BT, int nchunks, int kslices, int gps, int item_begin,
+              PFN_cuTensorMapEncodeTiled_v12000 encode) {
+  const int N = static_cast<int>(a.N), K = static_cast<int>(a.K);
+  E.s = a.s;
+  E.m = a.m;
+  E.y = a.Y;
+  E.ws = a.ws;
+  E.ldy = a.ldy;
+  E.N = N;
+  E.K = K;
+  E.G = K / 128;
+  E.nchunks = nchunks;
+  E.kslices = kslices;
+  E.gps = gps;
+  E.item_begin = item_begin;
   {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(N)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K / 2)};
     const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kRows)};
     const cuuint32_t es[2] = {1, 1};
-    if (encode(&p.qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.q), dims, strides, box, es,
+    if (encode(&E.qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.q), dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return RB_ERR_SHAPE;
@@ -555,15 +574,15 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
     const cuuint64_t strides3[2] = {static_cast<cuuint64_t>(a.ldx) * 2, 128};
     const cuuint32_t box3[3] = {64, static_cast<cuuint32_t>(BT), 2};
     const cuuint32_t es3[3] = {1, 1, 1};
-    p.x3d = encode(&p.xmap, xt, 3, const_cast<void*>(a.X), dims3, strides3, box3, es3, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    E.x3d = encode(&E.xmap, xt, 3, const_cast<void*>(a.X), dims3, strides3, box3, es3, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-    if (!p.x3d) {
+    if (!E.x3d) {
       const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
       const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.ldx) * 2};
       const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(BT)};
       const cuuint32_t es[2] = {1, 1};
-      if (encode(&p.xmap, xt, 2, const_cast<void*>(a.X), dims, strides, box, es,
+      if (encode(&E.xmap, xt, 2, const_cast<void*>(a.X), dims, strides, box, es,
                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return RB_ERR_SHAPE;
@@ -573,37 +592,42 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   // workspace [kslices, M, N] when N % 4 == 0; otherwise plain stores. Tokens past M and rows past N are clipped.
   // A round stores tc tokens: all BT in fp16/bf16 (BT <= 128 fits the 32 KB tile); in fp32 BT when BT <= 64,
   // else 64 or 32 (BT is then a multiple of 32, or the chunk is the call's only one and tokens past M are clipped).
-  p.ostore = 0;
-  p.tc = 0;
+  E.ostore = 0;
+  E.tc = 0;
   if (BT > 128) {
     // plain stores
-  } else if (p.kslices == 1) {
+  } else if (kslices == 1) {
     if ((reinterpret_cast<uintptr_t>(a.Y) & 15u) == 0 && (a.ldy * 2) % 16 == 0) {
-      p.tc = BT;
+      E.tc = BT;
       const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
       const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.ldy) * 2};
-      const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRows), static_cast<cuuint32_t>(p.tc)};
+      const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRows), static_cast<cuuint32_t>(E.tc)};
       const cuuint32_t es[2] = {1, 1};
       const CUtensorMapDataType yt =
           a.y_dtype == RB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-      if (encode(&p.omap, yt, 2, a.Y, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      if (encode(&E.omap, yt, 2, a.Y, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
-        p.ostore = 1;
+        E.ostore = 1;
     }
   } else if (N % 4 == 0 && (reinterpret_cast<uintptr_t>(a.ws) & 15u) == 0) {
-    p.tc = BT <= 64 ? BT : (BT % 64 == 0 || p.nchunks == 1 ? 64 : 32);
+    E.tc = BT <= 64 ? BT : (BT % 64 == 0 || nchunks == 1 ? 64 : 32);
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M),
-                                static_cast<cuuint64_t>(p.kslices)};
+                                static_cast<cuuint64_t>(kslices)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(N) * 4, static_cast<cuuint64_t>(M) * N * 4};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kRows), static_cast<cuuint32_t>(p.tc), 1};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kRows), static_cast<cuuint32_t>(E.tc), 1};
     const cuuint32_t es[3] = {1, 1, 1};
-    if (encode(&p.omap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.ws, dims, strides, box, es,
+    if (encode(&E.omap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.ws, dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
-      p.ostore = 2;
+      E.ostore = 2;
   }
-  void (*kern)(MmtParams) = a.x_dtype == RB_BF16 ? mm_int4_tc_kernel<true> : mm_int4_tc_kernel<false>;
+  return RB_OK;
+}
+
+template <int kE>
+int launch_kernel(const MmtParams<kE>& p, int x_dtype, uint32_t smem, int num_sms, int flags, cudaStream_t stream) {
+  void (*kern)(MmtParams<kE>) = x_dtype == RB_BF16 ? mm_int4_tc_kernel<true, kE> : mm_int4_tc_kernel<false, kE>;
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemMax);
   if (e != cudaSuccess) return RB_ERR_LAUNCH;
   cudaLaunchConfig_t cfg = {};
@@ -613,22 +637,87 @@ int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = (a.flags & RB_FLAG_PDL) ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = (flags & RB_FLAG_PDL) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, p);
-  if (e != cudaSuccess) return RB_ERR_LAUNCH;
-  if (p.kslices > 1) {
+  return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? RB_OK : RB_ERR_LAUNCH;
+}
+
+}  // namespace mm4t
+
+int launch_mm_int4_tc(const MmArgs& a, int num_sms, cudaStream_t stream) {
+  using namespace mm4t;
+  if (a.x_dtype != RB_F16 && a.x_dtype != RB_BF16) return RB_ERR_DTYPE;
+  // the work-item count must fit the kernel's int arithmetic
+  if ((a.N + kRows - 1) / kRows * ((a.M + 15) / 16) > (int64_t(1) << 30)) return RB_ERR_SHAPE;
+  auto encode = mm4::encode_fn();
+  if (!encode) return RB_ERR_DEVICE;
+  const int M = static_cast<int>(a.M), N = static_cast<int>(a.N), K = static_cast<int>(a.K);
+  MmPlan pl = mm_plan(M, N, K, num_sms);
+  if (pl.kslices > 1 && (!a.ws || a.ws_bytes < static_cast<int64_t>(pl.kslices) * M * N * 4)) {
+    pl.kslices = 1;  // no (or too small a) workspace: no split
+    pl.gps = K / 128;
+  }
+  MmtParams<1> p;
+  const uint32_t smem = set_layout(p, M, pl.BT, a.y_dtype);
+  if (!smem) return RB_ERR_SHAPE;
+  p.count = 1;
+  p.nitems = ((N + kRows - 1) / kRows) * pl.nchunks * pl.kslices;
+  int st = set_entry(p.e[0], a, M, pl.BT, pl.nchunks, pl.kslices, pl.gps, 0, encode);
+  if (st != RB_OK) return st;
+  st = launch_kernel(p, a.x_dtype, smem, num_sms, a.flags, stream);
+  if (st != RB_OK) return st;
+  if (pl.kslices > 1) {
     cudaLaunchConfig_t rc = {};
     const int64_t total = static_cast<int64_t>(M) * N;
     rc.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 4 * num_sms)));
     rc.blockDim = dim3(256);
     rc.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = (a.flags & RB_FLAG_PDL) ? 1 : 0;
     rc.attrs = attr;
     rc.numAttrs = 1;
-    e = cudaLaunchKernelEx(&rc, mm_int4_reduce_kernel, static_cast<const float*>(p.ws), a.Y, a.ldy, M, N,
-                           p.kslices, p.y_bf16);
-    if (e != cudaSuccess) return RB_ERR_LAUNCH;
+    if (cudaLaunchKernelEx(&rc, mm_int4_reduce_kernel, static_cast<const float*>(a.ws), a.Y, a.ldy, M, N,
+                           pl.kslices, p.y_bf16) != cudaSuccess)
+      return RB_ERR_LAUNCH;
+  }
+  return RB_OK;
+}
+
+// A list of prefill matrices with one token count M in persistent launches of up to kListEntries entries each:
+// items of all entries dealt round-robin to one CTA per SM, no K split (a list has items enough to fill the SMs).
+// Chunk width: M <= 128 one chunk of roundup16(M) tokens; otherwise chunks of up to 256 (a multiple of 32).
+int launch_mm_int4_list(const MmArgs* a, int count, int num_sms, cudaStream_t stream) {
+  using namespace mm4t;
+  if (count <= 0) return RB_OK;
+  auto encode = mm4::encode_fn();
+  if (!encode) return RB_ERR_DEVICE;
+  const int M = static_cast<int>(a[0].M);
+  const MmPlan pl = mm_plan_width(M, 1, 256, num_sms, M <= 128 ? 128 : kMaxBT);  // BT and chunks depend on M only
+  for (int done = 0; done < count;) {
+    const int n = std::min(count - done, kListEntries);
+    auto* p = new (std::nothrow) MmtParams<kListEntries>;  // ~27 KB: not on the stack
+    if (!p) return RB_ERR_LAUNCH;
+    const uint32_t smem = set_layout(*p, M, pl.BT, a[done].y_dtype);
+    if (!smem) {
+      delete p;
+      return RB_ERR_SHAPE;
+    }
+    int items = 0, st = RB_OK;
+    for (int i = 0; i < n && st == RB_OK; ++i) {
+      const MmArgs& x = a[done + i];
+      if ((x.N + kRows - 1) / kRows * pl.nchunks + items > (int64_t(1) << 30)) st = RB_ERR_SHAPE;
+      if (st == RB_OK)
+        st = set_entry(p->e[i], x, M, pl.BT, pl.nchunks, 1, static_cast<int>(x.K / 128), items, encode);
+      items += static_cast<int>((x.N + kRows - 1) / kRows) * pl.nchunks;
+    }
+    p->count = n;
+    p->nitems = items;
+    if (st == RB_OK) st = launch_kernel(*p, a[done].x_dtype, smem, num_sms, a[done].flags, stream);
+    delete p;
+    if (st != RB_OK) return st;
+    done += n;
   }
   return RB_OK;
 }

@@ -50,6 +50,46 @@ def mm_int4(x, q, s, m, BM=None, BN=64, num_warps=4, num_stages=3, out=None):
     return y
 
 
+class MmInt4Set:
+    """A fixed list of independent prefill products with one token count, run as persistent launches of up to 52
+    products each (rb_mm_int4_list): entries (x [M, K], q, s, m, y [M, N]) in mm_int4's layout, one x dtype and
+    one y dtype. Built once; every call launches the list (graph-capture safe). The products' work items share
+    one launch instead of one launch, fill and tail each, and no split-K workspace is needed."""
+
+    def __init__(self, entries):
+        _require(len(entries) > 0, "empty product list")
+        self.entries = list(entries)
+        x0, y0 = self.entries[0][0], self.entries[0][4]
+        self.device, self.M = x0.device, x0.shape[0]
+        self.x_dtype, self.y_dtype = x0.dtype, y0.dtype
+        _require(self.x_dtype in (torch.float16, torch.bfloat16), f"x must be fp16 or bf16, got {self.x_dtype}")
+        _require(self.y_dtype in (torch.float16, torch.bfloat16), f"y must be fp16 or bf16, got {self.y_dtype}")
+        descs = (_lib.MmDesc * len(self.entries))()
+        for i, (x, q, s, m, y) in enumerate(self.entries):
+            N, K = q.shape[0], q.shape[1] * 2
+            _require(x.is_cuda and x.device == self.device and x.dim() == 2 and x.shape == (self.M, K),
+                     f"entry {i}: x must be a CUDA [{self.M}, {K}] tensor on {self.device}")
+            _require(x.dtype == self.x_dtype and y.dtype == self.y_dtype, "one x dtype and one y dtype per list")
+            _require(x.stride(1) == 1 and x.stride(0) % 8 == 0, f"entry {i}: x rows must be contiguous, pitch % 8 == 0")
+            _require(q.dtype == torch.uint8 and q.is_contiguous(), f"entry {i}: q must be a contiguous uint8 [N, K/2]")
+            _require(K % G == 0, f"entry {i}: K={K} must be a multiple of {G}")
+            for t, nm in ((s, "s"), (m, "m")):
+                _require(t.dtype == torch.float16 and t.is_contiguous() and tuple(t.shape) == (N, K // G),
+                         f"entry {i}: {nm} must be a contiguous fp16 [{N}, {K // G}] tensor")
+            _require(y.shape == (self.M, N) and y.stride(1) == 1 and y.stride(0) % 8 == 0,
+                     f"entry {i}: y must be [{self.M}, {N}] with unit column stride and pitch % 8 == 0")
+            descs[i] = _lib.MmDesc(x.data_ptr(), x.stride(0), q.data_ptr(), s.data_ptr(), m.data_ptr(),
+                                   y.data_ptr(), y.stride(0), N, K)
+        self._descs = descs
+
+    def __call__(self):
+        L = _lib.lib()
+        with _on_device(self.device):
+            st = L.rb_mm_int4_list(self._descs, len(self.entries), self.M, _lib.dtype_code(self.x_dtype),
+                                   _lib.dtype_code(self.y_dtype), config.flags(), _lib.stream_ptr(self.device))
+        _lib.check("rb_mm_int4_list", st)
+
+
 _WS = {}
 _RETIRED = []  # outgrown workspaces stay allocated: work already queued on the stream may still use them
 

@@ -117,3 +117,24 @@ def test_gemv_list_int8_entry_validation(native_lib):
     d.w8 = _lib.W8_OFFSET
     assert L.rb_gemv_int4_fused((_lib.GemvDesc * 1)(d), None, 1, None, None, None, 0, _lib.F16, _lib.F16, 0,
                                 None) == _lib.ERR_SHAPE
+
+
+def test_mm_int4_list_validation(native_lib):
+    L = native_lib
+
+    def lst(M=8, xd=_lib.F16, **kw):
+        d = _lib.MmDesc(A, 256, A, A, A, A, 64, 64, 256)
+        for k, v in kw.items():
+            setattr(d, k, v)
+        return L.rb_mm_int4_list((_lib.MmDesc * 1)(d), 1, M, xd, _lib.F16, 0, None)
+
+    assert lst(M=0) == _lib.OK
+    assert lst(M=-1) == _lib.ERR_SHAPE
+    assert lst(K=200) == _lib.ERR_SHAPE
+    assert lst(ldx=128) == _lib.ERR_SHAPE
+    assert lst(X=None) == _lib.ERR_NULL
+    assert lst(m=None) == _lib.ERR_NULL
+    assert lst(xd=_lib.F32) == _lib.ERR_DTYPE
+    assert lst(ldy=68) == _lib.ERR_ALIGN
+    assert lst(q=A + 8) == _lib.ERR_ALIGN
+    assert L.rb_mm_int4_list(None, 1, 8, _lib.F16, _lib.F16, 0, None) == _lib.ERR_NULL

@@ -138,3 +138,60 @@ def test_wrapper_launches_only_the_library_kernels():
         torch.cuda.synchronize()
     names = {e.name for e in prof.events() if e.device_type.name == "CUDA"}
     assert names and all("mm_int4" in n for n in names), names
+
+
+@pytest.mark.parametrize("M", [34, 256, 700])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_list(M, dtype):
+    """rb_mm_int4_list / MmInt4Set: a config-1 layer's four products (QKV, o_proj, gate_up with one X, down with
+    another) plus a ragged one, in one persistent launch, against the oracle; two calls give the same bits."""
+    from rumik_fast_b200.mm_int4 import MmInt4Set
+    g = syn.generator(M * 7 + 1, "cpu")
+    xs = {k: syn.activations((M, k), g, "cpu", dtype=dtype) for k in (3072, 8192, 1024)}
+    shapes = [(n, k) for _, n, k in syn.LAYER_SHAPES] + [(1000, 1024)]
+    host, ent = [], []
+    for n, k in shapes:
+        q, s, m = syn.int4_weights(n, k, g, "cpu")
+        host.append((xs[k], q, s, m))
+        ent.append((None, q.to(DEV), s.to(DEV), m.to(DEV), torch.full((M, n), float("nan"), device=DEV, dtype=dtype)))
+    xd = {k: v.to(DEV) for k, v in xs.items()}
+    ent = [(xd[q.shape[1] * 2], q, s, m, y) for _, q, s, m, y in ent]
+    st = MmInt4Set(ent)
+    st()
+    torch.cuda.synchronize()
+    for i, ((X, q, s, m), e) in enumerate(zip(host, ent)):
+        n = q.shape[0]
+        cols = np.sort(np.random.default_rng(n + i).choice(n, min(n, 256), replace=False))
+        assert_close(e[4].cpu()[:, cols], mm_ref(X, q, s, m, cols), f"list M={M} entry {i} (N={n}, K={X.shape[1]})")
+    first = [e[4].clone() for e in ent]
+    st()
+    torch.cuda.synchronize()
+    assert all(torch.equal(a, e[4]) for a, e in zip(first, ent))
+
+
+def test_list_longer_than_one_launch_and_graph():
+    """60 products (more than the 52 of one launch): two launches; replayed from a CUDA graph."""
+    from rumik_fast_b200.mm_int4 import MmInt4Set
+    M = 48
+    g = syn.generator(99, "cpu")
+    X = syn.activations((M, 256), g, "cpu")
+    host, ent = [], []
+    xd = X.to(DEV)
+    for i in range(60):
+        n = 64 + 40 * (i % 5)
+        q, s, m = syn.int4_weights(n, 256, g, "cpu")
+        host.append((q, s, m))
+        ent.append((xd, q.to(DEV), s.to(DEV), m.to(DEV), torch.full((M, n), float("nan"), device=DEV,
+                                                                   dtype=torch.float16)))
+    st = MmInt4Set(ent)
+    st()
+    torch.cuda.synchronize()
+    for e in ent:
+        e[4].fill_(float("nan"))
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        st()
+    gr.replay()
+    torch.cuda.synchronize()
+    for i, ((q, s, m), e) in enumerate(zip(host, ent)):
+        assert_close(e[4].cpu(), mm_ref(X, q, s, m), f"list entry {i}")
