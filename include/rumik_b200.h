@@ -53,7 +53,10 @@ enum rb_flags {
   /* With RB_FLAG_PDL: also stream the weights (q, s, m) into shared memory BEFORE that wait. Only valid
    * when the weights are not written by the kernel immediately before this one on the stream, which holds
    * for inference weights loaded once. This is what lets a chain of GEMVs keep HBM busy across kernel
-   * boundaries. */
+   * boundaries. rb_attn_decode with this flag reads the position and the K/V rows of the slots before it
+   * ahead of the wait, and only q and the position's own slot after it: valid when the kernels just before it
+   * on the stream write neither the position nor any other slot of the caches (a decode step's input launch
+   * writes q and the token's slot). */
   RB_FLAG_PREFETCH_WEIGHTS = 2,
   /* GEMV lists (rb_gemv_int4_multi / _multi_ws / _fused): run on the tcgen05 kernel, or on the warp-MMA kernel,
    * whatever the list's size. Without either, lists whose codes total less than 128 MiB (a decode layer's

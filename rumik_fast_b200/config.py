@@ -8,6 +8,8 @@ Weight prefetch is off by default. When on, a GEMV starts streaming its weights 
 that wait, which hides the kernel-boundary bubble in a chain of GEMVs. It is only correct when the weights
 are not written by the kernel that runs immediately before the GEMV on the same stream - true for inference
 weights loaded once (the decode loop of an engine), not for a kernel that has just produced the weights.
+The same switch lets the decode attention read the position and the K/V rows of the slots before it ahead of
+its wait (only q and the token's own slot come from the launch before it in a decode step).
 """
 import contextlib
 

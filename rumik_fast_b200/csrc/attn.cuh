@@ -35,6 +35,9 @@ struct AttnParams {
   int64_t S;
   float scale;
   int nsplit, bf16;
+  // standalone kernel only: issue the position load and the K/V rows of slots before the position ahead of the
+  // dependency wait (griddepcontrol.wait); only q and the position's own slot wait for the preceding kernel
+  int pre;
 };
 
 __device__ __forceinline__ void unpack4(uint2 u, bool bf, float (&f)[4]) {
@@ -114,16 +117,24 @@ __device__ __forceinline__ uint2 ld_row8(const uint8_t* p) {
     return __ldg(reinterpret_cast<const uint2*>(p));
 }
 
-template <int REP, bool kLean, bool kCoherent = false>
+// kPre (standalone launch with programmatic dependent launch): the CTA reads the position and the K/V rows of its
+// first step's slots before the position BEFORE it waits for the preceding kernel (griddepcontrol.wait, called
+// here), then q and the position's own slot. Valid when the preceding kernels write only q and that slot (the
+// decode step: the layer's input launch writes q and the token's K/V slot).
+template <int REP, bool kLean, bool kCoherent = false, bool kPre = false>
 __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id, float (*sm_m)[REP],
                          float (*sm_l)[REP], float (*sm_o)[REP][kHd], int* is_last) {
+  static_assert(!(kPre && (kLean || kCoherent)), "the early loads are the standalone kernel's");
   const int warp = tid >> 5, lane = tid & 31;
   const bool bf = p.bf16 != 0;
   uint2 qraw[REP];  // issued together with the position load: one round trip for both
+  auto load_q = [&]() {
 #pragma unroll
-  for (int r = 0; r < REP; ++r)
-    qraw[r] = __ldcg(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(p.q) +
-                                                    (static_cast<int64_t>(g * REP + r) * kHd + 4 * lane) * 2));
+    for (int r = 0; r < REP; ++r)
+      qraw[r] = __ldcg(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(p.q) +
+                                                      (static_cast<int64_t>(g * REP + r) * kHd + 4 * lane) * 2));
+  };
+  if constexpr (!kPre) load_q();
   const int64_t pos = __ldcg(p.pos);
   if (pos < 0 || pos >= p.S) {  // the same decision in every CTA: none takes a ticket
     if (tid == 0 && blockIdx.x == 0) atomicOr(&g_device_error, ERR_ARG);
@@ -134,6 +145,32 @@ __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id
   const int active = static_cast<int>((n + ch - 1) / ch);  // splits with slots; the others leave at once
   if (sp >= active) return;
   const int64_t start = static_cast<int64_t>(sp) * ch, end = start + ch < n ? start + ch : n;
+
+  const uint8_t* kb = static_cast<const uint8_t*>(p.kc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
+  const uint8_t* vb = static_cast<const uint8_t*>(p.vc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
+  uint2 kr[kStep], vr[kStep];  // the non-lean path's first step
+  auto load_rows = [&](int64_t t, uint2 (&kk)[kStep], uint2 (&vv)[kStep], int64_t lim) {
+#pragma unroll
+    for (int j = 0; j < kStep; ++j) {
+      const bool in = t + j < lim;
+      kk[j] = in ? ld_row8<kCoherent>(kb + (t + j) * kHd * 2) : make_uint2(0u, 0u);
+      vv[j] = in ? ld_row8<kCoherent>(vb + (t + j) * kHd * 2) : make_uint2(0u, 0u);
+    }
+  };
+  if constexpr (kPre) {
+    const int64_t t0 = start + warp * kStep;
+    load_rows(t0, kr, vr, end < pos ? end : pos);  // slots before the position: not written by the launches before
+    griddep_wait();                                // q and the position's slot come from the previous kernel
+    load_q();
+#pragma unroll
+    for (int j = 0; j < kStep; ++j)
+      if (t0 + j == pos) {  // end == pos + 1 in the split that holds the position
+        kr[j] = ld_row8<kCoherent>(kb + pos * kHd * 2);
+        vr[j] = ld_row8<kCoherent>(vb + pos * kHd * 2);
+      }
+  } else if constexpr (!kLean) {
+    load_rows(start + warp * kStep, kr, vr, end);
+  }
 
   float qv[REP][4], m[REP], l[REP], o[REP][4];
 #pragma unroll
@@ -147,8 +184,6 @@ __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id
     m[r] = -INFINITY;
     l[r] = 0.f;
   }
-  const uint8_t* kb = static_cast<const uint8_t*>(p.kc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
-  const uint8_t* vb = static_cast<const uint8_t*>(p.vc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
   const int jl = lane >> 2;  // the slot of the step whose score this lane ends up holding
   if constexpr (kLean) {  // one step's rows at a time, keys unpacked per head: fits 128 registers
     for (int64_t t0 = start + warp * kStep; t0 < end; t0 += kWarps * kStep) {
@@ -173,19 +208,10 @@ __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id
       }
     }
   } else {
-    uint2 kr[kStep], vr[kStep];  // this step's K and V rows; the next step's are loaded before this one's math
-    auto load_rows = [&](int64_t t, uint2 (&kk)[kStep], uint2 (&vv)[kStep]) {
-  #pragma unroll
-      for (int j = 0; j < kStep; ++j) {
-        const bool in = t + j < end;
-        kk[j] = in ? ld_row8<kCoherent>(kb + (t + j) * kHd * 2) : make_uint2(0u, 0u);
-        vv[j] = in ? ld_row8<kCoherent>(vb + (t + j) * kHd * 2) : make_uint2(0u, 0u);
-      }
-    };
-    load_rows(start + warp * kStep, kr, vr);
+    // kr / vr: this step's K and V rows (loaded above); the next step's are loaded before this one's math
     for (int64_t t0 = start + warp * kStep; t0 < end; t0 += kWarps * kStep) {
       uint2 kn[kStep], vn[kStep];
-      load_rows(t0 + kWarps * kStep, kn, vn);  // past the end: nothing loaded
+      load_rows(t0 + kWarps * kStep, kn, vn, end);  // past the end: nothing loaded
       float kf[kStep][4];
   #pragma unroll
       for (int j = 0; j < kStep; ++j) unpack4(kr[j], bf, kf[j]);

@@ -14,6 +14,10 @@
 // warps and writes an fp32 partial (acc, max, sum); the last CTA of each key-value head to finish (an atomic
 // ticket) merges the nsplit partials in split order and writes the heads' outputs, so no second launch.
 // HBM-bound at long contexts: 2 x (pos + 1) x 256 bytes per key-value head.
+// With programmatic dependent launch and RB_FLAG_PREFETCH_WEIGHTS, a CTA loads the position and its first step's
+// K/V rows of the slots before the position ahead of griddepcontrol.wait, so that round trip overlaps the tail of
+// the launch before it (the layer's input launch, which writes only q and the position's slot); q and that slot
+// are read after the wait.
 #include "attn.cuh"
 #include "kernels.h"
 
@@ -27,8 +31,14 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
   __shared__ __align__(16) float sm_o[kWarps][REP][kHd];
   __shared__ int is_last;
   griddep_launch_dependents();
-  griddep_wait();  // q and the cache slot of this token come from the previous kernel
-  attn_cta<REP, false>(p, blockIdx.x / p.nsplit, blockIdx.x % p.nsplit, threadIdx.x, 0, sm_m, sm_l, sm_o, &is_last);
+  if (p.pre) {  // the early loads, then the wait (inside)
+    attn_cta<REP, false, false, true>(p, blockIdx.x / p.nsplit, blockIdx.x % p.nsplit, threadIdx.x, 0, sm_m, sm_l,
+                                      sm_o, &is_last);
+  } else {
+    griddep_wait();  // q and the cache slot of this token come from the previous kernel
+    attn_cta<REP, false>(p, blockIdx.x / p.nsplit, blockIdx.x % p.nsplit, threadIdx.x, 0, sm_m, sm_l, sm_o,
+                         &is_last);
+  }
 }
 
 
@@ -53,6 +63,7 @@ int launch_attn_decode(const void* q, const void* kc, const void* vc, const int6
   p.scale = scale;
   p.bf16 = dtype == RB_BF16;
   p.nsplit = static_cast<int>(nsplit_for(nkv, num_sms));
+  p.pre = (flags & RB_FLAG_PDL) && (flags & RB_FLAG_PREFETCH_WEIGHTS) ? 1 : 0;
   uint8_t* w = static_cast<uint8_t*>(ws);
   p.ticket = reinterpret_cast<unsigned int*>(w);
   p.heads_done = nullptr;

@@ -35,9 +35,12 @@ def oracle(q, kc, vc, pos, nq, nkv):
     return O.attention_ref(qa, np_act(kc)[0], np_act(vc)[0], pos, nq, nkv, 128, 128 ** -0.5, t)
 
 
+@pytest.mark.parametrize("early", [False, True])
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("nq,nkv", [(24, 8), (16, 4), (8, 8), (16, 2)])
-def test_attention_matches_oracle(dt, nq, nkv):
+def test_attention_matches_oracle(dt, nq, nkv, early):
+    """early: with weight prefetch on, the position and the earlier slots' K/V rows are read before the wait."""
+    from rumik_fast_b200 import config
     S = 2048
     q, kc, vc = setup(nq, nkv, S, dt, seed=nq + nkv)
     qd, kd, vd = q.to(DEV), kc.to(DEV), vc.to(DEV)
@@ -46,7 +49,8 @@ def test_attention_matches_oracle(dt, nq, nkv):
     attn = DecodeAttention(qd, kd, vd, pos, out, nq, nkv)
     for p in (0, 1, 31, 33, 200, 1500, S - 1):
         pos.fill_(p)
-        attn()
+        with config.weight_prefetch(early):
+            attn()
         torch.cuda.synchronize()
         assert_close(out, oracle(q, kc, vc, p, nq, nkv), f"attention at position {p}")
 
@@ -183,3 +187,53 @@ def test_fused_attention_in_a_cuda_graph_and_out_of_range():
     torch.cuda.synchronize()
     assert rb.device_error() & _lib.DEVERR_ARG
     assert torch.count_nonzero(layer.ws[:512]) == 0
+
+
+@pytest.mark.parametrize("p", [0, 40, 511, 2047])
+@pytest.mark.parametrize("graph", [False, True])
+def test_early_loads_wait_for_the_producer_of_q_and_the_slot(p, graph):
+    """With weight prefetch on, the attention launch reads the position and the K/V rows of the slots before it
+    ahead of its dependency wait. Here the launch just before it (a GEMV list launched with programmatic
+    dependent launch) writes q and the token's K/V slot of every key-value head, which hold NaN until then: the
+    output must match the oracle on the values that launch wrote, so no early load may have seen the stale ones."""
+    from rumik_fast_b200 import config, synthetic as syn
+    dt, nq, nkv, S, K = torch.float16, 24, 8, 2048, 1024
+    q, kc, vc = (t.to(DEV) for t in setup(nq, nkv, S, dt, seed=11 + p))
+    g = syn.generator(p, "cpu")
+    x = syn.activations((K,), g, "cpu").to(DEV)
+    wq = tuple(t.to(DEV) for t in syn.int4_weights(nq * 128, K, g, "cpu"))
+    wk = [tuple(t.to(DEV) for t in syn.int4_weights(128, K, g, "cpu")) for _ in range(2 * nkv)]
+    entries = [(x, *wq, q)] + [(x, *wk[h], kc[h, p]) for h in range(nkv)] + \
+              [(x, *wk[nkv + h], vc[h, p]) for h in range(nkv)]
+    pos = torch.tensor([p], dtype=torch.int64, device=DEV)
+    out = torch.empty(nq * 128, device=DEV, dtype=dt)
+    with config.weight_prefetch(True):
+        producer = rb.Int4GemvSet(entries, kernel="mma")
+        attn = DecodeAttention(q, kc, vc, pos, out, nq, nkv)
+
+        def run():
+            producer()
+            attn()
+
+        def stale():
+            q.fill_(float("nan"))
+            kc[:, p].fill_(float("nan"))
+            vc[:, p].fill_(float("nan"))
+            out.fill_(float("nan"))
+
+        if graph:
+            run()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                run()
+            for _ in range(3):
+                stale()
+                gr.replay()
+        else:
+            for _ in range(3):
+                stale()
+                run()
+    torch.cuda.synchronize()
+    assert not torch.isnan(q).any() and not torch.isnan(kc[:, p]).any() and not torch.isnan(vc[:, p]).any()
+    assert_close(out, oracle(q.cpu(), kc.cpu(), vc.cpu(), p, nq, nkv), f"early loads at position {p}")
