@@ -701,33 +701,34 @@ def measure_chain(w, steps, warmup, world):
 
 
 # ---------------------------------------------------------------------------------------------- arms
-def run_tp(a, rank, world, dev):
+def measure_tp(nlayers, collective, steps, warmup, rank, world, dev, clk):
     """Tensor-parallel decode step (config 4): every rank holds 1/world of each projection (column-parallel
     QKV/gate_up, row-parallel o/down, row-split int8 head); per layer one multi-GEMV launch of the rank's
-    shards and one NCCL all-reduce of the 6 KB hidden vector, then the head and an all-gather of the logits."""
+    shards and one all-reduce of the 6 KB hidden vector, then the head and an all-gather of the logits.
+    Every rank runs it (its collectives are the same on all ranks). Returns (ms per step, ms per step end to
+    end, this rank's bytes per step, the whole model's bytes per step, clock summary, logits elements)."""
     from rumik_fast_b200 import synthetic as syn
     from rumik_fast_b200.tensor_parallel import TPDecodeStep
     gen = syn.generator(1234, dev)                    # the same full model on every rank; each keeps its shards
     layers = []
-    for _ in range(a.layers):
+    for _ in range(nlayers):
         full = [syn.int4_weights(n, k, gen, dev) for _, n, k in syn.LAYER_SHAPES]
         layers.append((full[0], full[1], full[2], full[3]))
     head = syn.int8_weights(*syn.HEAD_SHAPE, gen, dev)
     x_h = syn.activations((3072,), gen, dev)
     x_attn = syn.activations((3072,), gen, dev)
     x_act = syn.activations((8192,), gen, dev)
-    step = TPDecodeStep(layers, x_attn, x_act, head, rank, world, collective=a.collective)
+    step = TPDecodeStep(layers, x_attn, x_act, head, rank, world, collective=collective)
     del layers, head
     torch.cuda.empty_cache()
     step.h[0].copy_(x_h)
     g = capture(step)
-    full_bytes = a.layers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES) + syn.int8_bytes(*syn.HEAD_SHAPE)
-    with ClockSampler(dev) as clk:
-        m0 = clk.mark()
-        ms = timed(g.replay, a.steps, a.warmup, world)
-        m1 = clk.mark()
-    clocks = clk.summary(m0, m1)
-    ms_step = ms / a.steps
+    full_bytes = nlayers * sum(syn.int4_bytes(n, k) for _, n, k in syn.LAYER_SHAPES) + syn.int8_bytes(*syn.HEAD_SHAPE)
+    m0 = clk.mark() if clk else 0
+    ms = timed(g.replay, steps, warmup, world)
+    m1 = clk.mark() if clk else 0
+    clocks = clk.summary(m0, m1) if clk else None
+    ms_step = ms / steps
     hx = x_h.cpu().pin_memory()
     hl = torch.empty(step.logits_all.numel(), dtype=torch.float16).pin_memory()
 
@@ -735,10 +736,43 @@ def run_tp(a, rank, world, dev):
         step.h[0].copy_(hx, non_blocking=True)
         g.replay()
         hl.copy_(step.logits_all, non_blocking=True)
-    e2e_steps = max(1, a.steps // 2)
-    ms_e2e = timed(e2e_step, e2e_steps, a.warmup, world) / e2e_steps
+    e2e_steps = max(1, steps // 2)
+    ms_e2e = timed(e2e_step, e2e_steps, warmup, world) / e2e_steps
+    rank_bytes = step.bytes
+    del g, e2e_step
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    step.close()
+    del step
+    free()
+    return ms_step, ms_e2e, rank_bytes, full_bytes, clocks, hl.numel()
+
+
+def tp_record(ms_tp, rank_bytes, full_bytes, world, collective, ms_one_gpu):
+    """The bench line's `tp` sub-record at N > 1: the tensor-parallel step beside this run's one-GPU step."""
+    peak, kind, _ = peaks()
+    rank_gbs = rank_bytes / (ms_tp * 1e-3) / 1e9
+    return {"ms_per_step": round(ms_tp, 5), "tok_s": round(1e3 / ms_tp, 1), "world": world, "collective": collective,
+            "model_gbs": round(full_bytes / (ms_tp * 1e-3) / 1e9, 1), "rank_gbs": round(rank_gbs, 1),
+            "rank_roofline_frac": round(rank_gbs / peak, 4), "peak_kind": kind,
+            "one_gpu_ms_per_step": round(ms_one_gpu, 5), "speedup_vs_one_gpu": round(ms_one_gpu / ms_tp, 3),
+            "limit": "per layer: one multi-GEMV launch of the rank's shards plus a 6 KB all-reduce of the hidden "
+                     "vector, each latency-bound (a few microseconds of launch, ramp and tail per launch)",
+            "workload": "config-4 tensor-parallel step: the config-1 36-layer projection set + int8 head sharded "
+                        "(column-parallel QKV/gate_up, row-parallel o/down, row-split head), one all-reduce per "
+                        "layer, batch 1; one_gpu = the same bytes on one GPU as this run's single projection-set "
+                        "launch"}
+
+
+def run_tp(a, rank, world, dev):
+    """Tensor-parallel decode step alone (--parallel tp): the step as the line's value."""
+    with ClockSampler(dev) as clk:
+        ms_step, ms_e2e, rank_bytes, full_bytes, clocks, nlog = measure_tp(
+            a.layers, a.collective, a.steps, a.warmup, rank, world, dev, clk)
     peak, peak_kind, _ = peaks()
-    rank_gbs = step.bytes / (ms_step * 1e-3) / 1e9
+    rank_gbs = rank_bytes / (ms_step * 1e-3) / 1e9
     if rank == 0:
         gbs = full_bytes / (ms_step * 1e-3) / 1e9
         line = {
@@ -755,7 +789,7 @@ def run_tp(a, rank, world, dev):
                        "l2": "no flush: 1.98 GB of weights per step over all ranks > 126 MB L2 per GPU"},
             "tok_s": round(1e3 / ms_step, 1),
             "e2e": {"value": round(full_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": UNIT,
-                    "h2d_bytes_per_step": 3072 * 2, "d2h_bytes_per_step": hl.numel() * 2,
+                    "h2d_bytes_per_step": 3072 * 2, "d2h_bytes_per_step": nlog * 2,
                     "ms_per_step": round(ms_e2e, 5)},
             "roofline": {"bound": "hbm", "achieved": round(rank_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(rank_gbs / peak, 4), "peak_kind": peak_kind,
@@ -765,12 +799,6 @@ def run_tp(a, rank, world, dev):
             "gpu_launches": a.steps * (a.layers + 1), "mode": "tp",
         }
         print(json.dumps(line), flush=True)
-    del g
-    torch.cuda.synchronize()
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-    step.close()
     return 0
 
 
@@ -851,6 +879,9 @@ def run_ours(a):
             extras["batched"] = measure_batched(dev, 99 + rank, BATCHES, LAYERS, a.steps, a.warmup, world, clk)
             extras["prefill"] = measure_prefill(dev, 4321 + rank, PREFILL_TOKENS, LAYERS, a.steps, a.warmup, world,
                                                 clk)
+            if world > 1:  # the same projection set + head tensor-parallel over the ranks
+                ms_tp, _, rb_, fb_, _, _ = measure_tp(LAYERS, a.collective, a.steps, a.warmup, rank, world, dev, None)
+                extras["tp"] = tp_record(ms_tp, rb_, fb_, world, a.collective, ms_step)
     clocks = clk.summary(m0, m1)
 
     if rank == 0:

@@ -62,7 +62,10 @@ enum rb_flags {
    * whatever the list's size. Without either, lists whose codes total less than 128 MiB (a decode layer's
    * projections, latency-bound) run on the warp-MMA kernel and longer lists on the tcgen05 kernel. */
   RB_FLAG_KERNEL_TC = 4,
-  RB_FLAG_KERNEL_MMA = 8
+  RB_FLAG_KERNEL_MMA = 8,
+  /* rb_attn_decode: merge the splits through global partials and a per-head ticket (the form that needs no
+   * thread-block clusters) even where the device can run the cluster form. */
+  RB_FLAG_ATTN_TICKET = 16
 };
 
 /*
@@ -330,6 +333,9 @@ int rb_add_layernorm(const rb_add_ln* ln, int dtype, int flags, void* stream);
  *   in `dtype` (RB_F16 / RB_BF16); *pos on the device (int64), 0 <= *pos < cache_len, else nothing is written
  *   and the RB_DEVERR_ARG bit of the device error word is set. head_dim == 128, rep = n_q_heads / n_kv_heads
  *   in 1..8, n_kv_heads <= 64. Scores, softmax and the weighted sum are fp32.
+ *   Where the device can schedule them, one thread-block cluster of 16 CTAs per key-value head splits the slots
+ *   and merges its splits through distributed shared memory (the workspace is then untouched); otherwise, or
+ *   with RB_FLAG_ATTN_TICKET, about SMs / n_kv_heads CTAs per head merge through fp32 partials in the workspace.
  *   ws: rb_attn_decode_workspace(...) bytes of device memory, 16-byte aligned; its first 256 bytes (per-head
  *   completion counters) must be zero before the first call and are zero again after each call. Calls that
  *   share a workspace must not overlap in time (one stream).

@@ -15,7 +15,7 @@ OK, ERR_NULL, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_LAUNCH, ERR_DEVICE, ERR_TIMEO
 # dtype codes (enum rb_dtype)
 F16, BF16, F32 = 0, 1, 2
 # launch flags (enum rb_flags)
-FLAG_PDL, FLAG_PREFETCH_WEIGHTS, FLAG_KERNEL_TC, FLAG_KERNEL_MMA = 1, 2, 4, 8
+FLAG_PDL, FLAG_PREFETCH_WEIGHTS, FLAG_KERNEL_TC, FLAG_KERNEL_MMA, FLAG_ATTN_TICKET = 1, 2, 4, 8, 16
 KERNEL_FLAGS = {None: 0, "tc": FLAG_KERNEL_TC, "mma": FLAG_KERNEL_MMA}
 
 _DTYPE_CODE = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}

@@ -16,9 +16,13 @@ from .cuda_gemv import _on_device, _require
 class DecodeAttention:
     """q [n_q_heads * 128], k_cache / v_cache [n_kv_heads, cache_len, 128], out [n_q_heads * 128] (one dtype,
     fp16 or bf16), pos an int64 [1] device tensor. Owns its workspace (per-head completion counters + fp32
-    partials); calls sharing one object must be issued on one stream."""
+    partials); calls sharing one object must be issued on one stream. merge: "auto" (a thread-block cluster
+    per key-value head merging through distributed shared memory where the device can schedule it) or
+    "ticket" (fp32 partials in the workspace and a per-head ticket)."""
 
-    def __init__(self, q, k_cache, v_cache, pos, out, n_q_heads, n_kv_heads, scale=None):
+    def __init__(self, q, k_cache, v_cache, pos, out, n_q_heads, n_kv_heads, scale=None, merge="auto"):
+        _require(merge in ("auto", "ticket"), f"merge must be 'auto' or 'ticket', got {merge!r}")
+        self.extra_flags = _lib.FLAG_ATTN_TICKET if merge == "ticket" else 0
         dt = q.dtype
         _require(dt in (torch.float16, torch.bfloat16), "q must be fp16 or bf16")
         nkv, S, hd = k_cache.shape
@@ -41,7 +45,8 @@ class DecodeAttention:
         with _on_device(self.device):
             st = _lib.lib().rb_attn_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), out.data_ptr(),
                                            self.nq, self.nkv, self.hd, self.S, self.scale, self.ws.data_ptr(),
-                                           self.ws.numel(), _lib.dtype_code(self.dtype), config.flags(),
+                                           self.ws.numel(), _lib.dtype_code(self.dtype),
+                                           config.flags() | self.extra_flags,
                                            _lib.stream_ptr(self.device))
         _lib.check("rb_attn_decode", st)
 

@@ -121,10 +121,15 @@ __device__ __forceinline__ uint2 ld_row8(const uint8_t* p) {
 // first step's slots before the position BEFORE it waits for the preceding kernel (griddepcontrol.wait, called
 // here), then q and the position's own slot. Valid when the preceding kernels write only q and that slot (the
 // decode step: the layer's input launch writes q and the token's K/V slot).
-template <int REP, bool kLean, bool kCoherent = false, bool kPre = false>
-__device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id, float (*sm_m)[REP],
-                         float (*sm_l)[REP], float (*sm_o)[REP][kHd], int* is_last) {
-  static_assert(!(kPre && (kLean || kCoherent)), "the early loads are the standalone kernel's");
+// kCluster (standalone launch in clusters of nsplit CTAs, one cluster per key-value head): the CTA leaves its merged
+// partial in shared memory - the accumulator in sm_o[0], the maximum and the sum in cml[r] and cml[REP + r] - for
+// the cluster's merge through distributed shared memory, instead of the global partials and the ticket.
+// Returns the number of splits with slots (the same in every CTA of the launch), or -1 for a position outside
+// the cache (nothing written).
+template <int REP, bool kLean, bool kCoherent = false, bool kPre = false, bool kCluster = false>
+__device__ int attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id, float (*sm_m)[REP],
+                        float (*sm_l)[REP], float (*sm_o)[REP][kHd], int* is_last, float* cml = nullptr) {
+  static_assert(!((kPre || kCluster) && (kLean || kCoherent)), "the early loads are the standalone kernel's");
   const int warp = tid >> 5, lane = tid & 31;
   const bool bf = p.bf16 != 0;
   uint2 qraw[REP];  // issued together with the position load: one round trip for both
@@ -138,12 +143,12 @@ __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id
   const int64_t pos = __ldcg(p.pos);
   if (pos < 0 || pos >= p.S) {  // the same decision in every CTA: none takes a ticket
     if (tid == 0 && blockIdx.x == 0) atomicOr(&g_device_error, ERR_ARG);
-    return;
+    return -1;
   }
   const int64_t n = pos + 1;
   const int64_t ch = ((n + p.nsplit - 1) / p.nsplit + kWarps * kStep - 1) / (kWarps * kStep) * (kWarps * kStep);
   const int active = static_cast<int>((n + ch - 1) / ch);  // splits with slots; the others leave at once
-  if (sp >= active) return;
+  if (sp >= active) return active;
   const int64_t start = static_cast<int64_t>(sp) * ch, end = start + ch < n ? start + ch : n;
 
   const uint8_t* kb = static_cast<const uint8_t*>(p.kc) + static_cast<int64_t>(g) * p.S * kHd * 2 + lane * 8;
@@ -262,6 +267,14 @@ __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id
       store_out(p.out, static_cast<int64_t>(g * REP + r) * kHd + tid, O / L, bf);
       continue;
     }
+    if constexpr (kCluster) {  // each thread rewrites only its own column of sm_o[0]
+      sm_o[0][r][tid] = O;
+      if (tid == 0) {
+        cml[r] = M;
+        cml[REP + r] = L;
+      }
+      continue;
+    }
     const int64_t hs = static_cast<int64_t>(g * REP + r) * p.nsplit + sp;
     p.po[hs * kHd + tid] = O;
     if (tid == 0) {
@@ -274,8 +287,9 @@ __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id
       named_bar_sync(bar_id, kThreads);
       if (tid == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.heads_done) : "memory");
     }
-    return;
+    return active;
   }
+  if constexpr (kCluster) return active;
   // The counter add releases this CTA's partial (the barrier orders every thread's stores before thread 0's
   // release) and, for the last CTA, acquires the others' (its loads follow the barrier after the acquire).
   named_bar_sync(bar_id, kThreads);
@@ -285,7 +299,7 @@ __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id
     *is_last = prev == static_cast<unsigned int>(active - 1);
   }
   named_bar_sync(bar_id, kThreads);
-  if (!*is_last) return;
+  if (!*is_last) return active;
   // The last CTA of key-value head g merges the active partials of its query heads. Warp w takes splits
   // w, w + 4, ... and every lane 4 dimensions (16-byte loads), merging with an online rescale (running max) so
   // that all loads of a warp - maxima, sums and accumulators of its splits for every head - are independent
@@ -347,6 +361,7 @@ __device__ void attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id
     named_bar_sync(bar_id, kThreads);
     if (tid == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.heads_done) : "memory");
   }
+  return active;
 }
 
 // Splits per key-value head: about one CTA per SM over all heads.

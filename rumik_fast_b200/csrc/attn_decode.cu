@@ -18,12 +18,75 @@
 // K/V rows of the slots before the position ahead of griddepcontrol.wait, so that round trip overlaps the tail of
 // the launch before it (the layer's input launch, which writes only q and the position's slot); q and that slot
 // are read after the wait.
+//
+// Cluster form (the default where the device can co-schedule it): one cluster of kClusterSplits CTAs per
+// key-value head. Each CTA leaves its merged partial in its own shared memory; after a cluster barrier (release /
+// acquire), CTA r of the cluster merges query head r of the group from every split's shared memory (distributed
+// shared memory loads, all in flight together) and writes it; a second barrier keeps every CTA's shared memory
+// alive until those loads are done. No global partials, no ticket, no workspace traffic.
+#include <atomic>
+
+#include <cooperative_groups.h>
+
 #include "attn.cuh"
 #include "kernels.h"
 
 namespace rb {
 
 namespace attn {
+
+constexpr int kClusterSplits = 16;  // splits per key-value head = CTAs per cluster (a non-portable cluster size)
+
+template <int REP>
+__global__ void __launch_bounds__(kThreads) attn_cluster_kernel(const __grid_constant__ AttnParams p) {
+  static_assert(REP <= kClusterSplits, "one merging CTA per query head of the group");
+  namespace cg = cooperative_groups;
+  __shared__ float sm_m[kWarps][REP], sm_l[kWarps][REP];
+  __shared__ __align__(16) float sm_o[kWarps][REP][kHd];
+  __shared__ float cml[2 * REP];
+  __shared__ int is_last;
+  griddep_launch_dependents();
+  cg::cluster_group cl = cg::this_cluster();
+  const int g = blockIdx.x / kClusterSplits, sp = static_cast<int>(cl.block_rank()), tid = threadIdx.x;
+  int active;
+  if (p.pre) {
+    active = attn_cta<REP, false, false, true, true>(p, g, sp, tid, 0, sm_m, sm_l, sm_o, &is_last, cml);
+  } else {
+    griddep_wait();
+    active = attn_cta<REP, false, false, false, true>(p, g, sp, tid, 0, sm_m, sm_l, sm_o, &is_last, cml);
+  }
+  // Every thread of every CTA takes both barriers whatever its path, so that no CTA can wait at one for a CTA
+  // that took another path. active <= 1: the position is outside the cache, or one split wrote the outputs.
+  cl.sync();  // every split's partial is in its shared memory
+  if (active > 1 && sp < REP) {
+    const int r = sp;
+    float ms[kClusterSplits], ls[kClusterSplits], os[kClusterSplits];
+#pragma unroll
+    for (int s = 0; s < kClusterSplits; ++s) {
+      if (s < active) {
+        const float* rc = cl.map_shared_rank(cml, s);
+        ms[s] = rc[r];
+        ls[s] = rc[REP + r];
+        os[s] = cl.map_shared_rank(&sm_o[0][0][0], s)[r * kHd + tid];
+      }
+    }
+    float M = ms[0];
+#pragma unroll
+    for (int s = 1; s < kClusterSplits; ++s)
+      if (s < active) M = fmaxf(M, ms[s]);
+    float O = 0.f, L = 0.f;
+#pragma unroll
+    for (int s = 0; s < kClusterSplits; ++s) {
+      if (s < active) {  // in split order
+        const float e = __expf(ms[s] - M);
+        O = fmaf(e, os[s], O);
+        L = fmaf(e, ls[s], L);
+      }
+    }
+    store_out(p.out, static_cast<int64_t>(g * REP + r) * kHd + tid, O / L, p.bf16 != 0);
+  }
+  cl.sync();  // no CTA leaves while another still reads its shared memory
+}
 
 template <int REP>
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
@@ -50,6 +113,63 @@ int64_t attn_decode_workspace(int nq, int nkv, int hd) {
   return kTicketBytes + static_cast<int64_t>(nq) * kMaxSplit * (kHd + 2) * 4;
 }
 
+namespace attn {
+
+// Whether clusters of kClusterSplits CTAs of attn_cluster_kernel<REP> can be scheduled on the current device
+// (checked once per device and group size; the non-portable cluster size is enabled on the way).
+template <int REP>
+bool cluster_ok(int dev) {
+  static std::atomic<int> state[64] = {};  // 0 unknown, 1 yes, 2 no
+  if (dev < 0 || dev >= 64) return false;
+  int st = state[dev].load(std::memory_order_acquire);
+  if (st == 0) {
+    st = 2;
+    if (cudaFuncSetAttribute(attn_cluster_kernel<REP>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+        cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(kClusterSplits);
+      cfg.blockDim = dim3(kThreads);
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = kClusterSplits;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, attn_cluster_kernel<REP>, &cfg) == cudaSuccess && n >= 1) st = 1;
+    }
+    (void)cudaGetLastError();
+    state[dev].store(st, std::memory_order_release);
+  }
+  return st == 1;
+}
+
+template <int REP>
+cudaError_t launch_rep(AttnParams p, int nkv, int num_sms, int flags, cudaStream_t stream) {
+  int dev = 0;
+  const bool cluster = !(flags & RB_FLAG_ATTN_TICKET) && cudaGetDevice(&dev) == cudaSuccess && cluster_ok<REP>(dev);
+  p.nsplit = cluster ? kClusterSplits : static_cast<int>(nsplit_for(nkv, num_sms));
+  p.pm = p.po + static_cast<int64_t>(nkv) * REP * p.nsplit * kHd;
+  p.pl = p.pm + static_cast<int64_t>(nkv) * REP * p.nsplit;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nkv * p.nsplit);
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = (flags & RB_FLAG_PDL) ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = kClusterSplits;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cluster ? 2 : 1;
+  return cluster ? cudaLaunchKernelEx(&cfg, attn_cluster_kernel<REP>, p) : cudaLaunchKernelEx(&cfg, attn_decode_kernel<REP>, p);
+}
+
+}  // namespace attn
+
 int launch_attn_decode(const void* q, const void* kc, const void* vc, const int64_t* pos, void* out, int nq, int nkv,
                        int64_t S, float scale, void* ws, int dtype, int flags, int num_sms, cudaStream_t stream) {
   using namespace attn;
@@ -62,33 +182,21 @@ int launch_attn_decode(const void* q, const void* kc, const void* vc, const int6
   p.S = S;
   p.scale = scale;
   p.bf16 = dtype == RB_BF16;
-  p.nsplit = static_cast<int>(nsplit_for(nkv, num_sms));
   p.pre = (flags & RB_FLAG_PDL) && (flags & RB_FLAG_PREFETCH_WEIGHTS) ? 1 : 0;
   uint8_t* w = static_cast<uint8_t*>(ws);
   p.ticket = reinterpret_cast<unsigned int*>(w);
   p.heads_done = nullptr;
   p.po = reinterpret_cast<float*>(w + kTicketBytes);
-  p.pm = p.po + static_cast<int64_t>(nq) * p.nsplit * kHd;
-  p.pl = p.pm + static_cast<int64_t>(nq) * p.nsplit;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nkv * p.nsplit);
-  cfg.blockDim = dim3(kThreads);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = (flags & RB_FLAG_PDL) ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   cudaError_t e;
   switch (nq / nkv) {
-    case 1: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<1>, p); break;
-    case 2: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<2>, p); break;
-    case 3: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<3>, p); break;
-    case 4: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<4>, p); break;
-    case 5: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<5>, p); break;
-    case 6: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<6>, p); break;
-    case 7: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<7>, p); break;
-    case 8: e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<8>, p); break;
+    case 1: e = launch_rep<1>(p, nkv, num_sms, flags, stream); break;
+    case 2: e = launch_rep<2>(p, nkv, num_sms, flags, stream); break;
+    case 3: e = launch_rep<3>(p, nkv, num_sms, flags, stream); break;
+    case 4: e = launch_rep<4>(p, nkv, num_sms, flags, stream); break;
+    case 5: e = launch_rep<5>(p, nkv, num_sms, flags, stream); break;
+    case 6: e = launch_rep<6>(p, nkv, num_sms, flags, stream); break;
+    case 7: e = launch_rep<7>(p, nkv, num_sms, flags, stream); break;
+    case 8: e = launch_rep<8>(p, nkv, num_sms, flags, stream); break;
     default: return RB_ERR_SHAPE;
   }
   return e == cudaSuccess ? RB_OK : RB_ERR_LAUNCH;

@@ -35,19 +35,21 @@ def oracle(q, kc, vc, pos, nq, nkv):
     return O.attention_ref(qa, np_act(kc)[0], np_act(vc)[0], pos, nq, nkv, 128, 128 ** -0.5, t)
 
 
+@pytest.mark.parametrize("merge", ["auto", "ticket"])
 @pytest.mark.parametrize("early", [False, True])
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("nq,nkv", [(24, 8), (16, 4), (8, 8), (16, 2)])
-def test_attention_matches_oracle(dt, nq, nkv, early):
-    """early: with weight prefetch on, the position and the earlier slots' K/V rows are read before the wait."""
+@pytest.mark.parametrize("nq,nkv", [(24, 8), (16, 4), (8, 8), (16, 2), (64, 8)])
+def test_attention_matches_oracle(dt, nq, nkv, early, merge):
+    """early: with weight prefetch on, the position and the earlier slots' K/V rows are read before the wait.
+    merge: the cluster form (distributed shared memory) or the ticket form (global partials)."""
     from rumik_fast_b200 import config
     S = 2048
     q, kc, vc = setup(nq, nkv, S, dt, seed=nq + nkv)
     qd, kd, vd = q.to(DEV), kc.to(DEV), vc.to(DEV)
     pos = torch.zeros(1, dtype=torch.int64, device=DEV)
     out = torch.full((nq * 128,), float("nan"), device=DEV, dtype=dt)
-    attn = DecodeAttention(qd, kd, vd, pos, out, nq, nkv)
-    for p in (0, 1, 31, 33, 200, 1500, S - 1):
+    attn = DecodeAttention(qd, kd, vd, pos, out, nq, nkv, merge=merge)
+    for p in (0, 1, 31, 33, 200, 511, 512, 1500, S - 1):
         pos.fill_(p)
         with config.weight_prefetch(early):
             attn()
@@ -55,12 +57,13 @@ def test_attention_matches_oracle(dt, nq, nkv, early):
         assert_close(out, oracle(q, kc, vc, p, nq, nkv), f"attention at position {p}")
 
 
-def test_attention_is_deterministic_and_reusable():
+@pytest.mark.parametrize("merge", ["auto", "ticket"])
+def test_attention_is_deterministic_and_reusable(merge):
     dt, nq, nkv, S = torch.float16, 24, 8, 512
     q, kc, vc = (t.to(DEV) for t in setup(nq, nkv, S, dt, seed=3))
     pos = torch.tensor([300], dtype=torch.int64, device=DEV)
     out = torch.empty(nq * 128, device=DEV, dtype=dt)
-    attn = DecodeAttention(q, kc, vc, pos, out, nq, nkv)
+    attn = DecodeAttention(q, kc, vc, pos, out, nq, nkv, merge=merge)
     attn()
     first = out.clone()
     for _ in range(5):          # the completion counters reset themselves after every call
@@ -189,9 +192,10 @@ def test_fused_attention_in_a_cuda_graph_and_out_of_range():
     assert torch.count_nonzero(layer.ws[:512]) == 0
 
 
+@pytest.mark.parametrize("merge", ["auto", "ticket"])
 @pytest.mark.parametrize("p", [0, 40, 511, 2047])
 @pytest.mark.parametrize("graph", [False, True])
-def test_early_loads_wait_for_the_producer_of_q_and_the_slot(p, graph):
+def test_early_loads_wait_for_the_producer_of_q_and_the_slot(p, graph, merge):
     """With weight prefetch on, the attention launch reads the position and the K/V rows of the slots before it
     ahead of its dependency wait. Here the launch just before it (a GEMV list launched with programmatic
     dependent launch) writes q and the token's K/V slot of every key-value head, which hold NaN until then: the
@@ -209,7 +213,7 @@ def test_early_loads_wait_for_the_producer_of_q_and_the_slot(p, graph):
     out = torch.empty(nq * 128, device=DEV, dtype=dt)
     with config.weight_prefetch(True):
         producer = rb.Int4GemvSet(entries, kernel="mma")
-        attn = DecodeAttention(q, kc, vc, pos, out, nq, nkv)
+        attn = DecodeAttention(q, kc, vc, pos, out, nq, nkv, merge=merge)
 
         def run():
             producer()
