@@ -35,7 +35,10 @@ namespace rb {
 
 namespace attn {
 
-constexpr int kClusterSplits = 16;  // splits per key-value head = CTAs per cluster (a non-portable cluster size)
+#ifndef RB_ATTN_CLUSTER
+#define RB_ATTN_CLUSTER 16
+#endif
+constexpr int kClusterSplits = RB_ATTN_CLUSTER;  // splits per key-value head = CTAs per cluster (16: non-portable)
 
 template <int REP>
 __global__ void __launch_bounds__(kThreads) attn_cluster_kernel(const __grid_constant__ AttnParams p) {
