@@ -59,13 +59,15 @@ __device__ __forceinline__ float key_value(long long key) {
   return __int_as_float(k32 ^ ((k32 >> 31) & 0x7FFFFFFF));
 }
 
+// The largest key of the warp, in every lane: the largest high word (signed, the value's order), then among the
+// lanes holding it the largest low word (unsigned, the row) - the 64-bit signed maximum, in two warp-wide integer
+// reductions instead of five rounds of 64-bit shuffles and compares.
 __device__ __forceinline__ long long warp_max_key(long long v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const long long t = __shfl_xor_sync(0xffffffffu, v, o);
-    v = t > v ? t : v;
-  }
-  return v;
+  const int hi = static_cast<int>(v >> 32);
+  const unsigned lo = static_cast<unsigned>(v & 0xFFFFFFFFll);
+  const int mh = __reduce_max_sync(0xffffffffu, hi);
+  const unsigned ml = __reduce_max_sync(0xffffffffu, hi == mh ? lo : 0u);
+  return static_cast<long long>((static_cast<unsigned long long>(static_cast<unsigned>(mh)) << 32) | ml);
 }
 
 // ---- first launch: the stop predictor's hidden layer, z1[row] = gelu(W1[row] . LayerNorm(h) + b1[row]) (exact
