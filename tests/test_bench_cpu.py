@@ -31,3 +31,17 @@ def test_cli_lists_the_workloads_and_scale_formats():
     assert r.returncode == 0
     for opt in ("--workload", "--scales", "--impl", "--gpus", "--steps", "--warmup"):
         assert opt in r.stdout
+
+
+def test_tp_record_reports_the_speedup_over_one_gpu():
+    """The default multi-GPU line's `tp` record: the tensor-parallel step beside the same run's one-GPU step."""
+    sys.path.insert(0, ROOT)
+    import bench
+    full = 36 * 53567488 + 50406404
+    rec = bench.tp_record(ms_tp=0.9, rank_bytes=full // 2, full_bytes=full, world=2, collective="nccl",
+                          ms_one_gpu=0.345)
+    assert rec["world"] == 2 and rec["collective"] == "nccl"
+    assert abs(rec["speedup_vs_one_gpu"] - round(0.345 / 0.9, 3)) < 1e-9
+    assert abs(rec["tok_s"] - round(1e3 / 0.9, 1)) < 1e-9
+    assert abs(rec["model_gbs"] - round(full / 0.9e-3 / 1e9, 1)) < 1e-9
+    assert 0 < rec["rank_roofline_frac"] < 1 and rec["limit"] and rec["workload"]
