@@ -163,9 +163,16 @@ __device__ int attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id,
     }
   };
   if constexpr (kPre) {
-    const int64_t t0 = start + warp * kStep;
-    load_rows(t0, kr, vr, end < pos ? end : pos);  // slots before the position: not written by the launches before
-    griddep_wait();                                // q and the position's slot come from the previous kernel
+    const int64_t t0 = start + warp * kStep, lim = end < pos ? end : pos;
+    load_rows(t0, kr, vr, lim);  // slots before the position: not written by the launches before
+    {  // the warp's later steps of such slots into L2: one 128-byte line per lane and step (slot lane / 4, K or V,
+       // half of the 256-byte row); a plain prefetch, nothing to wait for
+      const int j = lane >> 2;
+      const uint8_t* line = ((lane >> 1) & 1 ? vb : kb) - lane * 8 + (lane & 1) * 128;
+      for (int64_t t = t0 + kWarps * kStep; t < lim; t += kWarps * kStep)
+        if (t + j < lim) asm volatile("prefetch.global.L2 [%0];" ::"l"(line + (t + j) * kHd * 2));
+    }
+    griddep_wait();  // q and the position's slot come from the previous kernel
     load_q();
 #pragma unroll
     for (int j = 0; j < kStep; ++j)
