@@ -20,10 +20,9 @@
 // are read after the wait.
 //
 // Cluster form (the default where the device can co-schedule it): one cluster of kClusterSplits CTAs per
-// key-value head. Each CTA leaves its merged partial in its own shared memory; after a cluster barrier (release /
-// acquire), CTA r of the cluster merges query head r of the group from every split's shared memory (distributed
-// shared memory loads, all in flight together) and writes it; a second barrier keeps every CTA's shared memory
-// alive until those loads are done. No global partials, no ticket, no workspace traffic.
+// key-value head. Each CTA stores its merged partial of query head r straight into the shared memory of CTA r of
+// the cluster (distributed shared-memory stores); after one cluster barrier (release / acquire) CTA r merges head r
+// from its own shared memory and writes it. No global partials, no ticket, no workspace traffic.
 #include <atomic>
 
 #include <cooperative_groups.h>
@@ -48,8 +47,15 @@ __global__ void __launch_bounds__(kThreads) attn_cluster_kernel(const __grid_con
   __shared__ __align__(16) float sm_o[kWarps][REP][kHd];
   __shared__ float cml[2 * REP];
   __shared__ int is_last;
+  // the merging CTA's inbox (CTA r merges query head r of the group): every split's accumulator, maximum and sum
+  __shared__ __align__(16) float in_o[kClusterSplits][kHd];
+  __shared__ float in_m[kClusterSplits], in_l[kClusterSplits];
   griddep_launch_dependents();
   cg::cluster_group cl = cg::this_cluster();
+  // Cluster barrier phase 1, split: arrive now, wait just before the first store into another CTA's shared memory,
+  // so that no store reaches a CTA of the cluster that has not started. Every thread of every CTA takes both
+  // phases whatever its path, so that no CTA can wait for one that took another path.
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   const int g = blockIdx.x / kClusterSplits, sp = static_cast<int>(cl.block_rank()), tid = threadIdx.x;
   int active;
   if (p.pre) {
@@ -58,37 +64,37 @@ __global__ void __launch_bounds__(kThreads) attn_cluster_kernel(const __grid_con
     griddep_wait();
     active = attn_cta<REP, false, false, false, true>(p, g, sp, tid, 0, sm_m, sm_l, sm_o, &is_last, cml);
   }
-  // Every thread of every CTA takes both barriers whatever its path, so that no CTA can wait at one for a CTA
-  // that took another path. active <= 1: the position is outside the cache, or one split wrote the outputs.
-  cl.sync();  // every split's partial is in its shared memory
-  if (active > 1 && sp < REP) {
-    const int r = sp;
-    float ms[kClusterSplits], ls[kClusterSplits], os[kClusterSplits];
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  // active <= 1: the position is outside the cache, or one split wrote the outputs. Otherwise every split with
+  // slots pushes its partial of head r into CTA r's inbox (each thread its own column, written by itself above).
+  if (active > 1 && sp < active) {
 #pragma unroll
-    for (int s = 0; s < kClusterSplits; ++s) {
-      if (s < active) {
-        const float* rc = cl.map_shared_rank(cml, s);
-        ms[s] = rc[r];
-        ls[s] = rc[REP + r];
-        os[s] = cl.map_shared_rank(&sm_o[0][0][0], s)[r * kHd + tid];
+    for (int r = 0; r < REP; ++r) {
+      cl.map_shared_rank(&in_o[0][0], r)[sp * kHd + tid] = sm_o[0][r][tid];
+      if (tid == 0) {
+        cl.map_shared_rank(in_m, r)[sp] = cml[r];
+        cl.map_shared_rank(in_l, r)[sp] = cml[REP + r];
       }
     }
-    float M = ms[0];
+  }
+  cl.sync();  // phase 2 (release / acquire): the pushed partials are visible; no shared-memory access crosses CTAs
+              // after it, so every CTA may leave
+  if (active > 1 && sp < REP) {
+    float M = in_m[0];
 #pragma unroll
     for (int s = 1; s < kClusterSplits; ++s)
-      if (s < active) M = fmaxf(M, ms[s]);
+      if (s < active) M = fmaxf(M, in_m[s]);
     float O = 0.f, L = 0.f;
 #pragma unroll
     for (int s = 0; s < kClusterSplits; ++s) {
       if (s < active) {  // in split order
-        const float e = __expf(ms[s] - M);
-        O = fmaf(e, os[s], O);
-        L = fmaf(e, ls[s], L);
+        const float e = __expf(in_m[s] - M);
+        O = fmaf(e, in_o[s][tid], O);
+        L = fmaf(e, in_l[s], L);
       }
     }
-    store_out(p.out, static_cast<int64_t>(g * REP + r) * kHd + tid, O / L, p.bf16 != 0);
+    store_out(p.out, static_cast<int64_t>(g * REP + sp) * kHd + tid, O / L, p.bf16 != 0);
   }
-  cl.sync();  // no CTA leaves while another still reads its shared memory
 }
 
 template <int REP>
