@@ -333,7 +333,7 @@ int rb_add_layernorm(const rb_add_ln* ln, int dtype, int flags, void* stream);
  *   in `dtype` (RB_F16 / RB_BF16); *pos on the device (int64), 0 <= *pos < cache_len, else nothing is written
  *   and the RB_DEVERR_ARG bit of the device error word is set. head_dim == 128, rep = n_q_heads / n_kv_heads
  *   in 1..8, n_kv_heads <= 64. Scores, softmax and the weighted sum are fp32.
- *   Where the device can schedule them, one thread-block cluster of 16 CTAs per key-value head splits the slots
+ *   Where the device can schedule them, one thread-block cluster of 8 CTAs of 8 warps per key-value head splits the slots
  *   and merges its splits through distributed shared memory (the workspace is then untouched); otherwise, or
  *   with RB_FLAG_ATTN_TICKET, about SMs / n_kv_heads CTAs per head merge through fp32 partials in the workspace.
  *   ws: rb_attn_decode_workspace(...) bytes of device memory, 16-byte aligned; its first 256 bytes (per-head

@@ -126,10 +126,14 @@ __device__ __forceinline__ uint2 ld_row8(const uint8_t* p) {
 // the cluster's merge through distributed shared memory, instead of the global partials and the ticket.
 // Returns the number of splits with slots (the same in every CTA of the launch), or -1 for a position outside
 // the cache (nothing written).
-template <int REP, bool kLean, bool kCoherent = false, bool kPre = false, bool kCluster = false>
+// W: warps of the CTA (kWarps, or more in the cluster form: threads past the first kHd take part in the slots but
+// not in the CTA's merge).
+template <int REP, bool kLean, bool kCoherent = false, bool kPre = false, bool kCluster = false, int W = kWarps>
 __device__ int attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id, float (*sm_m)[REP],
                         float (*sm_l)[REP], float (*sm_o)[REP][kHd], int* is_last, float* cml = nullptr) {
   static_assert(!((kPre || kCluster) && (kLean || kCoherent)), "the early loads are the standalone kernel's");
+  static_assert(W == kWarps || kCluster, "other CTA widths only in the cluster form");
+  static_assert(W >= kWarps, "a merge thread per dimension");
   const int warp = tid >> 5, lane = tid & 31;
   const bool bf = p.bf16 != 0;
   uint2 qraw[REP];  // issued together with the position load: one round trip for both
@@ -146,7 +150,7 @@ __device__ int attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id,
     return -1;
   }
   const int64_t n = pos + 1;
-  const int64_t ch = ((n + p.nsplit - 1) / p.nsplit + kWarps * kStep - 1) / (kWarps * kStep) * (kWarps * kStep);
+  const int64_t ch = ((n + p.nsplit - 1) / p.nsplit + W * kStep - 1) / (W * kStep) * (W * kStep);
   const int active = static_cast<int>((n + ch - 1) / ch);  // splits with slots; the others leave at once
   if (sp >= active) return active;
   const int64_t start = static_cast<int64_t>(sp) * ch, end = start + ch < n ? start + ch : n;
@@ -169,7 +173,7 @@ __device__ int attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id,
        // half of the 256-byte row); a plain prefetch, nothing to wait for
       const int j = lane >> 2;
       const uint8_t* line = ((lane >> 1) & 1 ? vb : kb) - lane * 8 + (lane & 1) * 128;
-      for (int64_t t = t0 + kWarps * kStep; t < lim; t += kWarps * kStep)
+      for (int64_t t = t0 + W * kStep; t < lim; t += W * kStep)
         if (t + j < lim) asm volatile("prefetch.global.L2 [%0];" ::"l"(line + (t + j) * kHd * 2));
     }
     griddep_wait();  // q and the position's slot come from the previous kernel
@@ -198,7 +202,7 @@ __device__ int attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id,
   }
   const int jl = lane >> 2;  // the slot of the step whose score this lane ends up holding
   if constexpr (kLean) {  // one step's rows at a time, keys unpacked per head: fits 128 registers
-    for (int64_t t0 = start + warp * kStep; t0 < end; t0 += kWarps * kStep) {
+    for (int64_t t0 = start + warp * kStep; t0 < end; t0 += W * kStep) {
       uint2 kr[kStep], vr[kStep];
 #pragma unroll
       for (int j = 0; j < kStep; ++j) {
@@ -221,9 +225,9 @@ __device__ int attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id,
     }
   } else {
     // kr / vr: this step's K and V rows (loaded above); the next step's are loaded before this one's math
-    for (int64_t t0 = start + warp * kStep; t0 < end; t0 += kWarps * kStep) {
+    for (int64_t t0 = start + warp * kStep; t0 < end; t0 += W * kStep) {
       uint2 kn[kStep], vn[kStep];
-      load_rows(t0 + kWarps * kStep, kn, vn, end);  // past the end: nothing loaded
+      load_rows(t0 + W * kStep, kn, vn, end);  // past the end: nothing loaded
       float kf[kStep][4];
   #pragma unroll
       for (int j = 0; j < kStep; ++j) unpack4(kr[j], bf, kf[j]);
@@ -255,16 +259,17 @@ __device__ int attn_cta(const AttnParams& p, int g, int sp, int tid, int bar_id,
     }
     *reinterpret_cast<float4*>(&sm_o[warp][r][4 * lane]) = make_float4(o[r][0], o[r][1], o[r][2], o[r][3]);
   }
-  named_bar_sync(bar_id, kThreads);
+  named_bar_sync(bar_id, W * 32);
+  if (W > kWarps && tid >= kHd) return active;  // the CTA's merge: one thread per dimension
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w][r]);
+    for (int w = 0; w < W; ++w) M = fmaxf(M, sm_m[w][r]);
     float O = 0.f, L = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
+      for (int w = 0; w < W; ++w) {
         const float e = __expf(sm_m[w][r] - M);
         O = fmaf(e, sm_o[w][r][tid], O);
         L = fmaf(e, sm_l[w][r], L);

@@ -19,8 +19,8 @@
 // the launch before it (the layer's input launch, which writes only q and the position's slot); q and that slot
 // are read after the wait.
 //
-// Cluster form (the default where the device can co-schedule it): one cluster of kClusterSplits CTAs per
-// key-value head. Each CTA stores its merged partial of query head r straight into the shared memory of CTA r of
+// Cluster form (the default where the device can co-schedule it): one cluster of kClusterSplits CTAs of
+// kClusterWarps warps per key-value head. Each CTA stores its merged partial of query head r straight into the shared memory of CTA r of
 // the cluster (distributed shared-memory stores); after one cluster barrier (release / acquire) CTA r merges head r
 // from its own shared memory and writes it. No global partials, no ticket, no workspace traffic.
 #include <atomic>
@@ -34,17 +34,25 @@ namespace rb {
 
 namespace attn {
 
+// Splits per key-value head = CTAs per cluster, and warps per CTA: 8 x 8 measured faster than 16 x 4 (same warps
+// per head and slots per warp, half the SMs, so more of the next launch's CTAs start beside it) and needs no
+// non-portable cluster size.
 #ifndef RB_ATTN_CLUSTER
-#define RB_ATTN_CLUSTER 16
+#define RB_ATTN_CLUSTER 8
 #endif
-constexpr int kClusterSplits = RB_ATTN_CLUSTER;  // splits per key-value head = CTAs per cluster (16: non-portable)
+constexpr int kClusterSplits = RB_ATTN_CLUSTER;
+#ifndef RB_ATTN_CLUSTER_WARPS
+#define RB_ATTN_CLUSTER_WARPS 8
+#endif
+constexpr int kClusterWarps = RB_ATTN_CLUSTER_WARPS;  // warps per CTA of the cluster form
+constexpr int kClusterThreads = kClusterWarps * 32;
 
 template <int REP>
-__global__ void __launch_bounds__(kThreads) attn_cluster_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kClusterThreads) attn_cluster_kernel(const __grid_constant__ AttnParams p) {
   static_assert(REP <= kClusterSplits, "one merging CTA per query head of the group");
   namespace cg = cooperative_groups;
-  __shared__ float sm_m[kWarps][REP], sm_l[kWarps][REP];
-  __shared__ __align__(16) float sm_o[kWarps][REP][kHd];
+  __shared__ float sm_m[kClusterWarps][REP], sm_l[kClusterWarps][REP];
+  __shared__ __align__(16) float sm_o[kClusterWarps][REP][kHd];
   __shared__ float cml[2 * REP];
   __shared__ int is_last;
   // the merging CTA's inbox (CTA r merges query head r of the group): every split's accumulator, maximum and sum
@@ -59,15 +67,16 @@ __global__ void __launch_bounds__(kThreads) attn_cluster_kernel(const __grid_con
   const int g = blockIdx.x / kClusterSplits, sp = static_cast<int>(cl.block_rank()), tid = threadIdx.x;
   int active;
   if (p.pre) {
-    active = attn_cta<REP, false, false, true, true>(p, g, sp, tid, 0, sm_m, sm_l, sm_o, &is_last, cml);
+    active = attn_cta<REP, false, false, true, true, kClusterWarps>(p, g, sp, tid, 0, sm_m, sm_l, sm_o, &is_last, cml);
   } else {
     griddep_wait();
-    active = attn_cta<REP, false, false, false, true>(p, g, sp, tid, 0, sm_m, sm_l, sm_o, &is_last, cml);
+    active = attn_cta<REP, false, false, false, true, kClusterWarps>(p, g, sp, tid, 0, sm_m, sm_l, sm_o, &is_last,
+                                                                     cml);
   }
   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   // active <= 1: the position is outside the cache, or one split wrote the outputs. Otherwise every split with
   // slots pushes its partial of head r into CTA r's inbox (each thread its own column, written by itself above).
-  if (active > 1 && sp < active) {
+  if (active > 1 && sp < active && tid < kHd) {
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
       cl.map_shared_rank(&in_o[0][0], r)[sp * kHd + tid] = sm_o[0][r][tid];
@@ -79,7 +88,7 @@ __global__ void __launch_bounds__(kThreads) attn_cluster_kernel(const __grid_con
   }
   cl.sync();  // phase 2 (release / acquire): the pushed partials are visible; no shared-memory access crosses CTAs
               // after it, so every CTA may leave
-  if (active > 1 && sp < REP) {
+  if (active > 1 && sp < REP && tid < kHd) {
     float M = in_m[0];
 #pragma unroll
     for (int s = 1; s < kClusterSplits; ++s)
@@ -137,7 +146,7 @@ bool cluster_ok(int dev) {
         cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(kClusterSplits);
-      cfg.blockDim = dim3(kThreads);
+      cfg.blockDim = dim3(kClusterThreads);
       cudaLaunchAttribute at[1];
       at[0].id = cudaLaunchAttributeClusterDimension;
       at[0].val.clusterDim.x = kClusterSplits;
@@ -163,7 +172,7 @@ cudaError_t launch_rep(AttnParams p, int nkv, int num_sms, int flags, cudaStream
   p.pl = p.pm + static_cast<int64_t>(nkv) * REP * p.nsplit;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nkv * p.nsplit);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(cluster ? kClusterThreads : kThreads);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
